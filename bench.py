@@ -1,0 +1,425 @@
+"""Headline benchmark: 4096^3 BF16 GEMM on B200.
+
+Metric: "4096³ BF16 GEMM median µs & TFLOP/s (% BF16 peak) vs
+same-run cuBLAS; evals/sec @1–8 GPU".  ``value`` is TFLOP/s of the whole job:
+N GPUs each run the same GEMM (one candidate evaluation per GPU, no
+collective on the data path: weak scaling); value = N * 2MNK / max-over-ranks
+median launch time.
+
+Timing protocol: W warm-up launches, then K steps; each step flushes L2
+(writes a 512 MiB buffer; the 64 MiB of inputs would otherwise stay
+L2-resident) and times one launch with a CUDA event pair on the launching
+stream.  Same protocol, same run, for cuBLAS (torch.matmul).
+
+``--impl reference`` times the reference's CPU path for this workload
+(torch CPU BF16 matmul, all host threads) on rank 0 and prints the same line.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "gpu-kernel-mcts_b200"))
+sys.path.insert(0, str(ROOT))
+
+METRIC = "4096³ BF16 GEMM median µs & TFLOP/s (% BF16 peak) vs same-run cuBLAS; evals/sec @1–8 GPU"
+UNIT = "TFLOP/s"
+M = N = K = 4096
+FLOPS = 2.0 * M * N * K
+L2_FLUSH_BYTES = 512 << 20
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def parse_args() -> argparse.Namespace:
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=100)
+    p.add_argument("--warmup", type=int, default=20)
+    p.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    p.add_argument("--b-layout", choices=("row", "col"), default="row",
+                   help="row: BASELINE config (A/B row-major); col: the reference contract")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-e2e", action="store_true")
+    return p.parse_args()
+
+
+def load_peaks() -> tuple[dict, str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        return json.loads(path.read_text()), "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def profiled_traffic() -> float | None:
+    """DRAM bytes per launch of the GEMM kernel from the committed ncu summary."""
+    path = ROOT / "profiles" / "gemm_tcgen05_4096.md"
+    if not path.exists():
+        return None
+    for line in path.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].strip())
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """Samples nvidia-smi SM clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("clocks.sm", "clocks.max.sm", "power.draw", "clocks_event_reasons.active",
+              "clocks_event_reasons.hw_slowdown", "clocks_event_reasons.hw_thermal_slowdown",
+              "clocks_event_reasons.sw_thermal_slowdown", "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int) -> None:
+        self.device_index = device_index
+        self.samples: list[list[str]] = []
+        self._stop = threading.Event()
+        self._thread = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self) -> None:
+        cmd = ["nvidia-smi", f"--query-gpu={','.join(self.FIELDS)}", "--format=csv,noheader,nounits",
+               "-i", str(self.device_index)]
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(cmd, capture_output=True, text=True, timeout=5).stdout.strip()
+                if out:
+                    self.samples.append([v.strip() for v in out.split(",")])
+            except (OSError, subprocess.SubprocessError):
+                return
+            self._stop.wait(0.1)
+
+    def __enter__(self):
+        self._thread.start()
+        return self
+
+    def __exit__(self, *exc) -> None:
+        self._stop.set()
+        self._thread.join(timeout=10)
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"], "samples": 0}
+        def num(v):
+            try:
+                return float(v)
+            except ValueError:
+                return None
+        sm = [num(s[0]) for s in self.samples if num(s[0]) is not None]
+        mx = [num(s[1]) for s in self.samples if num(s[1]) is not None]
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({name for s in self.samples for name, v in zip(names, s[4:8]) if v.strip() == "Active"})
+        return {
+            "sm_mhz": statistics.median(sm) if sm else None,
+            "sm_max_mhz": max(mx) if mx else None,
+            "reasons": reasons,
+            "samples": len(self.samples),
+            "power_w_max": max((num(s[2]) or 0.0) for s in self.samples),
+        }
+
+
+# ---------------------------------------------------------------- reference arm
+
+
+def cpu_matmul_tflops(seconds: float, threads: int | None = None) -> dict:
+    """The reference's CPU path, torch CPU BF16 matmul,
+    on a bounded row-sample of the 4096^3 workload, repeated for ~`seconds`."""
+    import torch
+
+    from oracle import oracle
+
+    if threads:
+        torch.set_num_threads(threads)
+    rows = 256
+    a, b = oracle.randn_inputs(M, N, K, seed=0, b_layout="row")
+    sample_a = a[:rows].contiguous()
+    torch.matmul(sample_a, b)  # warm-up
+    # Grow the sample until one call takes >= 0.2 s (or covers all of M).
+    while True:
+        t0 = time.perf_counter()
+        torch.matmul(sample_a, b)
+        dt = time.perf_counter() - t0
+        if dt >= 0.2 or rows >= M:
+            break
+        rows = min(M, rows * 2)
+        sample_a = a[:rows].contiguous()
+    times = []
+    start = time.perf_counter()
+    while time.perf_counter() - start < seconds and len(times) < 1000:
+        t0 = time.perf_counter()
+        torch.matmul(sample_a, b)
+        times.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    return {
+        "value": 2.0 * rows * N * K / med / 1e12,
+        "unit": UNIT,
+        "cores": torch.get_num_threads(),
+        "rows": rows,
+        "median_s": med,
+        "calls": len(times),
+    }
+
+
+def run_reference(args: argparse.Namespace) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import torch
+
+    from oracle import oracle
+
+    cores = len(os.sched_getaffinity(0))
+    torch.set_num_threads(cores)
+    a, b = oracle.randn_inputs(M, N, K, seed=0, b_layout="row")
+    # Step = one row-sample of the workload sized to ~0.25 s of CPU work.
+    rows = 128
+    sample = a[:rows].contiguous()
+    torch.matmul(sample, b)
+    while rows < M:
+        t0 = time.perf_counter()
+        torch.matmul(sample, b)
+        if time.perf_counter() - t0 >= 0.25:
+            break
+        rows = min(M, rows * 2)
+        sample = a[:rows].contiguous()
+    for _ in range(args.warmup):
+        torch.matmul(sample, b)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        torch.matmul(sample, b)
+        times.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    value = 2.0 * rows * N * K / med / 1e12
+    sample_desc = (f"torch CPU BF16 matmul of rows [0,{rows}) of the 4096^3 N(0,1) workload "
+                   f"(A[{rows},4096] @ B[4096,4096] row-major), median of {args.steps}")
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": value,
+        "unit": UNIT,
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": med * 1e3,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic: torch.randn seed 0 cast to bf16",
+        "config": {"workload": "bf16_gemm_4096", "M": M, "N": N, "K": K, "b_layout": "row",
+                   "sample_rows": rows, "parallelism": "cpu"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": torch.get_num_threads(),
+                         "kind": "reference", "sample": sample_desc},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "gpu_launches": 0,
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------- our arm
+
+
+def time_launches(fn, steps: int, stream, flush) -> list[float]:
+    """Per-launch event timing (µs) with an L2 flush before each launch."""
+    import torch
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    stops = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    with torch.cuda.stream(stream):
+        for i in range(steps):
+            flush.fill_(i & 0xFF)
+            starts[i].record(stream)
+            fn()
+            stops[i].record(stream)
+    stream.synchronize()
+    return [s.elapsed_time(e) * 1e3 for s, e in zip(starts, stops)]
+
+
+def run_ours(args: argparse.Namespace) -> None:
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", device_id=device, timeout=timedelta(seconds=300))
+
+    from kernel_mcts_b200 import _native
+    from kernel_mcts_b200 import gemm as kg
+    from oracle import oracle
+
+    layout = args.b_layout
+    a_cpu, b_cpu = oracle.randn_inputs(M, N, K, seed=0, b_layout=layout)
+    a, b = a_cpu.to(device), b_cpu.to(device)
+    c = torch.empty((M, N), dtype=torch.bfloat16, device=device)
+    c_ref = torch.empty_like(c)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    stream = torch.cuda.Stream(device)
+    cfg = _native.default_config()
+    status = torch.zeros(1, dtype=torch.int32, device=device)
+
+    def ours():
+        kg.bf16_gemm(a, b, out=c, b_layout=layout, config=cfg, stream=stream, status=status)
+
+    b_for_torch = b if layout == "row" else b.T
+
+    def cublas():
+        torch.matmul(a, b_for_torch, out=c_ref)
+
+    # Warm-up (untimed).
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 3)):
+            ours()
+            cublas()
+    stream.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+        torch.cuda.synchronize(device)
+
+    with ClockSampler(local_rank) as clocks:
+        barrier()
+        launches0 = _native.launch_count()
+        ours_us = time_launches(ours, args.steps, stream, flush)
+        launches = _native.launch_count() - launches0
+        barrier()
+    cublas_us = time_launches(cublas, args.steps, stream, flush)
+    barrier()
+    if int(status.item()) != 0:
+        raise RuntimeError(f"device status {int(status.item()):#x}")
+
+    # Untimed correctness of the measured kernel against same-run cuBLAS.
+    parity = kg.compare(c, c_ref, stream=stream).as_dict()
+
+    med_ours = statistics.median(ours_us)
+    med_cublas = statistics.median(cublas_us)
+    mean_ours = statistics.fmean(ours_us)
+    t = torch.tensor([med_ours, med_cublas, mean_ours], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    med_ours, med_cublas, mean_ours = (float(v) for v in t.tolist())
+
+    # End-to-end through the public API with host buffers: pinned H2D of A and
+    # B, the GEMM, D2H of C — all inside the event-timed region.
+    e2e = None
+    if not args.no_e2e:
+        ha = a_cpu.pin_memory()
+        hb = b_cpu.pin_memory()
+        hc = torch.empty((M, N), dtype=torch.bfloat16).pin_memory()
+
+        def end_to_end():
+            a.copy_(ha, non_blocking=True)
+            b.copy_(hb, non_blocking=True)
+            kg.bf16_gemm(a, b, out=c, b_layout=layout, config=cfg, stream=stream, status=status)
+            hc.copy_(c, non_blocking=True)
+
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                end_to_end()
+        stream.synchronize()
+        e2e_steps = max(5, min(args.steps, 30))
+        e2e_us = time_launches(end_to_end, e2e_steps, stream, flush)
+        e2e_med = statistics.median(e2e_us)
+        te = torch.tensor([e2e_med], dtype=torch.float64, device=device)
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        e2e_med = float(te.item())
+        e2e = {
+            "value": world * FLOPS / (e2e_med * 1e-6) / 1e12,
+            "unit": UNIT,
+            "h2d_bytes_per_step": int(a.numel() * 2 + b.numel() * 2),
+            "d2h_bytes_per_step": int(c.numel() * 2),
+            "median_us": e2e_med,
+            "steps": e2e_steps,
+        }
+
+    if rank == 0:
+        peaks, peaks_kind = load_peaks()
+        achieved = FLOPS / (mean_ours * 1e-6) / 1e12
+        peak = float(peaks["bf16_tflops"])
+        value = world * FLOPS / (med_ours * 1e-6) / 1e12
+        cpu = None
+        if not args.no_cpu_baseline and world == 1:
+            cpu_info = cpu_matmul_tflops(seconds=12.0)
+            cpu = {
+                "value": cpu_info["value"],
+                "unit": UNIT,
+                "cores": cpu_info["cores"],
+                "kind": "reference",
+                "sample": (f"torch CPU BF16 matmul (the reference's CPU path) on rows [0,{cpu_info['rows']}) "
+                           f"of the 4096^3 N(0,1) workload, median of {cpu_info['calls']} calls over ~12 s"),
+            }
+        line = {
+            "metric": METRIC,
+            "value": value,
+            "unit": UNIT,
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": med_ours / 1e3,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic: torch.randn seed 0 (CPU generator) cast to bf16",
+            "config": {
+                "workload": "bf16_gemm_4096 (BASELINE config 2: M=N=K=4096, N(0,1) seed 0)",
+                "M": M, "N": N, "K": K,
+                "b_layout": layout,
+                "kernel": "tcgen05 persistent 128x%dx%d, %d stages" % (cfg.tile_n, cfg.tile_k, cfg.stages),
+                "parallelism": f"replicas x{world} (one evaluation per GPU, no collective)",
+                "timing": "per-launch CUDA events on the launching stream, median",
+                "l2": "flushed before every timed launch (512 MiB write)",
+            },
+            "median_us": med_ours,
+            "cublas_median_us": med_cublas,
+            "speedup_vs_cublas": med_cublas / med_ours,
+            "pct_bf16_peak": 100.0 * (FLOPS / (med_ours * 1e-6) / 1e12) / peak,
+            "parity_vs_cublas": parity,
+            "roofline": {
+                "bound": "tensor",
+                "achieved": achieved,
+                "peak": peak,
+                "unit": "TFLOP/s",
+                "frac": achieved / peak,
+                "traffic": profiled_traffic(),
+                "peak_source": f"{peaks_kind} bf16_tflops (burst; kernel timed alone)",
+                "algorithmic_flops_per_launch": FLOPS,
+            },
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": launches,
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+        dist.destroy_process_group()
+
+
+def main() -> None:
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,191 @@
+"""ctypes binding of libkmcts_gemm_sm100.so (C ABI in include/kmcts_gemm.h).
+
+There is no fallback: if the library is missing or fails to load, every call
+raises :class:`NativeLibraryError`.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+from .build import LIBRARY
+
+KMCTS_OK = 0
+KMCTS_EHANDLE = 1
+KMCTS_EGEMM = 2
+KMCTS_ESYNC = 3
+KMCTS_EINVAL = 4
+KMCTS_ESMEM = 5
+KMCTS_ETIMEOUT = 6
+KMCTS_ENOTSUP = 7
+
+ERROR_NAMES = {
+    KMCTS_OK: "ok",
+    KMCTS_EHANDLE: "handle",
+    KMCTS_EGEMM: "gemm_launch",
+    KMCTS_ESYNC: "synchronize",
+    KMCTS_EINVAL: "invalid_argument",
+    KMCTS_ESMEM: "shared_memory",
+    KMCTS_ETIMEOUT: "device_wait_timeout",
+    KMCTS_ENOTSUP: "not_supported",
+}
+
+B_COL = 0
+B_ROW = 1
+
+KERNEL_AUTO = 0
+KERNEL_TCGEN05 = 1
+KERNEL_SIMT = 2
+
+#: Every symbol include/kmcts_gemm.h declares.
+EXPORTED_SYMBOLS = (
+    "kmcts_default_config",
+    "kmcts_bf16_gemm",
+    "kmcts_bf16_gemm_ex",
+    "kmcts_config_legal",
+    "kmcts_config_smem_bytes",
+    "kmcts_version",
+    "kmcts_compare_workspace_bytes",
+    "kmcts_bf16_compare",
+    "kmcts_launch_count",
+)
+
+
+class NativeLibraryError(RuntimeError):
+    """The sm_100a library is not built or cannot be loaded."""
+
+
+class KmctsError(RuntimeError):
+    """A C-ABI call returned a non-zero status."""
+
+    def __init__(self, code: int, operation: str) -> None:
+        self.code = code
+        self.operation = operation
+        super().__init__(f"{operation} failed: {ERROR_NAMES.get(code, code)} ({code})")
+
+
+class GemmConfig(ctypes.Structure):
+    """Mirror of ``kmcts_gemm_config``."""
+
+    _fields_ = [
+        ("tile_m", ctypes.c_int32),
+        ("tile_n", ctypes.c_int32),
+        ("tile_k", ctypes.c_int32),
+        ("stages", ctypes.c_int32),
+        ("cluster_m", ctypes.c_int32),
+        ("cluster_n", ctypes.c_int32),
+        ("persistent", ctypes.c_int32),
+        ("raster_group", ctypes.c_int32),
+        ("kernel", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
+        ("wait_limit_ns", ctypes.c_int64),
+    ]
+
+    def as_dict(self) -> dict[str, int]:
+        return {name: int(getattr(self, name)) for name, _ in self._fields_ if name != "reserved"}
+
+
+class CompareResult(ctypes.Structure):
+    """Mirror of ``kmcts_compare_result``."""
+
+    _fields_ = [
+        ("maximum_error", ctypes.c_double),
+        ("mean_error", ctypes.c_double),
+        ("count", ctypes.c_int64),
+        ("n_tolerance_fail", ctypes.c_int64),
+        ("n_nonfinite", ctypes.c_int64),
+        ("ulp_hist", ctypes.c_int64 * 4),
+        ("max_ulp", ctypes.c_int32),
+        ("success", ctypes.c_int32),
+    ]
+
+
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+
+
+def library_path() -> Path:
+    return LIBRARY
+
+
+def load() -> ctypes.CDLL:
+    """Loads (once) and returns the native library."""
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not LIBRARY.exists():
+            raise NativeLibraryError(
+                f"{LIBRARY} is not built; run kernel_mcts_b200.build.build_all() (nvcc, sm_100a)"
+            )
+        try:
+            lib = ctypes.CDLL(str(LIBRARY))
+        except OSError as error:
+            raise NativeLibraryError(f"cannot load {LIBRARY}: {error}") from error
+        vp, i32, i64 = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64
+        lib.kmcts_default_config.argtypes = [ctypes.POINTER(GemmConfig)]
+        lib.kmcts_default_config.restype = i32
+        lib.kmcts_bf16_gemm.argtypes = [vp, vp, vp, i32, i32, i32]
+        lib.kmcts_bf16_gemm.restype = i32
+        lib.kmcts_bf16_gemm_ex.argtypes = [
+            vp, vp, vp, i32, i32, i32, i32, ctypes.POINTER(GemmConfig), vp, vp,
+        ]
+        lib.kmcts_bf16_gemm_ex.restype = i32
+        lib.kmcts_config_legal.argtypes = [
+            ctypes.POINTER(GemmConfig), i32, i32, i32, i32, ctypes.c_char_p, i32,
+        ]
+        lib.kmcts_config_legal.restype = i32
+        lib.kmcts_config_smem_bytes.argtypes = [ctypes.POINTER(GemmConfig), i32]
+        lib.kmcts_config_smem_bytes.restype = i64
+        lib.kmcts_version.argtypes = []
+        lib.kmcts_version.restype = ctypes.c_char_p
+        lib.kmcts_compare_workspace_bytes.argtypes = []
+        lib.kmcts_compare_workspace_bytes.restype = ctypes.c_size_t
+        lib.kmcts_bf16_compare.argtypes = [
+            vp, vp, i64, ctypes.c_double, ctypes.c_double, vp, vp, ctypes.POINTER(CompareResult),
+        ]
+        lib.kmcts_bf16_compare.restype = i32
+        lib.kmcts_launch_count.argtypes = []
+        lib.kmcts_launch_count.restype = i64
+        _lib = lib
+        return lib
+
+
+def default_config() -> GemmConfig:
+    cfg = GemmConfig()
+    check(load().kmcts_default_config(ctypes.byref(cfg)), "kmcts_default_config")
+    return cfg
+
+
+def make_config(**overrides: int) -> GemmConfig:
+    cfg = default_config()
+    for name, value in overrides.items():
+        if not hasattr(cfg, name):
+            raise ValueError(f"unknown config field {name!r}")
+        setattr(cfg, name, int(value))
+    return cfg
+
+
+def config_legal(cfg: GemmConfig, m: int, n: int, k: int, b_layout: int = B_COL) -> tuple[int, str]:
+    why = ctypes.create_string_buffer(256)
+    code = load().kmcts_config_legal(ctypes.byref(cfg), m, n, k, b_layout, why, len(why))
+    return int(code), why.value.decode()
+
+
+def config_smem_bytes(cfg: GemmConfig, b_layout: int = B_COL) -> int:
+    return int(load().kmcts_config_smem_bytes(ctypes.byref(cfg), b_layout))
+
+
+def version() -> str:
+    return load().kmcts_version().decode()
+
+
+def launch_count() -> int:
+    return int(load().kmcts_launch_count())
+
+
+def check(code: int, operation: str) -> None:
+    if code != KMCTS_OK:
+        raise KmctsError(int(code), operation)

@@ -1,0 +1,134 @@
+// extern "C" entry points of libkmcts_gemm_sm100.so (declared in include/kmcts_gemm.h).
+#include <cudaTypedefs.h>
+
+#include <cstring>
+#include <mutex>
+
+#include "kmcts_internal.h"
+
+namespace kmcts {
+
+std::atomic<int64_t> g_launches{0};
+
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static std::once_flag once;
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    std::call_once(once, [] {
+        void* entry = nullptr;
+        cudaDriverEntryPointQueryResult query;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &entry, 12000,
+                                             cudaEnableDefault, &query) == cudaSuccess &&
+            query == cudaDriverEntryPointSuccess) {
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(entry);
+        }
+    });
+    return fn;
+}
+
+cudaStream_t as_stream(void* stream) { return static_cast<cudaStream_t>(stream); }
+
+}  // namespace
+
+bool encode_tensor_map_2d(CUtensorMap* map, const void* base, uint64_t dim0, uint64_t dim1,
+                          uint64_t row_stride_bytes, uint32_t box0, uint32_t box1) {
+    auto encode = tensor_map_encoder();
+    if (!encode) return false;
+    const cuuint64_t dims[2] = {dim0, dim1};
+    const cuuint64_t strides[1] = {row_stride_bytes};
+    const cuuint32_t box[2] = {box0, box1};
+    const cuuint32_t element_strides[2] = {1, 1};
+    return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
+                  strides, box, element_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int multiprocessor_count() {
+    static int cached[64] = {};
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess) return 148;
+    if (device >= 0 && device < 64 && cached[device] > 0) return cached[device];
+    int count = 0;
+    if (cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, device) != cudaSuccess ||
+        count <= 0)
+        count = 148;
+    if (device >= 0 && device < 64) cached[device] = count;
+    return count;
+}
+
+}  // namespace kmcts
+
+using namespace kmcts;
+
+extern "C" {
+
+int kmcts_default_config(kmcts_gemm_config* cfg) {
+    if (!cfg) return KMCTS_EINVAL;
+    std::memset(cfg, 0, sizeof(*cfg));
+    cfg->tile_m = 128;
+    cfg->tile_n = 256;
+    cfg->tile_k = 64;
+    cfg->stages = 4;
+    cfg->cluster_m = 1;
+    cfg->cluster_n = 1;
+    cfg->persistent = 1;
+    cfg->raster_group = 8;
+    cfg->kernel = KMCTS_KERNEL_AUTO;
+    cfg->wait_limit_ns = 0;
+    return KMCTS_OK;
+}
+
+const char* kmcts_version(void) { return "kmcts_gemm_sm100 0.1.0 (sm_100a tcgen05)"; }
+
+int64_t kmcts_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int64_t kmcts_config_smem_bytes(const kmcts_gemm_config* cfg, int b_layout) {
+    if (!cfg) return 0;
+    return tcgen05_smem_bytes(*cfg, b_layout);
+}
+
+int kmcts_config_legal(const kmcts_gemm_config* cfg, int M, int N, int K, int b_layout, char* why,
+                       int len) {
+    if (!cfg) return KMCTS_EINVAL;
+    return tcgen05_legal(*cfg, M, N, K, b_layout, why, len);
+}
+
+int kmcts_bf16_gemm_ex(const void* A, const void* B, void* C, int M, int N, int K, int b_layout,
+                       const kmcts_gemm_config* cfg, void* stream, int* device_status) {
+    if (M < 0 || N < 0 || K < 0) return KMCTS_EINVAL;
+    if (b_layout != KMCTS_B_COL && b_layout != KMCTS_B_ROW) return KMCTS_EINVAL;
+    if ((M > 0 && N > 0) && (!C || (K > 0 && (!A || !B)))) return KMCTS_EINVAL;
+    kmcts_gemm_config local;
+    if (cfg) {
+        local = *cfg;
+    } else {
+        kmcts_default_config(&local);
+    }
+    cudaStream_t s = as_stream(stream);
+    if (local.kernel == KMCTS_KERNEL_SIMT) return launch_simt(A, B, C, M, N, K, b_layout, s);
+    const int rc = launch_tcgen05(A, B, C, M, N, K, b_layout, local, s, device_status);
+    if (rc == KMCTS_ENOTSUP && local.kernel == KMCTS_KERNEL_AUTO) {
+        return launch_simt(A, B, C, M, N, K, b_layout, s);
+    }
+    return rc;
+}
+
+int kmcts_bf16_gemm(const void* A, const void* B, void* C, int M, int N, int K) {
+    const int rc = kmcts_bf16_gemm_ex(A, B, C, M, N, K, KMCTS_B_COL, nullptr, nullptr, nullptr);
+    if (rc != KMCTS_OK) return rc;
+    if (cudaDeviceSynchronize() != cudaSuccess) return KMCTS_ESYNC;
+    int status = 0;
+    if (take_default_status(nullptr, &status) != KMCTS_OK) return KMCTS_ESYNC;
+    return status == 0 ? KMCTS_OK : KMCTS_ETIMEOUT;
+}
+
+size_t kmcts_compare_workspace_bytes(void) { return compare_workspace_bytes(); }
+
+int kmcts_bf16_compare(const void* C, const void* reference, int64_t count, double rtol,
+                       double atol, void* workspace, void* stream, kmcts_compare_result* out) {
+    return compare_bf16_device(C, reference, count, rtol, atol, workspace, as_stream(stream), out);
+}
+
+}  // extern "C"

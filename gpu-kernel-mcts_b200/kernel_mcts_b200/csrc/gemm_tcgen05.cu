@@ -1,0 +1,485 @@
+// Persistent, warp-specialised BF16 GEMM for sm_100a.
+//
+//   C[M,N] (bf16, row-major) = A[M,K] (bf16, row-major) · B  (FP32 accumulate)
+//
+// This is the B200 replacement for the candidate kernel the reference harness
+// launches (src/kernel_mcts/benchmarks/kernels/bf16_gemm_harness.cu:61-72,
+// root program bf16_gemm_root.cu:8-44): same arithmetic contract, new engine.
+//
+// Per CTA (one per SM when persistent), 192 threads in three roles:
+//   warp 0      TMA producer: one lane streams A/B K-slices into a ring of
+//               `STAGES` 128-byte-swizzled shared-memory stages (full/empty
+//               mbarriers, transaction-byte completion).
+//   warp 1      MMA issuer: owns the TMEM allocation; one lane issues
+//               tcgen05.mma (M=128, N=BN, K=16) into one of two TMEM
+//               accumulators and commits stage releases / accumulator-ready.
+//   warps 2-5   epilogue: tcgen05.ld each 32-lane quarter of the accumulator,
+//               round to BF16 (RNE), stage through swizzled shared memory and
+//               TMA-store.  Two TMEM accumulators let the epilogue of tile i
+//               overlap the main loop of tile i+1.
+// Every wait is bounded (limit_ns); on timeout the kernel records
+// KMCTS_ETIMEOUT in *status, drains its own copies and MMAs, frees TMEM and
+// returns.  No TMA multicast is used.
+#include <cuda_bf16.h>
+
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "kmcts_internal.h"
+#include "ptx_sm100.cuh"
+
+namespace kmcts {
+
+__device__ int g_default_status;
+
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kThreads = 192;
+constexpr int kEpilogueWarps = 4;
+constexpr int kStagingBytes = 32 * 128;  // one warp's 32 rows x 64 BF16 columns
+constexpr int kSmemReserve = 2048;       // barriers + 1024-byte alignment slack
+constexpr int kMaxDevices = 64;
+
+// Status codes written to the device status word (low byte = KMCTS_ETIMEOUT,
+// next byte = which role gave up).
+constexpr int kRoleProducer = 1, kRoleMma = 2, kRoleEpilogue = 3, kRoleDrain = 4;
+
+template <int BN, int BK, int STAGES, bool B_MN>
+struct Layout {
+    static constexpr int kABytes = kBM * BK * 2;
+    static constexpr int kBBytes = BN * BK * 2;
+    static constexpr int kStageBytes = kABytes + kBBytes;
+    static constexpr int kStagingOffset = STAGES * kStageBytes;
+    static constexpr int kBarrierOffset = kStagingOffset + kEpilogueWarps * 2 * kStagingBytes;
+    static constexpr int kSmemBytes = kBarrierOffset + kSmemReserve;
+    static constexpr uint32_t kTmemCols = (2 * BN <= 32)    ? 32
+                                          : (2 * BN <= 64)  ? 64
+                                          : (2 * BN <= 128) ? 128
+                                          : (2 * BN <= 256) ? 256
+                                                            : 512;
+    static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "BN must be 64..256, step 64");
+    static_assert(BK == 64 || BK == 128, "BK must be 64 or 128");
+    static_assert(kSmemBytes <= 232448, "shared memory budget exceeded");
+};
+
+struct TileCoord {
+    int m_blk, n_blk;
+};
+
+__device__ __forceinline__ TileCoord tile_coord(int t, int num_m, int num_n, int group) {
+    const int per_group = group * num_n;
+    const int g = t / per_group;
+    const int first_m = g * group;
+    const int rows = min(num_m - first_m, group);
+    const int r = t - g * per_group;
+    return {first_m + r % rows, r / rows};
+}
+
+__device__ __forceinline__ void record_failure(int* status, volatile int* abort, int role) {
+    *abort = 1;
+    atomicCAS(status, 0, KMCTS_ETIMEOUT | (role << 8));
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(uint32_t lo_bits, uint32_t hi_bits) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(__uint_as_float(lo_bits), __uint_as_float(hi_bits));
+    return *reinterpret_cast<uint32_t*>(&v);
+}
+
+template <int BN, int BK, int STAGES, bool B_MN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_bf16_tcgen05(const __grid_constant__ CUtensorMap map_a,
+                      const __grid_constant__ CUtensorMap map_b,
+                      const __grid_constant__ CUtensorMap map_c, int M, int N, int K, int group,
+                      uint64_t limit_ns, int* status) {
+    using L = Layout<BN, BK, STAGES, B_MN>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarrierOffset);
+    uint64_t* empty = full + STAGES;
+    uint64_t* tmem_full = empty + STAGES;
+    uint64_t* tmem_empty = tmem_full + 2;
+    uint64_t* drain = tmem_empty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    volatile int* no_abort = abort + 1;
+
+    if (status == nullptr) status = &g_default_status;
+    const int warp = threadIdx.x / 32;
+    const int lane = threadIdx.x % 32;
+    const int num_m = (M + kBM - 1) / kBM;
+    const int num_n = (N + BN - 1) / BN;
+    const int num_tiles = num_m * num_n;
+    const int num_kb = (K + BK - 1) / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            ptx::mbar_init(&full[s], 1);
+            ptx::mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            ptx::mbar_init(&tmem_full[a], 1);
+            ptx::mbar_init(&tmem_empty[a], kEpilogueWarps);
+        }
+        ptx::mbar_init(drain, 1);
+        *abort = 0;
+        *no_abort = 0;
+        ptx::fence_mbarrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        ptx::prefetch_tensormap(&map_a);
+        ptx::prefetch_tensormap(&map_b);
+        ptx::prefetch_tensormap(&map_c);
+    }
+    if (warp == 1) {
+        ptx::tmem_alloc(tmem_slot, L::kTmemCols);
+        ptx::tmem_relinquish();
+    }
+    ptx::tc_fence_before();
+    __syncthreads();
+    ptx::tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ producer
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t issued = 0, issued_phase = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+                const TileCoord tc = tile_coord(t, num_m, num_n, group);
+                const int m0 = tc.m_blk * kBM;
+                const int n0 = tc.n_blk * BN;
+                for (int kb = 0; kb < num_kb; ++kb) {
+                    if (!ptx::mbar_wait(&empty[stage], phase ^ 1u, limit_ns, abort)) {
+                        record_failure(status, abort, kRoleProducer);
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* sa = smem + stage * L::kStageBytes;
+                    uint8_t* sb = sa + L::kABytes;
+                    ptx::mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
+#pragma unroll
+                    for (int kh = 0; kh < BK / 64; ++kh) {
+                        const int k0 = kb * BK + kh * 64;
+                        ptx::tma_load_2d(sa + kh * (kBM * 128), &map_a, &full[stage], k0, m0);
+                        if constexpr (B_MN) {
+#pragma unroll
+                            for (int nb = 0; nb < BN / 64; ++nb) {
+                                ptx::tma_load_2d(sb + (kh * (BN / 64) + nb) * 8192, &map_b,
+                                                 &full[stage], n0 + nb * 64, k0);
+                            }
+                        } else {
+                            ptx::tma_load_2d(sb + kh * (BN * 128), &map_b, &full[stage], k0, n0);
+                        }
+                    }
+                    issued |= 1u << stage;
+                    issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            // Drain: every load this thread issued lands before the CTA exits.
+            for (int s = 0; s < STAGES; ++s) {
+                if (issued & (1u << s)) {
+                    if (!ptx::mbar_wait(&full[s], (issued_phase >> s) & 1u, limit_ns, no_abort)) {
+                        record_failure(status, abort, kRoleDrain);
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ----------------------------------------------------------------- MMA
+        if (lane == 0) {
+            constexpr uint32_t idesc = ptx::make_idesc_bf16(kBM, BN, B_MN);
+            int stage = 0;
+            uint32_t phase = 0;
+            int local = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++local) {
+                const int acc = local & 1;
+                const uint32_t acc_phase = (local >> 1) & 1;
+                if (!ptx::mbar_wait(&tmem_empty[acc], acc_phase ^ 1u, limit_ns, abort)) {
+                    record_failure(status, abort, kRoleMma);
+                    break;
+                }
+                ptx::tc_fence_after();
+                const uint32_t d_tmem = tmem_base + acc * BN;
+                for (int kb = 0; kb < num_kb; ++kb) {
+                    if (!ptx::mbar_wait(&full[stage], phase, limit_ns, abort)) {
+                        record_failure(status, abort, kRoleMma);
+                        ok = false;
+                        break;
+                    }
+                    ptx::tc_fence_after();
+                    const uint32_t sa = ptx::smem_addr(smem + stage * L::kStageBytes);
+                    const uint32_t sb = sa + L::kABytes;
+#pragma unroll
+                    for (int kk = 0; kk < BK / 16; ++kk) {
+                        const int kh = kk / 4;  // which 64-wide K half of the stage
+                        const int kq = kk % 4;  // 16-element step inside it
+                        const uint64_t adesc =
+                            ptx::make_sw128_desc(sa + kh * (kBM * 128) + kq * 32, 16, 1024);
+                        uint64_t bdesc;
+                        if constexpr (B_MN) {
+                            bdesc = ptx::make_sw128_desc(sb + kh * (BN / 64) * 8192 + kq * 2048,
+                                                         8192, 1024);
+                        } else {
+                            bdesc = ptx::make_sw128_desc(sb + kh * (BN * 128) + kq * 32, 16, 1024);
+                        }
+                        ptx::umma_bf16(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
+                    }
+                    ptx::umma_commit(&empty[stage]);
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (ok) ptx::umma_commit(&tmem_full[acc]);
+            }
+            // Drain: all MMAs issued by this thread complete before TMEM is freed.
+            ptx::umma_commit(drain);
+            if (!ptx::mbar_wait(drain, 0, limit_ns, no_abort)) {
+                record_failure(status, abort, kRoleDrain);
+            }
+        }
+    } else {
+        // ------------------------------------------------------------ epilogue
+        const int quarter = warp % 4;  // TMEM lanes this warp may access
+        const int e = warp - 2;
+        uint8_t* staging = smem + L::kStagingOffset + e * 2 * kStagingBytes;
+        int local = 0;
+        int chunk_count = 0;
+        for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
+            const TileCoord tc = tile_coord(t, num_m, num_n, group);
+            const int m0 = tc.m_blk * kBM;
+            const int n0 = tc.n_blk * BN;
+            const int acc = local & 1;
+            const uint32_t acc_phase = (local >> 1) & 1;
+            bool ok = ptx::mbar_wait(&tmem_full[acc], acc_phase, limit_ns, abort);
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) {
+                if (lane == 0) record_failure(status, abort, kRoleEpilogue);
+                break;
+            }
+            ptx::tc_fence_after();
+            const uint32_t row_addr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                                      static_cast<uint32_t>(acc * BN);
+#pragma unroll 1
+            for (int c = 0; c < BN / 64; ++c) {
+                uint32_t lo[32], hi[32];
+                ptx::tmem_ld_32x32b_x32(row_addr + c * 64, lo);
+                ptx::tmem_ld_32x32b_x32(row_addr + c * 64 + 32, hi);
+                ptx::tmem_wait_ld();
+                if (c == BN / 64 - 1) {
+                    ptx::tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) ptx::mbar_arrive(&tmem_empty[acc]);
+                }
+                uint32_t packed[32];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) packed[i] = pack_bf16x2(lo[2 * i], lo[2 * i + 1]);
+#pragma unroll
+                for (int i = 0; i < 16; ++i) packed[16 + i] = pack_bf16x2(hi[2 * i], hi[2 * i + 1]);
+                uint8_t* buf = staging + (chunk_count & 1) * kStagingBytes;
+                if (lane == 0) ptx::bulk_wait_group_read<1>();
+                __syncwarp();
+                uint8_t* row = buf + lane * 128;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const int phys = j ^ (lane & 7);
+                    *reinterpret_cast<uint4*>(row + phys * 16) =
+                        make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2],
+                                   packed[4 * j + 3]);
+                }
+                ptx::fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    ptx::tma_store_2d(&map_c, buf, n0 + c * 64, m0 + quarter * 32);
+                    ptx::bulk_commit_group();
+                }
+                ++chunk_count;
+            }
+        }
+        if (lane == 0) ptx::bulk_wait_group<0>();
+        __syncwarp();
+    }
+
+    ptx::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        ptx::tc_fence_after();
+        ptx::tmem_dealloc(tmem_base, L::kTmemCols);
+    }
+}
+
+// ------------------------------------------------------------------ host side
+
+template <int BN, int BK, int STAGES, bool B_MN>
+int launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, int M,
+                   int N, int K, int group, bool persistent, uint64_t limit_ns,
+                   cudaStream_t stream, int* status) {
+    using L = Layout<BN, BK, STAGES, B_MN>;
+    auto kernel = gemm_bf16_tcgen05<BN, BK, STAGES, B_MN>;
+    // The shared-memory opt-in is per device; set it once on each.
+    static std::mutex mu;
+    static bool configured[kMaxDevices] = {};
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kMaxDevices)
+        return KMCTS_EHANDLE;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (!configured[device]) {
+            if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     L::kSmemBytes) != cudaSuccess)
+                return KMCTS_EGEMM;
+            configured[device] = true;
+        }
+    }
+    const int tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
+    int grid = tiles;
+    if (persistent) grid = tiles < multiprocessor_count() ? tiles : multiprocessor_count();
+    kernel<<<grid, kThreads, L::kSmemBytes, stream>>>(ma, mb, mc, M, N, K, group, limit_ns,
+                                                      status);
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return cudaGetLastError() == cudaSuccess ? KMCTS_OK : KMCTS_EGEMM;
+}
+
+using Launcher = int (*)(const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, int, int,
+                         int, int, bool, uint64_t, cudaStream_t, int*);
+
+struct Variant {
+    int bn, bk, stages, b_mn;
+    Launcher fn;
+};
+
+#define KMCTS_VARIANT(BN, BK, ST, MN) {BN, BK, ST, MN, &launch_variant<BN, BK, ST, MN>}
+
+// The compiled schedule space.  Shared-memory budget: stages*(128+BN)*BK*2
+// bytes of operand ring + 32 KB epilogue staging + 2 KB <= 227 KB.
+const Variant kVariants[] = {
+    KMCTS_VARIANT(256, 64, 3, false), KMCTS_VARIANT(256, 64, 4, false),
+    KMCTS_VARIANT(256, 64, 3, true),  KMCTS_VARIANT(256, 64, 4, true),
+    KMCTS_VARIANT(128, 64, 4, false), KMCTS_VARIANT(128, 64, 5, false),
+    KMCTS_VARIANT(128, 64, 6, false), KMCTS_VARIANT(128, 64, 4, true),
+    KMCTS_VARIANT(128, 64, 5, true),  KMCTS_VARIANT(128, 64, 6, true),
+    KMCTS_VARIANT(128, 128, 3, false), KMCTS_VARIANT(128, 128, 3, true),
+    KMCTS_VARIANT(256, 128, 2, false), KMCTS_VARIANT(256, 128, 2, true),
+    KMCTS_VARIANT(192, 64, 4, false), KMCTS_VARIANT(192, 64, 4, true),
+    KMCTS_VARIANT(64, 64, 6, false),  KMCTS_VARIANT(64, 64, 6, true),
+};
+
+const Variant* find_variant(const kmcts_gemm_config& cfg, int b_layout) {
+    for (const Variant& v : kVariants) {
+        if (v.bn == cfg.tile_n && v.bk == cfg.tile_k && v.stages == cfg.stages &&
+            v.b_mn == (b_layout == KMCTS_B_ROW ? 1 : 0)) {
+            return &v;
+        }
+    }
+    return nullptr;
+}
+
+void put_reason(char* why, int len, const char* text) {
+    if (why && len > 0) {
+        std::strncpy(why, text, static_cast<size_t>(len) - 1);
+        why[len - 1] = '\0';
+    }
+}
+
+}  // namespace
+
+int64_t tcgen05_smem_bytes(const kmcts_gemm_config& cfg, int b_layout) {
+    (void)b_layout;
+    if (cfg.tile_m != kBM || cfg.tile_n <= 0 || cfg.tile_k <= 0 || cfg.stages <= 0) return 0;
+    return static_cast<int64_t>(cfg.stages) * (kBM + cfg.tile_n) * cfg.tile_k * 2 +
+           kEpilogueWarps * 2 * kStagingBytes + kSmemReserve;
+}
+
+int tcgen05_legal(const kmcts_gemm_config& cfg, int M, int N, int K, int b_layout, char* why,
+                  int len) {
+    if (b_layout != KMCTS_B_COL && b_layout != KMCTS_B_ROW) {
+        put_reason(why, len, "b_layout must be 0 (column-major) or 1 (row-major)");
+        return KMCTS_EINVAL;
+    }
+    if (cfg.tile_m != kBM) {
+        put_reason(why, len, "tile_m must be 128 (one UMMA M=128 per CTA)");
+        return KMCTS_ENOTSUP;
+    }
+    if (cfg.cluster_m != 1 || cfg.cluster_n != 1) {
+        put_reason(why, len, "clusters other than 1x1 are not built in this version");
+        return KMCTS_ENOTSUP;
+    }
+    const int64_t smem = tcgen05_smem_bytes(cfg, b_layout);
+    if (smem <= 0 || smem > 232448) {
+        put_reason(why, len, "shared memory per CTA exceeds 227 KB");
+        return KMCTS_ESMEM;
+    }
+    if (find_variant(cfg, b_layout) == nullptr) {
+        put_reason(why, len, "schedule (tile_n, tile_k, stages) is not compiled in");
+        return KMCTS_ENOTSUP;
+    }
+    if (cfg.raster_group < 1) {
+        put_reason(why, len, "raster_group must be >= 1");
+        return KMCTS_EINVAL;
+    }
+    if (M < 0 || N < 0 || K < 0) {
+        put_reason(why, len, "negative dimension");
+        return KMCTS_EINVAL;
+    }
+    // TMA: every global row stride must be a multiple of 16 bytes.
+    if (K % 8 != 0 || N % 8 != 0) {
+        put_reason(why, len, "TMA needs K and N to be multiples of 8");
+        return KMCTS_ENOTSUP;
+    }
+    put_reason(why, len, "ok");
+    return KMCTS_OK;
+}
+
+int launch_tcgen05(const void* A, const void* B, void* C, int M, int N, int K, int b_layout,
+                   const kmcts_gemm_config& cfg, cudaStream_t stream, int* device_status) {
+    int rc = tcgen05_legal(cfg, M, N, K, b_layout, nullptr, 0);
+    if (rc != KMCTS_OK) return rc;
+    if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B) |
+         reinterpret_cast<uintptr_t>(C)) &
+        15u) {
+        return KMCTS_ENOTSUP;
+    }
+    if (M == 0 || N == 0) return KMCTS_OK;
+    if (K == 0) {
+        g_launches.fetch_add(1, std::memory_order_relaxed);
+        return cudaMemsetAsync(C, 0, static_cast<size_t>(M) * N * 2, stream) == cudaSuccess
+                   ? KMCTS_OK
+                   : KMCTS_EGEMM;
+    }
+    const Variant* v = find_variant(cfg, b_layout);
+    CUtensorMap ma, mb, mc;
+    bool ok = encode_tensor_map_2d(&ma, A, K, M, static_cast<uint64_t>(K) * 2, 64, kBM);
+    if (b_layout == KMCTS_B_COL) {
+        ok = ok && encode_tensor_map_2d(&mb, B, K, N, static_cast<uint64_t>(K) * 2, 64, v->bn);
+    } else {
+        ok = ok && encode_tensor_map_2d(&mb, B, N, K, static_cast<uint64_t>(N) * 2, 64, 64);
+    }
+    ok = ok && encode_tensor_map_2d(&mc, C, N, M, static_cast<uint64_t>(N) * 2, 64, 32);
+    if (!ok) return KMCTS_EINVAL;
+    const uint64_t limit =
+        cfg.wait_limit_ns > 0 ? static_cast<uint64_t>(cfg.wait_limit_ns) : 2000000000ull;
+    return v->fn(ma, mb, mc, M, N, K, cfg.raster_group, cfg.persistent != 0, limit, stream,
+                 device_status);
+}
+
+int take_default_status(cudaStream_t stream, int* value) {
+    int zero = 0;
+    if (cudaStreamSynchronize(stream) != cudaSuccess) return KMCTS_ESYNC;
+    if (cudaMemcpyFromSymbol(value, g_default_status, sizeof(int)) != cudaSuccess)
+        return KMCTS_ESYNC;
+    if (*value != 0 && cudaMemcpyToSymbol(g_default_status, &zero, sizeof(int)) != cudaSuccess)
+        return KMCTS_ESYNC;
+    return KMCTS_OK;
+}
+
+}  // namespace kmcts

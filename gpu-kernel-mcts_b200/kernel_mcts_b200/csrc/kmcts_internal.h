@@ -1,0 +1,46 @@
+// Internal declarations shared by the translation units of libkmcts_gemm_sm100.so.
+#pragma once
+
+#include <atomic>
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "kmcts_gemm.h"
+
+namespace kmcts {
+
+// Counts every kernel launch the library makes (kmcts_launch_count()).
+extern std::atomic<int64_t> g_launches;
+
+// Encodes a 2-D BF16 tensor map (dim0 innermost) with 128-byte swizzle.
+// Returns false when the driver rejects it.
+bool encode_tensor_map_2d(CUtensorMap* map, const void* base, uint64_t dim0, uint64_t dim1,
+                          uint64_t row_stride_bytes, uint32_t box0, uint32_t box1);
+
+// tcgen05 path.  Returns KMCTS_OK or an error code; launches nothing on error.
+int launch_tcgen05(const void* A, const void* B, void* C, int M, int N, int K, int b_layout,
+                   const kmcts_gemm_config& cfg, cudaStream_t stream, int* device_status);
+
+// Static checks for the tcgen05 path (shape, alignment-free parts, schedule).
+int tcgen05_legal(const kmcts_gemm_config& cfg, int M, int N, int K, int b_layout, char* why,
+                  int len);
+int64_t tcgen05_smem_bytes(const kmcts_gemm_config& cfg, int b_layout);
+
+// CUDA-core path for any shape and alignment.
+int launch_simt(const void* A, const void* B, void* C, int M, int N, int K, int b_layout,
+                cudaStream_t stream);
+
+// Reads and clears the library's default device status word.
+int take_default_status(cudaStream_t stream, int* value);
+
+int multiprocessor_count();
+
+}  // namespace kmcts
+
+namespace kmcts {
+size_t compare_workspace_bytes();
+int compare_bf16_device(const void* C, const void* reference, int64_t count, double rtol,
+                        double atol, void* workspace, cudaStream_t stream,
+                        kmcts_compare_result* out);
+}  // namespace kmcts

@@ -1,0 +1,123 @@
+/*
+ * kmcts_gemm.h — C ABI of libkmcts_gemm_sm100.so, the B200 (sm_100a) BF16 GEMM
+ * behind the kernel_mcts evaluation contract.
+ *
+ * Tensors (all device pointers, caller-owned, BF16 = 16-bit bfloat16 bits):
+ *   A: [M, K] row-major.
+ *   B: [K, N] column-major (element (k, j) at B[j*K + k]) when
+ *      b_layout == KMCTS_B_COL — the reference contract,
+ *      src/kernel_mcts/benchmarks/bf16_gemm.py:24-28 — or row-major
+ *      (B[k*N + j]) when b_layout == KMCTS_B_ROW.
+ *   C: [M, N] row-major.
+ * Arithmetic: C = A·B with FP32 accumulation, one round-to-nearest-even to BF16.
+ *
+ * No function here allocates device memory per call except where stated.
+ */
+#ifndef KMCTS_GEMM_H
+#define KMCTS_GEMM_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Return codes.  0..3 keep the meaning of the reference's cuBLAS reference
+ * entry point (src/kernel_mcts/benchmarks/kernels/bf16_reference.cu:5-41):
+ * 0 ok, 1 handle/setup failure, 2 GEMM launch failure, 3 synchronize failure. */
+#define KMCTS_OK 0
+#define KMCTS_EHANDLE 1
+#define KMCTS_EGEMM 2
+#define KMCTS_ESYNC 3
+#define KMCTS_EINVAL 4   /* bad pointer, shape, layout or config */
+#define KMCTS_ESMEM 5    /* config needs more shared memory than a CTA has */
+#define KMCTS_ETIMEOUT 6 /* a device-side bounded wait gave up (see device_status) */
+#define KMCTS_ENOTSUP 7  /* the requested kernel cannot run this shape */
+
+#define KMCTS_B_COL 0 /* B column-major [K,N] == [N,K] row-major (K-major) */
+#define KMCTS_B_ROW 1 /* B row-major [K,N] (N-major) */
+
+#define KMCTS_KERNEL_AUTO 0    /* tcgen05 when the shape allows it, else SIMT */
+#define KMCTS_KERNEL_TCGEN05 1 /* tcgen05/TMA/TMEM kernel only (ENOTSUP otherwise) */
+#define KMCTS_KERNEL_SIMT 2    /* CUDA-core kernel, any shape */
+
+/* Kernel schedule.  Zero-initialise and call kmcts_default_config() first. */
+typedef struct kmcts_gemm_config {
+    int32_t tile_m;       /* CTA tile rows: 128 */
+    int32_t tile_n;       /* CTA tile columns: 64, 128, 192 or 256 */
+    int32_t tile_k;       /* K per pipeline stage: 64 or 128 */
+    int32_t stages;       /* shared-memory pipeline depth: 2..8 */
+    int32_t cluster_m;    /* must be 1 in this version */
+    int32_t cluster_n;    /* must be 1 in this version */
+    int32_t persistent;   /* 1: one CTA per SM loops over tiles; 0: one CTA per tile */
+    int32_t raster_group; /* M-tiles per raster group (L2 locality), >= 1 */
+    int32_t kernel;       /* KMCTS_KERNEL_* */
+    int32_t reserved;
+    int64_t wait_limit_ns; /* bound on each device-side wait; 0 = 2 s default */
+} kmcts_gemm_config;
+
+/* Fills *cfg with the tuned default schedule for B200. Returns KMCTS_OK. */
+int kmcts_default_config(kmcts_gemm_config* cfg);
+
+/* Drop-in for the reference's ctypes entry point kernel_mcts_bf16_reference
+ * (src/kernel_mcts/benchmarks/kernels/bf16_reference.cu:5-41, loaded as in
+ * src/kernel_mcts/cute_baseline.py:595-616): same arguments, column-major B,
+ * default stream, synchronises, same return codes (plus KMCTS_EINVAL,
+ * KMCTS_ETIMEOUT). */
+int kmcts_bf16_gemm(const void* A, const void* B, void* C, int M, int N, int K);
+
+/* Asynchronous GEMM on `stream` (a cudaStream_t; NULL = default stream).
+ * cfg may be NULL (default schedule).  device_status, if not NULL, is a device
+ * int that the kernel sets non-zero when a bounded wait gives up; the caller
+ * zeroes it and reads it after synchronising.  Replaces the fixed 16x16
+ * launch_candidate of src/kernel_mcts/benchmarks/kernels/bf16_gemm_harness.cu:61-72
+ * with a launcher that owns grid, cluster and shared-memory attributes. */
+int kmcts_bf16_gemm_ex(const void* A, const void* B, void* C, int M, int N, int K, int b_layout,
+                       const kmcts_gemm_config* cfg, void* stream, int* device_status);
+
+/* Static legality of a schedule for a shape (no GPU work).  Returns KMCTS_OK,
+ * KMCTS_EINVAL, KMCTS_ESMEM or KMCTS_ENOTSUP, with a reason in why[0..len).
+ * Used to mark sweep points STATICALLY_REJECTED without charging a trial, as
+ * validate_cute_schedule does (src/kernel_mcts/cute_schedule.py:41-78). */
+int kmcts_config_legal(const kmcts_gemm_config* cfg, int M, int N, int K, int b_layout, char* why,
+                       int len);
+
+/* Shared-memory bytes a schedule needs per CTA (0 if the schedule is invalid). */
+int64_t kmcts_config_smem_bytes(const kmcts_gemm_config* cfg, int b_layout);
+
+/* Library version string. */
+const char* kmcts_version(void);
+
+/* Result of the device-side comparison of an output against a reference. */
+typedef struct kmcts_compare_result {
+    double maximum_error;  /* max |c - ref| over finite pairs (NaN/inf counted below) */
+    double mean_error;     /* sum |c - ref| / count */
+    int64_t count;
+    int64_t n_tolerance_fail; /* elements failing |c-ref| <= atol + rtol*|ref| or non-finite */
+    int64_t n_nonfinite;      /* non-finite elements of c */
+    int64_t ulp_hist[4];      /* elements at 0, 1, 2 and >2 BF16 ulps from ref */
+    int32_t max_ulp;          /* largest ulp distance (65535 for NaN) */
+    int32_t success;          /* n_tolerance_fail == 0 */
+} kmcts_compare_result;
+
+/* Bytes of device workspace kmcts_bf16_compare needs. */
+size_t kmcts_compare_workspace_bytes(void);
+
+/* Device-side restatement of the reference harness's host error scan
+ * (src/kernel_mcts/benchmarks/kernels/bf16_gemm_harness.cu:154-164) with added
+ * ulp statistics.  `workspace` is caller-owned device memory of
+ * kmcts_compare_workspace_bytes() bytes.  Runs on `stream`, synchronises it,
+ * and writes *out on the host. */
+int kmcts_bf16_compare(const void* C, const void* reference, int64_t count, double rtol,
+                       double atol, void* workspace, void* stream, kmcts_compare_result* out);
+
+/* Number of kernels this library has launched in this process (all entry
+ * points).  Lets callers count GPU launches inside a timed region. */
+int64_t kmcts_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KMCTS_GEMM_H */

@@ -1,0 +1,212 @@
+"""Parity of the sm_100a GEMM (through the C ABI) with the CPU oracle.
+
+Bars (written into the asserts below):
+* integer-valued inputs: bit-exact against the oracle (FP32 sums are exact);
+* the SIMT kernel: bit-exact against the root-order oracle for any input;
+* N(0,1) / U(-0.25,0.25) inputs on the tcgen05 kernel: every element within
+  1 BF16 ulp of the FP32-accumulated oracle, or within
+  0.5 ulp(ref64) + K*2^-24*(|A||B|)_ij of the FP64 product.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from kernel_mcts_b200 import _native
+from kernel_mcts_b200 import gemm as kg
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+
+def to_cuda(bits: np.ndarray) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(bits).view(np.int16)).view(torch.bfloat16).cuda()
+
+
+def bits_of(t: torch.Tensor) -> np.ndarray:
+    return oracle.torch_bits(t)
+
+
+def run(a, b, layout="col", **cfg):
+    config = _native.make_config(**cfg) if cfg else None
+    status = torch.zeros(1, dtype=torch.int32, device=a.device)
+    c = kg.bf16_gemm(a, b, b_layout=layout, config=config, status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0, f"device status {int(status.item()):#x}"
+    return c
+
+
+def b_for(layout: str, b_nk: torch.Tensor) -> torch.Tensor:
+    return b_nk if layout == "col" else b_nk.T.contiguous()
+
+
+# ---------------------------------------------------------------- oracle pin
+
+
+def test_reference_root_kernel_matches_cpu_oracle(cuda_device):
+    """The reference's own root kernel (built from its source for sm_100a)
+    and the C oracle agree bit for bit: the oracle restates it exactly."""
+    if not oracle.REF_ROOT_LIB.exists():
+        pytest.skip("oracle/_ref/libref_root.so not built")
+    lib = ctypes.CDLL(str(oracle.REF_ROOT_LIB))
+    lib.kmcts_ref_root_gemm.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int] * 3
+    for m, n, k, seed in [(37, 29, 53, 7), (128, 96, 256, 0), (256, 256, 256, 0)]:
+        a, b = oracle.uniform_inputs(m, n, k, seed)
+        da, db = to_cuda(a), to_cuda(b)
+        dc = torch.zeros((m, n), dtype=torch.bfloat16, device="cuda")
+        assert lib.kmcts_ref_root_gemm(da.data_ptr(), db.data_ptr(), dc.data_ptr(), m, n, k) == 0
+        np.testing.assert_array_equal(bits_of(dc), oracle.root_gemm(a, b))
+
+
+# ---------------------------------------------------------------- SIMT path
+
+
+@pytest.mark.parametrize("layout", ["col", "row"])
+@pytest.mark.parametrize("shape", [(37, 29, 53), (64, 64, 64), (130, 70, 301)])
+def test_simt_kernel_bit_exact_with_root_order(cuda_device, layout, shape):
+    m, n, k = shape
+    a, b = oracle.uniform_inputs(m, n, k, 1)
+    c = run(to_cuda(a), b_for(layout, to_cuda(b)), layout, kernel=_native.KERNEL_SIMT)
+    np.testing.assert_array_equal(bits_of(c), oracle.root_gemm(a, b))
+
+
+# ------------------------------------------------------------- tcgen05 path
+
+
+@pytest.mark.parametrize("layout", ["col", "row"])
+@pytest.mark.parametrize(
+    "shape", [(128, 256, 64), (256, 256, 256), (300, 264, 200), (1024, 768, 512), (64, 8, 8)]
+)
+def test_tcgen05_integer_inputs_bit_exact(cuda_device, layout, shape):
+    m, n, k = shape
+    a_t, b_t = oracle.integer_inputs(m, n, k, seed=0)
+    expect = oracle.root_gemm(oracle.torch_bits(a_t), oracle.torch_bits(b_t))
+    c = run(a_t.cuda(), b_for(layout, b_t.cuda()), layout, kernel=_native.KERNEL_TCGEN05)
+    np.testing.assert_array_equal(bits_of(c), expect)
+
+
+@pytest.mark.parametrize("layout", ["col", "row"])
+def test_tcgen05_uniform_inputs_within_criterion(cuda_device, layout):
+    m, n, k = 512, 384, 1024
+    a, b = oracle.uniform_inputs(m, n, k, 0)
+    c = run(to_cuda(a), b_for(layout, to_cuda(b)), layout, kernel=_native.KERNEL_TCGEN05)
+    a_t = torch.from_numpy(a.view(np.int16)).view(torch.bfloat16)
+    b_t = torch.from_numpy(b.view(np.int16)).view(torch.bfloat16)
+    ref64, mag = oracle.fp64_reference(a_t, b_t)
+    report = oracle.parity_report(bits_of(c), oracle.root_gemm(a, b), ref64, mag, k)
+    assert report["passed"], report
+    assert oracle.harness_check(bits_of(c), oracle.root_gemm(a, b))["success"]
+
+
+VARIANTS = [
+    (256, 64, 3), (256, 64, 4), (128, 64, 4), (128, 64, 5), (128, 64, 6),
+    (128, 128, 3), (256, 128, 2), (192, 64, 4), (64, 64, 6),
+]
+
+
+@pytest.mark.parametrize("layout", ["col", "row"])
+@pytest.mark.parametrize("tile_n,tile_k,stages", VARIANTS)
+@pytest.mark.parametrize("persistent", [1, 0])
+def test_every_compiled_schedule_bit_exact(cuda_device, layout, tile_n, tile_k, stages, persistent):
+    m, n, k = 392, 520, 328  # ragged against every tile size
+    a_t, b_t = oracle.integer_inputs(m, n, k, seed=7)
+    expect = oracle.root_gemm(oracle.torch_bits(a_t), oracle.torch_bits(b_t))
+    c = run(a_t.cuda(), b_for(layout, b_t.cuda()), layout, kernel=_native.KERNEL_TCGEN05,
+            tile_n=tile_n, tile_k=tile_k, stages=stages, persistent=persistent, raster_group=3)
+    np.testing.assert_array_equal(bits_of(c), expect)
+
+
+def test_tcgen05_4096_integer_bit_exact_and_matches_cublas(cuda_device):
+    """4096^3, integers in {-2..2}; exact, so the torch CPU
+    FP32 reference, cuBLAS and this kernel must agree bit for bit."""
+    n = 4096
+    a_t, b_t = oracle.integer_inputs(n, n, n, seed=0)
+    ref = oracle.torch_reference(a_t, b_t).cuda()
+    a, b = a_t.cuda(), b_t.cuda()
+    c = run(a, b, "col")
+    cmp = kg.compare(c, ref)
+    assert cmp.ulp_hist[0] == n * n, cmp
+    cublas = torch.matmul(a, b.T)
+    assert kg.compare(cublas, ref).ulp_hist[0] == n * n
+    c_row = run(a, b.T.contiguous(), "row")
+    assert kg.compare(c_row, ref).ulp_hist[0] == n * n
+
+
+def test_tcgen05_4096_randn_within_one_ulp_or_bound(cuda_device):
+    """4096^3 N(0,1) BF16 inputs, seed 0."""
+    n = 4096
+    a_t, b_t = oracle.randn_inputs(n, n, n, seed=0)
+    c = run(a_t.cuda(), b_t.cuda(), "col")
+    ref32 = oracle.torch_bits(oracle.torch_reference(a_t, b_t))
+    ref64, mag = oracle.fp64_reference(a_t, b_t)
+    report = oracle.parity_report(bits_of(c), ref32, ref64, mag, n)
+    assert report["passed"], report
+    assert report["max_ulp_where_ref_ge_2^-6"] <= 1, report
+
+
+# ------------------------------------------------------------- ABI details
+
+
+def test_dropin_entry_point_matches_oracle(cuda_device):
+    m, n, k = 256, 256, 256
+    a, b = oracle.uniform_inputs(m, n, k, 0)
+    da, db = to_cuda(a), to_cuda(b)
+    dc = torch.empty((m, n), dtype=torch.bfloat16, device="cuda")
+    assert kg.bf16_gemm_sync(da, db, dc) == 0
+    report = oracle.harness_check(bits_of(dc), oracle.root_gemm(a, b))
+    assert report["success"], report
+
+
+def test_degenerate_shapes(cuda_device):
+    a = torch.ones((64, 0), dtype=torch.bfloat16, device="cuda")
+    b = torch.ones((32, 0), dtype=torch.bfloat16, device="cuda")
+    c = torch.full((64, 32), 7.0, dtype=torch.bfloat16, device="cuda")
+    kg.bf16_gemm(a, b, out=c)
+    torch.cuda.synchronize()
+    assert torch.count_nonzero(c).item() == 0  # K == 0 gives zeros
+    e = kg.bf16_gemm(torch.ones((0, 16), dtype=torch.bfloat16, device="cuda"),
+                     torch.ones((8, 16), dtype=torch.bfloat16, device="cuda"))
+    assert e.shape == (0, 8)
+
+
+def test_auto_falls_back_to_simt_for_unaligned_k(cuda_device):
+    m, n, k = 96, 64, 45  # K % 8 != 0: TMA cannot take it
+    a, b = oracle.uniform_inputs(m, n, k, 4)
+    c = run(to_cuda(a), to_cuda(b), "col")
+    np.testing.assert_array_equal(bits_of(c), oracle.root_gemm(a, b))
+    with pytest.raises(kg.KmctsError):
+        run(to_cuda(a), to_cuda(b), "col", kernel=_native.KERNEL_TCGEN05)
+
+
+def test_compare_kernel_matches_harness_check(cuda_device):
+    a, b = oracle.uniform_inputs(200, 136, 64, 2)
+    c_bits = oracle.root_gemm(a, b)
+    ref_bits = c_bits.copy()
+    ref_bits.ravel()[::97] ^= np.uint16(0x0003)  # perturb some mantissas
+    ref_bits.ravel()[5] = oracle.float_to_bf16_bits(np.array([0.5], np.float32))[0]
+    expect = oracle.harness_check(c_bits, ref_bits)
+    got = kg.compare(to_cuda(c_bits), to_cuda(ref_bits))
+    assert got.success == expect["success"]
+    assert got.maximum_error == pytest.approx(expect["maximum_error"], rel=0, abs=0)
+    assert got.mean_error == pytest.approx(expect["mean_error"], rel=1e-12)
+    d = oracle.ulp_distance(c_bits, ref_bits).ravel()
+    assert got.max_ulp == int(d.max())
+    assert got.ulp_hist == (int((d == 0).sum()), int((d == 1).sum()), int((d == 2).sum()), int((d > 2).sum()))
+    nan_bits = c_bits.copy()
+    nan_bits.ravel()[0] = 0x7FC0
+    bad = kg.compare(to_cuda(nan_bits), to_cuda(c_bits))
+    assert not bad.success and bad.n_nonfinite == 1
+
+
+def test_launch_counter_counts_library_launches(cuda_device):
+    a_t, b_t = oracle.integer_inputs(256, 256, 256, seed=1)
+    a, b = a_t.cuda(), b_t.cuda()
+    before = _native.launch_count()
+    for _ in range(3):
+        kg.bf16_gemm(a, b)
+    torch.cuda.synchronize()
+    assert _native.launch_count() - before == 3

@@ -1,0 +1,78 @@
+"""The C-ABI library loads, exports what include/kmcts_gemm.h declares, and
+its host-only entry points (no GPU work) behave."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+import kernel_mcts_b200 as km
+from kernel_mcts_b200 import _native
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def _declared_functions() -> set[str]:
+    names: set[str] = set()
+    for header in (ROOT / "include").glob("*.h"):
+        text = re.sub(r"/\*.*?\*/", " ", header.read_text(), flags=re.S)
+        names |= set(re.findall(r"\b(kmcts_\w+)\s*\(", text))
+    return names
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    lib = _native.load()
+    declared = _declared_functions()
+    assert declared, "no declarations parsed"
+    missing = [name for name in sorted(declared) if not hasattr(lib, name)]
+    assert not missing, missing
+    assert set(_native.EXPORTED_SYMBOLS) == declared
+
+
+def test_struct_sizes_match_header():
+    assert ctypes.sizeof(_native.GemmConfig) == 48
+    assert ctypes.sizeof(_native.CompareResult) == 8 * 2 + 8 * 3 + 8 * 4 + 4 * 2
+
+
+def test_version_and_default_config():
+    assert "sm_100a" in km.version()
+    cfg = km.default_config()
+    assert (cfg.tile_m, cfg.tile_n, cfg.tile_k) == (128, 256, 64)
+    assert km.config_legal(cfg, 4096, 4096, 4096) == (0, "ok")
+
+
+@pytest.mark.parametrize(
+    "overrides,shape,code",
+    [
+        ({"tile_n": 256, "stages": 5}, (4096, 4096, 4096), _native.KMCTS_ESMEM),
+        ({"tile_m": 256}, (4096, 4096, 4096), _native.KMCTS_ENOTSUP),
+        ({"cluster_m": 2}, (4096, 4096, 4096), _native.KMCTS_ENOTSUP),
+        ({}, (4096, 4096, 4100), _native.KMCTS_ENOTSUP),  # K not a multiple of 8
+        ({}, (4096, 4100, 4096), _native.KMCTS_ENOTSUP),  # N not a multiple of 8
+        ({"raster_group": 0}, (256, 256, 256), _native.KMCTS_EINVAL),
+        ({"tile_n": 128, "stages": 6}, (256, 256, 256), _native.KMCTS_OK),
+        ({"tile_n": 128, "tile_k": 128, "stages": 3}, (256, 256, 256), _native.KMCTS_OK),
+    ],
+)
+def test_config_legality(overrides, shape, code):
+    cfg = km.make_config(**overrides)
+    got, why = km.config_legal(cfg, *shape)
+    assert got == code, why
+    assert why
+
+
+def test_smem_accounting():
+    cfg = km.make_config(tile_n=256, tile_k=64, stages=4)
+    assert km.config_smem_bytes(cfg) == 4 * (128 + 256) * 64 * 2 + 4 * 2 * 4096 + 2048
+    assert km.config_smem_bytes(cfg) <= 232448
+
+
+def test_bad_arguments_rejected_without_gpu_work():
+    lib = _native.load()
+    assert lib.kmcts_bf16_gemm_ex(None, None, None, -1, 4, 4, 0, None, None, None) == _native.KMCTS_EINVAL
+    assert lib.kmcts_bf16_gemm_ex(None, None, None, 4, 4, 4, 7, None, None, None) == _native.KMCTS_EINVAL
+    assert lib.kmcts_bf16_gemm_ex(None, None, None, 4, 4, 4, 0, None, None, None) == _native.KMCTS_EINVAL
+    assert lib.kmcts_default_config(None) == _native.KMCTS_EINVAL
