@@ -74,32 +74,48 @@ def profiled_traffic() -> float | None:
 
 
 class ClockSampler:
-    """Samples nvidia-smi SM clocks and throttle reasons during the timed region."""
+    """Samples SM clock and clock-event (throttle) reasons through NVML every
+    ~2 ms while the timed region runs (nvidia-smi is too slow to catch a
+    region of a few tens of ms)."""
 
-    FIELDS = ("clocks.sm", "clocks.max.sm", "power.draw", "clocks_event_reasons.active",
-              "clocks_event_reasons.hw_slowdown", "clocks_event_reasons.hw_thermal_slowdown",
-              "clocks_event_reasons.sw_thermal_slowdown", "clocks_event_reasons.sw_power_cap")
+    # NVML clocks-event reason bits (nvml.h: nvmlClocksEventReason*).
+    REASONS = {
+        0x8: "hw_slowdown",
+        0x20: "sw_thermal_slowdown",
+        0x40: "hw_thermal_slowdown",
+        0x4: "sw_power_cap",
+        0x80: "hw_power_brake_slowdown",
+    }
 
     def __init__(self, device_index: int) -> None:
         self.device_index = device_index
-        self.samples: list[list[str]] = []
+        self.samples: list[tuple[float, int, float]] = []
+        self.max_mhz: float | None = None
+        self.error: str | None = None
         self._stop = threading.Event()
         self._thread = threading.Thread(target=self._run, daemon=True)
 
     def _run(self) -> None:
-        cmd = ["nvidia-smi", f"--query-gpu={','.join(self.FIELDS)}", "--format=csv,noheader,nounits",
-               "-i", str(self.device_index)]
-        while not self._stop.is_set():
-            try:
-                out = subprocess.run(cmd, capture_output=True, text=True, timeout=5).stdout.strip()
-                if out:
-                    self.samples.append([v.strip() for v in out.split(",")])
-            except (OSError, subprocess.SubprocessError):
-                return
-            self._stop.wait(0.1)
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+            index = int(visible.split(",")[self.device_index]) if visible else self.device_index
+            handle = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(handle, pynvml.NVML_CLOCK_SM))
+            while not self._stop.is_set():
+                sm = float(pynvml.nvmlDeviceGetClockInfo(handle, pynvml.NVML_CLOCK_SM))
+                reasons = int(pynvml.nvmlDeviceGetCurrentClocksEventReasons(handle))
+                power = pynvml.nvmlDeviceGetPowerUsage(handle) / 1000.0
+                self.samples.append((sm, reasons, power))
+                time.sleep(0.002)
+        except Exception as error:  # NVML missing or refused: report it, do not fail the bench
+            self.error = f"{type(error).__name__}: {error}"
 
     def __enter__(self):
         self._thread.start()
+        time.sleep(0.05)
         return self
 
     def __exit__(self, *exc) -> None:
@@ -108,22 +124,17 @@ class ClockSampler:
 
     def summary(self) -> dict:
         if not self.samples:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"], "samples": 0}
-        def num(v):
-            try:
-                return float(v)
-            except ValueError:
-                return None
-        sm = [num(s[0]) for s in self.samples if num(s[0]) is not None]
-        mx = [num(s[1]) for s in self.samples if num(s[1]) is not None]
-        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        reasons = sorted({name for s in self.samples for name, v in zip(names, s[4:8]) if v.strip() == "Active"})
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unavailable"],
+                    "samples": 0, "error": self.error}
+        reasons = sorted({name for _, bits, _ in self.samples for bit, name in self.REASONS.items() if bits & bit})
         return {
-            "sm_mhz": statistics.median(sm) if sm else None,
-            "sm_max_mhz": max(mx) if mx else None,
+            "sm_mhz": statistics.median(s for s, _, _ in self.samples),
+            "sm_min_mhz": min(s for s, _, _ in self.samples),
+            "sm_max_mhz": self.max_mhz,
             "reasons": reasons,
             "samples": len(self.samples),
-            "power_w_max": max((num(s[2]) or 0.0) for s in self.samples),
+            "power_w_max": max(p for _, _, p in self.samples),
+            "source": "NVML, ~2 ms polling during the timed region",
         }
 
 

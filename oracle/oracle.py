@@ -237,6 +237,7 @@ def parity_report(c_bits: np.ndarray, ref32_bits: np.ndarray, ref64: np.ndarray,
         "count": int(c.size),
         "max_ulp": int(d.max()) if d.size else 0,
         "max_ulp_where_ref_ge_2^-6": int(d[big].max()) if big.any() else 0,
+        "max_ulp_where_ref_ge_0.5": int(d[np.abs(ref64) >= 0.5].max()) if (np.abs(ref64) >= 0.5).any() else 0,
         "n_gt_1ulp": int((d > 1).sum()),
         "n_fail_bound": int((~passed).sum()),
         "max_abs_error_vs_fp64": float(np.abs(cf - ref64).max()) if c.size else 0.0,
