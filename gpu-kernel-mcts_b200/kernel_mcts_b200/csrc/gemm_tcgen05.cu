@@ -20,14 +20,12 @@
 // Every wait is bounded (limit_ns); on timeout the kernel records
 // KMCTS_ETIMEOUT in *status, drains its own copies and MMAs, frees TMEM and
 // returns.  No TMA multicast is used.
-#include <cuda_bf16.h>
-
 #include <cstdio>
 #include <cstring>
 #include <mutex>
 
+#include "gemm_common.cuh"
 #include "kmcts_internal.h"
-#include "ptx_sm100.cuh"
 
 namespace kmcts {
 
@@ -35,16 +33,10 @@ __device__ int g_default_status;
 
 namespace {
 
-constexpr int kBM = 128;
-constexpr int kThreads = 192;
-constexpr int kEpilogueWarps = 4;
-constexpr int kStagingBytes = 32 * 128;  // one warp's 32 rows x 64 BF16 columns
-constexpr int kSmemReserve = 2048;       // barriers + 1024-byte alignment slack
-constexpr int kMaxDevices = 64;
+using namespace gemm;
 
-// Status codes written to the device status word (low byte = KMCTS_ETIMEOUT,
-// next byte = which role gave up).
-constexpr int kRoleProducer = 1, kRoleMma = 2, kRoleEpilogue = 3, kRoleDrain = 4;
+constexpr int kBM = 128;
+constexpr int kMaxDevices = 64;
 
 template <int BN, int BK, int STAGES, bool B_MN>
 struct Layout {
@@ -54,38 +46,11 @@ struct Layout {
     static constexpr int kStagingOffset = STAGES * kStageBytes;
     static constexpr int kBarrierOffset = kStagingOffset + kEpilogueWarps * 2 * kStagingBytes;
     static constexpr int kSmemBytes = kBarrierOffset + kSmemReserve;
-    static constexpr uint32_t kTmemCols = (2 * BN <= 32)    ? 32
-                                          : (2 * BN <= 64)  ? 64
-                                          : (2 * BN <= 128) ? 128
-                                          : (2 * BN <= 256) ? 256
-                                                            : 512;
+    static constexpr uint32_t kTmemCols = tmem_columns_for(2 * BN);
     static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "BN must be 64..256, step 64");
     static_assert(BK == 64 || BK == 128, "BK must be 64 or 128");
-    static_assert(kSmemBytes <= 232448, "shared memory budget exceeded");
+    static_assert(kSmemBytes <= kMaxSmem, "shared memory budget exceeded");
 };
-
-struct TileCoord {
-    int m_blk, n_blk;
-};
-
-__device__ __forceinline__ TileCoord tile_coord(int t, int num_m, int num_n, int group) {
-    const int per_group = group * num_n;
-    const int g = t / per_group;
-    const int first_m = g * group;
-    const int rows = min(num_m - first_m, group);
-    const int r = t - g * per_group;
-    return {first_m + r % rows, r / rows};
-}
-
-__device__ __forceinline__ void record_failure(int* status, volatile int* abort, int role) {
-    *abort = 1;
-    atomicCAS(status, 0, KMCTS_ETIMEOUT | (role << 8));
-}
-
-__device__ __forceinline__ uint32_t pack_bf16x2(uint32_t lo_bits, uint32_t hi_bits) {
-    __nv_bfloat162 v = __floats2bfloat162_rn(__uint_as_float(lo_bits), __uint_as_float(hi_bits));
-    return *reinterpret_cast<uint32_t*>(&v);
-}
 
 template <int BN, int BK, int STAGES, bool B_MN>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -281,29 +246,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     __syncwarp();
                     if (lane == 0) ptx::mbar_arrive(&tmem_empty[acc]);
                 }
-                uint32_t packed[32];
-#pragma unroll
-                for (int i = 0; i < 16; ++i) packed[i] = pack_bf16x2(lo[2 * i], lo[2 * i + 1]);
-#pragma unroll
-                for (int i = 0; i < 16; ++i) packed[16 + i] = pack_bf16x2(hi[2 * i], hi[2 * i + 1]);
-                uint8_t* buf = staging + (chunk_count & 1) * kStagingBytes;
-                if (lane == 0) ptx::bulk_wait_group_read<1>();
-                __syncwarp();
-                uint8_t* row = buf + lane * 128;
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const int phys = j ^ (lane & 7);
-                    *reinterpret_cast<uint4*>(row + phys * 16) =
-                        make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2],
-                                   packed[4 * j + 3]);
-                }
-                ptx::fence_proxy_async_smem();
-                __syncwarp();
-                if (lane == 0) {
-                    ptx::tma_store_2d(&map_c, buf, n0 + c * 64, m0 + quarter * 32);
-                    ptx::bulk_commit_group();
-                }
-                ++chunk_count;
+                store_chunk(&map_c, staging, chunk_count, lo, hi, lane, n0 + c * 64, m0 + quarter * 32);
             }
         }
         if (lane == 0) ptx::bulk_wait_group<0>();
@@ -360,11 +303,13 @@ struct Variant {
 
 #define KMCTS_VARIANT(BN, BK, ST, MN) {BN, BK, ST, MN, &launch_variant<BN, BK, ST, MN>}
 
-// The compiled schedule space.  Shared-memory budget: stages*(128+BN)*BK*2
-// bytes of operand ring + 32 KB epilogue staging + 2 KB <= 227 KB.
+// The compiled 1-CTA schedule space: every (tile_n, tile_k, stages) of the
+// sweep grid that fits 227 KB (stages*(128+BN)*BK*2 + 32 KB staging + 2 KB),
+// plus a few off-grid shapes.
 const Variant kVariants[] = {
     KMCTS_VARIANT(256, 64, 3, false), KMCTS_VARIANT(256, 64, 4, false),
     KMCTS_VARIANT(256, 64, 3, true),  KMCTS_VARIANT(256, 64, 4, true),
+    KMCTS_VARIANT(128, 64, 3, false), KMCTS_VARIANT(128, 64, 3, true),
     KMCTS_VARIANT(128, 64, 4, false), KMCTS_VARIANT(128, 64, 5, false),
     KMCTS_VARIANT(128, 64, 6, false), KMCTS_VARIANT(128, 64, 4, true),
     KMCTS_VARIANT(128, 64, 5, true),  KMCTS_VARIANT(128, 64, 6, true),
@@ -391,11 +336,15 @@ void put_reason(char* why, int len, const char* text) {
     }
 }
 
+bool is_pair(const kmcts_gemm_config& cfg) { return cfg.tile_m == 256; }
+
 }  // namespace
 
 int64_t tcgen05_smem_bytes(const kmcts_gemm_config& cfg, int b_layout) {
     (void)b_layout;
-    if (cfg.tile_m != kBM || cfg.tile_n <= 0 || cfg.tile_k <= 0 || cfg.stages <= 0) return 0;
+    if (cfg.tile_n <= 0 || cfg.tile_k <= 0 || cfg.stages <= 0) return 0;
+    if (cfg.tile_m == 256) return pair_smem_bytes(cfg.tile_n, cfg.tile_k, cfg.stages);
+    if (cfg.tile_m != kBM) return 0;
     return static_cast<int64_t>(cfg.stages) * (kBM + cfg.tile_n) * cfg.tile_k * 2 +
            kEpilogueWarps * 2 * kStagingBytes + kSmemReserve;
 }
@@ -406,30 +355,52 @@ int tcgen05_legal(const kmcts_gemm_config& cfg, int M, int N, int K, int b_layou
         put_reason(why, len, "b_layout must be 0 (column-major) or 1 (row-major)");
         return KMCTS_EINVAL;
     }
-    if (cfg.tile_m != kBM) {
-        put_reason(why, len, "tile_m must be 128 (one UMMA M=128 per CTA)");
-        return KMCTS_ENOTSUP;
-    }
-    if (cfg.cluster_m != 1 || cfg.cluster_n != 1) {
-        put_reason(why, len, "clusters other than 1x1 are not built in this version");
-        return KMCTS_ENOTSUP;
-    }
-    const int64_t smem = tcgen05_smem_bytes(cfg, b_layout);
-    if (smem <= 0 || smem > 232448) {
-        put_reason(why, len, "shared memory per CTA exceeds 227 KB");
-        return KMCTS_ESMEM;
-    }
-    if (find_variant(cfg, b_layout) == nullptr) {
-        put_reason(why, len, "schedule (tile_n, tile_k, stages) is not compiled in");
-        return KMCTS_ENOTSUP;
+    if (M < 0 || N < 0 || K < 0) {
+        put_reason(why, len, "negative dimension");
+        return KMCTS_EINVAL;
     }
     if (cfg.raster_group < 1) {
         put_reason(why, len, "raster_group must be >= 1");
         return KMCTS_EINVAL;
     }
-    if (M < 0 || N < 0 || K < 0) {
-        put_reason(why, len, "negative dimension");
+    if (cfg.cluster_m < 1 || cfg.cluster_n < 1) {
+        put_reason(why, len, "cluster dimensions must be positive");
         return KMCTS_EINVAL;
+    }
+    if (cfg.cluster_n != 1) {
+        put_reason(why, len,
+                   "cluster_n > 1 only pays with a TMA multicast of A across the cluster, "
+                   "which this library never issues");
+        return KMCTS_ENOTSUP;
+    }
+    if (cfg.tile_m == kBM) {
+        if (cfg.cluster_m != 1) {
+            put_reason(why, len, "tile_m 128 runs one CTA per tile (cluster 1x1)");
+            return KMCTS_ENOTSUP;
+        }
+    } else if (cfg.tile_m == 256) {
+        if (cfg.cluster_m != 2) {
+            put_reason(why, len, "tile_m 256 is one CTA pair (cluster 2x1, tcgen05 cta_group::2)");
+            return KMCTS_ENOTSUP;
+        }
+        if (cfg.tile_n != 128 && cfg.tile_n != 256) {
+            put_reason(why, len, "a CTA pair takes tile_n 128 or 256");
+            return KMCTS_ENOTSUP;
+        }
+    } else {
+        put_reason(why, len, "tile_m must be 128 (one CTA) or 256 (CTA pair)");
+        return KMCTS_ENOTSUP;
+    }
+    const int64_t smem = tcgen05_smem_bytes(cfg, b_layout);
+    if (smem <= 0 || smem > kMaxSmem) {
+        put_reason(why, len, "shared memory per CTA exceeds 227 KB");
+        return KMCTS_ESMEM;
+    }
+    const bool compiled = is_pair(cfg) ? pair_variant_exists(cfg.tile_n, cfg.tile_k, cfg.stages, b_layout)
+                                       : find_variant(cfg, b_layout) != nullptr;
+    if (!compiled) {
+        put_reason(why, len, "schedule (tile_m, tile_n, tile_k, stages) is not compiled in");
+        return KMCTS_ENOTSUP;
     }
     // TMA: every global row stride must be a multiple of 16 bytes.
     if (K % 8 != 0 || N % 8 != 0) {
@@ -456,18 +427,22 @@ int launch_tcgen05(const void* A, const void* B, void* C, int M, int N, int K, i
                    ? KMCTS_OK
                    : KMCTS_EGEMM;
     }
-    const Variant* v = find_variant(cfg, b_layout);
+    const bool pair = is_pair(cfg);
+    // Each CTA stages 128 rows of A, and BN (one CTA) or BN/2 (pair) of B.
+    const uint32_t b_rows = pair ? cfg.tile_n / 2 : cfg.tile_n;
     CUtensorMap ma, mb, mc;
     bool ok = encode_tensor_map_2d(&ma, A, K, M, static_cast<uint64_t>(K) * 2, 64, kBM);
     if (b_layout == KMCTS_B_COL) {
-        ok = ok && encode_tensor_map_2d(&mb, B, K, N, static_cast<uint64_t>(K) * 2, 64, v->bn);
+        ok = ok && encode_tensor_map_2d(&mb, B, K, N, static_cast<uint64_t>(K) * 2, 64, b_rows);
     } else {
         ok = ok && encode_tensor_map_2d(&mb, B, N, K, static_cast<uint64_t>(N) * 2, 64, 64);
     }
     ok = ok && encode_tensor_map_2d(&mc, C, N, M, static_cast<uint64_t>(N) * 2, 64, 32);
     if (!ok) return KMCTS_EINVAL;
     const uint64_t limit =
-        cfg.wait_limit_ns > 0 ? static_cast<uint64_t>(cfg.wait_limit_ns) : 2000000000ull;
+        cfg.wait_limit_ns > 0 ? static_cast<uint64_t>(cfg.wait_limit_ns) : kDefaultWaitNs;
+    if (pair) return launch_pair(ma, mb, mc, M, N, K, b_layout, cfg, limit, stream, device_status);
+    const Variant* v = find_variant(cfg, b_layout);
     return v->fn(ma, mb, mc, M, N, K, cfg.raster_group, cfg.persistent != 0, limit, stream,
                  device_status);
 }

@@ -28,11 +28,11 @@ def main() -> None:
     p.add_argument("--b-layout", choices=("col", "row"), default="row")
     p.add_argument("--launches", type=int, default=3)
     p.add_argument("--kernel", choices=("auto", "tcgen05", "simt"), default="tcgen05")
-    for name in ("tile_n", "tile_k", "stages", "persistent", "raster_group"):
+    for name in ("tile_m", "tile_n", "tile_k", "stages", "cluster_m", "persistent", "raster_group"):
         p.add_argument(f"--{name.replace('_', '-')}", type=int, default=None)
     args = p.parse_args()
 
-    overrides = {name: getattr(args, name) for name in ("tile_n", "tile_k", "stages", "persistent", "raster_group")
+    overrides = {name: getattr(args, name) for name in ("tile_m", "tile_n", "tile_k", "stages", "cluster_m", "persistent", "raster_group")
                  if getattr(args, name) is not None}
     overrides["kernel"] = {"auto": _native.KERNEL_AUTO, "tcgen05": _native.KERNEL_TCGEN05,
                            "simt": _native.KERNEL_SIMT}[args.kernel]

@@ -120,6 +120,38 @@ def test_every_compiled_schedule_bit_exact(cuda_device, layout, tile_n, tile_k, 
     np.testing.assert_array_equal(bits_of(c), expect)
 
 
+PAIR_VARIANTS = [
+    (256, 64, 3), (256, 64, 4), (256, 64, 5), (256, 64, 6), (256, 128, 3),
+    (128, 64, 3), (128, 64, 4), (128, 64, 5), (128, 64, 6), (128, 128, 3), (128, 128, 4),
+]
+
+
+@pytest.mark.parametrize("layout", ["col", "row"])
+@pytest.mark.parametrize("tile_n,tile_k,stages", PAIR_VARIANTS)
+@pytest.mark.parametrize("persistent", [1, 0])
+def test_every_cta_pair_schedule_bit_exact(cuda_device, layout, tile_n, tile_k, stages, persistent):
+    """tile_m 256 = one CTA pair (cluster 2x1, tcgen05.mma.cta_group::2)."""
+    m, n, k = 392, 520, 328  # ragged: the last pair tile has an empty second CTA
+    a_t, b_t = oracle.integer_inputs(m, n, k, seed=11)
+    expect = oracle.root_gemm(oracle.torch_bits(a_t), oracle.torch_bits(b_t))
+    c = run(a_t.cuda(), b_for(layout, b_t.cuda()), layout, kernel=_native.KERNEL_TCGEN05, tile_m=256,
+            cluster_m=2, tile_n=tile_n, tile_k=tile_k, stages=stages, persistent=persistent, raster_group=2)
+    np.testing.assert_array_equal(bits_of(c), expect)
+
+
+@pytest.mark.parametrize("layout", ["col", "row"])
+def test_cta_pair_uniform_inputs_within_criterion(cuda_device, layout):
+    m, n, k = 1024, 768, 2048
+    a, b = oracle.uniform_inputs(m, n, k, 3)
+    c = run(to_cuda(a), b_for(layout, to_cuda(b)), layout, kernel=_native.KERNEL_TCGEN05, tile_m=256,
+            cluster_m=2, tile_n=256, tile_k=64, stages=6)
+    a_t = torch.from_numpy(a.view(np.int16)).view(torch.bfloat16)
+    b_t = torch.from_numpy(b.view(np.int16)).view(torch.bfloat16)
+    ref64, mag = oracle.fp64_reference(a_t, b_t)
+    report = oracle.parity_report(bits_of(c), oracle.root_gemm(a, b), ref64, mag, k)
+    assert report["passed"], report
+
+
 def test_tcgen05_4096_integer_bit_exact_and_matches_cublas(cuda_device):
     """4096^3, integers in {-2..2}; exact, so the torch CPU
     FP32 reference, cuBLAS and this kernel must agree bit for bit."""
