@@ -39,6 +39,8 @@ KERNEL_AUTO = 0
 KERNEL_TCGEN05 = 1
 KERNEL_SIMT = 2
 
+FLAG_NO_TAIL_SPLIT = 1
+
 #: Every symbol include/kmcts_gemm.h declares.
 EXPORTED_SYMBOLS = (
     "kmcts_default_config",
@@ -79,12 +81,12 @@ class GemmConfig(ctypes.Structure):
         ("persistent", ctypes.c_int32),
         ("raster_group", ctypes.c_int32),
         ("kernel", ctypes.c_int32),
-        ("reserved", ctypes.c_int32),
+        ("flags", ctypes.c_int32),
         ("wait_limit_ns", ctypes.c_int64),
     ]
 
     def as_dict(self) -> dict[str, int]:
-        return {name: int(getattr(self, name)) for name, _ in self._fields_ if name != "reserved"}
+        return {name: int(getattr(self, name)) for name, _ in self._fields_}
 
 
 class CompareResult(ctypes.Structure):

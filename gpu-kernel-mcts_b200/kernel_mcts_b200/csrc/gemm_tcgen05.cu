@@ -430,18 +430,22 @@ int launch_tcgen05(const void* A, const void* B, void* C, int M, int N, int K, i
     const bool pair = is_pair(cfg);
     // Each CTA stages 128 rows of A, and BN (one CTA) or BN/2 (pair) of B.
     const uint32_t b_rows = pair ? cfg.tile_n / 2 : cfg.tile_n;
-    CUtensorMap ma, mb, mc;
+    CUtensorMap ma, mb, mb_half, mc;
     bool ok = encode_tensor_map_2d(&ma, A, K, M, static_cast<uint64_t>(K) * 2, 64, kBM);
     if (b_layout == KMCTS_B_COL) {
         ok = ok && encode_tensor_map_2d(&mb, B, K, N, static_cast<uint64_t>(K) * 2, 64, b_rows);
+        // Half-width units of a pair stage b_rows / 2 columns of B.
+        ok = ok && (!pair || encode_tensor_map_2d(&mb_half, B, K, N, static_cast<uint64_t>(K) * 2, 64,
+                                                  b_rows / 2));
     } else {
         ok = ok && encode_tensor_map_2d(&mb, B, N, K, static_cast<uint64_t>(N) * 2, 64, 64);
+        mb_half = mb;
     }
     ok = ok && encode_tensor_map_2d(&mc, C, N, M, static_cast<uint64_t>(N) * 2, 64, 32);
     if (!ok) return KMCTS_EINVAL;
     const uint64_t limit =
         cfg.wait_limit_ns > 0 ? static_cast<uint64_t>(cfg.wait_limit_ns) : kDefaultWaitNs;
-    if (pair) return launch_pair(ma, mb, mc, M, N, K, b_layout, cfg, limit, stream, device_status);
+    if (pair) return launch_pair(ma, mb, mb_half, mc, M, N, K, b_layout, cfg, limit, stream, device_status);
     const Variant* v = find_variant(cfg, b_layout);
     return v->fn(ma, mb, mc, M, N, K, cfg.raster_group, cfg.persistent != 0, limit, stream,
                  device_status);

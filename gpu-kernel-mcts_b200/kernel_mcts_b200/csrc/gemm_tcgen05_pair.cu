@@ -48,12 +48,34 @@ struct PairLayout {
     static_assert(kSmemBytes <= kMaxSmem, "shared memory budget exceeded");
 };
 
+// Work units.  Tiles [0, full_tiles) (in raster order) run whole; each later
+// tile runs as two BN/2-wide halves, so a last partial wave of R <= W/2 tiles
+// costs half a tile of time instead of a whole one.  Every output element is
+// still one full-K UMMA chain: splitting changes no result bit.
+struct Unit {
+    int m_blk, n0, width;
+};
+
+template <int BN>
+__device__ __forceinline__ Unit pair_unit(int u, int full_tiles, int num_m, int num_n, int group) {
+    int t = u, half = 0, width = BN;
+    if (u >= full_tiles) {
+        const int v = u - full_tiles;
+        t = full_tiles + v / 2;
+        half = v & 1;
+        width = BN / 2;
+    }
+    const TileCoord tc = tile_coord(t, num_m, num_n, group);
+    return {tc.m_blk, tc.n_blk * BN + half * (BN / 2), width};
+}
+
 template <int BN, int BK, int STAGES, bool B_MN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_tcgen05_pair(const __grid_constant__ CUtensorMap map_a,
                            const __grid_constant__ CUtensorMap map_b,
+                           const __grid_constant__ CUtensorMap map_b_half,
                            const __grid_constant__ CUtensorMap map_c, int M, int N, int K, int group,
-                           uint64_t limit_ns, int* status) {
+                           int full_tiles, uint64_t limit_ns, int* status) {
     using L = PairLayout<BN, BK, STAGES, B_MN>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -77,6 +99,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int num_m = (M + 255) / 256;
     const int num_n = (N + BN - 1) / BN;
     const int num_tiles = num_m * num_n;
+    const int num_units = full_tiles + 2 * (num_tiles - full_tiles);
     const int num_kb = (K + BK - 1) / BK;
 
     if (threadIdx.x == 0) {
@@ -96,6 +119,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 0 && lane == 0) {
         ptx::prefetch_tensormap(&map_a);
         ptx::prefetch_tensormap(&map_b);
+        ptx::prefetch_tensormap(&map_b_half);
         ptx::prefetch_tensormap(&map_c);
     }
     if (warp == 1) {
@@ -115,10 +139,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t phase = 0;
             uint32_t issued = 0, issued_phase = 0;
             bool ok = true;
-            for (int t = cluster_id; t < num_tiles && ok; t += num_clusters) {
-                const TileCoord tc = tile_coord(t, num_m, num_n, group);
-                const int m0 = tc.m_blk * 256 + static_cast<int>(rank) * 128;
-                const int nb0 = tc.n_blk * BN + static_cast<int>(rank) * L::kHalfN;
+            for (int u = cluster_id; u < num_units && ok; u += num_clusters) {
+                const Unit w = pair_unit<BN>(u, full_tiles, num_m, num_n, group);
+                const int m0 = w.m_blk * 256 + static_cast<int>(rank) * 128;
+                const int b_cols = w.width / 2;  // B columns this CTA stages
+                const int nb0 = w.n0 + static_cast<int>(rank) * b_cols;
+                const uint32_t unit_bytes = 2u * (L::kABytes + b_cols * BK * 2);
+                const CUtensorMap* mb = w.width == BN ? &map_b : &map_b_half;
                 for (int kb = 0; kb < num_kb; ++kb) {
                     if (!ptx::mbar_wait(&empty[stage], phase ^ 1u, limit_ns, abort)) {
                         record_failure(status, abort, kRoleProducer);
@@ -127,20 +154,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     uint8_t* sa = smem + stage * L::kStageBytes;
                     uint8_t* sb = sa + L::kABytes;
-                    if (leader) ptx::mbar_arrive_expect_tx(&full[stage], 2 * L::kStageBytes);
+                    if (leader) ptx::mbar_arrive_expect_tx(&full[stage], unit_bytes);
                     const uint32_t bar = ptx::mapa_shared(ptx::smem_addr(&full[stage]), 0);
 #pragma unroll
                     for (int kh = 0; kh < BK / 64; ++kh) {
                         const int k0 = kb * BK + kh * 64;
                         ptx::tma_load_2d_pair(sa + kh * (128 * 128), &map_a, bar, k0, m0);
                         if constexpr (B_MN) {
-#pragma unroll
-                            for (int nb = 0; nb < L::kHalfN / 64; ++nb) {
+                            for (int nb = 0; nb < b_cols / 64; ++nb) {
                                 ptx::tma_load_2d_pair(sb + (kh * (L::kHalfN / 64) + nb) * 8192, &map_b, bar,
                                                       nb0 + nb * 64, k0);
                             }
                         } else {
-                            ptx::tma_load_2d_pair(sb + kh * (L::kHalfN * 128), &map_b, bar, k0, nb0);
+                            ptx::tma_load_2d_pair(sb + kh * (L::kHalfN * 128), mb, bar, k0, nb0);
                         }
                     }
                     issued |= 1u << stage;
@@ -164,12 +190,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == 1) {
         // ----------------------------------------------------------------- MMA
         if (lane == 0 && leader) {
-            constexpr uint32_t idesc = ptx::make_idesc_bf16(256, BN, B_MN);
+            constexpr uint32_t idesc_full = ptx::make_idesc_bf16(256, BN, B_MN);
+            constexpr uint32_t idesc_half = ptx::make_idesc_bf16(256, BN / 2, B_MN);
             int stage = 0;
             uint32_t phase = 0;
             int local = 0;
             bool ok = true;
-            for (int t = cluster_id; t < num_tiles && ok; t += num_clusters, ++local) {
+            for (int u = cluster_id; u < num_units && ok; u += num_clusters, ++local) {
+                const uint32_t idesc = u < full_tiles ? idesc_full : idesc_half;
                 const int acc = local & 1;
                 const uint32_t acc_phase = (local >> 1) & 1;
                 if (!ptx::mbar_wait(&tmem_empty[acc], acc_phase ^ 1u, limit_ns, abort)) {
@@ -217,10 +245,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint8_t* staging = smem + L::kStagingOffset + (warp - 2) * 2 * kStagingBytes;
         int local = 0;
         int chunk_count = 0;
-        for (int t = cluster_id; t < num_tiles; t += num_clusters, ++local) {
-            const TileCoord tc = tile_coord(t, num_m, num_n, group);
-            const int m0 = tc.m_blk * 256 + static_cast<int>(rank) * 128;
-            const int n0 = tc.n_blk * BN;
+        for (int u = cluster_id; u < num_units; u += num_clusters, ++local) {
+            const Unit w = pair_unit<BN>(u, full_tiles, num_m, num_n, group);
+            const int m0 = w.m_blk * 256 + static_cast<int>(rank) * 128;
+            const int n0 = w.n0;
+            const int chunks = w.width / 64;
             const int acc = local & 1;
             const uint32_t acc_phase = (local >> 1) & 1;
             bool ok = ptx::mbar_wait(&tmem_full[acc], acc_phase, limit_ns, abort);
@@ -233,12 +262,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t row_addr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                                       static_cast<uint32_t>(acc * BN);
 #pragma unroll 1
-            for (int c = 0; c < BN / 64; ++c) {
+            for (int c = 0; c < chunks; ++c) {
                 uint32_t lo[32], hi[32];
                 ptx::tmem_ld_32x32b_x32(row_addr + c * 64, lo);
                 ptx::tmem_ld_32x32b_x32(row_addr + c * 64 + 32, hi);
                 ptx::tmem_wait_ld();
-                if (c == BN / 64 - 1) {
+                if (c == chunks - 1) {
                     ptx::tc_fence_before();
                     __syncwarp();
                     if (lane == 0) ptx::mbar_arrive_cluster(ptx::mapa_shared(ptx::smem_addr(&tmem_empty[acc]), 0));
@@ -271,9 +300,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 constexpr int kMaxDevices = 64;
 
 template <int BN, int BK, int STAGES, bool B_MN>
-int launch_pair_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, int M, int N,
-                        int K, int group, bool persistent, uint64_t limit_ns, cudaStream_t stream,
-                        int* status) {
+int launch_pair_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb_half,
+                        const CUtensorMap& mc, int M, int N, int K, int group, bool persistent, bool split_tail,
+                        uint64_t limit_ns, cudaStream_t stream, int* status) {
     using L = PairLayout<BN, BK, STAGES, B_MN>;
     auto kernel = gemm_bf16_tcgen05_pair<BN, BK, STAGES, B_MN>;
     static std::mutex mu;
@@ -307,15 +336,28 @@ int launch_pair_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUte
         }
     }
     const int tiles = ((M + 255) / 256) * ((N + BN - 1) / BN);
-    const int clusters = persistent ? (tiles < max_clusters[device] ? tiles : max_clusters[device]) : tiles;
+    const int workers = max_clusters[device];
+    int full_tiles = tiles;
+    int clusters = tiles;
+    if (persistent) {
+        // Split the last partial wave into half-width units when it fits in
+        // one round of half units (2R <= W); half tiles need BN/2 to be a
+        // whole number of 64-column TMA boxes per CTA for row-major B.
+        const int rem = tiles % workers;
+        const bool can_split = split_tail && BN == 256 && rem != 0 && 2 * rem <= workers;
+        full_tiles = can_split ? tiles - rem : tiles;
+        const int units = full_tiles + 2 * (tiles - full_tiles);
+        clusters = units < workers ? units : workers;
+    }
     config.gridDim = dim3(2 * clusters, 1, 1);
-    const cudaError_t err = cudaLaunchKernelEx(&config, kernel, ma, mb, mc, M, N, K, group, limit_ns, status);
+    const cudaError_t err = cudaLaunchKernelEx(&config, kernel, ma, mb, mb_half, mc, M, N, K, group, full_tiles,
+                                               limit_ns, status);
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return err == cudaSuccess ? KMCTS_OK : KMCTS_EGEMM;
 }
 
-using PairLauncher = int (*)(const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, int, int, int, int,
-                             bool, uint64_t, cudaStream_t, int*);
+using PairLauncher = int (*)(const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, int,
+                             int, int, int, bool, bool, uint64_t, cudaStream_t, int*);
 
 struct PairVariant {
     int bn, bk, stages, b_mn;
@@ -352,13 +394,14 @@ int64_t pair_smem_bytes(int bn, int bk, int stages) {
            kSmemReserve;
 }
 
-int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, int M, int N, int K,
-                int b_layout, const kmcts_gemm_config& cfg, uint64_t limit_ns, cudaStream_t stream,
-                int* status) {
+int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb_half, const CUtensorMap& mc,
+                int M, int N, int K, int b_layout, const kmcts_gemm_config& cfg, uint64_t limit_ns,
+                cudaStream_t stream, int* status) {
     const int mn = b_layout == KMCTS_B_ROW ? 1 : 0;
     for (const PairVariant& v : kPairVariants) {
         if (v.bn == cfg.tile_n && v.bk == cfg.tile_k && v.stages == cfg.stages && v.b_mn == mn) {
-            return v.fn(ma, mb, mc, M, N, K, cfg.raster_group, cfg.persistent != 0, limit_ns, stream, status);
+            return v.fn(ma, mb, mb_half, mc, M, N, K, cfg.raster_group, cfg.persistent != 0,
+                        (cfg.flags & KMCTS_FLAG_NO_TAIL_SPLIT) == 0, limit_ns, stream, status);
         }
     }
     return KMCTS_ENOTSUP;

@@ -39,9 +39,9 @@ int multiprocessor_count();
 // CTA-pair (cta_group::2) kernels, gemm_tcgen05_pair.cu.
 bool pair_variant_exists(int bn, int bk, int stages, int b_layout);
 int64_t pair_smem_bytes(int bn, int bk, int stages);
-int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, int M, int N, int K,
-                int b_layout, const kmcts_gemm_config& cfg, uint64_t limit_ns, cudaStream_t stream,
-                int* status);
+int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb_half, const CUtensorMap& mc,
+                int M, int N, int K, int b_layout, const kmcts_gemm_config& cfg, uint64_t limit_ns,
+                cudaStream_t stream, int* status);
 
 }  // namespace kmcts
 

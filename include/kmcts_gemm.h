@@ -42,18 +42,24 @@ extern "C" {
 #define KMCTS_KERNEL_TCGEN05 1 /* tcgen05/TMA/TMEM kernel only (ENOTSUP otherwise) */
 #define KMCTS_KERNEL_SIMT 2    /* CUDA-core kernel, any shape */
 
+/* Schedule flags.  By default a persistent CTA-pair launch whose last partial
+ * wave has R <= W/2 tiles (W = co-resident pairs) runs those R tiles as 2R
+ * half-width units, so the tail costs half a tile of time; results are
+ * bit-identical either way.  This flag keeps every tile whole. */
+#define KMCTS_FLAG_NO_TAIL_SPLIT 1
+
 /* Kernel schedule.  Zero-initialise and call kmcts_default_config() first. */
 typedef struct kmcts_gemm_config {
-    int32_t tile_m;       /* CTA tile rows: 128 */
-    int32_t tile_n;       /* CTA tile columns: 64, 128, 192 or 256 */
+    int32_t tile_m;       /* 128: one CTA per tile; 256: one CTA pair per tile */
+    int32_t tile_n;       /* tile columns: 64, 128, 192, 256 (one CTA); 128, 256 (pair) */
     int32_t tile_k;       /* K per pipeline stage: 64 or 128 */
-    int32_t stages;       /* shared-memory pipeline depth: 2..8 */
-    int32_t cluster_m;    /* must be 1 in this version */
-    int32_t cluster_n;    /* must be 1 in this version */
+    int32_t stages;       /* shared-memory pipeline depth: 2..6 */
+    int32_t cluster_m;    /* 1 with tile_m 128; 2 with tile_m 256 (tcgen05 cta_group::2) */
+    int32_t cluster_n;    /* must be 1: no TMA multicast is used */
     int32_t persistent;   /* 1: one CTA per SM loops over tiles; 0: one CTA per tile */
     int32_t raster_group; /* M-tiles per raster group (L2 locality), >= 1 */
     int32_t kernel;       /* KMCTS_KERNEL_* */
-    int32_t reserved;
+    int32_t flags;        /* KMCTS_FLAG_* bits */
     int64_t wait_limit_ns; /* bound on each device-side wait; 0 = 2 s default */
 } kmcts_gemm_config;
 

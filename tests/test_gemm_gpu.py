@@ -152,6 +152,32 @@ def test_cta_pair_uniform_inputs_within_criterion(cuda_device, layout):
     assert report["passed"], report
 
 
+@pytest.mark.parametrize("layout", ["col", "row"])
+def test_cta_pair_split_tail_bit_exact(cuda_device, layout):
+    """1024x2048: 32 pair tiles < 74 co-resident pairs, so every tile runs as
+    two half-width units; integer inputs stay bit-exact."""
+    m, n, k = 1024, 2048, 512
+    a_t, b_t = oracle.integer_inputs(m, n, k, seed=5)
+    expect = oracle.root_gemm(oracle.torch_bits(a_t), oracle.torch_bits(b_t))
+    c = run(a_t.cuda(), b_for(layout, b_t.cuda()), layout, kernel=_native.KERNEL_TCGEN05, tile_m=256,
+            cluster_m=2, tile_n=256, tile_k=64, stages=6)
+    np.testing.assert_array_equal(bits_of(c), expect)
+
+
+@pytest.mark.parametrize("layout", ["col", "row"])
+@pytest.mark.parametrize("shape", [(4096, 4096, 4096), (1024, 2048, 512), (3072, 5120, 1024)])
+def test_cta_pair_split_tail_changes_no_bit(cuda_device, layout, shape):
+    """Splitting the last wave into half-width units keeps every output one
+    full-K UMMA chain: N(0,1) results are bit-identical with and without it."""
+    m, n, k = shape
+    a_t, b_t = oracle.randn_inputs(m, n, k, seed=2, b_layout=layout)
+    a, b = a_t.cuda(), b_t.cuda()
+    base = dict(kernel=_native.KERNEL_TCGEN05, tile_m=256, cluster_m=2, tile_n=256, tile_k=64, stages=6)
+    split = run(a, b, layout, **base)
+    whole = run(a, b, layout, flags=_native.FLAG_NO_TAIL_SPLIT, **base)
+    assert torch.equal(split.view(torch.int16), whole.view(torch.int16))
+
+
 def test_tcgen05_4096_integer_bit_exact_and_matches_cublas(cuda_device):
     """4096^3, integers in {-2..2}; exact, so the torch CPU
     FP32 reference, cuBLAS and this kernel must agree bit for bit."""
