@@ -52,6 +52,7 @@ EXPORTED_SYMBOLS = (
     "kmcts_compare_workspace_bytes",
     "kmcts_bf16_compare",
     "kmcts_launch_count",
+    "kmcts_gemm_plan_query",
 )
 
 
@@ -83,6 +84,24 @@ class GemmConfig(ctypes.Structure):
         ("kernel", ctypes.c_int32),
         ("flags", ctypes.c_int32),
         ("wait_limit_ns", ctypes.c_int64),
+    ]
+
+    def as_dict(self) -> dict[str, int]:
+        return {name: int(getattr(self, name)) for name, _ in self._fields_}
+
+
+class GemmPlan(ctypes.Structure):
+    """Mirror of ``kmcts_gemm_plan``."""
+
+    _fields_ = [
+        ("kernel", ctypes.c_int32),
+        ("ctas", ctypes.c_int32),
+        ("cluster_size", ctypes.c_int32),
+        ("workers", ctypes.c_int32),
+        ("tiles", ctypes.c_int32),
+        ("full_tiles", ctypes.c_int32),
+        ("units", ctypes.c_int32),
+        ("smem_bytes", ctypes.c_int32),
     ]
 
     def as_dict(self) -> dict[str, int]:
@@ -149,6 +168,8 @@ def load() -> ctypes.CDLL:
             vp, vp, i64, ctypes.c_double, ctypes.c_double, vp, vp, ctypes.POINTER(CompareResult),
         ]
         lib.kmcts_bf16_compare.restype = i32
+        lib.kmcts_gemm_plan_query.argtypes = [ctypes.POINTER(GemmConfig), i32, i32, i32, i32, ctypes.POINTER(GemmPlan)]
+        lib.kmcts_gemm_plan_query.restype = i32
         lib.kmcts_launch_count.argtypes = []
         lib.kmcts_launch_count.restype = i64
         _lib = lib
@@ -178,6 +199,15 @@ def config_legal(cfg: GemmConfig, m: int, n: int, k: int, b_layout: int = B_COL)
 
 def config_smem_bytes(cfg: GemmConfig, b_layout: int = B_COL) -> int:
     return int(load().kmcts_config_smem_bytes(ctypes.byref(cfg), b_layout))
+
+
+def plan(cfg: GemmConfig | None, m: int, n: int, k: int, b_layout: int = B_COL) -> dict[str, int]:
+    """Launch shape of a schedule on the current CUDA device (no launch)."""
+    out = GemmPlan()
+    code = load().kmcts_gemm_plan_query(ctypes.byref(cfg) if cfg is not None else None, m, n, k, b_layout,
+                                        ctypes.byref(out))
+    check(code, "kmcts_gemm_plan_query")
+    return out.as_dict()
 
 
 def version() -> str:

@@ -124,6 +124,28 @@ int kmcts_bf16_gemm(const void* A, const void* B, void* C, int M, int N, int K) 
     return status == 0 ? KMCTS_OK : KMCTS_ETIMEOUT;
 }
 
+int kmcts_gemm_plan_query(const kmcts_gemm_config* cfg, int M, int N, int K, int b_layout, kmcts_gemm_plan* out) {
+    if (!out) return KMCTS_EINVAL;
+    kmcts_gemm_config local;
+    if (cfg) {
+        local = *cfg;
+    } else {
+        kmcts_default_config(&local);
+    }
+    if (local.kernel != KMCTS_KERNEL_SIMT) {
+        const int rc = plan_tcgen05(local, M, N, K, b_layout, out);
+        if (rc != KMCTS_ENOTSUP || local.kernel == KMCTS_KERNEL_TCGEN05) return rc;
+    }
+    kmcts_gemm_plan plan = {};
+    plan.kernel = 3;
+    plan.cluster_size = 1;
+    plan.tiles = ((M + 63) / 64) * ((N + 63) / 64);
+    plan.full_tiles = plan.units = plan.ctas = plan.tiles;
+    plan.workers = multiprocessor_count();
+    *out = plan;
+    return KMCTS_OK;
+}
+
 size_t kmcts_compare_workspace_bytes(void) { return compare_workspace_bytes(); }
 
 int kmcts_bf16_compare(const void* C, const void* reference, int64_t count, double rtol,

@@ -451,6 +451,23 @@ int launch_tcgen05(const void* A, const void* B, void* C, int M, int N, int K, i
                  device_status);
 }
 
+int plan_tcgen05(const kmcts_gemm_config& cfg, int M, int N, int K, int b_layout, kmcts_gemm_plan* out) {
+    const int rc = tcgen05_legal(cfg, M, N, K, b_layout, nullptr, 0);
+    if (rc != KMCTS_OK) return rc;
+    if (is_pair(cfg)) return plan_pair(cfg, M, N, b_layout, out);
+    kmcts_gemm_plan plan = {};
+    plan.kernel = 1;
+    plan.cluster_size = 1;
+    plan.workers = multiprocessor_count();
+    plan.tiles = ((M + kBM - 1) / kBM) * ((N + cfg.tile_n - 1) / cfg.tile_n);
+    plan.full_tiles = plan.tiles;
+    plan.units = plan.tiles;
+    plan.ctas = cfg.persistent ? (plan.tiles < plan.workers ? plan.tiles : plan.workers) : plan.tiles;
+    plan.smem_bytes = static_cast<int32_t>(tcgen05_smem_bytes(cfg, b_layout));
+    *out = plan;
+    return KMCTS_OK;
+}
+
 int take_default_status(cudaStream_t stream, int* value) {
     int zero = 0;
     if (cudaStreamSynchronize(stream) != cudaSuccess) return KMCTS_ESYNC;

@@ -299,59 +299,96 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 constexpr int kMaxDevices = 64;
 
+// Co-resident CTA pairs of a pair kernel on the current device (cached).
+template <int BN, int BK, int STAGES, bool B_MN>
+int pair_workers(int device) {
+    using L = PairLayout<BN, BK, STAGES, B_MN>;
+    auto kernel = gemm_bf16_tcgen05_pair<BN, BK, STAGES, B_MN>;
+    static std::mutex mu;
+    static int max_clusters[kMaxDevices] = {};
+    std::lock_guard<std::mutex> lock(mu);
+    if (max_clusters[device] == 0) {
+        if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmemBytes) != cudaSuccess)
+            return -1;
+        cudaLaunchConfig_t config = {};
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        config.gridDim = dim3(2 * (multiprocessor_count() / 2), 1, 1);
+        config.blockDim = dim3(kThreads, 1, 1);
+        config.dynamicSmemBytes = L::kSmemBytes;
+        config.attrs = attr;
+        config.numAttrs = 1;
+        int clusters = 0;
+        if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &config) != cudaSuccess || clusters <= 0) {
+            cudaGetLastError();
+            clusters = multiprocessor_count() / 2;
+        }
+        max_clusters[device] = clusters;
+    }
+    return max_clusters[device];
+}
+
+// The launch shape: how many pairs run, and which tiles run whole.
+template <int BN>
+kmcts_gemm_plan make_pair_plan(int M, int N, int workers, bool persistent, bool split_tail, int64_t smem) {
+    kmcts_gemm_plan plan = {};
+    plan.kernel = 2;
+    plan.cluster_size = 2;
+    plan.workers = workers;
+    plan.tiles = ((M + 255) / 256) * ((N + BN - 1) / BN);
+    plan.full_tiles = plan.tiles;
+    plan.units = plan.tiles;
+    int clusters = plan.tiles;
+    if (persistent) {
+        // Split the last partial wave into half-width units when it fits in
+        // one round of half units (2R <= W); half tiles need BN/2 to be a
+        // whole number of 64-column TMA boxes per CTA for row-major B.
+        const int rem = plan.tiles % workers;
+        const bool can_split = split_tail && BN == 256 && rem != 0 && 2 * rem <= workers;
+        plan.full_tiles = can_split ? plan.tiles - rem : plan.tiles;
+        plan.units = plan.full_tiles + 2 * (plan.tiles - plan.full_tiles);
+        clusters = plan.units < workers ? plan.units : workers;
+    }
+    plan.ctas = 2 * clusters;
+    plan.smem_bytes = static_cast<int32_t>(smem);
+    return plan;
+}
+
+template <int BN, int BK, int STAGES, bool B_MN>
+int plan_pair_variant(int M, int N, bool persistent, bool split_tail, kmcts_gemm_plan* out) {
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kMaxDevices) return KMCTS_EHANDLE;
+    const int workers = pair_workers<BN, BK, STAGES, B_MN>(device);
+    if (workers <= 0) return KMCTS_EGEMM;
+    *out = make_pair_plan<BN>(M, N, workers, persistent, split_tail, PairLayout<BN, BK, STAGES, B_MN>::kSmemBytes);
+    return KMCTS_OK;
+}
+
 template <int BN, int BK, int STAGES, bool B_MN>
 int launch_pair_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb_half,
                         const CUtensorMap& mc, int M, int N, int K, int group, bool persistent, bool split_tail,
                         uint64_t limit_ns, cudaStream_t stream, int* status) {
     using L = PairLayout<BN, BK, STAGES, B_MN>;
-    auto kernel = gemm_bf16_tcgen05_pair<BN, BK, STAGES, B_MN>;
-    static std::mutex mu;
-    static int max_clusters[kMaxDevices] = {};
-    int device = 0;
-    if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kMaxDevices) return KMCTS_EHANDLE;
+    kmcts_gemm_plan plan;
+    const int rc = plan_pair_variant<BN, BK, STAGES, B_MN>(M, N, persistent, split_tail, &plan);
+    if (rc != KMCTS_OK) return rc;
     cudaLaunchConfig_t config = {};
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    config.gridDim = dim3(plan.ctas, 1, 1);
     config.blockDim = dim3(kThreads, 1, 1);
     config.dynamicSmemBytes = L::kSmemBytes;
     config.stream = stream;
     config.attrs = attr;
     config.numAttrs = 1;
-    {
-        std::lock_guard<std::mutex> lock(mu);
-        if (max_clusters[device] == 0) {
-            if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmemBytes) !=
-                cudaSuccess)
-                return KMCTS_EGEMM;
-            config.gridDim = dim3(2 * 74, 1, 1);
-            int clusters = 0;
-            if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &config) != cudaSuccess || clusters <= 0) {
-                cudaGetLastError();
-                clusters = multiprocessor_count() / 2;
-            }
-            max_clusters[device] = clusters;
-        }
-    }
-    const int tiles = ((M + 255) / 256) * ((N + BN - 1) / BN);
-    const int workers = max_clusters[device];
-    int full_tiles = tiles;
-    int clusters = tiles;
-    if (persistent) {
-        // Split the last partial wave into half-width units when it fits in
-        // one round of half units (2R <= W); half tiles need BN/2 to be a
-        // whole number of 64-column TMA boxes per CTA for row-major B.
-        const int rem = tiles % workers;
-        const bool can_split = split_tail && BN == 256 && rem != 0 && 2 * rem <= workers;
-        full_tiles = can_split ? tiles - rem : tiles;
-        const int units = full_tiles + 2 * (tiles - full_tiles);
-        clusters = units < workers ? units : workers;
-    }
-    config.gridDim = dim3(2 * clusters, 1, 1);
-    const cudaError_t err = cudaLaunchKernelEx(&config, kernel, ma, mb, mb_half, mc, M, N, K, group, full_tiles,
-                                               limit_ns, status);
+    const cudaError_t err = cudaLaunchKernelEx(&config, gemm_bf16_tcgen05_pair<BN, BK, STAGES, B_MN>, ma, mb,
+                                               mb_half, mc, M, N, K, group, plan.full_tiles, limit_ns, status);
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return err == cudaSuccess ? KMCTS_OK : KMCTS_EGEMM;
 }
@@ -359,12 +396,16 @@ int launch_pair_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUte
 using PairLauncher = int (*)(const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, int,
                              int, int, int, bool, bool, uint64_t, cudaStream_t, int*);
 
+using PairPlanner = int (*)(int, int, bool, bool, kmcts_gemm_plan*);
+
 struct PairVariant {
     int bn, bk, stages, b_mn;
     PairLauncher fn;
+    PairPlanner plan;
 };
 
-#define KMCTS_PAIR(BN, BK, ST, MN) {BN, BK, ST, MN, &launch_pair_variant<BN, BK, ST, MN>}
+#define KMCTS_PAIR(BN, BK, ST, MN) \
+    {BN, BK, ST, MN, &launch_pair_variant<BN, BK, ST, MN>, &plan_pair_variant<BN, BK, ST, MN>}
 
 // Every pair schedule of the sweep grid that fits 227 KB:
 // stages * (128 + BN/2) * BK * 2 + 32 KB staging + 2 KB.
@@ -392,6 +433,16 @@ bool pair_variant_exists(int bn, int bk, int stages, int b_layout) {
 int64_t pair_smem_bytes(int bn, int bk, int stages) {
     return static_cast<int64_t>(stages) * (128 + bn / 2) * bk * 2 + kEpilogueWarps * 2 * kStagingBytes +
            kSmemReserve;
+}
+
+int plan_pair(const kmcts_gemm_config& cfg, int M, int N, int b_layout, kmcts_gemm_plan* out) {
+    const int mn = b_layout == KMCTS_B_ROW ? 1 : 0;
+    for (const PairVariant& v : kPairVariants) {
+        if (v.bn == cfg.tile_n && v.bk == cfg.tile_k && v.stages == cfg.stages && v.b_mn == mn) {
+            return v.plan(M, N, cfg.persistent != 0, (cfg.flags & KMCTS_FLAG_NO_TAIL_SPLIT) == 0, out);
+        }
+    }
+    return KMCTS_ENOTSUP;
 }
 
 int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb_half, const CUtensorMap& mc,

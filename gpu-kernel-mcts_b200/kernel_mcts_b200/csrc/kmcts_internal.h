@@ -18,6 +18,9 @@ extern std::atomic<int64_t> g_launches;
 bool encode_tensor_map_2d(CUtensorMap* map, const void* base, uint64_t dim0, uint64_t dim1,
                           uint64_t row_stride_bytes, uint32_t box0, uint32_t box1);
 
+// Launch shape of a legal tcgen05 schedule on the current device.
+int plan_tcgen05(const kmcts_gemm_config& cfg, int M, int N, int K, int b_layout, kmcts_gemm_plan* out);
+
 // tcgen05 path.  Returns KMCTS_OK or an error code; launches nothing on error.
 int launch_tcgen05(const void* A, const void* B, void* C, int M, int N, int K, int b_layout,
                    const kmcts_gemm_config& cfg, cudaStream_t stream, int* device_status);
@@ -39,6 +42,7 @@ int multiprocessor_count();
 // CTA-pair (cta_group::2) kernels, gemm_tcgen05_pair.cu.
 bool pair_variant_exists(int bn, int bk, int stages, int b_layout);
 int64_t pair_smem_bytes(int bn, int bk, int stages);
+int plan_pair(const kmcts_gemm_config& cfg, int M, int N, int b_layout, kmcts_gemm_plan* out);
 int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb_half, const CUtensorMap& mc,
                 int M, int N, int K, int b_layout, const kmcts_gemm_config& cfg, uint64_t limit_ns,
                 cudaStream_t stream, int* status);

@@ -56,7 +56,9 @@ def main() -> None:
     if int(status.item()) != 0:
         raise SystemExit(f"device status {int(status.item()):#x}")
     flops = 2.0 * args.M * args.N * args.K
-    print(json.dumps({"config": cfg.as_dict(), "shape": [args.M, args.N, args.K], "b_layout": args.b_layout,
+    layout_code = _native.B_ROW if args.b_layout == "row" else _native.B_COL
+    plan = _native.plan(cfg, args.M, args.N, args.K, layout_code)
+    print(json.dumps({"config": cfg.as_dict(), "plan": plan, "shape": [args.M, args.N, args.K], "b_layout": args.b_layout,
                       "times_us": times, "median_us": statistics.median(times),
                       "tflops": flops / (statistics.median(times) * 1e-6) / 1e12}))
 

@@ -92,6 +92,23 @@ int kmcts_config_legal(const kmcts_gemm_config* cfg, int M, int N, int K, int b_
 /* Shared-memory bytes a schedule needs per CTA (0 if the schedule is invalid). */
 int64_t kmcts_config_smem_bytes(const kmcts_gemm_config* cfg, int b_layout);
 
+/* How a schedule would launch on the current device. */
+typedef struct kmcts_gemm_plan {
+    int32_t kernel;       /* 1: one CTA per tile; 2: CTA pair; 3: SIMT */
+    int32_t ctas;         /* grid size in CTAs */
+    int32_t cluster_size; /* CTAs per cluster */
+    int32_t workers;      /* clusters that can be resident at once */
+    int32_t tiles;        /* output tiles */
+    int32_t full_tiles;   /* tiles run whole; the rest run as two half-width units */
+    int32_t units;        /* work units the grid walks */
+    int32_t smem_bytes;   /* dynamic shared memory per CTA */
+} kmcts_gemm_plan;
+
+/* Fills *out with the launch shape kmcts_bf16_gemm_ex would use for this
+ * schedule and shape on the current device (queries occupancy; launches
+ * nothing).  Returns KMCTS_OK or the error kmcts_bf16_gemm_ex would return. */
+int kmcts_gemm_plan_query(const kmcts_gemm_config* cfg, int M, int N, int K, int b_layout, kmcts_gemm_plan* out);
+
 /* Library version string. */
 const char* kmcts_version(void);
 
