@@ -61,7 +61,7 @@ def load_peaks() -> tuple[dict, str]:
 
 def profiled_traffic() -> float | None:
     """DRAM bytes per launch of the GEMM kernel from the committed ncu summary."""
-    path = ROOT / "profiles" / "gemm_tcgen05_4096.md"
+    path = ROOT / "profiles" / "gemm_tcgen05_pair_4096.md"
     if not path.exists():
         return None
     for line in path.read_text().splitlines():
@@ -242,18 +242,26 @@ def run_reference(args: argparse.Namespace) -> None:
 
 def time_launches(fn, steps: int, stream, flush) -> list[float]:
     """Per-launch event timing (µs) with an L2 flush before each launch."""
+    return time_interleaved([fn], steps, stream, flush)[0]
+
+
+def time_interleaved(fns, steps: int, stream, flush) -> list[list[float]]:
+    """Per-launch event timing (µs) of several callables, interleaved step by
+    step (flush, fn0, flush, fn1, ...) so clock and power drift hit all of
+    them alike.  Events are recorded on the launching stream."""
     import torch
 
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
-    stops = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    starts = [[torch.cuda.Event(enable_timing=True) for _ in range(steps)] for _ in fns]
+    stops = [[torch.cuda.Event(enable_timing=True) for _ in range(steps)] for _ in fns]
     with torch.cuda.stream(stream):
         for i in range(steps):
-            flush.fill_(i & 0xFF)
-            starts[i].record(stream)
-            fn()
-            stops[i].record(stream)
+            for j, fn in enumerate(fns):
+                flush.fill_((i + j) & 0xFF)
+                starts[j][i].record(stream)
+                fn()
+                stops[j][i].record(stream)
     stream.synchronize()
-    return [s.elapsed_time(e) * 1e3 for s, e in zip(starts, stops)]
+    return [[s.elapsed_time(e) * 1e3 for s, e in zip(starts[j], stops[j])] for j in range(len(fns))]
 
 
 def run_ours(args: argparse.Namespace) -> None:
@@ -282,6 +290,7 @@ def run_ours(args: argparse.Namespace) -> None:
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
     stream = torch.cuda.Stream(device)
     cfg = _native.default_config()
+    plan = _native.plan(cfg, M, N, K, _native.B_ROW if layout == "row" else _native.B_COL)
     status = torch.zeros(1, dtype=torch.int32, device=device)
 
     def ours():
@@ -307,11 +316,9 @@ def run_ours(args: argparse.Namespace) -> None:
     with ClockSampler(local_rank) as clocks:
         barrier()
         launches0 = _native.launch_count()
-        ours_us = time_launches(ours, args.steps, stream, flush)
+        ours_us, cublas_us = time_interleaved([ours, cublas], args.steps, stream, flush)
         launches = _native.launch_count() - launches0
         barrier()
-    cublas_us = time_launches(cublas, args.steps, stream, flush)
-    barrier()
     if int(status.item()) != 0:
         raise RuntimeError(f"device status {int(status.item()):#x}")
 
@@ -393,9 +400,12 @@ def run_ours(args: argparse.Namespace) -> None:
                 "workload": "bf16_gemm_4096 (BASELINE config 2: M=N=K=4096, N(0,1) seed 0)",
                 "M": M, "N": N, "K": K,
                 "b_layout": layout,
-                "kernel": "tcgen05 persistent 128x%dx%d, %d stages" % (cfg.tile_n, cfg.tile_k, cfg.stages),
+                "kernel": ("tcgen05 persistent %s %dx%dx%d, %d stages"
+                           % ("CTA-pair (cta_group::2)" if cfg.tile_m == 256 else "1-CTA",
+                              cfg.tile_m, cfg.tile_n, cfg.tile_k, cfg.stages)),
+                "plan": plan,
                 "parallelism": f"replicas x{world} (one evaluation per GPU, no collective)",
-                "timing": "per-launch CUDA events on the launching stream, median",
+                "timing": "per-launch CUDA events on the launching stream, median; ours and cuBLAS interleaved step by step",
                 "l2": "flushed before every timed launch (512 MiB write)",
             },
             "median_us": med_ours,

@@ -67,11 +67,13 @@ extern "C" {
 int kmcts_default_config(kmcts_gemm_config* cfg) {
     if (!cfg) return KMCTS_EINVAL;
     std::memset(cfg, 0, sizeof(*cfg));
-    cfg->tile_m = 128;
+    // CTA pair, 256 x 256 tile, BK 128, 3 stages: the fastest schedule of the
+    // sweep at 4096^3 on B200 (ties cuBLAS; see the profiles directory).
+    cfg->tile_m = 256;
     cfg->tile_n = 256;
-    cfg->tile_k = 64;
-    cfg->stages = 4;
-    cfg->cluster_m = 1;
+    cfg->tile_k = 128;
+    cfg->stages = 3;
+    cfg->cluster_m = 2;
     cfg->cluster_n = 1;
     cfg->persistent = 1;
     cfg->raster_group = 8;

@@ -40,21 +40,25 @@ def test_struct_sizes_match_header():
 def test_version_and_default_config():
     assert "sm_100a" in km.version()
     cfg = km.default_config()
-    assert (cfg.tile_m, cfg.tile_n, cfg.tile_k) == (128, 256, 64)
+    assert (cfg.tile_m, cfg.tile_n, cfg.tile_k, cfg.stages, cfg.cluster_m) == (256, 256, 128, 3, 2)
     assert km.config_legal(cfg, 4096, 4096, 4096) == (0, "ok")
 
 
 @pytest.mark.parametrize(
     "overrides,shape,code",
     [
-        ({"tile_n": 256, "stages": 5}, (4096, 4096, 4096), _native.KMCTS_ESMEM),
-        ({"tile_m": 256}, (4096, 4096, 4096), _native.KMCTS_ENOTSUP),
-        ({"cluster_m": 2}, (4096, 4096, 4096), _native.KMCTS_ENOTSUP),
+        ({"tile_m": 128, "cluster_m": 1, "tile_n": 256, "tile_k": 64, "stages": 5}, (4096, 4096, 4096), _native.KMCTS_ESMEM),
+        ({"tile_m": 256, "cluster_m": 1}, (4096, 4096, 4096), _native.KMCTS_ENOTSUP),
+        ({"tile_m": 128, "cluster_m": 2}, (4096, 4096, 4096), _native.KMCTS_ENOTSUP),
+        ({"cluster_n": 2}, (4096, 4096, 4096), _native.KMCTS_ENOTSUP),
+        ({"tile_k": 128, "stages": 4}, (4096, 4096, 4096), _native.KMCTS_ESMEM),
+        ({"tile_n": 192}, (4096, 4096, 4096), _native.KMCTS_ENOTSUP),
         ({}, (4096, 4096, 4100), _native.KMCTS_ENOTSUP),  # K not a multiple of 8
         ({}, (4096, 4100, 4096), _native.KMCTS_ENOTSUP),  # N not a multiple of 8
         ({"raster_group": 0}, (256, 256, 256), _native.KMCTS_EINVAL),
-        ({"tile_n": 128, "stages": 6}, (256, 256, 256), _native.KMCTS_OK),
-        ({"tile_n": 128, "tile_k": 128, "stages": 3}, (256, 256, 256), _native.KMCTS_OK),
+        ({"tile_m": 128, "cluster_m": 1, "tile_n": 128, "tile_k": 64, "stages": 6}, (256, 256, 256), _native.KMCTS_OK),
+        ({"tile_m": 128, "cluster_m": 1, "tile_n": 128, "tile_k": 128, "stages": 3}, (256, 256, 256), _native.KMCTS_OK),
+        ({"tile_n": 128, "tile_k": 64, "stages": 6}, (256, 256, 256), _native.KMCTS_OK),
     ],
 )
 def test_config_legality(overrides, shape, code):
@@ -65,9 +69,11 @@ def test_config_legality(overrides, shape, code):
 
 
 def test_smem_accounting():
-    cfg = km.make_config(tile_n=256, tile_k=64, stages=4)
+    cfg = km.make_config(tile_m=128, cluster_m=1, tile_n=256, tile_k=64, stages=4)
     assert km.config_smem_bytes(cfg) == 4 * (128 + 256) * 64 * 2 + 4 * 2 * 4096 + 2048
     assert km.config_smem_bytes(cfg) <= 232448
+    pair = km.default_config()  # each CTA of a pair stages 128 rows of A and BN/2 of B
+    assert km.config_smem_bytes(pair) == 3 * (128 + 128) * 128 * 2 + 4 * 2 * 4096 + 2048
 
 
 def test_bad_arguments_rejected_without_gpu_work():
