@@ -20,6 +20,7 @@ KMCTS_EINVAL = 4
 KMCTS_ESMEM = 5
 KMCTS_ETIMEOUT = 6
 KMCTS_ENOTSUP = 7
+KMCTS_ENOSCRATCH = 8
 
 ERROR_NAMES = {
     KMCTS_OK: "ok",
@@ -30,6 +31,7 @@ ERROR_NAMES = {
     KMCTS_ESMEM: "shared_memory",
     KMCTS_ETIMEOUT: "device_wait_timeout",
     KMCTS_ENOTSUP: "not_supported",
+    KMCTS_ENOSCRATCH: "static_scratch_too_small",
 }
 
 B_COL = 0
@@ -53,6 +55,7 @@ EXPORTED_SYMBOLS = (
     "kmcts_bf16_compare",
     "kmcts_launch_count",
     "kmcts_gemm_plan_query",
+    "kmcts_bf16_compare_noalloc",
 )
 
 
@@ -168,6 +171,10 @@ def load() -> ctypes.CDLL:
             vp, vp, i64, ctypes.c_double, ctypes.c_double, vp, vp, ctypes.POINTER(CompareResult),
         ]
         lib.kmcts_bf16_compare.restype = i32
+        lib.kmcts_bf16_compare_noalloc.argtypes = [
+            vp, vp, i64, ctypes.c_double, ctypes.c_double, vp, ctypes.POINTER(CompareResult),
+        ]
+        lib.kmcts_bf16_compare_noalloc.restype = i32
         lib.kmcts_gemm_plan_query.argtypes = [ctypes.POINTER(GemmConfig), i32, i32, i32, i32, ctypes.POINTER(GemmPlan)]
         lib.kmcts_gemm_plan_query.restype = i32
         lib.kmcts_launch_count.argtypes = []

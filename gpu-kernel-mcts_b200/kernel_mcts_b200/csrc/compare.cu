@@ -10,6 +10,7 @@
 #include <cuda_bf16.h>
 
 #include <cstring>
+#include <mutex>
 
 #include "kmcts_internal.h"
 
@@ -118,3 +119,62 @@ int compare_bf16_device(const void* C, const void* reference, int64_t count, dou
 }
 
 }  // namespace kmcts
+
+// ---------------------------------------------------------------------------
+// Allocation-free comparison.
+//
+// Some callers cannot call cudaMalloc at the moment they want a correctness
+// check: a worker in the middle of an evaluation whose memory budget is fully
+// owned by another allocator (a framework caching allocator that must see
+// every device allocation), code running while a stream is being captured
+// (where cudaMalloc is not permitted), or an embedding host whose only device
+// memory is the inputs and outputs it already passes in.  For them the
+// comparison's scratch (its reduction accumulators) lives in this file-scope
+// device array instead of a caller-provided workspace.  Every GPU that loads
+// the library holds these bytes until the process exits.
+namespace kmcts {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = KMCTS_NOALLOC_SCRATCH_BYTES;
+static __device__ __align__(256) unsigned char g_compare_scratch[kNoAllocScratchBytes];
+
+// Device address of g_compare_scratch, looked up once per device with that
+// device current (host code cannot use the symbol itself as a pointer).
+void* noalloc_scratch_address(int* rc) {
+    static std::mutex mu;
+    static void* address[64] = {};
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= 64) {
+        *rc = KMCTS_EHANDLE;
+        return nullptr;
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    if (address[device] == nullptr) {
+        void* ptr = nullptr;
+        if (cudaGetSymbolAddress(&ptr, g_compare_scratch) != cudaSuccess || ptr == nullptr) {
+            cudaGetLastError();
+            *rc = KMCTS_EHANDLE;
+            return nullptr;
+        }
+        address[device] = ptr;
+    }
+    *rc = KMCTS_OK;
+    return address[device];
+}
+
+}  // namespace
+}  // namespace kmcts
+
+extern "C" int kmcts_bf16_compare_noalloc(const void* C, const void* reference, int64_t count, double rtol,
+                                          double atol, void* stream, kmcts_compare_result* out) {
+    using namespace kmcts;
+    if (!C || !reference || !out || count < 0) return KMCTS_EINVAL;
+    // The scratch this comparison needs does not grow with `count`; a call
+    // whose need exceeded the static array would be refused here.
+    if (compare_workspace_bytes() > kNoAllocScratchBytes) return KMCTS_ENOSCRATCH;
+    int rc = KMCTS_OK;
+    void* scratch = noalloc_scratch_address(&rc);
+    if (rc != KMCTS_OK) return rc;
+    // compare_bf16_device zeroes the accumulators on `stream` before it reduces.
+    return compare_bf16_device(C, reference, count, rtol, atol, scratch, static_cast<cudaStream_t>(stream), out);
+}

@@ -34,6 +34,7 @@ extern "C" {
 #define KMCTS_ESMEM 5    /* config needs more shared memory than a CTA has */
 #define KMCTS_ETIMEOUT 6 /* a device-side bounded wait gave up (see device_status) */
 #define KMCTS_ENOTSUP 7  /* the requested kernel cannot run this shape */
+#define KMCTS_ENOSCRATCH 8 /* the call needs more scratch than the static array holds */
 
 #define KMCTS_B_COL 0 /* B column-major [K,N] == [N,K] row-major (K-major) */
 #define KMCTS_B_ROW 1 /* B row-major [K,N] (N-major) */
@@ -134,6 +135,24 @@ size_t kmcts_compare_workspace_bytes(void);
  * and writes *out on the host. */
 int kmcts_bf16_compare(const void* C, const void* reference, int64_t count, double rtol,
                        double atol, void* workspace, void* stream, kmcts_compare_result* out);
+
+/* No counterpart in the reference.  kmcts_bf16_compare without a workspace
+ * argument, for callers that cannot allocate device memory when they check a
+ * result: a worker whose device memory is owned by another allocator, code
+ * running while a stream is being captured (cudaMalloc is not permitted
+ * there), or a host that only holds the tensors it passes in.  The scratch is
+ * a file-scope device array of KMCTS_NOALLOC_SCRATCH_BYTES (256 bytes) that
+ * every GPU loading this library keeps until the process exits; the
+ * comparison needs that much for any `count`, and a call needing more would
+ * return KMCTS_ENOSCRATCH.  The first call on each device looks up the
+ * array's device address (cudaGetSymbolAddress), so make that first call
+ * before any stream capture.  Each call zeroes the accumulators it uses, but
+ * all calls share the one array: calls that overlap on the GPU (different
+ * streams or threads) race and corrupt each other's results.  Allocates no
+ * device memory; synchronises `stream`; writes *out on the host. */
+#define KMCTS_NOALLOC_SCRATCH_BYTES 256
+int kmcts_bf16_compare_noalloc(const void* C, const void* reference, int64_t count, double rtol,
+                               double atol, void* stream, kmcts_compare_result* out);
 
 /* Number of kernels this library has launched in this process (all entry
  * points).  Lets callers count GPU launches inside a timed region. */
