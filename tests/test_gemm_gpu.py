@@ -85,8 +85,11 @@ def test_tcgen05_integer_inputs_bit_exact(cuda_device, layout, shape):
     m, n, k = shape
     a_t, b_t = oracle.integer_inputs(m, n, k, seed=0)
     expect = oracle.root_gemm(oracle.torch_bits(a_t), oracle.torch_bits(b_t))
-    c = run(a_t.cuda(), b_for(layout, b_t.cuda()), layout, kernel=_native.KERNEL_TCGEN05)
+    c = run(a_t.cuda(), b_for(layout, b_t.cuda()), layout, kernel=_native.KERNEL_TCGEN05)  # default: pair
     np.testing.assert_array_equal(bits_of(c), expect)
+    c1 = run(a_t.cuda(), b_for(layout, b_t.cuda()), layout, kernel=_native.KERNEL_TCGEN05, tile_m=128,
+             cluster_m=1, tile_n=256, tile_k=64, stages=4)
+    np.testing.assert_array_equal(bits_of(c1), expect)
 
 
 @pytest.mark.parametrize("layout", ["col", "row"])
@@ -103,7 +106,7 @@ def test_tcgen05_uniform_inputs_within_criterion(cuda_device, layout):
 
 
 VARIANTS = [
-    (256, 64, 3), (256, 64, 4), (128, 64, 4), (128, 64, 5), (128, 64, 6),
+    (256, 64, 3), (256, 64, 4), (128, 64, 3), (128, 64, 4), (128, 64, 5), (128, 64, 6),
     (128, 128, 3), (256, 128, 2), (192, 64, 4), (64, 64, 6),
 ]
 
@@ -111,12 +114,13 @@ VARIANTS = [
 @pytest.mark.parametrize("layout", ["col", "row"])
 @pytest.mark.parametrize("tile_n,tile_k,stages", VARIANTS)
 @pytest.mark.parametrize("persistent", [1, 0])
-def test_every_compiled_schedule_bit_exact(cuda_device, layout, tile_n, tile_k, stages, persistent):
+def test_every_one_cta_schedule_bit_exact(cuda_device, layout, tile_n, tile_k, stages, persistent):
+    """tile_m 128 = one CTA per tile (tcgen05.mma.cta_group::1)."""
     m, n, k = 392, 520, 328  # ragged against every tile size
     a_t, b_t = oracle.integer_inputs(m, n, k, seed=7)
     expect = oracle.root_gemm(oracle.torch_bits(a_t), oracle.torch_bits(b_t))
-    c = run(a_t.cuda(), b_for(layout, b_t.cuda()), layout, kernel=_native.KERNEL_TCGEN05,
-            tile_n=tile_n, tile_k=tile_k, stages=stages, persistent=persistent, raster_group=3)
+    c = run(a_t.cuda(), b_for(layout, b_t.cuda()), layout, kernel=_native.KERNEL_TCGEN05, tile_m=128,
+            cluster_m=1, tile_n=tile_n, tile_k=tile_k, stages=stages, persistent=persistent, raster_group=3)
     np.testing.assert_array_equal(bits_of(c), expect)
 
 
