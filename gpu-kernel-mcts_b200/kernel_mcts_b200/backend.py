@@ -44,7 +44,7 @@ from .evaluation import (
     CandidateTimeoutError,
     EvaluationInfrastructureError,
 )
-from .profiling import parse_ncu_csv, resolve_metric_set
+from .profiling import ProfileParseError, parse_ncu_csv, resolve_metric_set
 
 CANDIDATE_BACKEND = "cuda_cpp"
 SCHEDULE_BACKEND = "kmcts_sm100"
@@ -218,10 +218,10 @@ class CudaSm100Backend:
             return Sm100CompilationResult(False, None, "", f"statically rejected: {why}",
                                           time.monotonic() - started)
         harness = native_build.build_harness()
+        resolved = cfg.as_dict()
         args = tuple(
-            f"--{name.replace('_', '-')}={schedule[name]}"
-            for name in ("tile_n", "tile_k", "stages", "persistent", "raster_group")
-            if name in schedule
+            f"--{name.replace('_', '-')}={resolved[name]}"
+            for name in ("tile_m", "cluster_m", "tile_n", "tile_k", "stages", "persistent", "raster_group")
         ) + ("--kernel=tcgen05",)
         digest = hashlib.sha256()
         digest.update(harness.read_bytes())
@@ -416,8 +416,15 @@ class CudaSm100Backend:
             raise EvaluationInfrastructureError("Nsight Compute profiling could not be completed") from error
         if result.returncode != 0:
             raise EvaluationInfrastructureError("Nsight Compute profiling failed: " + _bounded(result.stderr + result.stdout, 2000))
-        metrics = parse_ncu_csv(result.stdout if "Metric Name" in result.stdout or definition.metrics[0] in result.stdout else result.stderr,
-                                definition.metrics)
+        metrics = None
+        for text in (result.stdout, result.stderr):
+            try:
+                metrics = parse_ncu_csv(text, definition.metrics)
+                break
+            except ProfileParseError:
+                continue
+        if metrics is None:
+            raise EvaluationInfrastructureError("Nsight Compute returned malformed CSV")
         return {
             "schema_version": definition.schema_version,
             "profiler": "ncu",

@@ -80,14 +80,32 @@ def build_library(verbose: bool = False) -> Path:
     return LIBRARY
 
 
+def cutlass_include() -> Path | None:
+    """CUTLASS headers vendored in this image (flashinfer's copy), if present.
+    Used only for the CUTLASS column of the vendor baselines."""
+    import importlib.util
+
+    spec = importlib.util.find_spec("flashinfer")
+    if spec is None or spec.origin is None:
+        return None
+    path = Path(spec.origin).parent / "data" / "cutlass" / "include"
+    return path if (path / "cutlass" / "gemm" / "device" / "gemm.h").exists() else None
+
+
 def build_harness(verbose: bool = False) -> Path:
     src = CSRC / "harness.cu"
     if not src.exists():
         return HARNESS
     lib = build_library(verbose)
-    if _stale(HARNESS, [src, lib, INCLUDE / "kmcts_gemm.h", Path(__file__)]):
+    sources = [src]
+    flags = ["-DKMCTS_HAVE_CUTLASS=0"]
+    cutlass = cutlass_include()
+    if cutlass is not None:
+        sources.append(CSRC / "vendor_cutlass.cu")
+        flags = ["-DKMCTS_HAVE_CUTLASS=1", f"-I{cutlass}"]
+    if _stale(HARNESS, [*sources, lib, INCLUDE / "kmcts_gemm.h", Path(__file__)]):
         cmd = [
-            nvcc(), *COMMON_FLAGS, str(src), "-o", str(HARNESS),
+            nvcc(), *COMMON_FLAGS, *flags, *map(str, sources), "-o", str(HARNESS),
             f"-L{LIB_DIR}", "-lkmcts_gemm_sm100", "-lcublas",
             "-Xlinker", f"-rpath={LIB_DIR}", "-Xlinker", "-rpath=$ORIGIN",
         ]

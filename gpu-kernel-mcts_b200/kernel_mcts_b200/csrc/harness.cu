@@ -9,8 +9,11 @@
 // (src/kernel_mcts/cuda_backend.py:466-503).
 //
 // Additive flags: --b-layout=col|row, --inputs=uniform|randn|int,
-// --kernel=auto|tcgen05|simt|candidate, --tile-n --tile-k --stages
-// --persistent --raster-group --wait-limit-ns, --flush-l2=0|1.
+// --kernel=auto|tcgen05|simt|candidate|cublas|cutlass_sm80, --tile-m
+// --cluster-m --tile-n --tile-k --stages --persistent --raster-group --flags
+// --wait-limit-ns, --flush-l2=0|1.  cublas and cutlass_sm80 are the vendor
+// baseline columns (src/kernel_mcts/vendor_baselines.py), timed under the
+// same protocol as the library kernel.
 // Additive JSON keys: max_ulp, n_gt_1ulp, ulp_hist, n_nonfinite, kernel.
 //
 // Candidate programs: compiled together with this file and
@@ -34,6 +37,11 @@
 #include <vector>
 
 #include "kmcts_gemm.h"
+
+#if KMCTS_HAVE_CUTLASS
+extern "C" int kmcts_vendor_cutlass_sm80_gemm(const void* A, const void* B, void* C, int M, int N, int K,
+                                              cudaStream_t stream);
+#endif
 
 #if defined(KMCTS_CANDIDATE_ROOT)
 extern "C" __global__ void bf16_gemm_root(const __nv_bfloat16* A, const __nv_bfloat16* B,
@@ -130,12 +138,27 @@ void integer_inputs(int seed, std::vector<__nv_bfloat16>& a, std::vector<__nv_bf
     for (auto& v : b) v = __float2bfloat16(static_cast<float>(distribution(generator)));
 }
 
+enum class Impl { kLibrary, kCublas, kCutlass };
+
 struct Launch {
     int M, N, K, b_layout;
     kmcts_gemm_config cfg;
     cudaStream_t stream;
     int* status;
+    Impl impl;
+    cublasHandle_t cublas;
 };
+
+// cuBLAS exactly as the reference calls it (bf16_gemm_harness.cu:117-143):
+// row-major C viewed as column-major C^T = B^T * A^T, FP32 compute.
+bool cublas_gemm(const Launch& l, const void* A, const void* B, void* C) {
+    const float alpha = 1.0f, beta = 0.0f;
+    const cublasOperation_t op_b = l.b_layout == KMCTS_B_COL ? CUBLAS_OP_T : CUBLAS_OP_N;
+    const int ldb = l.b_layout == KMCTS_B_COL ? l.K : l.N;
+    return cublasGemmEx(l.cublas, op_b, CUBLAS_OP_N, l.N, l.M, l.K, &alpha, B, CUDA_R_16BF, ldb, A,
+                        CUDA_R_16BF, l.K, &beta, C, CUDA_R_16BF, l.N, CUBLAS_COMPUTE_32F,
+                        CUBLAS_GEMM_DEFAULT_TENSOR_OP) == CUBLAS_STATUS_SUCCESS;
+}
 
 // Returns 0 on success.
 int launch_candidate(const Launch& l, const void* A, const void* B, void* C) {
@@ -149,16 +172,24 @@ int launch_candidate(const Launch& l, const void* A, const void* B, void* C) {
 #elif defined(KMCTS_CANDIDATE_LAUNCHER)
     return bf16_gemm_launch(A, B, C, l.M, l.N, l.K, l.stream) == 0 ? 0 : 1;
 #else
+    if (l.impl == Impl::kCublas) return cublas_gemm(l, A, B, C) ? 0 : 1;
+#if KMCTS_HAVE_CUTLASS
+    if (l.impl == Impl::kCutlass) return kmcts_vendor_cutlass_sm80_gemm(A, B, C, l.M, l.N, l.K, l.stream) == 0 ? 0 : 1;
+#endif
     return kmcts_bf16_gemm_ex(A, B, C, l.M, l.N, l.K, l.b_layout, &l.cfg, l.stream, l.status);
 #endif
 }
 
-const char* kernel_name() {
+const char* kernel_name(const Launch& l) {
 #if defined(KMCTS_CANDIDATE_ROOT)
+    (void)l;
     return "candidate:bf16_gemm_root";
 #elif defined(KMCTS_CANDIDATE_LAUNCHER)
+    (void)l;
     return "candidate:bf16_gemm_launch";
 #else
+    if (l.impl == Impl::kCublas) return "vendor:cublasGemmEx";
+    if (l.impl == Impl::kCutlass) return "vendor:cutlass_sm80_128x128x32";
     return "library:kmcts_bf16_gemm_ex";
 #endif
 }
@@ -198,19 +229,33 @@ int main(int argc, char** argv) {
     l.K = static_cast<int>(K);
     l.b_layout = layout == "row" ? KMCTS_B_ROW : KMCTS_B_COL;
     kmcts_default_config(&l.cfg);
+    l.cfg.tile_m = static_cast<int>(int_arg(argc, argv, "tile-m", l.cfg.tile_m));
+    l.cfg.cluster_m = static_cast<int>(int_arg(argc, argv, "cluster-m", l.cfg.cluster_m));
+    l.cfg.flags = static_cast<int>(int_arg(argc, argv, "flags", l.cfg.flags));
     l.cfg.tile_n = static_cast<int>(int_arg(argc, argv, "tile-n", l.cfg.tile_n));
     l.cfg.tile_k = static_cast<int>(int_arg(argc, argv, "tile-k", l.cfg.tile_k));
     l.cfg.stages = static_cast<int>(int_arg(argc, argv, "stages", l.cfg.stages));
     l.cfg.persistent = static_cast<int>(int_arg(argc, argv, "persistent", l.cfg.persistent));
     l.cfg.raster_group = static_cast<int>(int_arg(argc, argv, "raster-group", l.cfg.raster_group));
     l.cfg.wait_limit_ns = int_arg(argc, argv, "wait-limit-ns", 0);
+    l.impl = Impl::kLibrary;
     if (kernel == "tcgen05") {
         l.cfg.kernel = KMCTS_KERNEL_TCGEN05;
     } else if (kernel == "simt") {
         l.cfg.kernel = KMCTS_KERNEL_SIMT;
+    } else if (kernel == "cublas") {
+        l.impl = Impl::kCublas;
+    } else if (kernel == "cutlass_sm80") {
+#if KMCTS_HAVE_CUTLASS
+        if (layout != "col") infrastructure_failure("cutlass_layout");
+        l.impl = Impl::kCutlass;
+#else
+        infrastructure_failure("cutlass_unavailable");
+#endif
     } else if (kernel != "auto" && kernel != "candidate") {
         infrastructure_failure("arguments");
     }
+
 
     const size_t a_count = static_cast<size_t>(M) * K;
     const size_t b_count = static_cast<size_t>(K) * N;
@@ -234,6 +279,8 @@ int main(int argc, char** argv) {
     require(cudaMemcpy(dA, hA.data(), a_count * 2, cudaMemcpyHostToDevice), "copy_A");
     require(cudaMemcpy(dB, hB.data(), b_count * 2, cudaMemcpyHostToDevice), "copy_B");
     require(cudaStreamCreateWithFlags(&l.stream, cudaStreamNonBlocking), "stream");
+    if (cublasCreate(&l.cublas) != CUBLAS_STATUS_SUCCESS) infrastructure_failure("cublasCreate");
+    if (cublasSetStream(l.cublas, l.stream) != CUBLAS_STATUS_SUCCESS) infrastructure_failure("cublasSetStream");
 
     if (launch_candidate(l, dA, dB, dC) != 0) launch_failure("launch");
     if (cudaStreamSynchronize(l.stream) != cudaSuccess) launch_failure("synchronize");
@@ -241,19 +288,7 @@ int main(int argc, char** argv) {
 
     if (mode == "correctness") {
         require(cudaMalloc(&dRef, c_count * 2), "cudaMalloc_reference");
-        cublasHandle_t handle;
-        if (cublasCreate(&handle) != CUBLAS_STATUS_SUCCESS) infrastructure_failure("cublasCreate");
-        if (cublasSetStream(handle, l.stream) != CUBLAS_STATUS_SUCCESS)
-            infrastructure_failure("cublasSetStream");
-        const float alpha = 1.0f, beta = 0.0f;
-        // Row-major C viewed as column-major C^T = B^T * A^T.
-        const cublasOperation_t op_b = l.b_layout == KMCTS_B_COL ? CUBLAS_OP_T : CUBLAS_OP_N;
-        const int ldb = l.b_layout == KMCTS_B_COL ? l.K : l.N;
-        if (cublasGemmEx(handle, op_b, CUBLAS_OP_N, l.N, l.M, l.K, &alpha, dB, CUDA_R_16BF, ldb,
-                         dA, CUDA_R_16BF, l.K, &beta, dRef, CUDA_R_16BF, l.N, CUBLAS_COMPUTE_32F,
-                         CUBLAS_GEMM_DEFAULT_TENSOR_OP) != CUBLAS_STATUS_SUCCESS) {
-            infrastructure_failure("cublasGemmEx");
-        }
+        if (!cublas_gemm(l, dA, dB, dRef)) infrastructure_failure("cublasGemmEx");
         require(cudaStreamSynchronize(l.stream), "reference_synchronize");
         require(cudaMalloc(&dWork, kmcts_compare_workspace_bytes()), "cudaMalloc_workspace");
         kmcts_compare_result r;
@@ -275,8 +310,7 @@ int main(int argc, char** argv) {
                     r.max_ulp, static_cast<long long>(r.ulp_hist[2] + r.ulp_hist[3]),
                     static_cast<long long>(r.ulp_hist[0]), static_cast<long long>(r.ulp_hist[1]),
                     static_cast<long long>(r.ulp_hist[2]), static_cast<long long>(r.ulp_hist[3]),
-                    static_cast<long long>(r.n_nonfinite), kernel_name());
-        cublasDestroy(handle);
+                    static_cast<long long>(r.n_nonfinite), kernel_name(l));
     } else {
         // Reference protocol (bf16_gemm_harness.cu:177-212): warm-up launches,
         // one synchronize, then one event pair per measured launch.
@@ -308,7 +342,7 @@ int main(int argc, char** argv) {
             if (i) std::printf(",");
             std::printf("%.9g", timings[static_cast<size_t>(i)]);
         }
-        std::printf("],\"kernel\":\"%s\"}\n", kernel_name());
+        std::printf("],\"kernel\":\"%s\"}\n", kernel_name(l));
         cudaEventDestroy(start);
         cudaEventDestroy(stop);
     }
@@ -319,6 +353,7 @@ int main(int argc, char** argv) {
     cudaFree(dWork);
     cudaFree(dFlush);
     cudaFree(l.status);
+    cublasDestroy(l.cublas);
     cudaStreamDestroy(l.stream);
     return 0;
 }

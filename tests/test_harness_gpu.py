@@ -1,0 +1,131 @@
+"""The harness executable, the sm_100a backend, the evaluator and the vendor
+columns on a B200: real nvcc builds of candidates with both ABIs, real runs."""
+
+from __future__ import annotations
+
+import json
+import math
+import subprocess
+
+import pytest
+
+from kernel_mcts_b200 import build as native_build
+from kernel_mcts_b200.backend import CudaSm100Backend, CudaSm100Config, schedule_program
+from kernel_mcts_b200.domain import InvalidReason, KernelProgram, ProposalStatus
+from kernel_mcts_b200.evaluation import BackendKernelEvaluator, EvaluationContext
+from kernel_mcts_b200.vendor_baselines import VendorBaselineSuite
+from kernel_mcts_b200.workloads import gemm_workload
+
+pytestmark = pytest.mark.gpu
+
+# A deliberately simple candidate with the reference ABI (one thread per output).
+NAIVE_ROOT = r"""
+#include <cuda_bf16.h>
+extern "C" __global__ void bf16_gemm_root(const __nv_bfloat16* A, const __nv_bfloat16* B,
+                                          __nv_bfloat16* C, int M, int N, int K) {
+    int row = blockIdx.y * blockDim.y + threadIdx.y, col = blockIdx.x * blockDim.x + threadIdx.x;
+    if (row >= M || col >= N) return;
+    float acc = 0.0f;
+    for (int k = 0; k < K; ++k) acc += __bfloat162float(A[row * K + k]) * __bfloat162float(B[col * K + k]);
+    C[row * N + col] = __float2bfloat16(acc);
+}
+"""
+# The same kernel but it forgets the last k: wrong results.
+WRONG_ROOT = NAIVE_ROOT.replace("k < K;", "k < K - 1;")
+# A host-launcher candidate that owns its launch: the library's tcgen05 kernel.
+LAUNCHER = r"""
+#include <cuda_runtime.h>
+#include "kmcts_gemm.h"
+extern "C" int bf16_gemm_launch(const void* A, const void* B, void* C, int M, int N, int K, cudaStream_t s) {
+    return kmcts_bf16_gemm_ex(A, B, C, M, N, K, KMCTS_B_COL, nullptr, s, nullptr);
+}
+"""
+FAILING_LAUNCHER = LAUNCHER.replace("return kmcts_bf16_gemm_ex", "(void)kmcts_bf16_gemm_ex; return 1; //")
+
+WORKLOAD = gemm_workload("bf16_gemm_512_test", 512, 512, 512)
+CONTEXT = EvaluationContext("test-worker", "test-manifest", {}, {"gpu": "B200"})
+
+
+@pytest.fixture(scope="module")
+def backend(tmp_path_factory, cuda_device):
+    native_build.build_all()
+    return CudaSm100Backend(CudaSm100Config(artifact_root=tmp_path_factory.mktemp("artifacts"),
+                                            warmup_count=2, measurement_count=5))
+
+
+@pytest.fixture(scope="module")
+def evaluator(backend):
+    root = backend.compile(KernelProgram(NAIVE_ROOT), WORKLOAD)
+    assert root.success, root.stderr
+    root_bench = backend.benchmark(root.artifact, WORKLOAD)
+    return BackendKernelEvaluator(backend=backend, root_benchmark=root_bench, context=CONTEXT)
+
+
+def run_harness(*args: str) -> dict:
+    out = subprocess.run([str(native_build.HARNESS), *args], capture_output=True, text=True, timeout=300)
+    payload = json.loads(out.stdout.strip().splitlines()[-1])
+    payload["_returncode"] = out.returncode
+    return payload
+
+
+def test_harness_correctness_and_benchmark_modes(backend):
+    ok = run_harness("--mode=correctness", "--M=512", "--N=384", "--K=1024", "--seed=3")
+    assert ok["status"] == "ok" and ok["success"] is True and ok["_returncode"] == 0
+    assert ok["reference_metadata"]["implementation"] == "cuBLAS" and ok["max_ulp"] <= 1
+    bench = run_harness("--mode=benchmark", "--M=512", "--N=384", "--K=1024", "--warmups=3", "--measurements=7")
+    assert bench["status"] == "ok" and len(bench["timings_us"]) == 7 and all(t > 0 for t in bench["timings_us"])
+    bad = run_harness("--mode=nonsense", "--M=1", "--N=1", "--K=1")
+    assert bad == {"status": "infrastructure_failure", "operation": "arguments", "_returncode": 2}
+
+
+def test_harness_integer_inputs_match_cublas_bit_for_bit(backend):
+    for layout in ("col", "row"):
+        res = run_harness("--mode=correctness", "--M=1024", "--N=1024", "--K=2048", "--inputs=int",
+                          f"--b-layout={layout}")
+        assert res["success"] and res["max_ulp"] == 0 and res["maximum_error"] == 0.0, res
+
+
+def test_vendor_columns_under_the_same_protocol(backend):
+    results = VendorBaselineSuite(backend).run(gemm_workload("vendor_1024", 1024, 1024, 1024))
+    assert set(results) == {"cublas", "cutlass"}
+    for name in ("cublas", "cutlass"):
+        column = results[name]
+        assert column["correctness"]["success"] is True, column
+        assert column["benchmark"].median_us > 0
+
+
+def test_root_abi_candidate_is_valid(evaluator):
+    result = evaluator.evaluate(KernelProgram(NAIVE_ROOT + "\n// same kernel, new text\n"), WORKLOAD)
+    assert result.status == ProposalStatus.VALID, result
+    assert abs(result.reward) < 1.0  # the same kernel as the root
+
+
+def test_launcher_candidate_owns_its_launch_and_is_much_faster(evaluator):
+    result = evaluator.evaluate(KernelProgram(LAUNCHER), WORKLOAD)
+    assert result.status == ProposalStatus.VALID, result
+    assert result.reward > math.log(3.0), result.reward
+
+
+def test_wrong_candidate_fails_correctness(evaluator):
+    result = evaluator.evaluate(KernelProgram(WRONG_ROOT), WORKLOAD)
+    assert result.status == ProposalStatus.INVALID
+    assert result.invalid_reason == InvalidReason.CORRECTNESS_FAILURE
+
+
+def test_launch_failure_is_reported(evaluator):
+    result = evaluator.evaluate(KernelProgram(FAILING_LAUNCHER), WORKLOAD)
+    assert result.invalid_reason == InvalidReason.LAUNCH_FAILURE
+
+
+def test_compile_error_is_reported(evaluator):
+    result = evaluator.evaluate(KernelProgram(NAIVE_ROOT.replace("float acc", "flot acc")), WORKLOAD)
+    assert result.invalid_reason == InvalidReason.COMPILE_FAILURE
+
+
+def test_schedule_programs_evaluate_without_nvcc(evaluator):
+    good = evaluator.evaluate(schedule_program(tile_m=256, cluster_m=2, tile_n=256, tile_k=128, stages=3), WORKLOAD)
+    assert good.status == ProposalStatus.VALID and good.reward > 0
+    one_cta = evaluator.evaluate(schedule_program(tile_m=128, cluster_m=1, tile_n=128, tile_k=64, stages=4), WORKLOAD)
+    assert one_cta.status == ProposalStatus.VALID
+    rejected = evaluator.evaluate(schedule_program(tile_m=256, cluster_m=2, tile_n=256, tile_k=128, stages=5), WORKLOAD)
+    assert rejected.invalid_reason == InvalidReason.COMPILE_FAILURE
