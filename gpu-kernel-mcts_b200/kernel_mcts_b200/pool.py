@@ -1,0 +1,244 @@
+"""Parallel candidate evaluation: one worker process per GPU.
+
+The reference serialises every evaluation behind one lock on device 0
+(src/kernel_mcts/worker_protocol.py:124-135; cuda_backend.py:264 ``--id=0``).
+Candidate and schedule evaluations are independent units, so here each GPU
+gets its own worker process (spawned, ``CUDA_VISIBLE_DEVICES`` pinned before
+anything touches CUDA) with its own backend and evaluator, and jobs are handed
+to whichever worker is idle.  There is no collective: the path shards by
+evaluation.
+
+Failure handling (host side only; nothing here touches a GPU):
+* a worker that dies or stops answering has its in-flight job re-queued on
+  another worker and is restarted;
+* a job whose attempts all end in dead workers comes back as an
+  INFRASTRUCTURE_FAILURE result, as an infrastructure retry in the reference
+  would report it (src/kernel_mcts/orchestration.py:256-272).
+
+``evaluate_many`` keeps the KernelEvaluator call shape
+(src/kernel_mcts/interfaces.py:8-9) for a batch; ``evaluate`` is the single
+call, so MCTS runs unchanged on top.
+"""
+
+from __future__ import annotations
+
+import importlib
+import multiprocessing as mp
+import os
+import queue
+import time
+import traceback
+from dataclasses import dataclass, field
+from typing import Any, Callable, Mapping, Sequence
+
+from .domain import EvaluationResult, KernelProgram, ProposalStatus, WorkloadContract
+from .serialization import deserialize_evaluation, deserialize_workload, serialize_evaluation, serialize_workload
+
+
+@dataclass(frozen=True)
+class WorkerSpec:
+    """How a worker builds its evaluator: ``factory`` is "module:function",
+    called as ``function(device_index, **options)`` inside the worker and
+    returning an object with ``evaluate(program, workload)``."""
+
+    factory: str
+    options: Mapping[str, Any] = field(default_factory=dict)
+
+
+def _resolve(factory: str) -> Callable[..., Any]:
+    module, _, name = factory.partition(":")
+    return getattr(importlib.import_module(module), name)
+
+
+def _worker_main(slot: int, device: str, spec: WorkerSpec, jobs: "mp.Queue", results: "mp.Queue") -> None:
+    # Pin the GPU before any CUDA context can exist in this process.
+    os.environ["CUDA_VISIBLE_DEVICES"] = device
+    try:
+        evaluator = _resolve(spec.factory)(int(device) if device.isdigit() else 0, **dict(spec.options))
+    except Exception:  # the worker could not start: report and exit
+        results.put(("startup_error", slot, None, traceback.format_exc()))
+        return
+    results.put(("ready", slot, None, None))
+    while True:
+        item = jobs.get()
+        if item is None:
+            return
+        job_id, program_value, workload_value = item
+        program = KernelProgram(program_value["source"], program_value["backend"])
+        workload = deserialize_workload(workload_value)
+        try:
+            evaluation = evaluator.evaluate(program, workload)
+            results.put(("result", slot, job_id, serialize_evaluation(evaluation)))
+        except Exception:
+            results.put(("error", slot, job_id, traceback.format_exc()))
+
+
+@dataclass
+class _Worker:
+    slot: int
+    device: str
+    process: Any
+    jobs: Any
+    job: int | None = None
+    started_at: float = 0.0
+    ready: bool = False
+
+
+class EvaluationPool:
+    """Fans evaluations out over GPUs, one worker process per device."""
+
+    def __init__(
+        self,
+        devices: Sequence[int | str],
+        spec: WorkerSpec,
+        *,
+        job_timeout_seconds: float = 1800.0,
+        max_attempts: int = 2,
+        startup_timeout_seconds: float = 600.0,
+    ) -> None:
+        if not devices:
+            raise ValueError("the pool needs at least one device")
+        self.devices = [str(d) for d in devices]
+        self.spec = spec
+        self.job_timeout = job_timeout_seconds
+        self.max_attempts = max_attempts
+        self.startup_timeout = startup_timeout_seconds
+        self._ctx = mp.get_context("spawn")
+        self._results = self._ctx.Queue()
+        self._workers: list[_Worker] = []
+        self.restarts = 0
+        for slot, device in enumerate(self.devices):
+            self._workers.append(self._start(slot, device))
+        self._await_ready()
+
+    # ------------------------------------------------------------- lifecycle
+
+    def _start(self, slot: int, device: str) -> _Worker:
+        jobs = self._ctx.Queue()
+        process = self._ctx.Process(target=_worker_main, args=(slot, device, self.spec, jobs, self._results),
+                                    daemon=True, name=f"kmcts-eval-gpu{device}")
+        process.start()
+        return _Worker(slot, device, process, jobs)
+
+    def _await_ready(self) -> None:
+        deadline = time.monotonic() + self.startup_timeout
+        while not all(w.ready for w in self._workers):
+            try:
+                kind, slot, _, payload = self._results.get(timeout=max(0.1, deadline - time.monotonic()))
+            except queue.Empty as error:
+                self.close()
+                raise RuntimeError("evaluation workers did not start in time") from error
+            if kind == "startup_error":
+                self.close()
+                raise RuntimeError(f"evaluation worker {slot} failed to start:\n{payload}")
+            if kind == "ready":
+                self._workers[slot].ready = True
+
+    def close(self) -> None:
+        for w in self._workers:
+            if w.process.is_alive():
+                try:
+                    w.jobs.put(None)
+                except (OSError, ValueError):
+                    pass
+        for w in self._workers:
+            w.process.join(timeout=10)
+            if w.process.is_alive():
+                w.process.kill()
+                w.process.join(timeout=5)
+
+    def __enter__(self) -> "EvaluationPool":
+        return self
+
+    def __exit__(self, *exc) -> None:
+        self.close()
+
+    @property
+    def size(self) -> int:
+        return len(self._workers)
+
+    def worker_pids(self) -> list[int]:
+        return [w.process.pid for w in self._workers]
+
+    # ------------------------------------------------------------ evaluation
+
+    def evaluate(self, program: KernelProgram, workload: WorkloadContract) -> EvaluationResult:
+        return self.evaluate_many([program], workload)[0]
+
+    def evaluate_many(self, programs: Sequence[KernelProgram], workload: WorkloadContract) -> list[EvaluationResult]:
+        workload_value = serialize_workload(workload)
+        pending = list(range(len(programs)))[::-1]  # pop() takes the lowest index first
+        attempts = [0] * len(programs)
+        out: list[EvaluationResult | None] = [None] * len(programs)
+        done = 0
+        while done < len(programs):
+            for w in self._workers:
+                if w.job is None and w.ready and pending:
+                    job = pending.pop()
+                    attempts[job] += 1
+                    p = programs[job]
+                    w.jobs.put((job, {"source": p.source, "backend": p.backend}, workload_value))
+                    w.job, w.started_at = job, time.monotonic()
+            try:
+                kind, slot, job, payload = self._results.get(timeout=0.5)
+            except queue.Empty:
+                kind = None
+            if kind == "ready":
+                self._workers[slot].ready = True
+            elif kind in ("result", "error"):
+                w = self._workers[slot]
+                if w.job == job:
+                    w.job = None
+                if out[job] is None:
+                    out[job] = (deserialize_evaluation(payload) if kind == "result"
+                                else _infrastructure_failure(programs[job], f"worker raised:\n{payload}"))
+                    done += 1
+            elif kind == "startup_error":
+                w = self._workers[slot]
+                w.ready = False
+            # Dead or stuck workers: re-queue their job and restart them.
+            for w in self._workers:
+                stuck = w.job is not None and time.monotonic() - w.started_at > self.job_timeout
+                if w.process.is_alive() and not stuck:
+                    continue
+                if w.process.is_alive():
+                    w.process.kill()
+                w.process.join(timeout=5)
+                job = w.job
+                if job is not None and out[job] is None:
+                    if attempts[job] < self.max_attempts:
+                        pending.append(job)
+                    else:
+                        out[job] = _infrastructure_failure(
+                            programs[job], f"worker on device {w.device} died {attempts[job]} time(s)")
+                        done += 1
+                self.restarts += 1
+                self._workers[w.slot] = self._start(w.slot, w.device)
+        return [r for r in out if r is not None]
+
+
+def _infrastructure_failure(program: KernelProgram, reason: str) -> EvaluationResult:
+    return EvaluationResult(status=ProposalStatus.INFRASTRUCTURE_FAILURE, program=program,
+                            metadata={"error_type": "WorkerFailure", "reason": reason[-2000:]})
+
+
+# --------------------------------------------------------------- factories
+
+
+def sm100_evaluator(device_index: int, *, artifact_root: str, root_us: float, warmup_count: int = 10,
+                    measurement_count: int = 30, flush_l2: bool = False, worker_id: str | None = None):
+    """The production worker: CudaSm100Backend + BackendKernelEvaluator on this
+    worker's GPU, rewarding against a root median of ``root_us``."""
+    from pathlib import Path
+
+    from .backend import CudaSm100Backend, CudaSm100Config
+    from .domain import BenchmarkResult
+    from .evaluation import BackendKernelEvaluator, EvaluationContext
+
+    backend = CudaSm100Backend(CudaSm100Config(
+        artifact_root=Path(artifact_root) / f"gpu{device_index}", warmup_count=warmup_count,
+        measurement_count=measurement_count, device_index=device_index, flush_l2=flush_l2))
+    context = EvaluationContext(worker_id or f"b200-gpu{device_index}", "kmcts-b200",
+                                {"launcher": "kmcts_bf16_gemm_ex"}, {"gpu": "B200", "arch": "sm_100a"})
+    return BackendKernelEvaluator(backend=backend, root_benchmark=BenchmarkResult((root_us,), root_us),
+                                  context=context)
