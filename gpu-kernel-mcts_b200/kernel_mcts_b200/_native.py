@@ -43,6 +43,8 @@ KERNEL_SIMT = 2
 
 FLAG_NO_TAIL_SPLIT = 1
 
+INPUTS = {"uniform": 0, "randn": 1, "int": 2}
+
 #: Every symbol include/kmcts_gemm.h declares.
 EXPORTED_SYMBOLS = (
     "kmcts_default_config",
@@ -56,6 +58,7 @@ EXPORTED_SYMBOLS = (
     "kmcts_launch_count",
     "kmcts_gemm_plan_query",
     "kmcts_bf16_compare_noalloc",
+    "kmcts_generate_inputs",
 )
 
 
@@ -177,6 +180,8 @@ def load() -> ctypes.CDLL:
         lib.kmcts_bf16_compare_noalloc.restype = i32
         lib.kmcts_gemm_plan_query.argtypes = [ctypes.POINTER(GemmConfig), i32, i32, i32, i32, ctypes.POINTER(GemmPlan)]
         lib.kmcts_gemm_plan_query.restype = i32
+        lib.kmcts_generate_inputs.argtypes = [i32, ctypes.c_uint32, ctypes.c_size_t, ctypes.c_size_t, vp, vp]
+        lib.kmcts_generate_inputs.restype = i32
         lib.kmcts_launch_count.argtypes = []
         lib.kmcts_launch_count.restype = i64
         _lib = lib
@@ -215,6 +220,17 @@ def plan(cfg: GemmConfig | None, m: int, n: int, k: int, b_layout: int = B_COL) 
                                         ctypes.byref(out))
     check(code, "kmcts_gemm_plan_query")
     return out.as_dict()
+
+
+def generate_inputs(kind: str, seed: int, a_count: int, b_count: int):
+    """Evaluation inputs as two uint16 numpy arrays of BF16 bits (host)."""
+    import numpy as np
+
+    a = np.empty(a_count, dtype=np.uint16)
+    b = np.empty(b_count, dtype=np.uint16)
+    check(load().kmcts_generate_inputs(INPUTS[kind], seed, a_count, b_count, a.ctypes.data, b.ctypes.data),
+          "kmcts_generate_inputs")
+    return a, b
 
 
 def version() -> str:

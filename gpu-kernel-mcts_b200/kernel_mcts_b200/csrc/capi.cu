@@ -1,8 +1,10 @@
 // extern "C" entry points of libkmcts_gemm_sm100.so (declared in include/kmcts_gemm.h).
+#include <cuda_bf16.h>
 #include <cudaTypedefs.h>
 
 #include <cstring>
 #include <mutex>
+#include <random>
 
 #include "kmcts_internal.h"
 
@@ -145,6 +147,36 @@ int kmcts_gemm_plan_query(const kmcts_gemm_config* cfg, int M, int N, int K, int
     plan.full_tiles = plan.units = plan.ctas = plan.tiles;
     plan.workers = multiprocessor_count();
     *out = plan;
+    return KMCTS_OK;
+}
+
+int kmcts_generate_inputs(int kind, uint32_t seed, size_t a_count, size_t b_count, uint16_t* a_out,
+                          uint16_t* b_out) {
+    if ((a_count && !a_out) || (b_count && !b_out)) return KMCTS_EINVAL;
+    auto store = [](uint16_t* dst, float v) {
+        const __nv_bfloat16 h = __float2bfloat16(v);
+        std::memcpy(dst, &h, sizeof(uint16_t));
+    };
+    if (kind == KMCTS_INPUTS_UNIFORM) {
+        // The repository contract's stream: one mt19937(seed), A then B,
+        // U(-0.25, 0.25), RNE to BF16 (bf16_gemm_harness.cu:92-95).
+        std::mt19937 generator(seed);
+        std::uniform_real_distribution<float> distribution(-0.25f, 0.25f);
+        for (size_t i = 0; i < a_count; ++i) store(a_out + i, distribution(generator));
+        for (size_t i = 0; i < b_count; ++i) store(b_out + i, distribution(generator));
+    } else if (kind == KMCTS_INPUTS_RANDN) {
+        std::mt19937_64 generator(seed);
+        std::normal_distribution<float> distribution(0.0f, 1.0f);
+        for (size_t i = 0; i < a_count; ++i) store(a_out + i, distribution(generator));
+        for (size_t i = 0; i < b_count; ++i) store(b_out + i, distribution(generator));
+    } else if (kind == KMCTS_INPUTS_INT) {
+        std::mt19937 generator(seed);
+        std::uniform_int_distribution<int> distribution(-2, 2);
+        for (size_t i = 0; i < a_count; ++i) store(a_out + i, static_cast<float>(distribution(generator)));
+        for (size_t i = 0; i < b_count; ++i) store(b_out + i, static_cast<float>(distribution(generator)));
+    } else {
+        return KMCTS_EINVAL;
+    }
     return KMCTS_OK;
 }
 

@@ -32,7 +32,6 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
-#include <random>
 #include <string>
 #include <vector>
 
@@ -113,29 +112,6 @@ void print_number(double v) {
     } else {
         std::printf("%.9g", v);
     }
-}
-
-// The reference input stream (bf16_gemm_harness.cu:92-95): A then B from one
-// mt19937(seed), U(-0.25, 0.25), rounded to BF16.
-void uniform_inputs(int seed, std::vector<__nv_bfloat16>& a, std::vector<__nv_bfloat16>& b) {
-    std::mt19937 generator(static_cast<unsigned>(seed));
-    std::uniform_real_distribution<float> distribution(-0.25f, 0.25f);
-    for (auto& v : a) v = __float2bfloat16(distribution(generator));
-    for (auto& v : b) v = __float2bfloat16(distribution(generator));
-}
-
-void randn_inputs(int seed, std::vector<__nv_bfloat16>& a, std::vector<__nv_bfloat16>& b) {
-    std::mt19937_64 generator(static_cast<unsigned long long>(seed));
-    std::normal_distribution<float> distribution(0.0f, 1.0f);
-    for (auto& v : a) v = __float2bfloat16(distribution(generator));
-    for (auto& v : b) v = __float2bfloat16(distribution(generator));
-}
-
-void integer_inputs(int seed, std::vector<__nv_bfloat16>& a, std::vector<__nv_bfloat16>& b) {
-    std::mt19937 generator(static_cast<unsigned>(seed));
-    std::uniform_int_distribution<int> distribution(-2, 2);
-    for (auto& v : a) v = __float2bfloat16(static_cast<float>(distribution(generator)));
-    for (auto& v : b) v = __float2bfloat16(static_cast<float>(distribution(generator)));
 }
 
 enum class Impl { kLibrary, kCublas, kCutlass };
@@ -260,13 +236,15 @@ int main(int argc, char** argv) {
     const size_t a_count = static_cast<size_t>(M) * K;
     const size_t b_count = static_cast<size_t>(K) * N;
     const size_t c_count = static_cast<size_t>(M) * N;
-    std::vector<__nv_bfloat16> hA(a_count), hB(b_count);
-    if (inputs == "uniform") {
-        uniform_inputs(seed, hA, hB);
-    } else if (inputs == "randn") {
-        randn_inputs(seed, hA, hB);
-    } else {
-        integer_inputs(seed, hA, hB);
+    // Inputs from the library's generator, so the in-process evaluator and
+    // this executable see the same bits for the same (inputs, seed).
+    std::vector<uint16_t> hA(a_count), hB(b_count);
+    const int kind = inputs == "uniform" ? KMCTS_INPUTS_UNIFORM
+                     : inputs == "randn" ? KMCTS_INPUTS_RANDN
+                                         : KMCTS_INPUTS_INT;
+    if (kmcts_generate_inputs(kind, static_cast<uint32_t>(seed), a_count, b_count, hA.data(), hB.data()) !=
+        KMCTS_OK) {
+        infrastructure_failure("inputs");
     }
 
     void *dA = nullptr, *dB = nullptr, *dC = nullptr, *dRef = nullptr, *dWork = nullptr,

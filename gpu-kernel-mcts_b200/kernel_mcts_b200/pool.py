@@ -226,18 +226,25 @@ def _infrastructure_failure(program: KernelProgram, reason: str) -> EvaluationRe
 
 
 def sm100_evaluator(device_index: int, *, artifact_root: str, root_us: float, warmup_count: int = 10,
-                    measurement_count: int = 30, flush_l2: bool = False, worker_id: str | None = None):
-    """The production worker: CudaSm100Backend + BackendKernelEvaluator on this
-    worker's GPU, rewarding against a root median of ``root_us``."""
+                    measurement_count: int = 30, flush_l2: bool = False, worker_id: str | None = None,
+                    inprocess: bool = True):
+    """The production worker: BackendKernelEvaluator on this worker's GPU over
+    the hybrid backend (schedule programs in process, candidate sources
+    through nvcc and the harness), rewarding against a root median of
+    ``root_us``."""
     from pathlib import Path
 
     from .backend import CudaSm100Backend, CudaSm100Config
     from .domain import BenchmarkResult
     from .evaluation import BackendKernelEvaluator, EvaluationContext
+    from .inprocess import HybridSm100Backend, InProcessSm100Backend
 
-    backend = CudaSm100Backend(CudaSm100Config(
+    subprocess_backend = CudaSm100Backend(CudaSm100Config(
         artifact_root=Path(artifact_root) / f"gpu{device_index}", warmup_count=warmup_count,
         measurement_count=measurement_count, device_index=device_index, flush_l2=flush_l2))
+    local = (InProcessSm100Backend(warmup_count=warmup_count, measurement_count=measurement_count,
+                                   flush_l2=flush_l2, device_index=device_index) if inprocess else None)
+    backend = HybridSm100Backend(subprocess_backend, local)
     context = EvaluationContext(worker_id or f"b200-gpu{device_index}", "kmcts-b200",
                                 {"launcher": "kmcts_bf16_gemm_ex"}, {"gpu": "B200", "arch": "sm_100a"})
     return BackendKernelEvaluator(backend=backend, root_benchmark=BenchmarkResult((root_us,), root_us),

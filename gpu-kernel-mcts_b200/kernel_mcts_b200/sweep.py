@@ -182,6 +182,8 @@ def main(argv: Sequence[str] | None = None) -> None:
     p.add_argument("--warmups", type=int, default=20)
     p.add_argument("--measurements", type=int, default=100)
     p.add_argument("--artifact-root", default="/tmp/kmcts-sweep")
+    p.add_argument("--subprocess", action="store_true",
+                   help="evaluate schedules through the harness executable instead of in process")
     p.add_argument("--out", default=None)
     args = p.parse_args(argv)
 
@@ -202,7 +204,7 @@ def main(argv: Sequence[str] | None = None) -> None:
     root_us = cublas["benchmark"].median_us if "benchmark" in cublas else 1.0
     spec = WorkerSpec("kernel_mcts_b200.pool:sm100_evaluator",
                       {"artifact_root": args.artifact_root, "root_us": root_us, "warmup_count": args.warmups,
-                       "measurement_count": args.measurements})
+                       "measurement_count": args.measurements, "inprocess": not args.subprocess})
     with EvaluationPool(devices, spec) as pool:
         report = run_schedule_sweep(pool, workload, cublas_json, schedules=schedule_grid(args.count, args.seed))
     report["devices"] = devices

@@ -110,6 +110,20 @@ typedef struct kmcts_gemm_plan {
  * nothing).  Returns KMCTS_OK or the error kmcts_bf16_gemm_ex would return. */
 int kmcts_gemm_plan_query(const kmcts_gemm_config* cfg, int M, int N, int K, int b_layout, kmcts_gemm_plan* out);
 
+/* Evaluation inputs (host memory, BF16 bits).  A (a_count values) then B
+ * (b_count values) from one generator:
+ *   KMCTS_INPUTS_UNIFORM  the repository contract's stream, std::mt19937(seed)
+ *                         with std::uniform_real_distribution<float>(-0.25, 0.25),
+ *                         as in src/kernel_mcts/benchmarks/kernels/bf16_gemm_harness.cu:92-95;
+ *   KMCTS_INPUTS_RANDN    std::mt19937_64(seed), N(0, 1);
+ *   KMCTS_INPUTS_INT      std::mt19937(seed), integers uniform in {-2..2}.
+ * Every value is rounded to BF16 with round-to-nearest-even. */
+#define KMCTS_INPUTS_UNIFORM 0
+#define KMCTS_INPUTS_RANDN 1
+#define KMCTS_INPUTS_INT 2
+int kmcts_generate_inputs(int kind, uint32_t seed, size_t a_count, size_t b_count, uint16_t* a_out,
+                          uint16_t* b_out);
+
 /* Library version string. */
 const char* kmcts_version(void);
 

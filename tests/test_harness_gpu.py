@@ -129,3 +129,37 @@ def test_schedule_programs_evaluate_without_nvcc(evaluator):
     assert one_cta.status == ProposalStatus.VALID
     rejected = evaluator.evaluate(schedule_program(tile_m=256, cluster_m=2, tile_n=256, tile_k=128, stages=5), WORKLOAD)
     assert rejected.invalid_reason == InvalidReason.COMPILE_FAILURE
+
+
+def test_inprocess_schedule_evaluation_matches_the_harness_path(backend):
+    """Schedule programs evaluated in process see the harness's inputs (the
+    library generator) and its acceptance test; results agree."""
+    from kernel_mcts_b200.domain import BenchmarkResult
+    from kernel_mcts_b200.inprocess import HybridSm100Backend, InProcessSm100Backend
+
+    workload = gemm_workload("inproc_1024", 1024, 768, 512)
+    hybrid = HybridSm100Backend(backend, InProcessSm100Backend(warmup_count=2, measurement_count=5))
+    ev_in = BackendKernelEvaluator(backend=hybrid, root_benchmark=BenchmarkResult((100.0,), 100.0), context=CONTEXT)
+    ev_sub = BackendKernelEvaluator(backend=backend, root_benchmark=BenchmarkResult((100.0,), 100.0), context=CONTEXT)
+    program = schedule_program(tile_m=256, cluster_m=2, tile_n=256, tile_k=128, stages=3)
+    fast = ev_in.evaluate(program, workload)
+    slow = ev_sub.evaluate(program, workload)
+    assert fast.status == slow.status == ProposalStatus.VALID
+    assert fast.correctness.maximum_error == slow.correctness.maximum_error
+    assert fast.correctness.reference_metadata["max_ulp"] <= 1
+    assert 0.5 < fast.benchmark.median_us / slow.benchmark.median_us < 2.0
+    cand = ev_in.evaluate(KernelProgram(LAUNCHER), workload)  # candidate sources still go through nvcc
+    assert cand.status == ProposalStatus.VALID
+
+
+def test_pool_sweep_on_one_gpu_in_process(backend, tmp_path):
+    from kernel_mcts_b200.pool import EvaluationPool, WorkerSpec
+    from kernel_mcts_b200.sweep import run_schedule_sweep, schedule_grid
+
+    workload = gemm_workload("sweep_2048", 2048, 2048, 2048, b_layout="row", inputs="randn")
+    spec = WorkerSpec("kernel_mcts_b200.pool:sm100_evaluator",
+                      {"artifact_root": str(tmp_path), "root_us": 100.0, "warmup_count": 2, "measurement_count": 5})
+    with EvaluationPool([0], spec) as pool:
+        report = run_schedule_sweep(pool, workload, {"benchmark": {"median_us": 50.0}}, schedules=schedule_grid(24, 3))
+    assert report["status"] == "ok" and report["evaluations"] > 0
+    assert all(t["status"] in ("VALID", "STATICALLY_REJECTED") for t in report["trials"]), report["trials"]
