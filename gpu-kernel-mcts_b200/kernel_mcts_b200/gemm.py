@@ -96,6 +96,38 @@ def bf16_gemm(
     return out
 
 
+class PreparedGemm:
+    """A GEMM whose operands, schedule and stream are fixed: the ctypes
+    arguments are built once, so each ``launch()`` costs one C call.  For
+    timed loops, where host overhead between a start event and the launch
+    would be counted as kernel time."""
+
+    def __init__(self, a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, *, b_layout: str | int = "col",
+                 config: GemmConfig | None = None, stream: torch.cuda.Stream | None = None,
+                 status: torch.Tensor | None = None) -> None:
+        code = layout_code(b_layout)
+        m, n, k = gemm_shapes(a, b, code)
+        _check_operand("A", a, (m, k))
+        _check_operand("B", b, (n, k) if code == B_COL else (k, n))
+        _check_operand("C", out, (m, n))
+        if status is not None and (status.dtype != torch.int32 or not status.is_cuda):
+            raise ValueError("status must be a CUDA int32 tensor")
+        self._keep = (a, b, out, status)  # operands stay alive while prepared
+        self.config = config if config is not None else _native.default_config()
+        stream = stream if stream is not None else torch.cuda.current_stream(a.device)
+        self._fn = _native.load().kmcts_bf16_gemm_ex
+        self._args = (
+            ctypes.c_void_p(a.data_ptr()), ctypes.c_void_p(b.data_ptr()), ctypes.c_void_p(out.data_ptr()),
+            m, n, k, code, ctypes.byref(self.config), ctypes.c_void_p(stream.cuda_stream),
+            ctypes.c_void_p(status.data_ptr()) if status is not None else None,
+        )
+
+    def launch(self) -> None:
+        rc = self._fn(*self._args)
+        if rc != 0:
+            _native.check(rc, "kmcts_bf16_gemm_ex")
+
+
 def bf16_gemm_sync(a: torch.Tensor, b_nk: torch.Tensor, out: torch.Tensor) -> int:
     """The drop-in entry point (column-major B, default stream, synchronising).
 
@@ -178,6 +210,7 @@ __all__ = [
     "Comparison",
     "GemmConfig",
     "KmctsError",
+    "PreparedGemm",
     "bf16_gemm",
     "bf16_gemm_sync",
     "compare",

@@ -120,13 +120,22 @@ class InProcessSm100Backend:
                                       compiler_context={"schedule": resolved,
                                                         "smem_bytes": _native.config_smem_bytes(cfg, layout)})
 
-    def _launch(self, artifact: ScheduleArtifact, workload: WorkloadContract):
+    def _prepared(self, artifact: ScheduleArtifact, workload: WorkloadContract):
         from . import gemm as kg
 
         a, b, c, _, layout = self._operands(workload)
-        cfg = _native.make_config(**artifact.schedule)
+        key = (id(c), artifact.artifact_id)
+        if getattr(self, "_prepared_key", None) != key:
+            self._prepared_gemm = kg.PreparedGemm(a, b, c, b_layout=layout,
+                                                  config=_native.make_config(**artifact.schedule),
+                                                  stream=self.torch.cuda.current_stream(self.device),
+                                                  status=self._status)
+            self._prepared_key = key
+        return self._prepared_gemm
+
+    def _launch(self, artifact: ScheduleArtifact, workload: WorkloadContract):
         try:
-            kg.bf16_gemm(a, b, out=c, b_layout=layout, config=cfg, status=self._status)
+            self._prepared(artifact, workload).launch()
         except _native.KmctsError as error:
             raise CandidateLaunchError(str(error)) from error
 
@@ -163,12 +172,14 @@ class InProcessSm100Backend:
             self._launch(artifact, workload)
         torch.cuda.synchronize(self.device)
         timings = []
-        for i in range(self.measurement_count):
+        prepared = self._prepared(artifact, workload)
+        events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                  for _ in range(self.measurement_count)]
+        for i, (start, stop) in enumerate(events):
             if self._flush is not None:
                 self._flush.fill_(i & 0xFF)
-            start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             start.record(stream)
-            self._launch(artifact, workload)
+            prepared.launch()
             stop.record(stream)
             stop.synchronize()
             timings.append(start.elapsed_time(stop) * 1e3)
