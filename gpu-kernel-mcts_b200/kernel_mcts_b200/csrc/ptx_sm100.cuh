@@ -193,8 +193,8 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
 //
 // A cluster of two CTAs shares one UMMA: rank 0 (the leader) issues
 // tcgen05.mma.cta_group::2; each CTA holds half of A and half of B in its own
-// shared memory and half of the accumulator rows in its own TMEM.  No load
-// here uses .multicast::cluster: each CTA fetches its own halves.
+// shared memory and half of the accumulator rows in its own TMEM.  Every load
+// is a plain per-CTA copy: each CTA fetches its own halves.
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
     uint32_t r;
