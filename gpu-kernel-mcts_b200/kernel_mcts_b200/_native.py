@@ -59,6 +59,10 @@ EXPORTED_SYMBOLS = (
     "kmcts_gemm_plan_query",
     "kmcts_bf16_compare_noalloc",
     "kmcts_generate_inputs",
+    "kmcts_ipc_export",
+    "kmcts_ipc_import",
+    "kmcts_ipc_close",
+    "kmcts_bf16_gemm_allgather",
 )
 
 
@@ -182,6 +186,15 @@ def load() -> ctypes.CDLL:
         lib.kmcts_gemm_plan_query.restype = i32
         lib.kmcts_generate_inputs.argtypes = [i32, ctypes.c_uint32, ctypes.c_size_t, ctypes.c_size_t, vp, vp]
         lib.kmcts_generate_inputs.restype = i32
+        lib.kmcts_ipc_export.argtypes = [vp, vp]
+        lib.kmcts_ipc_export.restype = i32
+        lib.kmcts_ipc_import.argtypes = [vp, ctypes.POINTER(ctypes.c_void_p)]
+        lib.kmcts_ipc_import.restype = i32
+        lib.kmcts_ipc_close.argtypes = [vp]
+        lib.kmcts_ipc_close.restype = i32
+        lib.kmcts_bf16_gemm_allgather.argtypes = [vp, vp, vp, i32, i32, i32, i32, i32, i32,
+                                                  ctypes.POINTER(GemmConfig), vp, vp]
+        lib.kmcts_bf16_gemm_allgather.restype = i32
         lib.kmcts_launch_count.argtypes = []
         lib.kmcts_launch_count.restype = i64
         _lib = lib

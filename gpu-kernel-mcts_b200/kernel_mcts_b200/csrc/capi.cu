@@ -150,6 +150,20 @@ int kmcts_gemm_plan_query(const kmcts_gemm_config* cfg, int M, int N, int K, int
     return KMCTS_OK;
 }
 
+int kmcts_bf16_gemm_allgather(const void* A, const void* B_shard, void* const* C_ranks, int num_ranks, int rank,
+                              int M, int N_total, int K, int b_layout, const kmcts_gemm_config* cfg, void* stream,
+                              int* device_status) {
+    kmcts_gemm_config local;
+    if (cfg) {
+        local = *cfg;
+    } else {
+        kmcts_default_config(&local);
+    }
+    if (b_layout != KMCTS_B_COL && b_layout != KMCTS_B_ROW) return KMCTS_EINVAL;
+    return launch_allgather_tcgen05(A, B_shard, C_ranks, num_ranks, rank, M, N_total, K, b_layout, local,
+                                    as_stream(stream), device_status);
+}
+
 int kmcts_generate_inputs(int kind, uint32_t seed, size_t a_count, size_t b_count, uint16_t* a_out,
                           uint16_t* b_out) {
     if ((a_count && !a_out) || (b_count && !b_out)) return KMCTS_EINVAL;

@@ -451,6 +451,46 @@ int launch_tcgen05(const void* A, const void* B, void* C, int M, int N, int K, i
                  device_status);
 }
 
+int launch_allgather_tcgen05(const void* A, const void* B_shard, void* const* C_ranks, int num_ranks, int rank,
+                             int M, int N_total, int K, int b_layout, const kmcts_gemm_config& cfg,
+                             cudaStream_t stream, int* device_status) {
+    if (num_ranks < 1 || num_ranks > KMCTS_MAX_RANKS || rank < 0 || rank >= num_ranks || !C_ranks || M < 0 ||
+        N_total < 0 || K < 0 || N_total % num_ranks != 0)
+        return KMCTS_EINVAL;
+    const int n_shard = N_total / num_ranks;
+    if (n_shard % 256 != 0 || !is_pair(cfg)) return KMCTS_ENOTSUP;
+    int rc = tcgen05_legal(cfg, M, n_shard, K, b_layout, nullptr, 0);
+    if (rc != KMCTS_OK) return rc;
+    void* own = C_ranks[rank];
+    void* peers[KMCTS_MAX_RANKS - 1];
+    int peer_count = 0;
+    for (int r = 0; r < num_ranks; ++r) {
+        if (!C_ranks[r]) return KMCTS_EINVAL;
+        if (r != rank) peers[peer_count++] = C_ranks[r];
+    }
+    if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B_shard) | reinterpret_cast<uintptr_t>(own)) &
+        15u)
+        return KMCTS_ENOTSUP;
+    if (M == 0 || n_shard == 0 || K == 0) return K == 0 ? KMCTS_ENOTSUP : KMCTS_OK;
+    const uint32_t b_rows = cfg.tile_n / 2;
+    CUtensorMap ma, mb, mb_half, mc;
+    bool ok = encode_tensor_map_2d(&ma, A, K, M, static_cast<uint64_t>(K) * 2, 64, kBM);
+    if (b_layout == KMCTS_B_COL) {
+        ok = ok && encode_tensor_map_2d(&mb, B_shard, K, n_shard, static_cast<uint64_t>(K) * 2, 64, b_rows);
+        ok = ok && encode_tensor_map_2d(&mb_half, B_shard, K, n_shard, static_cast<uint64_t>(K) * 2, 64, b_rows / 2);
+    } else {
+        ok = ok && encode_tensor_map_2d(&mb, B_shard, n_shard, K, static_cast<uint64_t>(n_shard) * 2, 64, 64);
+        mb_half = mb;
+    }
+    // This rank's C map covers the full [M, N_total] C; the kernel adds the
+    // rank's column offset to every store.
+    ok = ok && encode_tensor_map_2d(&mc, own, N_total, M, static_cast<uint64_t>(N_total) * 2, 64, 32);
+    if (!ok) return KMCTS_EINVAL;
+    const uint64_t limit = cfg.wait_limit_ns > 0 ? static_cast<uint64_t>(cfg.wait_limit_ns) : kDefaultWaitNs;
+    return launch_pair_allgather(ma, mb, mb_half, mc, M, n_shard, K, b_layout, cfg, limit, stream, device_status,
+                                 peers, peer_count, N_total, rank * n_shard);
+}
+
 int plan_tcgen05(const kmcts_gemm_config& cfg, int M, int N, int K, int b_layout, kmcts_gemm_plan* out) {
     const int rc = tcgen05_legal(cfg, M, N, K, b_layout, nullptr, 0);
     if (rc != KMCTS_OK) return rc;

@@ -48,6 +48,16 @@ struct PairLayout {
     static_assert(kSmemBytes <= kMaxSmem, "shared memory budget exceeded");
 };
 
+// Where a fused GEMM + all-gather also writes C: the other ranks' full C
+// buffers (IPC-mapped peer memory), their row stride, and this rank's column
+// offset inside the full C.  Unused (count 0, offset 0) by plain GEMMs.
+struct PeerOutputs {
+    __nv_bfloat16* ptr[KMCTS_MAX_RANKS - 1];
+    int count;
+    int ld;
+    int col_offset;
+};
+
 // Work units.  Tiles [0, full_tiles) (in raster order) run whole; each later
 // tile runs as two BN/2-wide halves, so a last partial wave of R <= W/2 tiles
 // costs half a tile of time instead of a whole one.  Every output element is
@@ -69,13 +79,14 @@ __device__ __forceinline__ Unit pair_unit(int u, int full_tiles, int num_m, int 
     return {tc.m_blk, tc.n_blk * BN + half * (BN / 2), width};
 }
 
-template <int BN, int BK, int STAGES, bool B_MN>
+template <int BN, int BK, int STAGES, bool B_MN, bool ALLGATHER>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_tcgen05_pair(const __grid_constant__ CUtensorMap map_a,
                            const __grid_constant__ CUtensorMap map_b,
                            const __grid_constant__ CUtensorMap map_b_half,
                            const __grid_constant__ CUtensorMap map_c, int M, int N, int K, int group,
-                           int full_tiles, uint64_t limit_ns, int* status) {
+                           int full_tiles, uint64_t limit_ns, int* status,
+                           const __grid_constant__ PeerOutputs peers) {
     using L = PairLayout<BN, BK, STAGES, B_MN>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -272,10 +283,31 @@ __global__ void __launch_bounds__(kThreads, 1)
                     __syncwarp();
                     if (lane == 0) ptx::mbar_arrive_cluster(ptx::mapa_shared(ptx::smem_addr(&tmem_empty[acc]), 0));
                 }
-                store_chunk(&map_c, staging, chunk_count, lo, hi, lane, n0 + c * 64, m0 + quarter * 32);
+                if constexpr (ALLGATHER) {
+                    // This lane's row of the chunk to every peer's C: 8 x 16-byte
+                    // stores of contiguous BF16 (plain P2P stores over NVLink).
+                    const int row = m0 + quarter * 32 + lane;
+                    if (row < M) {
+                        uint32_t w[32];
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) w[i] = pack_bf16x2(lo[2 * i], lo[2 * i + 1]);
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) w[16 + i] = pack_bf16x2(hi[2 * i], hi[2 * i + 1]);
+                        const size_t offset = static_cast<size_t>(row) * peers.ld + peers.col_offset + n0 + c * 64;
+                        for (int p = 0; p < peers.count; ++p) {
+                            uint4* dst = reinterpret_cast<uint4*>(peers.ptr[p] + offset);
+#pragma unroll
+                            for (int j = 0; j < 8; ++j)
+                                dst[j] = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+                        }
+                    }
+                }
+                store_chunk(&map_c, staging, chunk_count, lo, hi, lane, peers.col_offset + n0 + c * 64,
+                            m0 + quarter * 32);
             }
         }
         if (lane == 0) ptx::bulk_wait_group<0>();
+        if constexpr (ALLGATHER) __threadfence_system();  // peer stores performed before the grid ends
         __syncwarp();
     }
 
@@ -300,10 +332,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 constexpr int kMaxDevices = 64;
 
 // Co-resident CTA pairs of a pair kernel on the current device (cached).
-template <int BN, int BK, int STAGES, bool B_MN>
+template <int BN, int BK, int STAGES, bool B_MN, bool ALLGATHER = false>
 int pair_workers(int device) {
     using L = PairLayout<BN, BK, STAGES, B_MN>;
-    auto kernel = gemm_bf16_tcgen05_pair<BN, BK, STAGES, B_MN>;
+    auto kernel = gemm_bf16_tcgen05_pair<BN, BK, STAGES, B_MN, ALLGATHER>;
     static std::mutex mu;
     static int max_clusters[kMaxDevices] = {};
     std::lock_guard<std::mutex> lock(mu);
@@ -357,23 +389,24 @@ kmcts_gemm_plan make_pair_plan(int M, int N, int workers, bool persistent, bool 
     return plan;
 }
 
-template <int BN, int BK, int STAGES, bool B_MN>
+template <int BN, int BK, int STAGES, bool B_MN, bool ALLGATHER = false>
 int plan_pair_variant(int M, int N, bool persistent, bool split_tail, kmcts_gemm_plan* out) {
     int device = 0;
     if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kMaxDevices) return KMCTS_EHANDLE;
-    const int workers = pair_workers<BN, BK, STAGES, B_MN>(device);
+    const int workers = pair_workers<BN, BK, STAGES, B_MN, ALLGATHER>(device);
     if (workers <= 0) return KMCTS_EGEMM;
     *out = make_pair_plan<BN>(M, N, workers, persistent, split_tail, PairLayout<BN, BK, STAGES, B_MN>::kSmemBytes);
     return KMCTS_OK;
 }
 
-template <int BN, int BK, int STAGES, bool B_MN>
-int launch_pair_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb_half,
-                        const CUtensorMap& mc, int M, int N, int K, int group, bool persistent, bool split_tail,
-                        uint64_t limit_ns, cudaStream_t stream, int* status) {
+template <int BN, int BK, int STAGES, bool B_MN, bool ALLGATHER = false>
+int launch_pair_variant_peers(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb_half,
+                              const CUtensorMap& mc, int M, int N, int K, int group, bool persistent,
+                              bool split_tail, uint64_t limit_ns, cudaStream_t stream, int* status,
+                              const PeerOutputs& peers) {
     using L = PairLayout<BN, BK, STAGES, B_MN>;
     kmcts_gemm_plan plan;
-    const int rc = plan_pair_variant<BN, BK, STAGES, B_MN>(M, N, persistent, split_tail, &plan);
+    const int rc = plan_pair_variant<BN, BK, STAGES, B_MN, ALLGATHER>(M, N, persistent, split_tail, &plan);
     if (rc != KMCTS_OK) return rc;
     cudaLaunchConfig_t config = {};
     cudaLaunchAttribute attr[1];
@@ -387,10 +420,20 @@ int launch_pair_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUte
     config.stream = stream;
     config.attrs = attr;
     config.numAttrs = 1;
-    const cudaError_t err = cudaLaunchKernelEx(&config, gemm_bf16_tcgen05_pair<BN, BK, STAGES, B_MN>, ma, mb,
-                                               mb_half, mc, M, N, K, group, plan.full_tiles, limit_ns, status);
+    const cudaError_t err = cudaLaunchKernelEx(&config, gemm_bf16_tcgen05_pair<BN, BK, STAGES, B_MN, ALLGATHER>,
+                                               ma, mb, mb_half, mc, M, N, K, group, plan.full_tiles, limit_ns,
+                                               status, peers);
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return err == cudaSuccess ? KMCTS_OK : KMCTS_EGEMM;
+}
+
+template <int BN, int BK, int STAGES, bool B_MN>
+int launch_pair_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb_half,
+                        const CUtensorMap& mc, int M, int N, int K, int group, bool persistent, bool split_tail,
+                        uint64_t limit_ns, cudaStream_t stream, int* status) {
+    const PeerOutputs none = {};
+    return launch_pair_variant_peers<BN, BK, STAGES, B_MN, false>(ma, mb, mb_half, mc, M, N, K, group, persistent,
+                                                                  split_tail, limit_ns, stream, status, none);
 }
 
 using PairLauncher = int (*)(const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, int,
@@ -443,6 +486,28 @@ int plan_pair(const kmcts_gemm_config& cfg, int M, int N, int b_layout, kmcts_ge
         }
     }
     return KMCTS_ENOTSUP;
+}
+
+int launch_pair_allgather(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb_half,
+                          const CUtensorMap& mc, int M, int N_shard, int K, int b_layout,
+                          const kmcts_gemm_config& cfg, uint64_t limit_ns, cudaStream_t stream, int* status,
+                          void* const* peer_c, int peer_count, int ld, int col_offset) {
+    if (cfg.tile_n != 256 || cfg.tile_k != 128 || cfg.stages != 3 || peer_count < 0 ||
+        peer_count > KMCTS_MAX_RANKS - 1)
+        return KMCTS_ENOTSUP;
+    PeerOutputs peers = {};
+    for (int p = 0; p < peer_count; ++p) peers.ptr[p] = static_cast<__nv_bfloat16*>(peer_c[p]);
+    peers.count = peer_count;
+    peers.ld = ld;
+    peers.col_offset = col_offset;
+    const bool split = (cfg.flags & KMCTS_FLAG_NO_TAIL_SPLIT) == 0;
+    if (b_layout == KMCTS_B_ROW)
+        return launch_pair_variant_peers<256, 128, 3, true, true>(ma, mb, mb_half, mc, M, N_shard, K,
+                                                                  cfg.raster_group, cfg.persistent != 0, split,
+                                                                  limit_ns, stream, status, peers);
+    return launch_pair_variant_peers<256, 128, 3, false, true>(ma, mb, mb_half, mc, M, N_shard, K, cfg.raster_group,
+                                                               cfg.persistent != 0, split, limit_ns, stream, status,
+                                                               peers);
 }
 
 int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb_half, const CUtensorMap& mc,

@@ -43,6 +43,13 @@ int multiprocessor_count();
 bool pair_variant_exists(int bn, int bk, int stages, int b_layout);
 int64_t pair_smem_bytes(int bn, int bk, int stages);
 int plan_pair(const kmcts_gemm_config& cfg, int M, int N, int b_layout, kmcts_gemm_plan* out);
+int launch_pair_allgather(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb_half,
+                          const CUtensorMap& mc, int M, int N_shard, int K, int b_layout,
+                          const kmcts_gemm_config& cfg, uint64_t limit_ns, cudaStream_t stream, int* status,
+                          void* const* peer_c, int peer_count, int ld, int col_offset);
+int launch_allgather_tcgen05(const void* A, const void* B_shard, void* const* C_ranks, int num_ranks, int rank,
+                             int M, int N_total, int K, int b_layout, const kmcts_gemm_config& cfg,
+                             cudaStream_t stream, int* device_status);
 int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb_half, const CUtensorMap& mc,
                 int M, int N, int K, int b_layout, const kmcts_gemm_config& cfg, uint64_t limit_ns,
                 cudaStream_t stream, int* status);

@@ -214,6 +214,13 @@ class BackendKernelEvaluator:
                 metadata={**backend_metadata, "error_type": type(error).__name__},
             )
 
+    def prepare(self, workload: WorkloadContract) -> None:
+        """Lets the backend build per-workload state (inputs, references) ahead
+        of the evaluations that will be timed.  Optional for backends."""
+        prepare = getattr(self.backend, "prepare", None)
+        if callable(prepare):
+            prepare(workload)
+
     def lightweight_profile(self, evaluation: EvaluationResult, workload: WorkloadContract,
                             metric_set: str = "lightweight_v1") -> Mapping[str, object]:
         if evaluation.status != ProposalStatus.VALID:

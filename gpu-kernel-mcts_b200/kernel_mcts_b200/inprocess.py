@@ -97,6 +97,9 @@ class InProcessSm100Backend:
             self._cache[key] = (a, b, c, reference, layout)
         return self._cache[key]
 
+    def prepare(self, workload: WorkloadContract) -> None:
+        self._operands(workload)
+
     # -------------------------------------------------------------- protocol
 
     def normalize_program(self, program: KernelProgram) -> str:
@@ -218,6 +221,10 @@ class HybridSm100Backend:
         if isinstance(artifact, ScheduleArtifact) and self.inprocess_backend is not None:
             return self.inprocess_backend
         return self.subprocess_backend
+
+    def prepare(self, workload):
+        if self.inprocess_backend is not None:
+            self.inprocess_backend.prepare(workload)
 
     def normalize_program(self, program):
         return self._for_program(program).normalize_program(program)

@@ -63,6 +63,16 @@ def _worker_main(slot: int, device: str, spec: WorkerSpec, jobs: "mp.Queue", res
         item = jobs.get()
         if item is None:
             return
+        if item[0] == "prepare":
+            # Warm this worker for a workload (inputs, references) before timing starts.
+            try:
+                prepare = getattr(evaluator, "prepare", None)
+                if callable(prepare):
+                    prepare(deserialize_workload(item[1]))
+                results.put(("prepared", slot, None, None))
+            except Exception:
+                results.put(("prepared", slot, None, traceback.format_exc()))
+            continue
         job_id, program_value, workload_value = item
         program = KernelProgram(program_value["source"], program_value["backend"])
         workload = deserialize_workload(workload_value)
@@ -161,6 +171,26 @@ class EvaluationPool:
         return [w.process.pid for w in self._workers]
 
     # ------------------------------------------------------------ evaluation
+
+    def prepare(self, workload: WorkloadContract, timeout_seconds: float = 600.0) -> None:
+        """Has every worker build its per-workload state (device inputs, the
+        reference output) now, so later evaluations measure only evaluation."""
+        value = serialize_workload(workload)
+        for w in self._workers:
+            w.jobs.put(("prepare", value))
+        waiting = {w.slot for w in self._workers}
+        deadline = time.monotonic() + timeout_seconds
+        while waiting:
+            try:
+                kind, slot, _, payload = self._results.get(timeout=max(0.1, deadline - time.monotonic()))
+            except queue.Empty as error:
+                raise RuntimeError("workers did not finish preparing in time") from error
+            if kind == "prepared":
+                if payload:
+                    raise RuntimeError(f"worker {slot} failed to prepare:\n{payload}")
+                waiting.discard(slot)
+            elif kind == "ready":
+                self._workers[slot].ready = True
 
     def evaluate(self, program: KernelProgram, workload: WorkloadContract) -> EvaluationResult:
         return self.evaluate_many([program], workload)[0]

@@ -75,8 +75,12 @@ def run_schedule_sweep(
     *,
     schedules: Sequence[Mapping[str, int]] | None = None,
     default: Mapping[str, int] = DEFAULT_SCHEDULE,
+    repeat: int = 1,
 ) -> dict[str, Any]:
-    """``evaluator`` has ``evaluate_many`` (an EvaluationPool) or ``evaluate``."""
+    """``evaluator`` has ``evaluate_many`` (an EvaluationPool) or ``evaluate``.
+    ``repeat`` > 1 evaluates every legal point that many times (the trial keeps
+    the first result; throughput counts them all), to measure evaluations per
+    second on a batch large enough to keep every GPU busy."""
     candidates = [dict(s) for s in (schedules if schedules is not None else schedule_grid())]
     trials: list[dict[str, Any]] = []
     legal: list[int] = []
@@ -90,11 +94,15 @@ def run_schedule_sweep(
         trials.append(trial)
 
     programs = [schedule_program(**trials[i]["schedule"]) for i in legal]
+    prepare = getattr(evaluator, "prepare", None)
+    if callable(prepare):
+        prepare(workload)  # per-workload state is built before the clock starts
     started = time.monotonic()
+    batch = programs * max(1, repeat)
     if hasattr(evaluator, "evaluate_many"):
-        results = evaluator.evaluate_many(programs, workload)
+        results = evaluator.evaluate_many(batch, workload)
     else:
-        results = [evaluator.evaluate(p, workload) for p in programs]
+        results = [evaluator.evaluate(p, workload) for p in batch]
     wall = time.monotonic() - started
 
     attempted = 0
@@ -142,9 +150,9 @@ def run_schedule_sweep(
             "best_speedup_vs_default": (default_median / best_median
                                         if default_median and best_median else None),
         },
-        "evaluations": attempted,
+        "evaluations": len(batch),
         "wall_seconds": wall,
-        "evaluations_per_second": attempted / wall if wall > 0 else None,
+        "evaluations_per_second": len(batch) / wall if wall > 0 else None,
     }
 
 
@@ -178,6 +186,7 @@ def main(argv: Sequence[str] | None = None) -> None:
     p.add_argument("--b-layout", choices=("col", "row"), default="row")
     p.add_argument("--inputs", choices=("uniform", "randn", "int"), default="randn")
     p.add_argument("--count", type=int, default=96)
+    p.add_argument("--repeat", type=int, default=1, help="evaluate every legal point this many times")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--warmups", type=int, default=20)
     p.add_argument("--measurements", type=int, default=100)
@@ -206,7 +215,8 @@ def main(argv: Sequence[str] | None = None) -> None:
                       {"artifact_root": args.artifact_root, "root_us": root_us, "warmup_count": args.warmups,
                        "measurement_count": args.measurements, "inprocess": not args.subprocess})
     with EvaluationPool(devices, spec) as pool:
-        report = run_schedule_sweep(pool, workload, cublas_json, schedules=schedule_grid(args.count, args.seed))
+        report = run_schedule_sweep(pool, workload, cublas_json, schedules=schedule_grid(args.count, args.seed),
+                                    repeat=args.repeat)
     report["devices"] = devices
     if args.out:
         Path(args.out).write_text(json.dumps(report, indent=1))

@@ -110,6 +110,33 @@ typedef struct kmcts_gemm_plan {
  * nothing).  Returns KMCTS_OK or the error kmcts_bf16_gemm_ex would return. */
 int kmcts_gemm_plan_query(const kmcts_gemm_config* cfg, int M, int N, int K, int b_layout, kmcts_gemm_plan* out);
 
+/* ------------------------------------------------- N-sharded GEMM (multi-GPU)
+ * No counterpart in the reference (it has no multi-GPU code).  G ranks, one
+ * per GPU, each hold A [M,K] and their shard of B's columns; the fused call
+ * computes this rank's C columns [rank*N/G, (rank+1)*N/G) and stores every
+ * finished tile into all G ranks' full C [M, N] (row-major) — the GEMM and the
+ * all-gather of C in one kernel, over NVLink peer memory. */
+#define KMCTS_IPC_HANDLE_BYTES 72 /* cudaIpcMemHandle_t + 8-byte offset in the allocation */
+#define KMCTS_MAX_RANKS 8
+
+/* Writes a CUDA IPC handle for a device allocation (cudaIpcGetMemHandle). */
+int kmcts_ipc_export(const void* device_ptr, uint8_t* handle_out);
+/* Maps a peer's exported allocation into this process (cudaIpcOpenMemHandle). */
+int kmcts_ipc_import(const uint8_t* handle, void** device_ptr_out);
+/* Unmaps an imported allocation. */
+int kmcts_ipc_close(void* device_ptr);
+
+/* C_ranks[r] is rank r's full C (this rank's own buffer at index `rank`,
+ * IPC-imported peer buffers elsewhere).  B_shard is this rank's columns:
+ * [N/G, K] row-major for KMCTS_B_COL, [K, N/G] row-major for KMCTS_B_ROW.
+ * N_total/num_ranks must be a multiple of 256 and num_ranks <= 8.  The
+ * schedule must be a CTA pair (tile_m 256).  Asynchronous on `stream`; the
+ * caller synchronises its stream and then all ranks (a host barrier) before
+ * anyone reads C. */
+int kmcts_bf16_gemm_allgather(const void* A, const void* B_shard, void* const* C_ranks, int num_ranks, int rank,
+                              int M, int N_total, int K, int b_layout, const kmcts_gemm_config* cfg, void* stream,
+                              int* device_status);
+
 /* Evaluation inputs (host memory, BF16 bits).  A (a_count values) then B
  * (b_count values) from one generator:
  *   KMCTS_INPUTS_UNIFORM  the repository contract's stream, std::mt19937(seed)

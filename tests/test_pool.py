@@ -78,3 +78,9 @@ def test_single_evaluate_keeps_the_evaluator_call_shape(tmp_path):
     with EvaluationPool([3], spec(tmp_path)) as pool:
         result = pool.evaluate(KernelProgram("x"), WORKLOAD)
     assert result.status == ProposalStatus.VALID and result.metadata["visible_devices"] == "3"
+
+
+def test_prepare_reaches_every_worker(tmp_path):
+    with EvaluationPool([0, 1, 2], spec(tmp_path)) as pool:
+        pool.prepare(WORKLOAD)  # fake evaluators have no prepare hook: a no-op ack per worker
+        assert pool.evaluate(KernelProgram("x"), WORKLOAD).status == ProposalStatus.VALID

@@ -63,3 +63,4 @@ def test_report_schema_charging_and_best():
     assert report["default"]["schedule"] == {**DEFAULT_SCHEDULE}
     assert report["comparison"]["best_latency_ratio_vs_cublas"] == report["best"]["median_us"] / 95.0
     assert report["status"] == "ok" and report["evaluations"] == 18
+    assert run_schedule_sweep(FakeEvaluator(), BF16_GEMM_4096_RANDN, cublas, repeat=3)["evaluations"] == 54
