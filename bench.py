@@ -49,6 +49,9 @@ def parse_args() -> argparse.Namespace:
                    help="row: BASELINE config (A/B row-major); col: the reference contract")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-evals", action="store_true", help="skip the evaluation-throughput pass")
+    p.add_argument("--eval-repeat", type=int, default=3)
+    p.add_argument("--no-sharded", action="store_true", help="skip the sharded 8192x28672x8192 GEMM")
     return p.parse_args()
 
 
@@ -264,6 +267,107 @@ def time_interleaved(fns, steps: int, stream, flush) -> list[list[float]]:
     return [[s.elapsed_time(e) * 1e3 for s, e in zip(starts[j], stops[j])] for j in range(len(fns))]
 
 
+def evaluation_throughput(device, world: int, local_rank: int, a_cpu, b_cpu, layout: str, repeat: int) -> dict:
+    """Candidate-evaluation throughput, one evaluator per GPU (this rank's).
+    Every legal point of the 96-point schedule grid is evaluated ``repeat``
+    times through the tier-0 evaluator: compile (static legality), correctness
+    against cuBLAS, and the harness timing protocol (10 warm-ups, 30 event-timed
+    launches).  Inputs and the reference are prepared before the clock starts.
+    evals/sec = all ranks' evaluations / the slowest rank's wall time."""
+    import torch
+    import torch.distributed as dist
+
+    from kernel_mcts_b200.domain import BenchmarkResult, ProposalStatus
+    from kernel_mcts_b200.evaluation import BackendKernelEvaluator, EvaluationContext
+    from kernel_mcts_b200.inprocess import InProcessSm100Backend
+    from kernel_mcts_b200.sweep import schedule_grid, static_reasons
+    from kernel_mcts_b200.backend import schedule_program
+    from kernel_mcts_b200.workloads import gemm_workload
+
+    workload = gemm_workload("bf16_gemm_4096_randn_b200", M, N, K, b_layout=layout, inputs="randn")
+    backend = InProcessSm100Backend(warmup_count=10, measurement_count=30)
+    evaluator = BackendKernelEvaluator(backend=backend, root_benchmark=BenchmarkResult((100.0,), 100.0),
+                                       context=EvaluationContext(f"rank{local_rank}", "bench", {}, {}))
+    legal = [s for s in schedule_grid() if not static_reasons(s, workload)]
+    programs = [schedule_program(**s) for s in legal] * repeat
+    evaluator.prepare(workload)
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+    torch.cuda.synchronize(device)
+    start = time.perf_counter()
+    results = [evaluator.evaluate(p, workload) for p in programs]
+    torch.cuda.synchronize(device)
+    wall = torch.tensor([time.perf_counter() - start], dtype=torch.float64, device=device)
+    valid = torch.tensor([sum(r.status == ProposalStatus.VALID for r in results)], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(wall, op=dist.ReduceOp.MAX)
+        dist.all_reduce(valid, op=dist.ReduceOp.SUM)
+    total = len(programs) * world
+    return {
+        "value": total / float(wall.item()),
+        "unit": "evaluations/s",
+        "evaluations": total,
+        "valid": int(valid.item()),
+        "wall_s": float(wall.item()),
+        "per_evaluation": "static legality + correctness vs cuBLAS + 10 warm-up and 30 event-timed launches",
+        "schedules": len(legal),
+        "repeat": repeat,
+        "gpus": world,
+    }
+
+
+def sharded_gemm(device, world: int, local_rank: int, steps: int = 5, warmup: int = 2) -> dict:
+    """8192x28672x8192, N(0, 0.02^2) BF16, B and C sharded by
+    N columns over the ranks.  The fused kernel (GEMM + all-gather of C over
+    NVLink peer stores) against the same GEMM followed by NCCL all_gather and
+    a re-layout; aggregate TFLOP/s = 2MNK / max-over-ranks median time."""
+    import torch
+    import torch.distributed as dist
+
+    from kernel_mcts_b200.sharded import ShardedGemm
+
+    m, n, k = 8192, 28672, 8192
+    if world == 1:
+        dist_owned = False
+        if not dist.is_initialized():
+            dist.init_process_group("gloo", init_method="tcp://127.0.0.1:29555", rank=0, world_size=1)
+            dist_owned = True
+    g = torch.Generator(device=device).manual_seed(0)
+    a = (torch.randn((m, k), generator=g, device=device) * 0.02).to(torch.bfloat16)
+    sg = ShardedGemm(m, n, k, b_layout="row")
+    b_shard = (torch.randn((k, sg.shard_width), generator=g, device=device) * 0.02).to(torch.bfloat16)
+    stream = torch.cuda.current_stream(device)
+    out = {"workload": "8192x28672x8192 N(0,0.02) bf16, B/C sharded by N", "gpus": world}
+    try:
+        for name, fn in (("fused", sg.run), ("nccl", sg.run_nccl)):
+            if world == 1 and name == "nccl":
+                continue
+            for _ in range(warmup):
+                fn(a, b_shard)
+                sg.finish()
+            times = []
+            for _ in range(steps):
+                if world > 1:
+                    dist.barrier(device_ids=[local_rank])
+                torch.cuda.synchronize(device)
+                s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s0.record(stream)
+                fn(a, b_shard)
+                s1.record(stream)
+                sg.finish()
+                times.append(s0.elapsed_time(s1) * 1e3)
+            med = torch.tensor([statistics.median(times)], dtype=torch.float64, device=device)
+            if world > 1:
+                dist.all_reduce(med, op=dist.ReduceOp.MAX)
+            out[f"{name}_median_us"] = float(med.item())
+            out[f"{name}_tflops"] = 2.0 * m * n * k / (float(med.item()) * 1e-6) / 1e12
+    finally:
+        sg.close()
+        if world == 1 and dist_owned:
+            dist.destroy_process_group()
+    return out
+
+
 def run_ours(args: argparse.Namespace) -> None:
     import torch
     import torch.distributed as dist
@@ -367,6 +471,13 @@ def run_ours(args: argparse.Namespace) -> None:
             "steps": e2e_steps,
         }
 
+    evaluations = None
+    if not args.no_evals:
+        evaluations = evaluation_throughput(device, world, local_rank, a_cpu, b_cpu, layout, repeat=args.eval_repeat)
+    sharded = None
+    if not args.no_sharded:
+        sharded = sharded_gemm(device, world, local_rank)
+
     if rank == 0:
         peaks, peaks_kind = load_peaks()
         achieved = FLOPS / (mean_ours * 1e-6) / 1e12
@@ -427,6 +538,8 @@ def run_ours(args: argparse.Namespace) -> None:
             "e2e": e2e,
             "gpu_launches": launches,
             "clocks": clocks.summary(),
+            "evaluations": evaluations,
+            "sharded_gemm": sharded,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -142,7 +142,11 @@ class ShardedGemm:
         torch.cuda.synchronize(self.device)
         if int(self.status.item()) != 0:
             raise RuntimeError(f"device status {int(self.status.item()):#x}")
-        dist.barrier(group=self.group, device_ids=[self.device.index])
+        if self.world > 1:
+            if dist.get_backend(self.group) == "nccl":
+                dist.barrier(group=self.group, device_ids=[self.device.index])
+            else:
+                dist.barrier(group=self.group)
 
     def close(self) -> None:
         for r, ptr in enumerate(self.c_ptrs):
