@@ -57,7 +57,9 @@ class InProcessSm100Backend:
         if not torch.cuda.is_available():
             raise EvaluationInfrastructureError("no CUDA device for in-process evaluation")
         self.torch = torch
-        self.device = torch.device("cuda", 0)
+        # The caller's current device (a pool worker sees only its own GPU; a
+        # torchrun rank has selected its GPU with torch.cuda.set_device).
+        self.device = torch.device("cuda", torch.cuda.current_device())
         self.warmup_count = warmup_count
         self.measurement_count = measurement_count
         self.seed = seed
