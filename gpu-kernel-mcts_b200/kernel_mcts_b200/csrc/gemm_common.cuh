@@ -49,11 +49,13 @@ __device__ __forceinline__ uint32_t pack_bf16x2(uint32_t lo_bits, uint32_t hi_bi
 
 // One epilogue warp writes a 32-row x 64-column BF16 chunk (this lane's row,
 // 64 FP32 values in lo[0..31], hi[0..31]) into a 128-byte-swizzled staging
-// buffer and TMA-stores it at (col0, row0) of C.  Two staging buffers per
-// warp alternate; the wait keeps at most one store reading each.
+// buffer and TMA-stores it at (col0, row0) of C, and of each of `extra_count`
+// further tensors (the peers' C in a fused all-gather).  Two staging buffers
+// per warp alternate; the wait keeps at most one group of stores reading each.
 __device__ __forceinline__ void store_chunk(const CUtensorMap* map_c, uint8_t* staging, int& chunk_count,
                                             const uint32_t (&lo)[32], const uint32_t (&hi)[32], int lane,
-                                            int col0, int row0) {
+                                            int col0, int row0, const CUtensorMap* extra_maps = nullptr,
+                                            int extra_count = 0) {
     uint32_t packed[32];
 #pragma unroll
     for (int i = 0; i < 16; ++i) packed[i] = pack_bf16x2(lo[2 * i], lo[2 * i + 1]);
@@ -73,6 +75,7 @@ __device__ __forceinline__ void store_chunk(const CUtensorMap* map_c, uint8_t* s
     __syncwarp();
     if (lane == 0) {
         ptx::tma_store_2d(map_c, buf, col0, row0);
+        for (int i = 0; i < extra_count; ++i) ptx::tma_store_2d(&extra_maps[i], buf, col0, row0);
         ptx::bulk_commit_group();
     }
     ++chunk_count;

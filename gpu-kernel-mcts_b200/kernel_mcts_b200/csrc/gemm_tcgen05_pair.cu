@@ -52,9 +52,8 @@ struct PairLayout {
 // buffers (IPC-mapped peer memory), their row stride, and this rank's column
 // offset inside the full C.  Unused (count 0, offset 0) by plain GEMMs.
 struct PeerOutputs {
-    __nv_bfloat16* ptr[KMCTS_MAX_RANKS - 1];
+    CUtensorMap map[KMCTS_MAX_RANKS - 1];  // each peer's full C [M, N_total]
     int count;
-    int ld;
     int col_offset;
 };
 
@@ -283,31 +282,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                     __syncwarp();
                     if (lane == 0) ptx::mbar_arrive_cluster(ptx::mapa_shared(ptx::smem_addr(&tmem_empty[acc]), 0));
                 }
-                if constexpr (ALLGATHER) {
-                    // This lane's row of the chunk to every peer's C: 8 x 16-byte
-                    // stores of contiguous BF16 (plain P2P stores over NVLink).
-                    const int row = m0 + quarter * 32 + lane;
-                    if (row < M) {
-                        uint32_t w[32];
-#pragma unroll
-                        for (int i = 0; i < 16; ++i) w[i] = pack_bf16x2(lo[2 * i], lo[2 * i + 1]);
-#pragma unroll
-                        for (int i = 0; i < 16; ++i) w[16 + i] = pack_bf16x2(hi[2 * i], hi[2 * i + 1]);
-                        const size_t offset = static_cast<size_t>(row) * peers.ld + peers.col_offset + n0 + c * 64;
-                        for (int p = 0; p < peers.count; ++p) {
-                            uint4* dst = reinterpret_cast<uint4*>(peers.ptr[p] + offset);
-#pragma unroll
-                            for (int j = 0; j < 8; ++j)
-                                dst[j] = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
-                        }
-                    }
-                }
+                // Own C by TMA store; in a fused all-gather the same staged
+                // chunk also goes to every peer's C (TMA stores over NVLink).
                 store_chunk(&map_c, staging, chunk_count, lo, hi, lane, peers.col_offset + n0 + c * 64,
-                            m0 + quarter * 32);
+                            m0 + quarter * 32, ALLGATHER ? peers.map : nullptr, ALLGATHER ? peers.count : 0);
             }
         }
-        if (lane == 0) ptx::bulk_wait_group<0>();
-        if constexpr (ALLGATHER) __threadfence_system();  // peer stores performed before the grid ends
+        if (lane == 0) ptx::bulk_wait_group<0>();  // own and peer stores complete before the grid ends
         __syncwarp();
     }
 
@@ -496,9 +477,11 @@ int launch_pair_allgather(const CUtensorMap& ma, const CUtensorMap& mb, const CU
         peer_count > KMCTS_MAX_RANKS - 1)
         return KMCTS_ENOTSUP;
     PeerOutputs peers = {};
-    for (int p = 0; p < peer_count; ++p) peers.ptr[p] = static_cast<__nv_bfloat16*>(peer_c[p]);
+    for (int p = 0; p < peer_count; ++p) {
+        if (!encode_tensor_map_2d(&peers.map[p], peer_c[p], ld, M, static_cast<uint64_t>(ld) * 2, 64, 32))
+            return KMCTS_EINVAL;
+    }
     peers.count = peer_count;
-    peers.ld = ld;
     peers.col_offset = col_offset;
     const bool split = (cfg.flags & KMCTS_FLAG_NO_TAIL_SPLIT) == 0;
     if (b_layout == KMCTS_B_ROW)
