@@ -63,6 +63,7 @@ EXPORTED_SYMBOLS = (
     "kmcts_ipc_import",
     "kmcts_ipc_close",
     "kmcts_bf16_gemm_allgather",
+    "kmcts_selftest_bounded_wait",
 )
 
 
@@ -195,6 +196,8 @@ def load() -> ctypes.CDLL:
         lib.kmcts_bf16_gemm_allgather.argtypes = [vp, vp, vp, i32, i32, i32, i32, i32, i32,
                                                   ctypes.POINTER(GemmConfig), vp, vp]
         lib.kmcts_bf16_gemm_allgather.restype = i32
+        lib.kmcts_selftest_bounded_wait.argtypes = [i64, i32, vp, vp, vp]
+        lib.kmcts_selftest_bounded_wait.restype = i32
         lib.kmcts_launch_count.argtypes = []
         lib.kmcts_launch_count.restype = i64
         _lib = lib

@@ -18,6 +18,13 @@ constexpr int kSmemReserve = 2048;       // barriers + 1024-byte alignment slack
 constexpr int kMaxSmem = 232448;         // 227 KB opt-in per CTA
 constexpr uint64_t kDefaultWaitNs = 2000000000ull;
 
+// Drains (waiting for this CTA's own in-flight copies and MMAs before it
+// frees TMEM and exits) never use a shorter bound than the default, whatever
+// limit the caller set for the main-loop waits.
+__device__ __forceinline__ uint64_t drain_limit(uint64_t limit_ns) {
+    return limit_ns > kDefaultWaitNs ? limit_ns : kDefaultWaitNs;
+}
+
 // Status word: low byte KMCTS_ETIMEOUT, next byte the role that gave up.
 constexpr int kRoleProducer = 1, kRoleMma = 2, kRoleEpilogue = 3, kRoleDrain = 4;
 

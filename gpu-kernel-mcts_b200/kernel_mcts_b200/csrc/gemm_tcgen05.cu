@@ -152,7 +152,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // Drain: every load this thread issued lands before the CTA exits.
             for (int s = 0; s < STAGES; ++s) {
                 if (issued & (1u << s)) {
-                    if (!ptx::mbar_wait(&full[s], (issued_phase >> s) & 1u, limit_ns, no_abort)) {
+                    if (!ptx::mbar_wait(&full[s], (issued_phase >> s) & 1u, drain_limit(limit_ns), no_abort)) {
                         record_failure(status, abort, kRoleDrain);
                     }
                 }
@@ -209,7 +209,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             // Drain: all MMAs issued by this thread complete before TMEM is freed.
             ptx::umma_commit(drain);
-            if (!ptx::mbar_wait(drain, 0, limit_ns, no_abort)) {
+            if (!ptx::mbar_wait(drain, 0, drain_limit(limit_ns), no_abort)) {
                 record_failure(status, abort, kRoleDrain);
             }
         }

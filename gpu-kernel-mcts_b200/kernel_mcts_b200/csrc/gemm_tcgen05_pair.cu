@@ -191,7 +191,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (leader) {
                 for (int s = 0; s < STAGES; ++s) {
                     if ((issued & (1u << s)) &&
-                        !ptx::mbar_wait(&full[s], (issued_phase >> s) & 1u, limit_ns, no_abort)) {
+                        !ptx::mbar_wait(&full[s], (issued_phase >> s) & 1u, drain_limit(limit_ns), no_abort)) {
                         record_failure(status, abort, kRoleDrain);
                     }
                 }
@@ -298,7 +298,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Both CTAs: every UMMA that touches this CTA's TMEM and shared memory
         // has completed (the leader's final commit arrives here in both CTAs).
         // Waited only after this CTA's epilogue finished, so the wait is short.
-        if (lane == 0 && !ptx::mbar_wait(drain, 0, limit_ns, no_abort)) record_failure(status, abort, kRoleDrain);
+        if (lane == 0 && !ptx::mbar_wait(drain, 0, drain_limit(limit_ns), no_abort)) record_failure(status, abort, kRoleDrain);
         __syncwarp();
     }
     ptx::cluster_sync();  // no CTA leaves while its peer may still signal it

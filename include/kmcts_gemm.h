@@ -195,6 +195,15 @@ int kmcts_bf16_compare(const void* C, const void* reference, int64_t count, doub
 int kmcts_bf16_compare_noalloc(const void* C, const void* reference, int64_t count, double rtol,
                                double atol, void* stream, kmcts_compare_result* out);
 
+/* No counterpart in the reference.  Self-test of the bounded device-side wait
+ * behind every GEMM barrier: one thread waits on an mbarrier; with arrive = 1
+ * the phase is already complete, with arrive = 0 nothing ever arrives and the
+ * wait must give up after limit_ns (0 < limit_ns <= 10 s), setting
+ * *device_status to KMCTS_ETIMEOUT | role << 8.  *device_waited_ns receives the
+ * time spent waiting.  Asynchronous on `stream`; touches no TMA or TMEM. */
+int kmcts_selftest_bounded_wait(int64_t limit_ns, int arrive, void* stream, int* device_status,
+                                unsigned long long* device_waited_ns);
+
 /* Number of kernels this library has launched in this process (all entry
  * points).  Lets callers count GPU launches inside a timed region. */
 int64_t kmcts_launch_count(void);
