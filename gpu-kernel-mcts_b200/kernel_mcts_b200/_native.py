@@ -42,6 +42,12 @@ KERNEL_TCGEN05 = 1
 KERNEL_SIMT = 2
 
 FLAG_NO_TAIL_SPLIT = 1
+FLAG_TAIL_SPLIT_N = 2
+FLAG_TAIL_STREAM_K = 4
+
+TAIL_NONE = 0
+TAIL_SPLIT_N = 1
+TAIL_STREAM_K = 2
 
 INPUTS = {"uniform": 0, "randn": 1, "int": 2}
 
@@ -113,6 +119,9 @@ class GemmPlan(ctypes.Structure):
         ("full_tiles", ctypes.c_int32),
         ("units", ctypes.c_int32),
         ("smem_bytes", ctypes.c_int32),
+        ("tail_split", ctypes.c_int32),
+        ("tail_clusters", ctypes.c_int32),
+        ("tail_segments", ctypes.c_int32),
     ]
 
     def as_dict(self) -> dict[str, int]:

@@ -494,7 +494,7 @@ int launch_allgather_tcgen05(const void* A, const void* B_shard, void* const* C_
 int plan_tcgen05(const kmcts_gemm_config& cfg, int M, int N, int K, int b_layout, kmcts_gemm_plan* out) {
     const int rc = tcgen05_legal(cfg, M, N, K, b_layout, nullptr, 0);
     if (rc != KMCTS_OK) return rc;
-    if (is_pair(cfg)) return plan_pair(cfg, M, N, b_layout, out);
+    if (is_pair(cfg)) return plan_pair(cfg, M, N, K, b_layout, out);
     kmcts_gemm_plan plan = {};
     plan.kernel = 1;
     plan.cluster_size = 1;

@@ -21,6 +21,7 @@
 // Every wait is bounded; see gemm_tcgen05.cu for the failure protocol.
 #include <cstring>
 #include <mutex>
+#include <thread>
 
 #include "gemm_common.cuh"
 #include "kmcts_internal.h"
@@ -57,25 +58,131 @@ struct PeerOutputs {
     int col_offset;
 };
 
-// Work units.  Tiles [0, full_tiles) (in raster order) run whole; each later
-// tile runs as two BN/2-wide halves, so a last partial wave of R <= W/2 tiles
-// costs half a tile of time instead of a whole one.  Every output element is
-// still one full-K UMMA chain: splitting changes no result bit.
-struct Unit {
-    int m_blk, n0, width;
+// Work list.  Tiles [0, full_tiles) run whole, round-robin over the W
+// co-resident clusters.  With T tiles = q W + rem (0 < rem, q >= 1), a plain
+// round-robin leaves W - rem clusters idle for the whole last round; the
+// tiles after full_tiles run instead as:
+//   kTailStreamK  (opt-in) the last W + rem tiles' K blocks, cut into W
+//                 equal contiguous ranges, one per cluster (stream-K);
+//                 full_tiles = (q - 1) W.  A range is at least one tile long,
+//                 so a tile is either inside one range (run whole) or split
+//                 at one range boundary into a K prefix, the last unit of
+//                 cluster c - 1, and a K suffix, the first unit of cluster c.
+//                 Per (CTA, TMEM lane quarter) the segment that reaches its
+//                 epilogue first stores its FP32 rows to the boundary's
+//                 partial slot and raises a ready flag; the second waits
+//                 (bounded) for the flag, adds the partial, rounds once to
+//                 BF16 and clears the flags.  The second only ever waits on a
+//                 segment that has already arrived, so no wait depends on
+//                 scheduling; and as the suffix runs first in its range and
+//                 the prefix last in its, the partial is normally long stored
+//                 when the prefix arrives.  Each output of a split tile is the
+//                 FP32 sum of two K-ordered chains (addition commutes, so the
+//                 bits do not depend on which segment arrived first).
+//   kTailSplitN   (default; 2 rem <= W, BN 256) each of the last rem tiles as two
+//                 BN/2-wide halves on two clusters.  Every output stays one
+//                 full-K UMMA chain, bit-identical to whole tiles; but
+//                 half-width pair MMAs stage 1.5x the operand bytes per FLOP,
+//                 so a half unit takes about 3/4 of a whole tile's time.
+// Flags carry the launch's epoch (a per-workspace host counter), so values
+// left by an earlier failed launch are never taken for this launch's.
+constexpr int kTailWhole = 0, kTailSplitN = 1, kTailStreamK = 2;
+
+struct TailSplit {
+    float* partials;  // [boundary][CTA rank][quarter][BN/64 chunks][16 float4][32 lanes]
+    int* ready;       // [boundary][CTA rank][quarter]
+    int* arrivals;    // [boundary][CTA rank][quarter]
+    int epoch;
+    int mode;
 };
 
-template <int BN>
-__device__ __forceinline__ Unit pair_unit(int u, int full_tiles, int num_m, int num_n, int group) {
-    int t = u, half = 0, width = BN;
-    if (u >= full_tiles) {
-        const int v = u - full_tiles;
-        t = full_tiles + v / 2;
-        half = v & 1;
-        width = BN / 2;
+struct Unit {
+    int m_blk, n0, width, kb0, kb1;
+    int boundary;  // stream-K: the range boundary splitting this tile, else -1
+};
+
+// Stream-K ranges: cluster c owns K blocks [lo(c), lo(c + 1)) of the
+// stream-K tiles (tile-major, K blocks within a tile in order).
+__device__ __forceinline__ long long sk_lo(int c, long long total, int p) {
+    return static_cast<long long>(c) * total / p;
+}
+
+// The cluster whose range holds K block g: the largest c with lo(c) <= g.
+__device__ __forceinline__ int sk_owner(long long g, long long total, int p) {
+    return static_cast<int>(((g + 1) * p + total - 1) / total - 1);
+}
+
+// One cluster's work list: its whole tiles, then its tail units.
+struct Schedule {
+    int num_m, num_n, group, num_kb, full_tiles, clusters, cluster;
+    int n_full, n_tail;
+    long long g0, g1;  // stream-K range
+    long long total;   // stream-K K blocks
+
+    __device__ int count() const { return n_full + n_tail; }
+};
+
+__device__ __forceinline__ Schedule make_schedule(int M, int N, int K, int BN, int BK, int group, int full_tiles,
+                                                  int cluster, int clusters, const TailSplit& tail) {
+    Schedule s;
+    s.num_m = (M + 255) / 256;
+    s.num_n = (N + BN - 1) / BN;
+    s.group = group;
+    s.num_kb = (K + BK - 1) / BK;
+    s.full_tiles = full_tiles;
+    s.clusters = clusters;
+    s.cluster = cluster;
+    s.n_full = cluster < full_tiles ? (full_tiles - 1 - cluster) / clusters + 1 : 0;
+    s.n_tail = 0;
+    s.g0 = s.g1 = 0;
+    const int rest = s.num_m * s.num_n - full_tiles;
+    s.total = static_cast<long long>(rest) * s.num_kb;
+    if (rest > 0 && tail.mode == kTailSplitN) {
+        s.n_tail = cluster < 2 * rest ? 1 : 0;
+    } else if (rest > 0 && tail.mode == kTailStreamK) {
+        s.g0 = sk_lo(cluster, s.total, clusters);
+        s.g1 = sk_lo(cluster + 1, s.total, clusters);
+        s.n_tail = s.g1 > s.g0 ? static_cast<int>((s.g1 - 1) / s.num_kb - s.g0 / s.num_kb + 1) : 0;
     }
-    const TileCoord tc = tile_coord(t, num_m, num_n, group);
-    return {tc.m_blk, tc.n_blk * BN + half * (BN / 2), width};
+    return s;
+}
+
+template <int BN>
+__device__ __forceinline__ Unit schedule_unit(const Schedule& s, int i, const TailSplit& tail) {
+    Unit out = {0, 0, BN, 0, s.num_kb, -1};
+    int t, half_n = 0;
+    if (i < s.n_full) {
+        t = s.cluster + i * s.clusters;
+    } else if (tail.mode == kTailSplitN) {
+        t = s.full_tiles + s.cluster / 2;
+        half_n = s.cluster & 1;
+        out.width = BN / 2;
+    } else {
+        const long long tt = s.g0 / s.num_kb + (i - s.n_full);
+        const long long first_g = tt * s.num_kb;
+        out.kb0 = static_cast<int>((s.g0 > first_g ? s.g0 : first_g) - first_g);
+        out.kb1 = static_cast<int>((s.g1 < first_g + s.num_kb ? s.g1 : first_g + s.num_kb) - first_g);
+        const int last = sk_owner(first_g + s.num_kb - 1, s.total, s.clusters);
+        if (sk_owner(first_g, s.total, s.clusters) != last) out.boundary = last;
+        t = s.full_tiles + static_cast<int>(tt);
+    }
+    const TileCoord tc = tile_coord(t, s.num_m, s.num_n, s.group);
+    out.m_blk = tc.m_blk;
+    out.n0 = tc.n_blk * BN + half_n * (BN / 2);
+    return out;
+}
+
+// Chunk c (32 rows x 64 FP32) of the partial at a range boundary for (CTA
+// rank, lane quarter), stored as 16 float4 groups interleaved across the 32
+// lanes, so that every warp-wide store and load is coalesced.
+template <int BN>
+__device__ __forceinline__ float4* partial_chunk(const TailSplit& tail, int boundary, int rank, int quarter, int c) {
+    const size_t chunk = ((static_cast<size_t>(boundary) * 2 + rank) * 4 + quarter) * (BN / 64) + c;
+    return reinterpret_cast<float4*>(tail.partials + chunk * 32 * 64);
+}
+
+__device__ __forceinline__ size_t flag_index(int boundary, int rank, int quarter) {
+    return (static_cast<size_t>(boundary) * 2 + rank) * 4 + quarter;
 }
 
 template <int BN, int BK, int STAGES, bool B_MN, bool ALLGATHER>
@@ -85,7 +192,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                            const __grid_constant__ CUtensorMap map_b_half,
                            const __grid_constant__ CUtensorMap map_c, int M, int N, int K, int group,
                            int full_tiles, uint64_t limit_ns, int* status,
-                           const __grid_constant__ PeerOutputs peers) {
+                           const __grid_constant__ PeerOutputs peers, const TailSplit tail) {
     using L = PairLayout<BN, BK, STAGES, B_MN>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -95,22 +202,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* tmem_full = empty + STAGES;
     uint64_t* tmem_empty = tmem_full + 2;
     uint64_t* drain = tmem_empty + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    uint64_t* partial_full = drain + 1;  // one per epilogue warp: partial landed in shared memory
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(partial_full + kEpilogueWarps);
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
     volatile int* no_abort = abort + 1;
 
     if (status == nullptr) status = &g_default_status;
+    // A warp's rows of a stream-K partial (BN/64 chunks of 32 x 64 FP32) are
+    // staged in the pipeline buffers when those hold all four warps' rows.
+    constexpr uint32_t kPartialWarpBytes = (BN / 64) * 32 * 64 * 4;
+    constexpr bool kStagePartial = L::kStagingOffset >= kEpilogueWarps * static_cast<int>(kPartialWarpBytes);
     const int warp = threadIdx.x / 32;
     const int lane = threadIdx.x % 32;
     const uint32_t rank = ptx::cluster_ctarank();
     const bool leader = rank == 0;
-    const int cluster_id = blockIdx.x / 2;
-    const int num_clusters = gridDim.x / 2;
-    const int num_m = (M + 255) / 256;
-    const int num_n = (N + BN - 1) / BN;
-    const int num_tiles = num_m * num_n;
-    const int num_units = full_tiles + 2 * (num_tiles - full_tiles);
-    const int num_kb = (K + BK - 1) / BK;
+    const Schedule sched = make_schedule(M, N, K, BN, BK, group, full_tiles, blockIdx.x / 2, gridDim.x / 2, tail);
+    const int num_units = sched.count();
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -122,6 +229,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ptx::mbar_init(&tmem_empty[a], 2 * kEpilogueWarps);
         }
         ptx::mbar_init(drain, 1);
+        for (int w = 0; w < kEpilogueWarps; ++w) ptx::mbar_init(&partial_full[w], 1);
         *abort = 0;
         *no_abort = 0;
         ptx::fence_mbarrier_init();
@@ -149,14 +257,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t phase = 0;
             uint32_t issued = 0, issued_phase = 0;
             bool ok = true;
-            for (int u = cluster_id; u < num_units && ok; u += num_clusters) {
-                const Unit w = pair_unit<BN>(u, full_tiles, num_m, num_n, group);
+            for (int u = 0; u < num_units && ok; ++u) {
+                const Unit w = schedule_unit<BN>(sched, u, tail);
                 const int m0 = w.m_blk * 256 + static_cast<int>(rank) * 128;
                 const int b_cols = w.width / 2;  // B columns this CTA stages
                 const int nb0 = w.n0 + static_cast<int>(rank) * b_cols;
                 const uint32_t unit_bytes = 2u * (L::kABytes + b_cols * BK * 2);
                 const CUtensorMap* mb = w.width == BN ? &map_b : &map_b_half;
-                for (int kb = 0; kb < num_kb; ++kb) {
+                for (int kb = w.kb0; kb < w.kb1; ++kb) {
                     if (!ptx::mbar_wait(&empty[stage], phase ^ 1u, limit_ns, abort)) {
                         record_failure(status, abort, kRoleProducer);
                         ok = false;
@@ -206,8 +314,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t phase = 0;
             int local = 0;
             bool ok = true;
-            for (int u = cluster_id; u < num_units && ok; u += num_clusters, ++local) {
-                const uint32_t idesc = u < full_tiles ? idesc_full : idesc_half;
+            for (int u = 0; u < num_units && ok; ++u, ++local) {
+                const Unit w = schedule_unit<BN>(sched, u, tail);
+                const uint32_t idesc = w.width == BN ? idesc_full : idesc_half;
                 const int acc = local & 1;
                 const uint32_t acc_phase = (local >> 1) & 1;
                 if (!ptx::mbar_wait(&tmem_empty[acc], acc_phase ^ 1u, limit_ns, abort)) {
@@ -216,7 +325,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 ptx::tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * BN;
-                for (int kb = 0; kb < num_kb; ++kb) {
+                for (int kb = w.kb0; kb < w.kb1; ++kb) {
                     if (!ptx::mbar_wait(&full[stage], phase, limit_ns, abort)) {
                         record_failure(status, abort, kRoleMma);
                         ok = false;
@@ -236,7 +345,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         } else {
                             bdesc = ptx::make_sw128_desc(sb + kh * (L::kHalfN * 128) + kq * 32, 16, 1024);
                         }
-                        ptx::umma_bf16_pair(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
+                        ptx::umma_bf16_pair(d_tmem, adesc, bdesc, idesc, (kb != w.kb0 || kk != 0) ? 1u : 0u);
                     }
                     ptx::umma_commit_pair(&empty[stage], 0x3);
                     if (++stage == STAGES) {
@@ -255,15 +364,54 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint8_t* staging = smem + L::kStagingOffset + (warp - 2) * 2 * kStagingBytes;
         int local = 0;
         int chunk_count = 0;
-        for (int u = cluster_id; u < num_units; u += num_clusters, ++local) {
-            const Unit w = pair_unit<BN>(u, full_tiles, num_m, num_n, group);
+        for (int u = 0; u < num_units; ++u, ++local) {
+            const Unit w = schedule_unit<BN>(sched, u, tail);
             const int m0 = w.m_blk * 256 + static_cast<int>(rank) * 128;
             const int n0 = w.n0;
             const int chunks = w.width / 64;
             const int acc = local & 1;
             const uint32_t acc_phase = (local >> 1) & 1;
+            const bool split = w.boundary >= 0;
+            int* arrival = split ? tail.arrivals + flag_index(w.boundary, static_cast<int>(rank), quarter) : nullptr;
+            int* ready = split ? tail.ready + flag_index(w.boundary, static_cast<int>(rank), quarter) : nullptr;
+            // A partner that has already published its partial makes this
+            // segment the second; looked up while the MMAs still run.
+            int published = 0;
+            if (split && lane == 0) published = ptx::ld_acquire_gpu(ready) == tail.epoch;
             bool ok = ptx::mbar_wait(&tmem_full[acc], acc_phase, limit_ns, abort);
             ok = __all_sync(0xffffffffu, ok);
+            bool second = false;  // stream-K: the other segment arrived first; this one writes C
+            bool staged = false;  // stream-K: the partial is read from shared memory
+            if (ok && split) {
+                int prev = tail.epoch;
+                if (lane == 0 && !published) prev = atomicExch(arrival, tail.epoch);
+                second = __shfl_sync(0xffffffffu, prev, 0) == tail.epoch;
+                if (second) {
+                    // Wait (bounded) for the first segment's rows of the partial.
+                    const uint64_t start = ptx::global_timer_ns();
+                    while (ptx::ld_acquire_gpu(ready) != tail.epoch) {
+                        if (*abort || ptx::global_timer_ns() - start > limit_ns) {
+                            ok = false;
+                            break;
+                        }
+                    }
+                    ok = __all_sync(0xffffffffu, ok);
+                    // In the cluster's last unit every MMA is done and no TMA
+                    // load is left, so the pipeline stages are free: one bulk
+                    // load brings this warp's rows of the partial on chip.
+                    if (ok && kStagePartial && u == num_units - 1) {
+                        uint8_t* dst = smem + (warp - 2) * kPartialWarpBytes;
+                        if (lane == 0) {
+                            ptx::fence_proxy_async_global();
+                            ptx::mbar_arrive_expect_tx(&partial_full[warp - 2], kPartialWarpBytes);
+                            ptx::bulk_load(dst, partial_chunk<BN>(tail, w.boundary, static_cast<int>(rank), quarter, 0),
+                                           kPartialWarpBytes, &partial_full[warp - 2]);
+                        }
+                        ok = __all_sync(0xffffffffu, ptx::mbar_wait(&partial_full[warp - 2], 0, limit_ns, abort));
+                        staged = true;
+                    }
+                }
+            }
             if (!ok) {
                 if (lane == 0) record_failure(status, abort, kRoleEpilogue);
                 break;
@@ -282,13 +430,73 @@ __global__ void __launch_bounds__(kThreads, 1)
                     __syncwarp();
                     if (lane == 0) ptx::mbar_arrive_cluster(ptx::mapa_shared(ptx::smem_addr(&tmem_empty[acc]), 0));
                 }
+                if (split) {
+                    float4* part = partial_chunk<BN>(tail, w.boundary, static_cast<int>(rank), quarter, c);
+                    if (!second) {
+#pragma unroll
+                        for (int q = 0; q < 8; ++q)
+                            __stcg(part + q * 32 + lane,
+                                   make_float4(__uint_as_float(lo[4 * q]), __uint_as_float(lo[4 * q + 1]),
+                                               __uint_as_float(lo[4 * q + 2]), __uint_as_float(lo[4 * q + 3])));
+#pragma unroll
+                        for (int q = 0; q < 8; ++q)
+                            __stcg(part + (8 + q) * 32 + lane,
+                                   make_float4(__uint_as_float(hi[4 * q]), __uint_as_float(hi[4 * q + 1]),
+                                               __uint_as_float(hi[4 * q + 2]), __uint_as_float(hi[4 * q + 3])));
+                        continue;  // the second segment writes C
+                    }
+                    float4 p[16];  // all of the chunk's loads in flight at once
+                    if (staged) {
+                        const float4* sp = reinterpret_cast<const float4*>(smem + (warp - 2) * kPartialWarpBytes) +
+                                           c * 16 * 32;
+#pragma unroll
+                        for (int q = 0; q < 16; ++q) p[q] = sp[q * 32 + lane];
+                    } else {
+#pragma unroll
+                        for (int q = 0; q < 16; ++q) p[q] = __ldcg(part + q * 32 + lane);
+                    }
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) {
+                        lo[4 * q] = __float_as_uint(__uint_as_float(lo[4 * q]) + p[q].x);
+                        lo[4 * q + 1] = __float_as_uint(__uint_as_float(lo[4 * q + 1]) + p[q].y);
+                        lo[4 * q + 2] = __float_as_uint(__uint_as_float(lo[4 * q + 2]) + p[q].z);
+                        lo[4 * q + 3] = __float_as_uint(__uint_as_float(lo[4 * q + 3]) + p[q].w);
+                        hi[4 * q] = __float_as_uint(__uint_as_float(hi[4 * q]) + p[8 + q].x);
+                        hi[4 * q + 1] = __float_as_uint(__uint_as_float(hi[4 * q + 1]) + p[8 + q].y);
+                        hi[4 * q + 2] = __float_as_uint(__uint_as_float(hi[4 * q + 2]) + p[8 + q].z);
+                        hi[4 * q + 3] = __float_as_uint(__uint_as_float(hi[4 * q + 3]) + p[8 + q].w);
+                    }
+                }
                 // Own C by TMA store; in a fused all-gather the same staged
                 // chunk also goes to every peer's C (TMA stores over NVLink).
                 store_chunk(&map_c, staging, chunk_count, lo, hi, lane, peers.col_offset + n0 + c * 64,
                             m0 + quarter * 32, ALLGATHER ? peers.map : nullptr, ALLGATHER ? peers.count : 0);
             }
+            if (split) {
+                __syncwarp();
+                if (!second) {
+                    // Publish this warp's rows: every lane's stores, then one
+                    // release of the ready flag.
+                    __threadfence();
+                    __syncwarp();
+                    if (lane == 0) ptx::st_release_gpu(ready, tail.epoch);
+                } else if (lane == 0) {
+                    // Both segments are done with these flags: clear them, so
+                    // a replay of this very launch (same epoch) starts clean.
+                    *arrival = 0;
+                    *ready = 0;
+                }
+            }
         }
-        if (lane == 0) ptx::bulk_wait_group<0>();  // own and peer stores complete before the grid ends
+        if (lane == 0) {
+            // Shared memory must outlive the stores' reads of it; a fused
+            // all-gather also waits for its peer writes to complete.
+            if constexpr (ALLGATHER) {
+                ptx::bulk_wait_group<0>();
+            } else {
+                ptx::bulk_wait_group_read<0>();
+            }
+        }
         __syncwarp();
     }
 
@@ -344,9 +552,29 @@ int pair_workers(int device) {
     return max_clusters[device];
 }
 
-// The launch shape: how many pairs run, and which tiles run whole.
-template <int BN>
-kmcts_gemm_plan make_pair_plan(int M, int N, int workers, bool persistent, bool split_tail, int64_t smem) {
+// Which tail split a schedule asks for (the flags), before the shape decides
+// whether the tail can split at all.
+int requested_tail(int flags) {
+    if (flags & KMCTS_FLAG_NO_TAIL_SPLIT) return KMCTS_TAIL_NONE;
+    if (flags & KMCTS_FLAG_TAIL_STREAM_K) return KMCTS_TAIL_STREAM_K;
+    return KMCTS_TAIL_SPLIT_N;
+}
+
+// Work units of the stream-K tiles over p clusters (host copy of the
+// kernel's range arithmetic).
+int stream_k_units(long long total, int num_kb, int p) {
+    int units = 0;
+    for (int c = 0; c < p; ++c) {
+        const long long g0 = static_cast<long long>(c) * total / p, g1 = static_cast<long long>(c + 1) * total / p;
+        if (g1 > g0) units += static_cast<int>((g1 - 1) / num_kb - g0 / num_kb + 1);
+    }
+    return units;
+}
+
+// The launch shape: how many pairs run, which tiles run whole, and how the
+// tiles of the last partial wave are shared.
+template <int BN, int BK>
+kmcts_gemm_plan make_pair_plan(int M, int N, int K, int workers, bool persistent, int tail, int64_t smem) {
     kmcts_gemm_plan plan = {};
     plan.kernel = 2;
     plan.cluster_size = 2;
@@ -356,14 +584,27 @@ kmcts_gemm_plan make_pair_plan(int M, int N, int workers, bool persistent, bool 
     plan.units = plan.tiles;
     int clusters = plan.tiles;
     if (persistent) {
-        // Split the last partial wave into half-width units when it fits in
-        // one round of half units (2R <= W); half tiles need BN/2 to be a
-        // whole number of 64-column TMA boxes per CTA for row-major B.
+        clusters = plan.tiles < workers ? plan.tiles : workers;
         const int rem = plan.tiles % workers;
-        const bool can_split = split_tail && BN == 256 && rem != 0 && 2 * rem <= workers;
-        plan.full_tiles = can_split ? plan.tiles - rem : plan.tiles;
-        plan.units = plan.full_tiles + 2 * (plan.tiles - plan.full_tiles);
-        clusters = plan.units < workers ? plan.units : workers;
+        const int num_kb = (K + BK - 1) / BK;
+        if (rem != 0 && tail == KMCTS_TAIL_STREAM_K && plan.tiles > workers) {
+            // The last full wave and the partial one, shared by all W pairs.
+            plan.tail_split = KMCTS_TAIL_STREAM_K;
+            plan.full_tiles = (plan.tiles / workers - 1) * workers;
+            plan.tail_clusters = workers;
+            plan.tail_segments = 2;
+            const long long total = static_cast<long long>(plan.tiles - plan.full_tiles) * num_kb;
+            plan.units = plan.full_tiles + stream_k_units(total, num_kb, workers);
+            clusters = workers;
+        } else if (rem != 0 && tail != KMCTS_TAIL_NONE && BN == 256 && 2 * rem <= workers) {
+            // Half-width units: BN/2 must be whole 64-column TMA boxes per CTA.
+            plan.tail_split = KMCTS_TAIL_SPLIT_N;
+            plan.tail_clusters = 2 * rem;
+            plan.tail_segments = 1;
+            plan.full_tiles = plan.tiles - rem;
+            plan.units = plan.full_tiles + 2 * rem;
+            clusters = plan.units < workers ? plan.units : workers;
+        }
     }
     plan.ctas = 2 * clusters;
     plan.smem_bytes = static_cast<int32_t>(smem);
@@ -371,24 +612,99 @@ kmcts_gemm_plan make_pair_plan(int M, int N, int workers, bool persistent, bool 
 }
 
 template <int BN, int BK, int STAGES, bool B_MN, bool ALLGATHER = false>
-int plan_pair_variant(int M, int N, bool persistent, bool split_tail, kmcts_gemm_plan* out) {
+int plan_pair_variant(int M, int N, int K, bool persistent, int tail, kmcts_gemm_plan* out) {
     int device = 0;
     if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kMaxDevices) return KMCTS_EHANDLE;
     const int workers = pair_workers<BN, BK, STAGES, B_MN, ALLGATHER>(device);
     if (workers <= 0) return KMCTS_EGEMM;
-    *out = make_pair_plan<BN>(M, N, workers, persistent, split_tail, PairLayout<BN, BK, STAGES, B_MN>::kSmemBytes);
+    *out = make_pair_plan<BN, BK>(M, N, K, workers, persistent, tail, PairLayout<BN, BK, STAGES, B_MN>::kSmemBytes);
     return KMCTS_OK;
+}
+
+// FP32 partials and flags of stream-K tiles, one workspace per (device,
+// stream): launches on one stream run in order, so they may share it;
+// launches on different streams may overlap, so they may not.  One partial
+// slot per range boundary (W - 1 at most, sized for W = SMs / 2).  Allocated
+// and zeroed on a stream's first stream-K launch, kept for the process's
+// lifetime.
+struct TailWorkspace {
+    int device;
+    cudaStream_t stream;
+    std::thread::id thread;  // distinguishes per-thread default streams
+    float* partials;
+    int* flags;              // ready flags, then arrival flags
+    int epoch;
+};
+
+constexpr int kMaxTailWorkspaces = 64;
+constexpr size_t kPartialSlotBytes = 2 * 4 * (256 / 64) * 32 * 64 * sizeof(float);  // one 256 x 256 FP32 tile
+
+int boundary_slots() { return multiprocessor_count() / 2 + 1; }
+
+bool tail_workspace(cudaStream_t stream, int boundaries, TailSplit* out) {
+    static std::mutex mu;
+    static TailWorkspace spaces[kMaxTailWorkspaces];
+    static int count = 0;
+    const int slots = boundary_slots();
+    if (boundaries > slots) return false;
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess) return false;
+    const std::thread::id thread =
+        stream == cudaStreamPerThread ? std::this_thread::get_id() : std::thread::id();
+    std::lock_guard<std::mutex> lock(mu);
+    TailWorkspace* ws = nullptr;
+    for (int i = 0; i < count; ++i) {
+        if (spaces[i].device == device && spaces[i].stream == stream && spaces[i].thread == thread) ws = &spaces[i];
+    }
+    if (ws == nullptr) {
+        if (count == kMaxTailWorkspaces) return false;
+        // cudaMalloc may not run while the stream is being captured.
+        cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+        if (cudaStreamIsCapturing(stream, &capture) != cudaSuccess || capture != cudaStreamCaptureStatusNone) {
+            cudaGetLastError();
+            return false;
+        }
+        const size_t flag_bytes = static_cast<size_t>(slots) * 2 * 4 * 2 * sizeof(int);
+        void* partials = nullptr;
+        void* flags = nullptr;
+        if (cudaMalloc(&partials, slots * kPartialSlotBytes) != cudaSuccess) {
+            cudaGetLastError();
+            return false;
+        }
+        if (cudaMalloc(&flags, flag_bytes) != cudaSuccess || cudaMemset(flags, 0, flag_bytes) != cudaSuccess) {
+            cudaGetLastError();
+            cudaFree(partials);
+            if (flags) cudaFree(flags);
+            return false;
+        }
+        ws = &spaces[count++];
+        *ws = {device, stream, thread, static_cast<float*>(partials), static_cast<int*>(flags), 0};
+    }
+    ws->epoch = ws->epoch % 0x7fffffff + 1;  // never 0, the cleared state
+    out->partials = ws->partials;
+    out->ready = ws->flags;
+    out->arrivals = ws->flags + static_cast<size_t>(slots) * 2 * 4;
+    out->epoch = ws->epoch;
+    return true;
 }
 
 template <int BN, int BK, int STAGES, bool B_MN, bool ALLGATHER = false>
 int launch_pair_variant_peers(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb_half,
-                              const CUtensorMap& mc, int M, int N, int K, int group, bool persistent,
-                              bool split_tail, uint64_t limit_ns, cudaStream_t stream, int* status,
-                              const PeerOutputs& peers) {
+                              const CUtensorMap& mc, int M, int N, int K, int group, bool persistent, int tail_req,
+                              uint64_t limit_ns, cudaStream_t stream, int* status, const PeerOutputs& peers) {
     using L = PairLayout<BN, BK, STAGES, B_MN>;
     kmcts_gemm_plan plan;
-    const int rc = plan_pair_variant<BN, BK, STAGES, B_MN, ALLGATHER>(M, N, persistent, split_tail, &plan);
+    int rc = plan_pair_variant<BN, BK, STAGES, B_MN, ALLGATHER>(M, N, K, persistent, tail_req, &plan);
     if (rc != KMCTS_OK) return rc;
+    TailSplit tail = {};
+    if (plan.tail_split == KMCTS_TAIL_STREAM_K && !tail_workspace(stream, plan.tail_clusters, &tail)) {
+        // No workspace: the bit-identical N split (or whole tiles) instead.
+        rc = plan_pair_variant<BN, BK, STAGES, B_MN, ALLGATHER>(M, N, K, persistent, KMCTS_TAIL_SPLIT_N, &plan);
+        if (rc != KMCTS_OK) return rc;
+    }
+    tail.mode = plan.tail_split == KMCTS_TAIL_STREAM_K ? kTailStreamK
+                : plan.tail_split == KMCTS_TAIL_SPLIT_N ? kTailSplitN
+                                                        : kTailWhole;
     cudaLaunchConfig_t config = {};
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -403,24 +719,24 @@ int launch_pair_variant_peers(const CUtensorMap& ma, const CUtensorMap& mb, cons
     config.numAttrs = 1;
     const cudaError_t err = cudaLaunchKernelEx(&config, gemm_bf16_tcgen05_pair<BN, BK, STAGES, B_MN, ALLGATHER>,
                                                ma, mb, mb_half, mc, M, N, K, group, plan.full_tiles, limit_ns,
-                                               status, peers);
+                                               status, peers, tail);
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return err == cudaSuccess ? KMCTS_OK : KMCTS_EGEMM;
 }
 
 template <int BN, int BK, int STAGES, bool B_MN>
 int launch_pair_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb_half,
-                        const CUtensorMap& mc, int M, int N, int K, int group, bool persistent, bool split_tail,
+                        const CUtensorMap& mc, int M, int N, int K, int group, bool persistent, int tail_req,
                         uint64_t limit_ns, cudaStream_t stream, int* status) {
     const PeerOutputs none = {};
     return launch_pair_variant_peers<BN, BK, STAGES, B_MN, false>(ma, mb, mb_half, mc, M, N, K, group, persistent,
-                                                                  split_tail, limit_ns, stream, status, none);
+                                                                  tail_req, limit_ns, stream, status, none);
 }
 
 using PairLauncher = int (*)(const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, int,
-                             int, int, int, bool, bool, uint64_t, cudaStream_t, int*);
+                             int, int, int, bool, int, uint64_t, cudaStream_t, int*);
 
-using PairPlanner = int (*)(int, int, bool, bool, kmcts_gemm_plan*);
+using PairPlanner = int (*)(int, int, int, bool, int, kmcts_gemm_plan*);
 
 struct PairVariant {
     int bn, bk, stages, b_mn;
@@ -459,11 +775,11 @@ int64_t pair_smem_bytes(int bn, int bk, int stages) {
            kSmemReserve;
 }
 
-int plan_pair(const kmcts_gemm_config& cfg, int M, int N, int b_layout, kmcts_gemm_plan* out) {
+int plan_pair(const kmcts_gemm_config& cfg, int M, int N, int K, int b_layout, kmcts_gemm_plan* out) {
     const int mn = b_layout == KMCTS_B_ROW ? 1 : 0;
     for (const PairVariant& v : kPairVariants) {
         if (v.bn == cfg.tile_n && v.bk == cfg.tile_k && v.stages == cfg.stages && v.b_mn == mn) {
-            return v.plan(M, N, cfg.persistent != 0, (cfg.flags & KMCTS_FLAG_NO_TAIL_SPLIT) == 0, out);
+            return v.plan(M, N, K, cfg.persistent != 0, requested_tail(cfg.flags), out);
         }
     }
     return KMCTS_ENOTSUP;
@@ -483,7 +799,9 @@ int launch_pair_allgather(const CUtensorMap& ma, const CUtensorMap& mb, const CU
     }
     peers.count = peer_count;
     peers.col_offset = col_offset;
-    const bool split = (cfg.flags & KMCTS_FLAG_NO_TAIL_SPLIT) == 0;
+    // Only the N split: every output stays one full-K chain, so each rank's
+    // columns are bit-identical to the single-GPU kernel on the full problem.
+    const int split = requested_tail(cfg.flags) == KMCTS_TAIL_NONE ? KMCTS_TAIL_NONE : KMCTS_TAIL_SPLIT_N;
     if (b_layout == KMCTS_B_ROW)
         return launch_pair_variant_peers<256, 128, 3, true, true>(ma, mb, mb_half, mc, M, N_shard, K,
                                                                   cfg.raster_group, cfg.persistent != 0, split,
@@ -500,7 +818,7 @@ int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap&
     for (const PairVariant& v : kPairVariants) {
         if (v.bn == cfg.tile_n && v.bk == cfg.tile_k && v.stages == cfg.stages && v.b_mn == mn) {
             return v.fn(ma, mb, mb_half, mc, M, N, K, cfg.raster_group, cfg.persistent != 0,
-                        (cfg.flags & KMCTS_FLAG_NO_TAIL_SPLIT) == 0, limit_ns, stream, status);
+                        requested_tail(cfg.flags), limit_ns, stream, status);
         }
     }
     return KMCTS_ENOTSUP;

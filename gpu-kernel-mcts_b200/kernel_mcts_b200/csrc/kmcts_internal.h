@@ -42,7 +42,7 @@ int multiprocessor_count();
 // CTA-pair (cta_group::2) kernels, gemm_tcgen05_pair.cu.
 bool pair_variant_exists(int bn, int bk, int stages, int b_layout);
 int64_t pair_smem_bytes(int bn, int bk, int stages);
-int plan_pair(const kmcts_gemm_config& cfg, int M, int N, int b_layout, kmcts_gemm_plan* out);
+int plan_pair(const kmcts_gemm_config& cfg, int M, int N, int K, int b_layout, kmcts_gemm_plan* out);
 int launch_pair_allgather(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb_half,
                           const CUtensorMap& mc, int M, int N_shard, int K, int b_layout,
                           const kmcts_gemm_config& cfg, uint64_t limit_ns, cudaStream_t stream, int* status,

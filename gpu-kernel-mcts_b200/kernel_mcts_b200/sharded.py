@@ -12,9 +12,10 @@ ranks (one process per GPU).  Rank r owns columns [r·N/G, (r+1)·N/G).
   ``all_gather_into_tensor`` over NCCL, then the column-block-to-row-major
   copy.
 
-Both leave C bit-identical to the single-GPU kernel on the full problem:
-shard widths are whole 256-column tiles, so every output element has the
-same K-ordered accumulation.
+Both leave C bit-identical to the single-GPU kernel on the full problem
+under the N tail split (the default here): shard widths are whole
+256-column tiles, so every output element has the same K-ordered
+accumulation.
 
 The reference has no multi-GPU code (device 0 only); this is a B200
 addition, with its host logic tested on CPU (gloo) and the kernel on 2 GPUs.
@@ -95,7 +96,13 @@ class ShardedGemm:
         self.m, self.n, self.k = m, n, k
         self.col0, self.col1 = shard_columns(n, self.world, self.rank)
         self.layout = layout_code(b_layout)
-        self.config = config if config is not None else _native.default_config()
+        if config is None:
+            # The N tail split on both paths: every output stays one full-K
+            # chain, so C matches the single-GPU kernel bit for bit whatever
+            # the sharding (a K-split tail would depend on the tile count).
+            config = _native.default_config()
+            config.flags |= _native.FLAG_TAIL_SPLIT_N
+        self.config = config
         self.device = torch.device("cuda", torch.cuda.current_device())
         self.c = torch.empty((m, n), dtype=torch.bfloat16, device=self.device)
         self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
@@ -184,7 +191,7 @@ def _main(argv: Sequence[str] | None = None) -> None:
     out: dict[str, Any] = {"world": world, "shape": [args.M, args.N, args.K], "b_layout": args.b_layout}
     try:
         if args.check:
-            full = kg.bf16_gemm(a, b_full, b_layout=args.b_layout)
+            full = kg.bf16_gemm(a, b_full, b_layout=args.b_layout, config=sg.config)
             for name, fn in (("fused", sg.run), ("nccl", sg.run_nccl)):
                 sg.c.zero_()
                 dist.barrier(device_ids=[local_rank])

@@ -43,11 +43,27 @@ extern "C" {
 #define KMCTS_KERNEL_TCGEN05 1 /* tcgen05/TMA/TMEM kernel only (ENOTSUP otherwise) */
 #define KMCTS_KERNEL_SIMT 2    /* CUDA-core kernel, any shape */
 
-/* Schedule flags.  By default a persistent CTA-pair launch whose last partial
- * wave has R <= W/2 tiles (W = co-resident pairs) runs those R tiles as 2R
- * half-width units, so the tail costs half a tile of time; results are
- * bit-identical either way.  This flag keeps every tile whole. */
+/* Schedule flags.  A persistent CTA-pair launch of T = qW + R tiles (W =
+ * co-resident pairs, 0 < R < W) would leave W - R pairs idle for its whole
+ * last round.  By default, when 2R <= W and tile_n is 256, the last R tiles
+ * run as 2R half-width units, bit-identical to whole tiles.
+ * KMCTS_FLAG_TAIL_STREAM_K instead cuts the K blocks of the last W + R tiles
+ * (q >= 1) into W equal contiguous ranges, one per pair (stream-K): a tile
+ * cut by a range boundary runs as a K prefix and a K suffix on two pairs,
+ * whose FP32 partials meet in a per-stream library workspace before the
+ * single BF16 rounding.  Its results are deterministic, bit-exact on integer
+ * inputs and within the parity bound otherwise, but an output of a cut tile
+ * is the sum of two K-ordered chains; a stream-K launch on a stream that is
+ * being captured into a CUDA graph before that stream's workspace exists
+ * falls back to the N split.  KMCTS_FLAG_NO_TAIL_SPLIT keeps every tile
+ * whole.  The fused all-gather always uses the N split. */
 #define KMCTS_FLAG_NO_TAIL_SPLIT 1
+#define KMCTS_FLAG_TAIL_SPLIT_N 2  /* the default; kept for explicit requests */
+#define KMCTS_FLAG_TAIL_STREAM_K 4
+
+#define KMCTS_TAIL_NONE 0     /* kmcts_gemm_plan.tail_split: every tile whole */
+#define KMCTS_TAIL_SPLIT_N 1  /* last wave as half-width units */
+#define KMCTS_TAIL_STREAM_K 2 /* last W + R tiles as stream-K ranges */
 
 /* Kernel schedule.  Zero-initialise and call kmcts_default_config() first. */
 typedef struct kmcts_gemm_config {
@@ -100,9 +116,12 @@ typedef struct kmcts_gemm_plan {
     int32_t cluster_size; /* CTAs per cluster */
     int32_t workers;      /* clusters that can be resident at once */
     int32_t tiles;        /* output tiles */
-    int32_t full_tiles;   /* tiles run whole; the rest run as two half-width units */
+    int32_t full_tiles;   /* tiles run whole; the rest (the last wave) split */
     int32_t units;        /* work units the grid walks */
     int32_t smem_bytes;   /* dynamic shared memory per CTA */
+    int32_t tail_split;   /* KMCTS_TAIL_*: how the tiles after full_tiles split */
+    int32_t tail_clusters; /* pairs that share the tiles after full_tiles */
+    int32_t tail_segments; /* most units one tile runs as (2 when split) */
 } kmcts_gemm_plan;
 
 /* Fills *out with the launch shape kmcts_bf16_gemm_ex would use for this

@@ -156,30 +156,136 @@ def test_cta_pair_uniform_inputs_within_criterion(cuda_device, layout):
     assert report["passed"], report
 
 
+def plan_of(m, n, k, layout="col", **cfg):
+    return _native.plan(_native.make_config(**cfg), m, n, k, kg.layout_code(layout))
+
+
+PAIR_256 = dict(kernel=_native.KERNEL_TCGEN05, tile_m=256, cluster_m=2, tile_n=256, tile_k=64, stages=6)
+
+
 @pytest.mark.parametrize("layout", ["col", "row"])
-def test_cta_pair_split_tail_bit_exact(cuda_device, layout):
-    """1024x2048: 32 pair tiles < 74 co-resident pairs, so every tile runs as
-    two half-width units; integer inputs stay bit-exact."""
-    m, n, k = 1024, 2048, 512
+@pytest.mark.parametrize("shape,flags,mode", [
+    # 32 tiles < 74 pairs: the N split by default.
+    ((1024, 2048, 512), 0, _native.TAIL_SPLIT_N),
+    ((1024, 2048, 512), _native.FLAG_TAIL_SPLIT_N, _native.TAIL_SPLIT_N),
+    ((1024, 2048, 512), _native.FLAG_NO_TAIL_SPLIT, _native.TAIL_NONE),
+    # 128 tiles = 74 + 54: too many for the N split; stream-K on request.
+    ((2048, 4096, 512), 0, _native.TAIL_NONE),
+    ((2048, 4096, 512), _native.FLAG_TAIL_STREAM_K, _native.TAIL_STREAM_K),
+    # 256 tiles = 3 x 74 + 34: the N split by default, stream-K on request.
+    ((4096, 4096, 256), 0, _native.TAIL_SPLIT_N),
+    ((4096, 4096, 256), _native.FLAG_TAIL_STREAM_K, _native.TAIL_STREAM_K),
+])
+def test_cta_pair_split_tail_bit_exact(cuda_device, layout, shape, flags, mode):
+    """Every way the last wave can run keeps integer inputs bit-exact."""
+    m, n, k = shape
+    plan = plan_of(m, n, k, layout, flags=flags, **PAIR_256)
+    assert plan["tail_split"] == mode, plan
     a_t, b_t = oracle.integer_inputs(m, n, k, seed=5)
-    expect = oracle.root_gemm(oracle.torch_bits(a_t), oracle.torch_bits(b_t))
-    c = run(a_t.cuda(), b_for(layout, b_t.cuda()), layout, kernel=_native.KERNEL_TCGEN05, tile_m=256,
-            cluster_m=2, tile_n=256, tile_k=64, stages=6)
+    expect = oracle.torch_bits(oracle.torch_reference(a_t, b_t))  # exact for these integers
+    c = run(a_t.cuda(), b_for(layout, b_t.cuda()), layout, flags=flags, **PAIR_256)
     np.testing.assert_array_equal(bits_of(c), expect)
 
 
 @pytest.mark.parametrize("layout", ["col", "row"])
 @pytest.mark.parametrize("shape", [(4096, 4096, 4096), (1024, 2048, 512), (3072, 5120, 1024)])
-def test_cta_pair_split_tail_changes_no_bit(cuda_device, layout, shape):
+def test_cta_pair_n_split_tail_changes_no_bit(cuda_device, layout, shape):
     """Splitting the last wave into half-width units keeps every output one
     full-K UMMA chain: N(0,1) results are bit-identical with and without it."""
     m, n, k = shape
     a_t, b_t = oracle.randn_inputs(m, n, k, seed=2, b_layout=layout)
     a, b = a_t.cuda(), b_t.cuda()
-    base = dict(kernel=_native.KERNEL_TCGEN05, tile_m=256, cluster_m=2, tile_n=256, tile_k=64, stages=6)
-    split = run(a, b, layout, **base)
-    whole = run(a, b, layout, flags=_native.FLAG_NO_TAIL_SPLIT, **base)
+    split = run(a, b, layout, flags=_native.FLAG_TAIL_SPLIT_N, **PAIR_256)
+    whole = run(a, b, layout, flags=_native.FLAG_NO_TAIL_SPLIT, **PAIR_256)
     assert torch.equal(split.view(torch.int16), whole.view(torch.int16))
+
+
+SK = _native.FLAG_TAIL_STREAM_K
+
+
+def test_tail_plans(cuda_device):
+    """4096^3: 256 tiles = 3 W + rem on W pairs.  By default the last rem
+    tiles run as 2 rem half-width units; with the stream-K flag the first 2 W
+    tiles run whole and the last W + rem are shared by all W pairs."""
+    plan = plan_of(4096, 4096, 4096)
+    w = plan["workers"]
+    assert w > 0
+    q, rem = divmod(plan["tiles"], w)
+    if rem and 2 * rem <= w:
+        assert plan["tail_split"] == _native.TAIL_SPLIT_N
+        assert plan["full_tiles"] == plan["tiles"] - rem and plan["units"] == plan["full_tiles"] + 2 * rem
+    sk = plan_of(4096, 4096, 4096, flags=SK)
+    if rem and q >= 1:
+        assert sk["tail_split"] == _native.TAIL_STREAM_K
+        assert sk["full_tiles"] == (q - 1) * w
+        assert sk["tail_clusters"] == w and sk["tail_segments"] == 2
+        assert sk["ctas"] == 2 * w
+        assert sk["units"] > sk["tiles"]
+    # Fewer tiles than pairs: the N split, or whole tiles for tile_n 128.
+    assert plan_of(1024, 2048, 128, tile_k=128)["tail_split"] == _native.TAIL_SPLIT_N
+    assert plan_of(1024, 2048, 128, tile_k=128, flags=SK)["tail_split"] == _native.TAIL_SPLIT_N
+    narrow = dict(tile_n=128, tile_k=64, stages=4)
+    assert plan_of(1024, 1024, 512, **narrow)["tail_split"] == _native.TAIL_NONE
+    assert plan_of(2048, 4096, 512, flags=SK, **narrow)["tail_split"] == _native.TAIL_STREAM_K
+    # A whole number of waves runs whole.
+    assert plan_of(256 * 74, 256, 512, flags=SK)["tail_split"] == _native.TAIL_NONE
+
+
+@pytest.mark.parametrize("layout", ["col", "row"])
+@pytest.mark.parametrize("shape,cfg", [
+    ((4096, 4096, 4096), {}),
+    ((3072, 5120, 1024), {}),
+    ((2048, 4096, 2048), dict(tile_k=64, stages=6)),
+    ((2048, 2048, 8192), dict(tile_n=128, tile_k=128, stages=4)),
+])
+def test_stream_k_tail_within_criterion(cuda_device, layout, shape, cfg):
+    """A tile cut at a stream-K range boundary sums two FP32 chains (one
+    rounding more than a whole tile); N(0,1) outputs still meet the parity
+    criterion against the FP64 product, and sit within 1 ulp of the unsplit
+    kernel wherever |C| >= 0.5 (near-zero outputs of heavy cancellation
+    differ by more ulps, by less than the FP32 accumulation error).  Two
+    launches agree bit for bit."""
+    m, n, k = shape
+    a_t, b_t = oracle.randn_inputs(m, n, k, seed=4, b_layout=layout)
+    a, b = a_t.cuda(), b_t.cuda()
+    base = dict(kernel=_native.KERNEL_TCGEN05, tile_m=256, cluster_m=2, **cfg)
+    assert plan_of(m, n, k, layout, flags=SK, **base)["tail_split"] == _native.TAIL_STREAM_K
+    c = run(a, b, layout, flags=SK, **base)
+    again = run(a, b, layout, flags=SK, **base)
+    assert torch.equal(c.view(torch.int16), again.view(torch.int16))
+    whole = run(a, b, layout, flags=_native.FLAG_NO_TAIL_SPLIT, **base)
+    assert kg.compare(c, whole).success
+    # FP64 check on the last 512-row band, which holds stream-K tiles (they
+    # are the end of the raster order); the band keeps the CPU time short.
+    sub = slice(m - min(m, 512), m)
+    ref64, mag = oracle.fp64_reference(a_t[sub], b_t, layout)
+    report = oracle.parity_report(bits_of(c)[sub], bits_of(whole)[sub], ref64, mag, k)
+    assert report["passed"] and report["max_ulp_where_ref_ge_0.5"] <= 1, report
+
+
+def test_stream_k_repeat_and_concurrent_streams(cuda_device):
+    """Launch epochs keep repeated launches on one stream and overlapping
+    launches on two streams (each with its own workspace) exact."""
+    m, n, k = 2048, 4096, 1024
+    x_a, x_b = oracle.integer_inputs(m, n, k, seed=8)
+    y_a, y_b = oracle.integer_inputs(m, n, k, seed=9)
+    ex = oracle.torch_bits(oracle.torch_reference(x_a, x_b))  # exact for these integers
+    ey = oracle.torch_bits(oracle.torch_reference(y_a, y_b))
+    xa, xb, ya, yb = x_a.cuda(), x_b.cuda(), y_a.cuda(), y_b.cuda()
+    assert plan_of(m, n, k, flags=SK)["tail_split"] == _native.TAIL_STREAM_K
+    cfg = _native.make_config(flags=SK)
+    s1, s2 = torch.cuda.Stream(), torch.cuda.Stream()
+    status = torch.zeros(2, dtype=torch.int32, device="cuda")
+    outs = []
+    for _ in range(8):
+        cx = kg.bf16_gemm(xa, xb, config=cfg, stream=s1, status=status[0:1])
+        cy = kg.bf16_gemm(ya, yb, config=cfg, stream=s2, status=status[1:2])
+        outs.append((cx, cy))
+    torch.cuda.synchronize()
+    assert status.tolist() == [0, 0]
+    for cx, cy in outs:
+        np.testing.assert_array_equal(bits_of(cx), ex)
+        np.testing.assert_array_equal(bits_of(cy), ey)
 
 
 def test_tcgen05_4096_integer_bit_exact_and_matches_cublas(cuda_device):
@@ -211,9 +317,15 @@ def test_tcgen05_4096_randn_within_one_ulp_or_bound(cuda_device):
     # sums|) is far below half a BF16 ulp, so those elements sit within 1 ulp.
     d = oracle.ulp_distance(bits_of(c), ref32)
     assert int(d[np.abs(ref64) >= 0.5].max()) <= 1
-    # Same-run cuBLAS (tensor cores, FP32 accumulate) agrees within 1 ulp.
-    cublas = torch.matmul(a_t.cuda(), b_t.cuda().T)
-    assert kg.compare(c, cublas).max_ulp <= 1
+    # Same-run cuBLAS (tensor cores, FP32 accumulate, the same K order per
+    # output) gives the same bits.
+    cublas = oracle.torch_bits(torch.matmul(a_t.cuda(), b_t.cuda().T))
+    np.testing.assert_array_equal(bits_of(c), cublas)
+    # The stream-K tail sums two FP32 chains in its cut tiles: within 1 ulp of
+    # cuBLAS wherever |ref| >= 0.5, and within the criterion everywhere.
+    sk = bits_of(run(a_t.cuda(), b_t.cuda(), "col", flags=SK))
+    assert int(oracle.ulp_distance(sk, cublas)[np.abs(ref64) >= 0.5].max()) <= 1
+    assert oracle.parity_report(sk, cublas, ref64, mag, n)["passed"]
 
 
 # ------------------------------------------------------------- ABI details
