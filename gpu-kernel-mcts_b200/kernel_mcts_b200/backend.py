@@ -18,7 +18,9 @@ Differences, all B200-driven:
   prebuilt schedule of the library kernel: "compiling" is a static legality
   check, so schedule sweeps pay no nvcc time;
 * compiled executables are cached by (normalised source, flags, toolkit);
-* the fingerprint hashes the executable bytes — no disassembly.
+* the fingerprint hashes the executable bytes — no disassembly;
+* workloads with several weighted shapes are evaluated shape by shape (the
+  reference backend rejects them, cuda_backend.py:511-512).
 """
 
 from __future__ import annotations
@@ -166,6 +168,68 @@ def detect_candidate_abi(source: str) -> str:
     raise ValueError("candidate defines neither bf16_gemm_root nor bf16_gemm_launch")
 
 
+# ------------------------------------------------------- multi-shape workloads
+#
+# A WorkloadContract may carry several weighted shapes (domain.py); the
+# evaluator's reward already weights log(T_root / T) per shape
+# (evaluation.py).  The backends evaluate shape by shape (the harness keeps
+# one shape per run) and merge: correctness passes only if every shape passes,
+# and the benchmark reports each shape's median under its shape key plus the
+# weighted mean of the medians as ``median_us`` (the expected time of one
+# call of the weighted mix).  Single-shape workloads are reported exactly as
+# before (no per-shape map).
+
+
+def shape_mnk(dimensions: Mapping[str, int]) -> tuple[int, int, int]:
+    return int(dimensions["M"]), int(dimensions["N"]), int(dimensions["K"])
+
+
+def merge_correctness(workload: WorkloadContract,
+                      results: Sequence[Sm100CorrectnessResult]) -> Sm100CorrectnessResult:
+    if len(results) == 1:
+        return results[0]
+    from .evaluation import shape_key
+
+    keys = [shape_key(shape.dimensions) for shape in workload.shapes]
+    sizes = [shape_mnk(shape.dimensions)[0] * shape_mnk(shape.dimensions)[1] for shape in workload.shapes]
+    failed = next((key for key, result in zip(keys, results) if not result.success), None)
+    maxima = [r.maximum_error for r in results if r.maximum_error is not None]
+    means = [(r.mean_error, size) for r, size in zip(results, sizes) if r.mean_error is not None]
+    per_shape = {key: dict(r.statistics, success=r.success, maximum_error=r.maximum_error, mean_error=r.mean_error)
+                 for key, r in zip(keys, results)}
+    metadata = dict(results[0].reference_metadata)
+    metadata["per_shape"] = per_shape
+    return Sm100CorrectnessResult(
+        success=failed is None,
+        maximum_error=max(maxima) if maxima else None,
+        mean_error=(sum(m * n for m, n in means) / sum(n for _, n in means)) if means else None,
+        failed_test_id=failed,
+        reference_metadata=metadata,
+        statistics={"per_shape": per_shape},
+    )
+
+
+def merge_benchmarks(workload: WorkloadContract, results: Sequence[BenchmarkResult],
+                     gpu_operating_state: Mapping[str, object]) -> BenchmarkResult:
+    if len(results) == 1:
+        return results[0]
+    from .evaluation import shape_key
+
+    timings = tuple(t for r in results for t in r.timings_us)
+    per_shape = {shape_key(shape.dimensions): r.median_us for shape, r in zip(workload.shapes, results)}
+    return BenchmarkResult(
+        timings_us=timings,
+        median_us=sum(shape.weight * r.median_us for shape, r in zip(workload.shapes, results)),
+        warmup_count=results[0].warmup_count,
+        mean_us=statistics.fmean(timings),
+        stddev_us=statistics.pstdev(timings),
+        min_us=min(timings),
+        max_us=max(timings),
+        per_shape_median_us=per_shape,
+        gpu_operating_state=gpu_operating_state,
+    )
+
+
 def schedule_from_source(source: str) -> dict[str, int]:
     try:
         value = json.loads(source)
@@ -210,13 +274,13 @@ class CudaSm100Backend:
 
         started = time.monotonic()
         schedule = schedule_from_source(program.source)
-        shape = workload.shapes[0].dimensions
         layout = 1 if workload.metadata.get("b_layout", "col") == "row" else 0
         cfg = _native.make_config(**schedule, kernel=_native.KERNEL_TCGEN05)
-        code, why = _native.config_legal(cfg, int(shape["M"]), int(shape["N"]), int(shape["K"]), layout)
-        if code != _native.KMCTS_OK:
-            return Sm100CompilationResult(False, None, "", f"statically rejected: {why}",
-                                          time.monotonic() - started)
+        for shape in workload.shapes:
+            code, why = _native.config_legal(cfg, *shape_mnk(shape.dimensions), layout)
+            if code != _native.KMCTS_OK:
+                return Sm100CompilationResult(False, None, "", f"statically rejected: {why}",
+                                              time.monotonic() - started)
         harness = native_build.build_harness()
         resolved = cfg.as_dict()
         args = tuple(
@@ -288,37 +352,45 @@ class CudaSm100Backend:
     # ---------------------------------------------------------------- run
 
     def check_correctness(self, artifact: Sm100Artifact, workload: WorkloadContract) -> Sm100CorrectnessResult:
-        payload = self._execute(artifact, workload, "correctness")
-        extra = {k: payload[k] for k in ("max_ulp", "n_gt_1ulp", "ulp_hist", "n_nonfinite", "kernel") if k in payload}
-        return Sm100CorrectnessResult(
-            success=bool(payload["success"]),
-            maximum_error=_optional_float(payload.get("maximum_error")),
-            mean_error=_optional_float(payload.get("mean_error")),
-            failed_test_id=payload.get("failed_test_id"),
-            reference_metadata={**payload.get("reference_metadata", {}), **extra},
-            statistics=extra,
-        )
+        results = []
+        for shape in workload.shapes:
+            payload = self._execute(artifact, workload, "correctness", shape.dimensions)
+            extra = {k: payload[k] for k in ("max_ulp", "n_gt_1ulp", "ulp_hist", "n_nonfinite", "kernel")
+                     if k in payload}
+            results.append(Sm100CorrectnessResult(
+                success=bool(payload["success"]),
+                maximum_error=_optional_float(payload.get("maximum_error")),
+                mean_error=_optional_float(payload.get("mean_error")),
+                failed_test_id=payload.get("failed_test_id"),
+                reference_metadata={**payload.get("reference_metadata", {}), **extra},
+                statistics=extra,
+            ))
+        return merge_correctness(workload, results)
 
     def benchmark(self, artifact: Sm100Artifact, workload: WorkloadContract) -> BenchmarkResult:
         before = self.gpu_operating_state()
-        payload = self._execute(artifact, workload, "benchmark")
+        payloads = [self._execute(artifact, workload, "benchmark", shape.dimensions) for shape in workload.shapes]
         after = self.gpu_operating_state()
-        timings = tuple(float(v) for v in payload["timings_us"])
-        if len(timings) != self.config.measurement_count:
-            raise EvaluationInfrastructureError("worker returned an unexpected timing count")
-        return BenchmarkResult(
-            timings_us=timings,
-            median_us=statistics.median(timings),
-            warmup_count=self.config.warmup_count,
-            mean_us=statistics.fmean(timings),
-            stddev_us=statistics.pstdev(timings),
-            min_us=min(timings),
-            max_us=max(timings),
-            gpu_operating_state={"before": before, "after": after},
-        )
+        results = []
+        for payload in payloads:
+            timings = tuple(float(v) for v in payload["timings_us"])
+            if len(timings) != self.config.measurement_count:
+                raise EvaluationInfrastructureError("worker returned an unexpected timing count")
+            results.append(BenchmarkResult(
+                timings_us=timings,
+                median_us=statistics.median(timings),
+                warmup_count=self.config.warmup_count,
+                mean_us=statistics.fmean(timings),
+                stddev_us=statistics.pstdev(timings),
+                min_us=min(timings),
+                max_us=max(timings),
+                gpu_operating_state={"before": before, "after": after},
+            ))
+        return merge_benchmarks(workload, results, {"before": before, "after": after})
 
-    def _command(self, artifact: Sm100Artifact, workload: WorkloadContract, mode: str) -> list[str]:
-        shape = workload.shapes[0].dimensions
+    def _command(self, artifact: Sm100Artifact, workload: WorkloadContract, mode: str,
+                 dimensions: Mapping[str, int] | None = None) -> list[str]:
+        shape = dimensions if dimensions is not None else workload.shapes[0].dimensions
         command = [
             str(artifact.executable),
             f"--mode={mode}",
@@ -336,8 +408,9 @@ class CudaSm100Backend:
         ]
         return command + list(artifact.extra_args)
 
-    def _execute(self, artifact: Sm100Artifact, workload: WorkloadContract, mode: str) -> dict[str, object]:
-        command = self._command(artifact, workload, mode)
+    def _execute(self, artifact: Sm100Artifact, workload: WorkloadContract, mode: str,
+                 dimensions: Mapping[str, int] | None = None) -> dict[str, object]:
+        command = self._command(artifact, workload, mode, dimensions)
         try:
             result = self._runner(command, timeout=self.config.execution_timeout_seconds,
                                   env=self.config.subprocess_environment)
@@ -445,8 +518,6 @@ class CudaSm100Backend:
             raise ValueError(f"unsupported program backend {program.backend!r}")
         if workload.operation != "gemm" or workload.dtype != "bfloat16":
             raise ValueError("CudaSm100Backend supports only BF16 GEMM")
-        if len(workload.shapes) != 1:
-            raise ValueError("CudaSm100Backend currently requires one fixed GEMM shape")
         if workload.metadata.get("entry_point") != "bf16_gemm_root":
             raise ValueError("BF16 GEMM workload must use the bf16_gemm_root entry point")
 

@@ -34,7 +34,10 @@ from .backend import (
     CudaSm100Backend,
     Sm100CompilationResult,
     Sm100CorrectnessResult,
+    merge_benchmarks,
+    merge_correctness,
     schedule_from_source,
+    shape_mnk,
 )
 from .domain import BenchmarkResult, KernelProgram, WorkloadContract
 from .evaluation import CandidateLaunchError, EvaluationInfrastructureError
@@ -74,15 +77,15 @@ class InProcessSm100Backend:
 
     # ------------------------------------------------------------------ inputs
 
-    def _operands(self, workload: WorkloadContract):
+    def _operands(self, workload: WorkloadContract, dimensions=None):
         torch = self.torch
-        shape = workload.shapes[0].dimensions
-        m, n, k = int(shape["M"]), int(shape["N"]), int(shape["K"])
+        m, n, k = shape_mnk(dimensions if dimensions is not None else workload.shapes[0].dimensions)
         layout = workload.metadata.get("b_layout", "col")
         inputs = workload.metadata.get("inputs", "uniform")
         key = (m, n, k, layout, inputs, self.seed)
         if key not in self._cache:
-            self._cache.clear()  # one workload resident at a time
+            if len(self._cache) >= len(workload.shapes):
+                self._cache.clear()  # one workload's shapes resident at a time
             a_bits, b_bits = _native.generate_inputs(inputs, self.seed, m * k, k * n)
             a = torch.from_numpy(a_bits.view("int16")).view(torch.bfloat16).reshape(m, k).to(self.device)
             # The stream fills B in its storage order: [N, K] for column-major B.
@@ -100,7 +103,8 @@ class InProcessSm100Backend:
         return self._cache[key]
 
     def prepare(self, workload: WorkloadContract) -> None:
-        self._operands(workload)
+        for shape in workload.shapes:
+            self._operands(workload, shape.dimensions)
 
     # -------------------------------------------------------------- protocol
 
@@ -112,12 +116,13 @@ class InProcessSm100Backend:
         if program.backend != SCHEDULE_BACKEND:
             raise ValueError("the in-process backend evaluates schedule programs only")
         schedule = schedule_from_source(program.source)
-        shape = workload.shapes[0].dimensions
         layout = _native.B_ROW if workload.metadata.get("b_layout", "col") == "row" else _native.B_COL
         cfg = _native.make_config(**schedule, kernel=_native.KERNEL_TCGEN05)
-        code, why = _native.config_legal(cfg, int(shape["M"]), int(shape["N"]), int(shape["K"]), layout)
-        if code != _native.KMCTS_OK:
-            return Sm100CompilationResult(False, None, "", f"statically rejected: {why}", time.monotonic() - started)
+        for shape in workload.shapes:
+            code, why = _native.config_legal(cfg, *shape_mnk(shape.dimensions), layout)
+            if code != _native.KMCTS_OK:
+                return Sm100CompilationResult(False, None, "", f"statically rejected: {why}",
+                                              time.monotonic() - started)
         resolved = cfg.as_dict()
         digest = hashlib.sha256((self._library_digest + json.dumps(resolved, sort_keys=True)).encode()).hexdigest()
         artifact = ScheduleArtifact(digest, resolved)
@@ -125,10 +130,10 @@ class InProcessSm100Backend:
                                       compiler_context={"schedule": resolved,
                                                         "smem_bytes": _native.config_smem_bytes(cfg, layout)})
 
-    def _prepared(self, artifact: ScheduleArtifact, workload: WorkloadContract):
+    def _prepared(self, artifact: ScheduleArtifact, workload: WorkloadContract, dimensions=None):
         from . import gemm as kg
 
-        a, b, c, _, layout = self._operands(workload)
+        a, b, c, _, layout = self._operands(workload, dimensions)
         key = (id(c), artifact.artifact_id)
         if getattr(self, "_prepared_key", None) != key:
             self._prepared_gemm = kg.PreparedGemm(a, b, c, b_layout=layout,
@@ -138,9 +143,9 @@ class InProcessSm100Backend:
             self._prepared_key = key
         return self._prepared_gemm
 
-    def _launch(self, artifact: ScheduleArtifact, workload: WorkloadContract):
+    def _launch(self, artifact: ScheduleArtifact, workload: WorkloadContract, dimensions=None):
         try:
-            self._prepared(artifact, workload).launch()
+            self._prepared(artifact, workload, dimensions).launch()
         except _native.KmctsError as error:
             raise CandidateLaunchError(str(error)) from error
 
@@ -151,10 +156,14 @@ class InProcessSm100Backend:
             raise CandidateLaunchError(f"device-side wait gave up (status {value:#x})")
 
     def check_correctness(self, artifact: ScheduleArtifact, workload: WorkloadContract) -> Sm100CorrectnessResult:
+        return merge_correctness(workload, [self._check_shape(artifact, workload, shape.dimensions)
+                                            for shape in workload.shapes])
+
+    def _check_shape(self, artifact: ScheduleArtifact, workload: WorkloadContract, dimensions) -> Sm100CorrectnessResult:
         from . import gemm as kg
 
-        _, _, c, reference, _ = self._operands(workload)
-        self._launch(artifact, workload)
+        _, _, c, reference, _ = self._operands(workload, dimensions)
+        self._launch(artifact, workload, dimensions)
         self.torch.cuda.synchronize(self.device)
         self._check_status()
         cmp = kg.compare(c, reference, rtol=workload.rtol, atol=workload.atol, workspace=self._workspace)
@@ -169,15 +178,19 @@ class InProcessSm100Backend:
         )
 
     def benchmark(self, artifact: ScheduleArtifact, workload: WorkloadContract) -> BenchmarkResult:
+        return merge_benchmarks(workload, [self._benchmark_shape(artifact, workload, shape.dimensions)
+                                           for shape in workload.shapes], {"status": "in-process"})
+
+    def _benchmark_shape(self, artifact: ScheduleArtifact, workload: WorkloadContract, dimensions) -> BenchmarkResult:
         torch = self.torch
         stream = torch.cuda.current_stream(self.device)
         if self.flush_l2 and self._flush is None:
             self._flush = torch.empty(512 << 20, dtype=torch.uint8, device=self.device)
         for _ in range(self.warmup_count):
-            self._launch(artifact, workload)
+            self._launch(artifact, workload, dimensions)
         torch.cuda.synchronize(self.device)
         timings = []
-        prepared = self._prepared(artifact, workload)
+        prepared = self._prepared(artifact, workload, dimensions)
         events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                   for _ in range(self.measurement_count)]
         for i, (start, stop) in enumerate(events):

@@ -56,11 +56,26 @@ def gemm_workload(
     rtol: float = 2.0e-2,
     atol: float = 2.0e-2,
 ) -> WorkloadContract:
+    return multi_shape_gemm_workload(benchmark_id, [(m, n, k, 1.0)], b_layout=b_layout, inputs=inputs,
+                                     rtol=rtol, atol=atol)
+
+
+def multi_shape_gemm_workload(
+    benchmark_id: str,
+    shapes,
+    *,
+    b_layout: str = "col",
+    inputs: str = "uniform",
+    rtol: float = 2.0e-2,
+    atol: float = 2.0e-2,
+) -> WorkloadContract:
+    """A GEMM workload over weighted shapes ``[(M, N, K, weight), ...]``
+    (weights summing to 1): the reward weights log(T_root / T) per shape."""
     return WorkloadContract(
         benchmark_id=benchmark_id,
         operation="gemm",
         dtype="bfloat16",
-        shapes=(ShapeCase({"M": m, "N": n, "K": k}, 1.0),),
+        shapes=tuple(ShapeCase({"M": m, "N": n, "K": k}, float(w)) for m, n, k, w in shapes),
         rtol=rtol,
         atol=atol,
         metadata={
@@ -87,4 +102,11 @@ BF16_GEMM_4096_RANDN = gemm_workload("bf16_gemm_4096_randn_b200", 4096, 4096, 40
 #: BASELINE config 3: 4096^3 integers in {-2..2}: bit-exact expected.
 BF16_GEMM_4096_INT = gemm_workload("bf16_gemm_4096_int_b200", 4096, 4096, 4096, b_layout="row", inputs="int")
 
-ALL_WORKLOADS = (BF16_GEMM_4096_B200, BF16_GEMM_256_RANDN, BF16_GEMM_4096_RANDN, BF16_GEMM_4096_INT)
+#: A weighted mix of square and MLP-like shapes (N(0,1), A/B row-major).
+BF16_GEMM_MIX_RANDN = multi_shape_gemm_workload(
+    "bf16_gemm_mix_randn_b200",
+    [(4096, 4096, 4096, 0.5), (8192, 3584, 8192, 0.25), (2048, 14336, 4096, 0.25)],
+    b_layout="row", inputs="randn")
+
+ALL_WORKLOADS = (BF16_GEMM_4096_B200, BF16_GEMM_256_RANDN, BF16_GEMM_4096_RANDN, BF16_GEMM_4096_INT,
+                 BF16_GEMM_MIX_RANDN)

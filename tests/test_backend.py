@@ -27,7 +27,12 @@ from kernel_mcts_b200.evaluation import (
     EvaluationInfrastructureError,
 )
 from kernel_mcts_b200.profiling import SM100_V1_METRICS, parse_ncu_csv
-from kernel_mcts_b200.workloads import BF16_GEMM_4096_B200, BF16_GEMM_4096_RANDN, gemm_workload
+from kernel_mcts_b200.workloads import (
+    BF16_GEMM_4096_B200,
+    BF16_GEMM_4096_RANDN,
+    gemm_workload,
+    multi_shape_gemm_workload,
+)
 
 ROOT_SOURCE = """
 #include <cuda_bf16.h>
@@ -60,6 +65,7 @@ class FakeRunner:
         self.returncode = 0
         self.timeout_stage: str | None = None
         self.ncu_stdout = ""
+        self.by_m: dict[tuple[str, str], str] = {}  # (mode, "--M=...") -> stdout for that shape
 
     def __call__(self, command, *, timeout, env):
         command = list(command)
@@ -77,6 +83,9 @@ class FakeRunner:
         if self.timeout_stage == "execute":
             raise subprocess.TimeoutExpired(command, timeout)
         out = self.benchmark_stdout if "--mode=benchmark" in command else self.correctness_stdout
+        mode = "benchmark" if "--mode=benchmark" in command else "correctness"
+        for arg in command:
+            out = self.by_m.get((mode, arg), out)
         return subprocess.CompletedProcess(command, self.returncode, "some log line\n" + out + "\n", "")
 
 
@@ -250,3 +259,58 @@ def test_ncu_csv_long_and_wide_layouts():
     assert parse_ncu_csv(wide, SM100_V1_METRICS)[SM100_V1_METRICS[2]]["value"] == 2.0
     with pytest.raises(ValueError):
         parse_ncu_csv("garbage", SM100_V1_METRICS)
+
+
+MIX = multi_shape_gemm_workload("mix", [(512, 256, 128, 0.75), (1024, 512, 256, 0.25)], b_layout="row",
+                                inputs="randn")
+
+
+def test_multi_shape_benchmark_reports_each_shape_and_the_weighted_median(tmp_path):
+    runner = FakeRunner()
+    runner.by_m[("benchmark", "--M=512")] = json.dumps({"status": "ok", "timings_us": [10.0, 12.0, 11.0]})
+    runner.by_m[("benchmark", "--M=1024")] = json.dumps({"status": "ok", "timings_us": [40.0, 44.0, 42.0]})
+    result = make_backend(tmp_path, runner).benchmark(Sm100Artifact("id", tmp_path / "e"), MIX)
+    assert result.per_shape_median_us == {"K=128,M=512,N=256": 11.0, "K=256,M=1024,N=512": 42.0}
+    assert result.median_us == pytest.approx(0.75 * 11.0 + 0.25 * 42.0)
+    assert len(result.timings_us) == 6 and result.min_us == 10.0 and result.max_us == 44.0
+    runs = [c[0] for c in runner.calls if "--mode=benchmark" in c[0]]
+    assert [next(a for a in r if a.startswith("--M=")) for r in runs] == ["--M=512", "--M=1024"]
+
+
+def test_multi_shape_correctness_fails_on_any_shape_and_names_it(tmp_path):
+    runner = FakeRunner()
+    bad = json.loads(OK_CORRECTNESS)
+    bad.update(success=False, maximum_error=0.5, mean_error=0.01)
+    runner.by_m[("correctness", "--M=1024")] = json.dumps(bad)
+    result = make_backend(tmp_path, runner).check_correctness(Sm100Artifact("id", tmp_path / "e"), MIX)
+    assert not result.success and result.failed_test_id == "K=256,M=1024,N=512"
+    assert result.maximum_error == 0.5
+    assert set(result.reference_metadata["per_shape"]) == {"K=128,M=512,N=256", "K=256,M=1024,N=512"}
+    good = make_backend(tmp_path, FakeRunner()).check_correctness(Sm100Artifact("id", tmp_path / "e"), MIX)
+    assert good.success and good.failed_test_id is None
+
+
+def test_multi_shape_schedule_must_be_legal_on_every_shape(tmp_path):
+    backend = make_backend(tmp_path, FakeRunner())
+    ok = backend.compile(schedule_program(tile_m=256, cluster_m=2, tile_n=256, tile_k=128, stages=3), MIX)
+    assert ok.success
+    ragged = multi_shape_gemm_workload("r", [(512, 256, 128, 0.5), (512, 256, 100, 0.5)], b_layout="row")
+    rejected = backend.compile(schedule_program(tile_m=256, cluster_m=2, tile_n=256, tile_k=128, stages=3), ragged)
+    assert not rejected.success and "statically rejected" in rejected.stderr
+
+
+def test_multi_shape_reward_through_the_evaluator(tmp_path):
+    from kernel_mcts_b200.domain import BenchmarkResult
+    from kernel_mcts_b200.evaluation import BackendKernelEvaluator, EvaluationContext
+    import math
+
+    runner = FakeRunner()
+    runner.by_m[("benchmark", "--M=512")] = json.dumps({"status": "ok", "timings_us": [10.0, 10.0, 10.0]})
+    runner.by_m[("benchmark", "--M=1024")] = json.dumps({"status": "ok", "timings_us": [40.0, 40.0, 40.0]})
+    root = BenchmarkResult(timings_us=(1.0,), median_us=1.0, warmup_count=0,
+                           per_shape_median_us={"K=128,M=512,N=256": 20.0, "K=256,M=1024,N=512": 40.0})
+    context = EvaluationContext("w0", "env", {}, {})
+    evaluator = BackendKernelEvaluator(backend=make_backend(tmp_path, runner), root_benchmark=root, context=context)
+    result = evaluator.evaluate(schedule_program(tile_m=256, cluster_m=2, tile_n=256, tile_k=128, stages=3), MIX)
+    assert result.status.value == "VALID", result
+    assert result.reward == pytest.approx(0.75 * math.log(2.0) + 0.25 * math.log(1.0))

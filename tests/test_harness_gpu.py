@@ -163,3 +163,46 @@ def test_pool_sweep_on_one_gpu_in_process(backend, tmp_path):
         report = run_schedule_sweep(pool, workload, {"benchmark": {"median_us": 50.0}}, schedules=schedule_grid(24, 3))
     assert report["status"] == "ok" and report["evaluations"] > 0
     assert all(t["status"] in ("VALID", "STATICALLY_REJECTED") for t in report["trials"]), report["trials"]
+
+
+def test_multi_shape_workload_in_process_and_through_the_harness(backend):
+    """A weighted two-shape workload: both backends evaluate every shape and
+    report per-shape medians; the reward weights the per-shape speed-ups."""
+    from kernel_mcts_b200.domain import BenchmarkResult
+    from kernel_mcts_b200.inprocess import HybridSm100Backend, InProcessSm100Backend
+    from kernel_mcts_b200.workloads import multi_shape_gemm_workload
+
+    workload = multi_shape_gemm_workload("mix_small", [(1024, 1024, 1024, 0.5), (2048, 512, 1536, 0.5)],
+                                         b_layout="row", inputs="randn")
+    keys = {"K=1024,M=1024,N=1024", "K=1536,M=2048,N=512"}
+    root = BenchmarkResult((100.0,), 100.0, per_shape_median_us={k: 100.0 for k in keys})
+    program = schedule_program(tile_m=256, cluster_m=2, tile_n=256, tile_k=128, stages=3)
+    hybrid = HybridSm100Backend(backend, InProcessSm100Backend(warmup_count=2, measurement_count=5))
+    for be in (hybrid, backend):
+        result = BackendKernelEvaluator(backend=be, root_benchmark=root, context=CONTEXT).evaluate(program, workload)
+        assert result.status == ProposalStatus.VALID, result
+        assert set(result.benchmark.per_shape_median_us) == keys
+        expect = sum(0.5 * math.log(100.0 / t) for t in result.benchmark.per_shape_median_us.values())
+        assert result.reward == pytest.approx(expect)
+        assert set(result.correctness.reference_metadata["per_shape"]) == keys
+
+
+def test_pool_autotuner_on_one_gpu(tmp_path):
+    """The post-search autotuner over the in-process pool: every schedule
+    trial is evaluated (or statically rejected) and the best reward kept."""
+    from kernel_mcts_b200.autotune import PoolAutotuner, TuningConfig
+    from kernel_mcts_b200.pool import EvaluationPool, WorkerSpec
+
+    workload = gemm_workload("tune_2048", 2048, 2048, 2048, b_layout="row", inputs="randn")
+    spec = WorkerSpec("kernel_mcts_b200.pool:sm100_evaluator",
+                      {"artifact_root": str(tmp_path), "root_us": 100.0, "warmup_count": 2, "measurement_count": 5})
+    program = schedule_program(tile_m=256, cluster_m=2, tile_n=256, tile_k=128, stages=3)
+    with EvaluationPool([0], spec) as pool:
+        baseline = pool.evaluate(program, workload)
+        assert baseline.status == ProposalStatus.VALID
+        result = PoolAutotuner(pool, workload, TuningConfig(budget=8, method="random", seed=1)).run(baseline)
+    assert result.used == 8
+    statuses = {t.evaluation.status for t in result.trials}
+    assert statuses <= {ProposalStatus.VALID, ProposalStatus.INVALID}, statuses
+    assert any(t.evaluation.status == ProposalStatus.VALID for t in result.trials)
+    assert result.best is not None and result.best.reward >= baseline.reward
