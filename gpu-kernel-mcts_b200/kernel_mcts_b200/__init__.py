@@ -16,6 +16,7 @@ from ._native import (
     default_config,
     launch_count,
     make_config,
+    select_config,
     version,
 )
 
@@ -30,5 +31,6 @@ __all__ = [
     "default_config",
     "launch_count",
     "make_config",
+    "select_config",
     "version",
 ]

@@ -54,6 +54,7 @@ INPUTS = {"uniform": 0, "randn": 1, "int": 2}
 #: Every symbol include/kmcts_gemm.h declares.
 EXPORTED_SYMBOLS = (
     "kmcts_default_config",
+    "kmcts_select_config",
     "kmcts_bf16_gemm",
     "kmcts_bf16_gemm_ex",
     "kmcts_config_legal",
@@ -168,6 +169,8 @@ def load() -> ctypes.CDLL:
         vp, i32, i64 = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64
         lib.kmcts_default_config.argtypes = [ctypes.POINTER(GemmConfig)]
         lib.kmcts_default_config.restype = i32
+        lib.kmcts_select_config.argtypes = [i32, i32, i32, i32, ctypes.POINTER(GemmConfig)]
+        lib.kmcts_select_config.restype = i32
         lib.kmcts_bf16_gemm.argtypes = [vp, vp, vp, i32, i32, i32]
         lib.kmcts_bf16_gemm.restype = i32
         lib.kmcts_bf16_gemm_ex.argtypes = [
@@ -216,6 +219,13 @@ def load() -> ctypes.CDLL:
 def default_config() -> GemmConfig:
     cfg = GemmConfig()
     check(load().kmcts_default_config(ctypes.byref(cfg)), "kmcts_default_config")
+    return cfg
+
+
+def select_config(m: int, n: int, k: int, b_layout: int = B_COL) -> GemmConfig:
+    """The schedule a NULL config selects for this shape."""
+    cfg = GemmConfig()
+    check(load().kmcts_select_config(m, n, k, b_layout, ctypes.byref(cfg)), "kmcts_select_config")
     return cfg
 
 

@@ -84,6 +84,35 @@ int kmcts_default_config(kmcts_gemm_config* cfg) {
     return KMCTS_OK;
 }
 
+int kmcts_select_config(int M, int N, int K, int b_layout, kmcts_gemm_config* cfg) {
+    if (!cfg || M < 0 || N < 0 || K < 0) return KMCTS_EINVAL;
+    kmcts_default_config(cfg);
+    // Measured on B200 (CUDA-graph replays, warm L2): the CTA-pair 256 x 256
+    // schedule wins once its tiles fill the co-resident pairs; below that,
+    // one-CTA tiles give more CTAs: 128 x 256 while those fill the pairs'
+    // count and K is short (from K = 8192 the pair's faster mainloop wins
+    // back its idle SMs), else 128 x 128.
+    const int workers = multiprocessor_count() / 2;
+    const long long pair_tiles = static_cast<long long>((M + 255) / 256) * ((N + 255) / 256);
+    if (pair_tiles >= workers) return KMCTS_OK;
+    kmcts_gemm_config small = *cfg;
+    small.tile_m = 128;
+    small.cluster_m = 1;
+    const long long wide_tiles = static_cast<long long>((M + 127) / 128) * ((N + 255) / 256);
+    if (wide_tiles >= workers) {
+        if (K >= 4096) return KMCTS_OK;
+        small.tile_n = 256;
+        small.tile_k = 64;
+        small.stages = 4;
+    } else {
+        small.tile_n = 128;
+        small.tile_k = 128;
+        small.stages = 3;
+    }
+    if (tcgen05_legal(small, M, N, K, b_layout, nullptr, 0) == KMCTS_OK) *cfg = small;
+    return KMCTS_OK;
+}
+
 const char* kmcts_version(void) { return "kmcts_gemm_sm100 0.1.0 (sm_100a tcgen05)"; }
 
 int64_t kmcts_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
@@ -108,7 +137,7 @@ int kmcts_bf16_gemm_ex(const void* A, const void* B, void* C, int M, int N, int 
     if (cfg) {
         local = *cfg;
     } else {
-        kmcts_default_config(&local);
+        kmcts_select_config(M, N, K, b_layout, &local);
     }
     cudaStream_t s = as_stream(stream);
     if (local.kernel == KMCTS_KERNEL_SIMT) return launch_simt(A, B, C, M, N, K, b_layout, s);
@@ -134,7 +163,7 @@ int kmcts_gemm_plan_query(const kmcts_gemm_config* cfg, int M, int N, int K, int
     if (cfg) {
         local = *cfg;
     } else {
-        kmcts_default_config(&local);
+        kmcts_select_config(M, N, K, b_layout, &local);
     }
     if (local.kernel != KMCTS_KERNEL_SIMT) {
         const int rc = plan_tcgen05(local, M, N, K, b_layout, out);

@@ -204,7 +204,7 @@ int main(int argc, char** argv) {
     l.N = static_cast<int>(N);
     l.K = static_cast<int>(K);
     l.b_layout = layout == "row" ? KMCTS_B_ROW : KMCTS_B_COL;
-    kmcts_default_config(&l.cfg);
+    kmcts_select_config(l.M, l.N, l.K, l.b_layout, &l.cfg);  // explicit schedule flags override it
     l.cfg.tile_m = static_cast<int>(int_arg(argc, argv, "tile-m", l.cfg.tile_m));
     l.cfg.cluster_m = static_cast<int>(int_arg(argc, argv, "cluster-m", l.cfg.cluster_m));
     l.cfg.flags = static_cast<int>(int_arg(argc, argv, "flags", l.cfg.flags));

@@ -80,8 +80,17 @@ typedef struct kmcts_gemm_config {
     int64_t wait_limit_ns; /* bound on each device-side wait; 0 = 2 s default */
 } kmcts_gemm_config;
 
-/* Fills *cfg with the tuned default schedule for B200. Returns KMCTS_OK. */
+/* Fills *cfg with the tuned default schedule for B200 (the CTA-pair 256 x 256
+ * x 128, 3-stage schedule that is fastest at 4096^3). Returns KMCTS_OK. */
 int kmcts_default_config(kmcts_gemm_config* cfg);
+
+/* Fills *cfg with the schedule a NULL cfg selects for this shape: the default
+ * when its 256 x 256 pair tiles fill the co-resident CTA pairs; else one CTA
+ * per 128 x 256 tile while those fill them (the default again from K = 4096),
+ * else one CTA per 128 x 128 tile.  Every
+ * schedule gives results within the parity criterion and bit-exact ones on
+ * integer inputs.  Returns KMCTS_OK or KMCTS_EINVAL. */
+int kmcts_select_config(int M, int N, int K, int b_layout, kmcts_gemm_config* cfg);
 
 /* Drop-in for the reference's ctypes entry point kernel_mcts_bf16_reference
  * (src/kernel_mcts/benchmarks/kernels/bf16_reference.cu:5-41, loaded as in
@@ -91,7 +100,7 @@ int kmcts_default_config(kmcts_gemm_config* cfg);
 int kmcts_bf16_gemm(const void* A, const void* B, void* C, int M, int N, int K);
 
 /* Asynchronous GEMM on `stream` (a cudaStream_t; NULL = default stream).
- * cfg may be NULL (default schedule).  device_status, if not NULL, is a device
+ * cfg may be NULL (the schedule kmcts_select_config picks for the shape).  device_status, if not NULL, is a device
  * int that the kernel sets non-zero when a bounded wait gives up; the caller
  * zeroes it and reads it after synchronising.  Replaces the fixed 16x16
  * launch_candidate of src/kernel_mcts/benchmarks/kernels/bf16_gemm_harness.cu:61-72

@@ -45,6 +45,31 @@ def test_version_and_default_config():
 
 
 @pytest.mark.parametrize(
+    "shape,expect",
+    [
+        # 256 pair tiles >= 74 co-resident pairs (148 SMs assumed without a GPU): the default.
+        ((4096, 4096, 4096), (256, 256, 128, 3, 2)),
+        ((2048, 4096, 2048), (256, 256, 128, 3, 2)),
+        # 64 pair tiles, 128 one-CTA 128x256 tiles: one CTA per 128x256 tile.
+        ((2048, 2048, 2048), (128, 256, 64, 4, 1)),
+        # ... unless K is long: the pair's mainloop wins back its idle SMs.
+        ((2048, 2048, 8192), (256, 256, 128, 3, 2)),
+        # few tiles: one CTA per 128x128 tile.
+        ((1024, 1024, 1024), (128, 128, 128, 3, 1)),
+        ((256, 256, 256), (128, 128, 128, 3, 1)),
+        # N not a multiple of 8: no tensor-core schedule is legal; the default
+        # stays and AUTO launches go to the SIMT kernel.
+        ((256, 250, 256), (256, 256, 128, 3, 2)),
+    ],
+)
+def test_select_config_by_shape(shape, expect):
+    cfg = km.select_config(*shape, km.B_ROW)
+    assert (cfg.tile_m, cfg.tile_n, cfg.tile_k, cfg.stages, cfg.cluster_m) == expect
+    if shape[1] % 8 == 0:
+        assert km.config_legal(cfg, *shape, km.B_ROW) == (0, "ok")
+
+
+@pytest.mark.parametrize(
     "overrides,shape,code",
     [
         ({"tile_m": 128, "cluster_m": 1, "tile_n": 256, "tile_k": 64, "stages": 5}, (4096, 4096, 4096), _native.KMCTS_ESMEM),
