@@ -249,7 +249,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 store_chunk(&map_c, staging, chunk_count, lo, hi, lane, n0 + c * 64, m0 + quarter * 32);
             }
         }
-        if (lane == 0) ptx::bulk_wait_group<0>();
+        if (lane == 0) ptx::bulk_wait_group_read<0>();  // shared memory must outlive the stores' reads
         __syncwarp();
     }
 
