@@ -52,6 +52,7 @@ def parse_args() -> argparse.Namespace:
     p.add_argument("--no-evals", action="store_true", help="skip the evaluation-throughput pass")
     p.add_argument("--eval-repeat", type=int, default=3)
     p.add_argument("--no-sharded", action="store_true", help="skip the sharded 8192x28672x8192 GEMM")
+    p.add_argument("--no-skinny", action="store_true", help="skip the HBM-bound skinny shapes")
     return p.parse_args()
 
 
@@ -267,6 +268,62 @@ def time_interleaved(fns, steps: int, stream, flush) -> list[list[float]]:
     return [[s.elapsed_time(e) * 1e3 for s, e in zip(starts[j], stops[j])] for j in range(len(fns))]
 
 
+SKINNY_SHAPES = ((16, 8192, 8192), (128, 16384, 4096))
+
+
+def skinny_gemms(device, stream, flush, steps: int = 20) -> dict:
+    """HBM-bound shapes (north_star: HBM GB/s for the skinny shapes).  Our
+    call with a NULL config (the library's shape selection: split K here)
+    against same-run cuBLAS, L2 flushed, interleaved.  GB/s = the minimum
+    bytes (A and B read once, C written once) / median time, against the
+    measured HBM copy bandwidth."""
+    import torch
+
+    from kernel_mcts_b200 import _native
+    from kernel_mcts_b200 import gemm as kg
+
+    peaks, kind = load_peaks()
+    hbm = float(peaks["hbm_gbs"])
+    rows = []
+    for m, n, k in SKINNY_SHAPES:
+        g = torch.Generator(device=device).manual_seed(0)
+        a = torch.randn((m, k), generator=g, device=device).to(torch.bfloat16)
+        b = torch.randn((k, n), generator=g, device=device).to(torch.bfloat16)
+        c = torch.empty((m, n), dtype=torch.bfloat16, device=device)
+        c_ref = torch.empty_like(c)
+        status = torch.zeros(1, dtype=torch.int32, device=device)
+
+        def ours():
+            kg.bf16_gemm(a, b, out=c, b_layout="row", stream=stream, status=status)
+
+        def cublas():
+            torch.matmul(a, b, out=c_ref)
+
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                ours()
+                cublas()
+        ours_us, cublas_us = time_interleaved([ours, cublas], steps, stream, flush)
+        if int(status.item()) != 0:
+            raise RuntimeError(f"device status {int(status.item()):#x}")
+        parity = kg.compare(c, c_ref, stream=stream)
+        min_bytes = 2 * (m * k + k * n + m * n)
+        med, med_ref = statistics.median(ours_us), statistics.median(cublas_us)
+        cfg = _native.select_config(m, n, k, _native.B_ROW)
+        rows.append({
+            "shape": [m, n, k],
+            "schedule": {"tile_m": cfg.tile_m, "tile_n": cfg.tile_n, "tile_k": cfg.tile_k, "stages": cfg.stages,
+                         "k_splits": max(1, cfg.k_splits)},
+            "median_us": med, "cublas_median_us": med_ref,
+            "gbs": min_bytes / (med * 1e-6) / 1e9, "cublas_gbs": min_bytes / (med_ref * 1e-6) / 1e9,
+            "frac_of_hbm": min_bytes / (med * 1e-6) / 1e9 / hbm,
+            "parity_vs_cublas": {"success": parity.success, "max_ulp": parity.max_ulp,
+                                 "n_gt_1ulp": parity.ulp_hist[2] + parity.ulp_hist[3]},
+        })
+    return {"bound": "hbm", "peak_gbs": hbm, "peak_source": f"{kind} hbm_gbs (copy)",
+            "timing": "per-launch CUDA events, L2 flushed, interleaved with cuBLAS, medians", "shapes": rows}
+
+
 def evaluation_throughput(device, world: int, local_rank: int, a_cpu, b_cpu, layout: str, repeat: int) -> dict:
     """Candidate-evaluation throughput, one evaluator per GPU (this rank's).
     Every legal point of the 96-point schedule grid is evaluated ``repeat``
@@ -471,6 +528,10 @@ def run_ours(args: argparse.Namespace) -> None:
             "steps": e2e_steps,
         }
 
+    skinny = None
+    if not args.no_skinny:
+        skinny = skinny_gemms(device, stream, flush)
+
     evaluations = None
     if not args.no_evals:
         evaluations = evaluation_throughput(device, world, local_rank, a_cpu, b_cpu, layout, repeat=args.eval_repeat)
@@ -540,6 +601,7 @@ def run_ours(args: argparse.Namespace) -> None:
             "clocks": clocks.summary(),
             "evaluations": evaluations,
             "sharded_gemm": sharded,
+            "skinny_hbm": skinny,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

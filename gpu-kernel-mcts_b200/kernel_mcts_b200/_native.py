@@ -102,6 +102,8 @@ class GemmConfig(ctypes.Structure):
         ("kernel", ctypes.c_int32),
         ("flags", ctypes.c_int32),
         ("wait_limit_ns", ctypes.c_int64),
+        ("k_splits", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
     ]
 
     def as_dict(self) -> dict[str, int]:
@@ -123,6 +125,7 @@ class GemmPlan(ctypes.Structure):
         ("tail_split", ctypes.c_int32),
         ("tail_clusters", ctypes.c_int32),
         ("tail_segments", ctypes.c_int32),
+        ("k_splits", ctypes.c_int32),
     ]
 
     def as_dict(self) -> dict[str, int]:

@@ -50,7 +50,8 @@ from .profiling import ProfileParseError, parse_ncu_csv, resolve_metric_set
 
 CANDIDATE_BACKEND = "cuda_cpp"
 SCHEDULE_BACKEND = "kmcts_sm100"
-SCHEDULE_FIELDS = ("tile_m", "tile_n", "tile_k", "stages", "cluster_m", "cluster_n", "persistent", "raster_group")
+SCHEDULE_FIELDS = ("tile_m", "tile_n", "tile_k", "stages", "cluster_m", "cluster_n", "persistent", "raster_group",
+                   "k_splits")
 
 
 class CommandRunner(Protocol):
@@ -285,7 +286,7 @@ class CudaSm100Backend:
         resolved = cfg.as_dict()
         args = tuple(
             f"--{name.replace('_', '-')}={resolved[name]}"
-            for name in ("tile_m", "cluster_m", "tile_n", "tile_k", "stages", "persistent", "raster_group")
+            for name in ("tile_m", "cluster_m", "tile_n", "tile_k", "stages", "persistent", "raster_group", "k_splits")
         ) + ("--kernel=tcgen05",)
         digest = hashlib.sha256()
         digest.update(harness.read_bytes())

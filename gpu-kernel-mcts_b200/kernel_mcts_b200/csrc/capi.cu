@@ -108,6 +108,25 @@ int kmcts_select_config(int M, int N, int K, int b_layout, kmcts_gemm_config* cf
         small.tile_n = 128;
         small.tile_k = 128;
         small.stages = 3;
+        // Few 128 x 128 tiles over a long K (skinny M or N): split K so the
+        // operand streams run through more SMs.  Splits minimise
+        // waves x (K blocks per unit + 2), the 2 standing for a unit's fixed
+        // cost (fill, epilogue, partial store), with units of at least 16 K
+        // blocks (measured: splitting K = 1024 or 2048 loses).
+        const int sms = multiprocessor_count();
+        const long long tiles = static_cast<long long>((M + 127) / 128) * ((N + 127) / 128);
+        const int num_kb = (K + 127) / 128;
+        if (tiles > 0 && tiles < sms && num_kb >= 32) {
+            double best = 0.0;
+            for (int splits = 1; splits <= 16 && splits <= num_kb / 16; ++splits) {
+                const long long waves = (tiles * splits + sms - 1) / sms;
+                const double cost = static_cast<double>(waves) * (static_cast<double>(num_kb) / splits + 2.0);
+                if (splits == 1 || cost < best) {
+                    best = cost;
+                    small.k_splits = splits;
+                }
+            }
+        }
     }
     if (tcgen05_legal(small, M, N, K, b_layout, nullptr, 0) == KMCTS_OK) *cfg = small;
     return KMCTS_OK;
@@ -175,6 +194,7 @@ int kmcts_gemm_plan_query(const kmcts_gemm_config* cfg, int M, int N, int K, int
     plan.tiles = ((M + 63) / 64) * ((N + 63) / 64);
     plan.full_tiles = plan.units = plan.ctas = plan.tiles;
     plan.workers = multiprocessor_count();
+    plan.k_splits = 1;
     *out = plan;
     return KMCTS_OK;
 }

@@ -52,12 +52,42 @@ struct Layout {
     static_assert(kSmemBytes <= kMaxSmem, "shared memory budget exceeded");
 };
 
+// Split K: unit u is K range s = u % splits of tile u / splits.  Partials are
+// [tile][split][lane quarter][BN/64 chunks] blocks of 32 rows x 64 FP32, each
+// stored as 16 float4 groups interleaved across the 32 lanes (coalesced).
+struct SplitK {
+    int splits;
+    float* partials;
+    unsigned long long* counters;  // [tile][lane quarter]: epoch << 32 | units arrived
+    int epoch;
+};
+
+template <int BN>
+__device__ __forceinline__ float4* split_chunk(const SplitK& sk, int tile, int split, int quarter, int c) {
+    const size_t block = ((static_cast<size_t>(tile) * sk.splits + split) * 4 + quarter) * (BN / 64) + c;
+    return reinterpret_cast<float4*>(sk.partials + block * 32 * 64);
+}
+
+// Counts one arrival on an epoch-tagged counter; returns how many units
+// arrived before this one in this launch.
+__device__ __forceinline__ int arrive_counted(unsigned long long* counter, int epoch) {
+    const unsigned long long tag = static_cast<unsigned long long>(static_cast<unsigned>(epoch)) << 32;
+    unsigned long long old = *reinterpret_cast<volatile unsigned long long*>(counter);
+    while (true) {
+        const bool same = (old >> 32) == static_cast<unsigned>(epoch);
+        const unsigned long long next = same ? old + 1 : (tag | 1ull);
+        const unsigned long long seen = atomicCAS(counter, old, next);
+        if (seen == old) return same ? static_cast<int>(old & 0xffffffffull) : 0;
+        old = seen;  // another unit arrived in between: retry on its value
+    }
+}
+
 template <int BN, int BK, int STAGES, bool B_MN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_tcgen05(const __grid_constant__ CUtensorMap map_a,
                       const __grid_constant__ CUtensorMap map_b,
                       const __grid_constant__ CUtensorMap map_c, int M, int N, int K, int group,
-                      uint64_t limit_ns, int* status) {
+                      uint64_t limit_ns, int* status, const SplitK sk) {
     using L = Layout<BN, BK, STAGES, B_MN>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -78,6 +108,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int num_n = (N + BN - 1) / BN;
     const int num_tiles = num_m * num_n;
     const int num_kb = (K + BK - 1) / BK;
+    const int splits = sk.splits;
+    const int num_units = num_tiles * splits;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -114,11 +146,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t phase = 0;
             uint32_t issued = 0, issued_phase = 0;
             bool ok = true;
-            for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+            for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+                const int t = u / splits, s = u % splits;
                 const TileCoord tc = tile_coord(t, num_m, num_n, group);
                 const int m0 = tc.m_blk * kBM;
                 const int n0 = tc.n_blk * BN;
-                for (int kb = 0; kb < num_kb; ++kb) {
+                const int kb1 = (s + 1) * num_kb / splits;
+                for (int kb = s * num_kb / splits; kb < kb1; ++kb) {
                     if (!ptx::mbar_wait(&empty[stage], phase ^ 1u, limit_ns, abort)) {
                         record_failure(status, abort, kRoleProducer);
                         ok = false;
@@ -166,7 +200,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t phase = 0;
             int local = 0;
             bool ok = true;
-            for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++local) {
+            for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x, ++local) {
+                const int s = u % splits;
+                const int kb0 = s * num_kb / splits, kb1 = (s + 1) * num_kb / splits;
                 const int acc = local & 1;
                 const uint32_t acc_phase = (local >> 1) & 1;
                 if (!ptx::mbar_wait(&tmem_empty[acc], acc_phase ^ 1u, limit_ns, abort)) {
@@ -175,7 +211,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 ptx::tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * BN;
-                for (int kb = 0; kb < num_kb; ++kb) {
+                for (int kb = kb0; kb < kb1; ++kb) {
                     if (!ptx::mbar_wait(&full[stage], phase, limit_ns, abort)) {
                         record_failure(status, abort, kRoleMma);
                         ok = false;
@@ -197,7 +233,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         } else {
                             bdesc = ptx::make_sw128_desc(sb + kh * (BN * 128) + kq * 32, 16, 1024);
                         }
-                        ptx::umma_bf16(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
+                        ptx::umma_bf16(d_tmem, adesc, bdesc, idesc, (kb != kb0 || kk != 0) ? 1u : 0u);
                     }
                     ptx::umma_commit(&empty[stage]);
                     if (++stage == STAGES) {
@@ -220,7 +256,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint8_t* staging = smem + L::kStagingOffset + e * 2 * kStagingBytes;
         int local = 0;
         int chunk_count = 0;
-        for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
+        for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++local) {
+            const int t = u / splits, s = u % splits;
             const TileCoord tc = tile_coord(t, num_m, num_n, group);
             const int m0 = tc.m_blk * kBM;
             const int n0 = tc.n_blk * BN;
@@ -235,6 +272,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             ptx::tc_fence_after();
             const uint32_t row_addr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                                       static_cast<uint32_t>(acc * BN);
+            if (splits > 1 && m0 + quarter * 32 >= M) {
+                // Split K, and none of this warp's rows exist: nothing to store.
+                ptx::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) ptx::mbar_arrive(&tmem_empty[acc]);
+                continue;
+            }
 #pragma unroll 1
             for (int c = 0; c < BN / 64; ++c) {
                 uint32_t lo[32], hi[32];
@@ -246,7 +290,64 @@ __global__ void __launch_bounds__(kThreads, 1)
                     __syncwarp();
                     if (lane == 0) ptx::mbar_arrive(&tmem_empty[acc]);
                 }
+                if (splits > 1) {
+                    float4* part = split_chunk<BN>(sk, t, s, quarter, c);
+#pragma unroll
+                    for (int q = 0; q < 8; ++q)
+                        __stcg(part + q * 32 + lane, make_float4(__uint_as_float(lo[4 * q]), __uint_as_float(lo[4 * q + 1]),
+                                                                 __uint_as_float(lo[4 * q + 2]), __uint_as_float(lo[4 * q + 3])));
+#pragma unroll
+                    for (int q = 0; q < 8; ++q)
+                        __stcg(part + (8 + q) * 32 + lane,
+                               make_float4(__uint_as_float(hi[4 * q]), __uint_as_float(hi[4 * q + 1]),
+                                           __uint_as_float(hi[4 * q + 2]), __uint_as_float(hi[4 * q + 3])));
+                    continue;
+                }
                 store_chunk(&map_c, staging, chunk_count, lo, hi, lane, n0 + c * 64, m0 + quarter * 32);
+            }
+            if (splits > 1) {
+                // Publish this warp's partial rows, then count the unit.  The
+                // unit that arrives last sums every split's rows in split
+                // order and writes C; the others are done.
+                __threadfence();
+                __syncwarp();
+                unsigned long long* counter = sk.counters + static_cast<size_t>(t) * 4 + quarter;
+                int order = 0;
+                if (lane == 0) order = arrive_counted(counter, sk.epoch);
+                if (__shfl_sync(0xffffffffu, order, 0) != splits - 1) continue;
+                __threadfence();
+#pragma unroll 1
+                for (int c = 0; c < BN / 64; ++c) {
+                    float sum[64];
+#pragma unroll 1
+                    for (int j = 0; j < splits; ++j) {
+                        const float4* part = split_chunk<BN>(sk, t, j, quarter, c);
+#pragma unroll
+                        for (int q = 0; q < 16; ++q) {
+                            const float4 f = __ldcg(part + q * 32 + lane);
+                            if (j == 0) {
+                                sum[4 * q] = f.x;
+                                sum[4 * q + 1] = f.y;
+                                sum[4 * q + 2] = f.z;
+                                sum[4 * q + 3] = f.w;
+                            } else {
+                                sum[4 * q] += f.x;
+                                sum[4 * q + 1] += f.y;
+                                sum[4 * q + 2] += f.z;
+                                sum[4 * q + 3] += f.w;
+                            }
+                        }
+                    }
+                    uint32_t lo[32], hi[32];
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) {
+                        lo[e] = __float_as_uint(sum[e]);
+                        hi[e] = __float_as_uint(sum[32 + e]);
+                    }
+                    store_chunk(&map_c, staging, chunk_count, lo, hi, lane, n0 + c * 64, m0 + quarter * 32);
+                }
+                __syncwarp();
+                if (lane == 0) *counter = 0ull;  // every unit of the tile has arrived: clear for replays
             }
         }
         if (lane == 0) ptx::bulk_wait_group_read<0>();  // shared memory must outlive the stores' reads
@@ -263,9 +364,30 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // ------------------------------------------------------------------ host side
 
+// K splits a launch can use: at most one per K block; 1 when the stream's
+// workspace cannot be had (out of memory, or growth under graph capture).
+template <int BN, int BK>
+int resolve_splits(int M, int N, int K, int requested, cudaStream_t stream, SplitK* sk) {
+    *sk = SplitK{1, nullptr, nullptr, 0};
+    const int num_kb = (K + BK - 1) / BK;
+    int splits = requested < num_kb ? requested : num_kb;
+    if (splits <= 1) return 1;
+    const size_t tiles = static_cast<size_t>((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
+    const size_t partial_bytes = tiles * splits * 4 * (BN / 64) * 32 * 64 * sizeof(float);
+    const size_t counter_bytes = tiles * 4 * sizeof(unsigned long long);
+    void* base = nullptr;
+    int epoch = 0;
+    if (!stream_workspace(stream, kWorkspaceSplitK, counter_bytes + partial_bytes, &base, &epoch)) return 1;
+    sk->splits = splits;
+    sk->counters = static_cast<unsigned long long*>(base);
+    sk->partials = reinterpret_cast<float*>(static_cast<char*>(base) + counter_bytes);
+    sk->epoch = epoch;
+    return splits;
+}
+
 template <int BN, int BK, int STAGES, bool B_MN>
 int launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, int M,
-                   int N, int K, int group, bool persistent, uint64_t limit_ns,
+                   int N, int K, int group, bool persistent, int k_splits, uint64_t limit_ns,
                    cudaStream_t stream, int* status) {
     using L = Layout<BN, BK, STAGES, B_MN>;
     auto kernel = gemm_bf16_tcgen05<BN, BK, STAGES, B_MN>;
@@ -284,17 +406,19 @@ int launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorM
             configured[device] = true;
         }
     }
-    const int tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
-    int grid = tiles;
-    if (persistent) grid = tiles < multiprocessor_count() ? tiles : multiprocessor_count();
+    SplitK sk;
+    const int splits = resolve_splits<BN, BK>(M, N, K, k_splits, stream, &sk);
+    const int units = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN) * splits;
+    int grid = units;
+    if (persistent) grid = units < multiprocessor_count() ? units : multiprocessor_count();
     kernel<<<grid, kThreads, L::kSmemBytes, stream>>>(ma, mb, mc, M, N, K, group, limit_ns,
-                                                      status);
+                                                      status, sk);
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return cudaGetLastError() == cudaSuccess ? KMCTS_OK : KMCTS_EGEMM;
 }
 
 using Launcher = int (*)(const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, int, int,
-                         int, int, bool, uint64_t, cudaStream_t, int*);
+                         int, int, bool, int, uint64_t, cudaStream_t, int*);
 
 struct Variant {
     int bn, bk, stages, b_mn;
@@ -362,6 +486,14 @@ int tcgen05_legal(const kmcts_gemm_config& cfg, int M, int N, int K, int b_layou
     if (cfg.raster_group < 1) {
         put_reason(why, len, "raster_group must be >= 1");
         return KMCTS_EINVAL;
+    }
+    if (cfg.k_splits < 0) {
+        put_reason(why, len, "k_splits must be >= 0");
+        return KMCTS_EINVAL;
+    }
+    if (cfg.k_splits > 1 && cfg.tile_m != kBM) {
+        put_reason(why, len, "split K runs on one-CTA schedules (tile_m 128)");
+        return KMCTS_ENOTSUP;
     }
     if (cfg.cluster_m < 1 || cfg.cluster_n < 1) {
         put_reason(why, len, "cluster dimensions must be positive");
@@ -447,7 +579,7 @@ int launch_tcgen05(const void* A, const void* B, void* C, int M, int N, int K, i
         cfg.wait_limit_ns > 0 ? static_cast<uint64_t>(cfg.wait_limit_ns) : kDefaultWaitNs;
     if (pair) return launch_pair(ma, mb, mb_half, mc, M, N, K, b_layout, cfg, limit, stream, device_status);
     const Variant* v = find_variant(cfg, b_layout);
-    return v->fn(ma, mb, mc, M, N, K, cfg.raster_group, cfg.persistent != 0, limit, stream,
+    return v->fn(ma, mb, mc, M, N, K, cfg.raster_group, cfg.persistent != 0, cfg.k_splits, limit, stream,
                  device_status);
 }
 
@@ -501,8 +633,11 @@ int plan_tcgen05(const kmcts_gemm_config& cfg, int M, int N, int K, int b_layout
     plan.workers = multiprocessor_count();
     plan.tiles = ((M + kBM - 1) / kBM) * ((N + cfg.tile_n - 1) / cfg.tile_n);
     plan.full_tiles = plan.tiles;
-    plan.units = plan.tiles;
-    plan.ctas = cfg.persistent ? (plan.tiles < plan.workers ? plan.tiles : plan.workers) : plan.tiles;
+    const int num_kb = (K + cfg.tile_k - 1) / cfg.tile_k;
+    plan.k_splits = cfg.k_splits > 1 ? (cfg.k_splits < num_kb ? cfg.k_splits : num_kb) : 1;
+    if (plan.k_splits < 1) plan.k_splits = 1;
+    plan.units = plan.tiles * plan.k_splits;
+    plan.ctas = cfg.persistent ? (plan.units < plan.workers ? plan.units : plan.workers) : plan.units;
     plan.smem_bytes = static_cast<int32_t>(tcgen05_smem_bytes(cfg, b_layout));
     *out = plan;
     return KMCTS_OK;

@@ -21,7 +21,6 @@
 // Every wait is bounded; see gemm_tcgen05.cu for the failure protocol.
 #include <cstring>
 #include <mutex>
-#include <thread>
 
 #include "gemm_common.cuh"
 #include "kmcts_internal.h"
@@ -608,6 +607,7 @@ kmcts_gemm_plan make_pair_plan(int M, int N, int K, int workers, bool persistent
     }
     plan.ctas = 2 * clusters;
     plan.smem_bytes = static_cast<int32_t>(smem);
+    plan.k_splits = 1;
     return plan;
 }
 
@@ -621,70 +621,24 @@ int plan_pair_variant(int M, int N, int K, bool persistent, int tail, kmcts_gemm
     return KMCTS_OK;
 }
 
-// FP32 partials and flags of stream-K tiles, one workspace per (device,
-// stream): launches on one stream run in order, so they may share it;
-// launches on different streams may overlap, so they may not.  One partial
-// slot per range boundary (W - 1 at most, sized for W = SMs / 2).  Allocated
-// and zeroed on a stream's first stream-K launch, kept for the process's
-// lifetime.
-struct TailWorkspace {
-    int device;
-    cudaStream_t stream;
-    std::thread::id thread;  // distinguishes per-thread default streams
-    float* partials;
-    int* flags;              // ready flags, then arrival flags
-    int epoch;
-};
-
-constexpr int kMaxTailWorkspaces = 64;
+// FP32 partials and flags of stream-K tiles: one partial slot per range
+// boundary (W - 1 at most, sized for W = SMs / 2), then the ready and arrival
+// flags, in the stream's workspace.
 constexpr size_t kPartialSlotBytes = 2 * 4 * (256 / 64) * 32 * 64 * sizeof(float);  // one 256 x 256 FP32 tile
 
-int boundary_slots() { return multiprocessor_count() / 2 + 1; }
-
 bool tail_workspace(cudaStream_t stream, int boundaries, TailSplit* out) {
-    static std::mutex mu;
-    static TailWorkspace spaces[kMaxTailWorkspaces];
-    static int count = 0;
-    const int slots = boundary_slots();
-    if (boundaries > slots) return false;
-    int device = 0;
-    if (cudaGetDevice(&device) != cudaSuccess) return false;
-    const std::thread::id thread =
-        stream == cudaStreamPerThread ? std::this_thread::get_id() : std::thread::id();
-    std::lock_guard<std::mutex> lock(mu);
-    TailWorkspace* ws = nullptr;
-    for (int i = 0; i < count; ++i) {
-        if (spaces[i].device == device && spaces[i].stream == stream && spaces[i].thread == thread) ws = &spaces[i];
-    }
-    if (ws == nullptr) {
-        if (count == kMaxTailWorkspaces) return false;
-        // cudaMalloc may not run while the stream is being captured.
-        cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
-        if (cudaStreamIsCapturing(stream, &capture) != cudaSuccess || capture != cudaStreamCaptureStatusNone) {
-            cudaGetLastError();
-            return false;
-        }
-        const size_t flag_bytes = static_cast<size_t>(slots) * 2 * 4 * 2 * sizeof(int);
-        void* partials = nullptr;
-        void* flags = nullptr;
-        if (cudaMalloc(&partials, slots * kPartialSlotBytes) != cudaSuccess) {
-            cudaGetLastError();
-            return false;
-        }
-        if (cudaMalloc(&flags, flag_bytes) != cudaSuccess || cudaMemset(flags, 0, flag_bytes) != cudaSuccess) {
-            cudaGetLastError();
-            cudaFree(partials);
-            if (flags) cudaFree(flags);
-            return false;
-        }
-        ws = &spaces[count++];
-        *ws = {device, stream, thread, static_cast<float*>(partials), static_cast<int*>(flags), 0};
-    }
-    ws->epoch = ws->epoch % 0x7fffffff + 1;  // never 0, the cleared state
-    out->partials = ws->partials;
-    out->ready = ws->flags;
-    out->arrivals = ws->flags + static_cast<size_t>(slots) * 2 * 4;
-    out->epoch = ws->epoch;
+    const size_t slots = static_cast<size_t>(multiprocessor_count() / 2 + 1);
+    if (static_cast<size_t>(boundaries) > slots) return false;
+    const size_t flag_ints = slots * 2 * 4;
+    void* base = nullptr;
+    int epoch = 0;
+    if (!stream_workspace(stream, kWorkspaceStreamK, slots * kPartialSlotBytes + 2 * flag_ints * sizeof(int), &base,
+                          &epoch))
+        return false;
+    out->partials = static_cast<float*>(base);
+    out->ready = reinterpret_cast<int*>(static_cast<char*>(base) + slots * kPartialSlotBytes);
+    out->arrivals = out->ready + flag_ints;
+    out->epoch = epoch;
     return true;
 }
 

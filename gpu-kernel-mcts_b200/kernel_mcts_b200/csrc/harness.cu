@@ -9,7 +9,7 @@
 // (src/kernel_mcts/cuda_backend.py:466-503).
 //
 // Additive flags: --b-layout=col|row, --inputs=uniform|randn|int,
-// --kernel=auto|tcgen05|simt|candidate|cublas|cutlass_sm80, --tile-m
+// --kernel=auto|tcgen05|simt|candidate|cublas|cutlass_sm80, --k-splits, --tile-m
 // --cluster-m --tile-n --tile-k --stages --persistent --raster-group --flags
 // --wait-limit-ns, --flush-l2=0|1.  cublas and cutlass_sm80 are the vendor
 // baseline columns (src/kernel_mcts/vendor_baselines.py), timed under the
@@ -213,6 +213,7 @@ int main(int argc, char** argv) {
     l.cfg.stages = static_cast<int>(int_arg(argc, argv, "stages", l.cfg.stages));
     l.cfg.persistent = static_cast<int>(int_arg(argc, argv, "persistent", l.cfg.persistent));
     l.cfg.raster_group = static_cast<int>(int_arg(argc, argv, "raster-group", l.cfg.raster_group));
+    l.cfg.k_splits = static_cast<int>(int_arg(argc, argv, "k-splits", l.cfg.k_splits));
     l.cfg.wait_limit_ns = int_arg(argc, argv, "wait-limit-ns", 0);
     l.impl = Impl::kLibrary;
     if (kernel == "tcgen05") {

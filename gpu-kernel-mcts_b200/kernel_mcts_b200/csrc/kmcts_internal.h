@@ -39,6 +39,14 @@ int take_default_status(cudaStream_t stream, int* value);
 
 int multiprocessor_count();
 
+// A zeroed device workspace of at least `bytes` for kernels launched on
+// `stream` (one per device, stream and `user`), and the launch epoch to tag
+// its flags with.  False when none can be had now (out of memory, or growth
+// needed while the stream is being captured).  Returned buffers are never
+// freed, so graphs that captured them stay valid.  workspace.cu.
+constexpr int kWorkspaceStreamK = 0, kWorkspaceSplitK = 1;
+bool stream_workspace(cudaStream_t stream, int user, size_t bytes, void** ptr, int* epoch);
+
 // CTA-pair (cta_group::2) kernels, gemm_tcgen05_pair.cu.
 bool pair_variant_exists(int bn, int bk, int stages, int b_layout);
 int64_t pair_smem_bytes(int bn, int bk, int stages);

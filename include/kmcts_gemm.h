@@ -78,7 +78,21 @@ typedef struct kmcts_gemm_config {
     int32_t kernel;       /* KMCTS_KERNEL_* */
     int32_t flags;        /* KMCTS_FLAG_* bits */
     int64_t wait_limit_ns; /* bound on each device-side wait; 0 = 2 s default */
+    int32_t k_splits;     /* one-CTA schedules: K ranges per tile (0 or 1 = none); see below */
+    int32_t reserved;     /* zero */
 } kmcts_gemm_config;
+
+/* Split K (tile_m 128).  With k_splits = S > 1 each output tile runs as S
+ * units over consecutive K ranges, so a shape with few tiles (skinny M or N)
+ * still streams its operands through every SM.  Each unit stores its FP32
+ * partial in a per-stream library workspace and counts itself on the tile's
+ * epoch-tagged counter; the unit that arrives last adds the S partials in
+ * split order (deterministic) and writes the BF16 tile.  Nothing waits: the
+ * last arrival only reads partials already published.  S is capped at the
+ * number of K blocks; launches on a stream under CUDA-graph capture before its
+ * workspace is large enough run unsplit.  Workspaces are never freed, so a
+ * graph that captured one stays valid; graphs captured on one stream share
+ * that stream's workspace and must not replay concurrently. */
 
 /* Fills *cfg with the tuned default schedule for B200 (the CTA-pair 256 x 256
  * x 128, 3-stage schedule that is fastest at 4096^3). Returns KMCTS_OK. */
@@ -131,6 +145,7 @@ typedef struct kmcts_gemm_plan {
     int32_t tail_split;   /* KMCTS_TAIL_*: how the tiles after full_tiles split */
     int32_t tail_clusters; /* pairs that share the tiles after full_tiles */
     int32_t tail_segments; /* most units one tile runs as (2 when split) */
+    int32_t k_splits;     /* one-CTA split K: K ranges per tile (1 = none) */
 } kmcts_gemm_plan;
 
 /* Fills *out with the launch shape kmcts_bf16_gemm_ex would use for this

@@ -390,3 +390,63 @@ def test_launch_counter_counts_library_launches(cuda_device):
         kg.bf16_gemm(a, b)
     torch.cuda.synchronize()
     assert _native.launch_count() - before == 3
+
+
+# ------------------------------------------------------------------ split K
+
+SPLIT = dict(kernel=_native.KERNEL_TCGEN05, tile_m=128, cluster_m=1, tile_n=128, tile_k=128, stages=3)
+
+
+@pytest.mark.parametrize("layout", ["col", "row"])
+@pytest.mark.parametrize("shape,splits", [
+    ((16, 1024, 2048), 2), ((16, 1024, 2048), 5), ((100, 520, 1032), 3), ((300, 136, 640), 4),
+    ((8, 264, 256), 16),  # more splits than K blocks: capped at 2
+    ((8192, 16, 1024), 4),
+])
+def test_split_k_integer_inputs_bit_exact(cuda_device, layout, shape, splits):
+    """Each tile's K ranges add up exactly on integer inputs, whatever the
+    split count, the raggedness and the layout."""
+    m, n, k = shape
+    plan = plan_of(m, n, k, layout, k_splits=splits, **SPLIT)
+    assert plan["k_splits"] == min(splits, -(-k // 128)) and plan["units"] == plan["tiles"] * plan["k_splits"]
+    a_t, b_t = oracle.integer_inputs(m, n, k, seed=splits)
+    expect = oracle.torch_bits(oracle.torch_reference(a_t, b_t))
+    c = run(a_t.cuda(), b_for(layout, b_t.cuda()), layout, k_splits=splits, **SPLIT)
+    np.testing.assert_array_equal(bits_of(c), expect)
+
+
+@pytest.mark.parametrize("layout", ["col", "row"])
+def test_split_k_randn_within_criterion_and_deterministic(cuda_device, layout):
+    m, n, k = 64, 2048, 8192
+    a_t, b_t = oracle.randn_inputs(m, n, k, seed=6, b_layout=layout)
+    a, b = a_t.cuda(), b_t.cuda()
+    c = run(a, b, layout, k_splits=7, **SPLIT)
+    again = run(a, b, layout, k_splits=7, **SPLIT)
+    assert torch.equal(c.view(torch.int16), again.view(torch.int16))  # fixed split order
+    whole = run(a, b, layout, **SPLIT)
+    ref64, mag = oracle.fp64_reference(a_t, b_t, layout)
+    report = oracle.parity_report(bits_of(c), bits_of(whole), ref64, mag, k)
+    assert report["passed"] and report["max_ulp_where_ref_ge_0.5"] <= 1, report
+
+
+def test_split_k_concurrent_streams_and_selection(cuda_device):
+    """Skinny shapes select split K; two streams use separate workspaces."""
+    m, n, k = 16, 4096, 8192
+    sel = _native.select_config(m, n, k, _native.B_COL)
+    assert sel.tile_m == 128 and sel.k_splits > 1
+    x_a, x_b = oracle.integer_inputs(m, n, k, seed=1)
+    y_a, y_b = oracle.integer_inputs(m, n, k, seed=2)
+    ex = oracle.torch_bits(oracle.torch_reference(x_a, x_b))
+    ey = oracle.torch_bits(oracle.torch_reference(y_a, y_b))
+    xa, xb, ya, yb = x_a.cuda(), x_b.cuda(), y_a.cuda(), y_b.cuda()
+    s1, s2 = torch.cuda.Stream(), torch.cuda.Stream()
+    status = torch.zeros(2, dtype=torch.int32, device="cuda")
+    outs = []
+    for _ in range(6):
+        outs.append((kg.bf16_gemm(xa, xb, stream=s1, status=status[0:1]),   # NULL config: the selection
+                     kg.bf16_gemm(ya, yb, stream=s2, status=status[1:2])))
+    torch.cuda.synchronize()
+    assert status.tolist() == [0, 0]
+    for cx, cy in outs:
+        np.testing.assert_array_equal(bits_of(cx), ex)
+        np.testing.assert_array_equal(bits_of(cy), ey)

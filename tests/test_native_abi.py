@@ -33,7 +33,7 @@ def test_library_loads_and_exports_every_declared_symbol():
 
 
 def test_struct_sizes_match_header():
-    assert ctypes.sizeof(_native.GemmConfig) == 48
+    assert ctypes.sizeof(_native.GemmConfig) == 56
     assert ctypes.sizeof(_native.CompareResult) == 8 * 2 + 8 * 3 + 8 * 4 + 4 * 2
 
 
@@ -42,6 +42,15 @@ def test_version_and_default_config():
     cfg = km.default_config()
     assert (cfg.tile_m, cfg.tile_n, cfg.tile_k, cfg.stages, cfg.cluster_m) == (256, 256, 128, 3, 2)
     assert km.config_legal(cfg, 4096, 4096, 4096) == (0, "ok")
+
+
+def test_select_config_splits_k_for_skinny_shapes():
+    cfg = km.select_config(16, 8192, 8192, km.B_ROW)
+    assert (cfg.tile_m, cfg.tile_n, cfg.k_splits) == (128, 128, 2)  # 64 tiles -> 128 units
+    assert km.select_config(512, 512, 8192, km.B_ROW).k_splits == 4
+    assert km.select_config(1024, 1024, 1024, km.B_ROW).k_splits == 0  # short K: no split
+    assert km.select_config(4096, 4096, 4096, km.B_ROW).k_splits == 0
+    assert km.select_config(256, 256, 256, km.B_ROW).k_splits == 0  # K too short to split
 
 
 @pytest.mark.parametrize(
