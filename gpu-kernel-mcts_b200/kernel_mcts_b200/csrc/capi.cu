@@ -84,20 +84,68 @@ int kmcts_default_config(kmcts_gemm_config* cfg) {
     return KMCTS_OK;
 }
 
+namespace {
+
+// K splits for `tiles` one-CTA tiles over K: minimise
+// waves x (128-deep K blocks per unit + 2), the 2 standing for a unit's
+// fixed cost (fill, epilogue, partial store), with units of at least 16 K
+// blocks (measured: splitting K = 1024 or 2048 loses).  0 = no split.
+int choose_splits(long long tiles, int K, int sms) {
+    const int num_kb = (K + 127) / 128;
+    if (tiles <= 0 || tiles >= sms || num_kb < 32) return 0;
+    int chosen = 0;
+    double best = 0.0;
+    for (int splits = 1; splits <= 16 && splits <= num_kb / 16; ++splits) {
+        const long long waves = (tiles * splits + sms - 1) / sms;
+        const double cost = static_cast<double>(waves) * (static_cast<double>(num_kb) / splits + 2.0);
+        if (splits == 1 || cost < best) {
+            best = cost;
+            chosen = splits == 1 ? 0 : splits;
+        }
+    }
+    return chosen;
+}
+
+}  // namespace
+
 int kmcts_select_config(int M, int N, int K, int b_layout, kmcts_gemm_config* cfg) {
     if (!cfg || M < 0 || N < 0 || K < 0) return KMCTS_EINVAL;
     kmcts_default_config(cfg);
-    // Measured on B200 (CUDA-graph replays, warm L2): the CTA-pair 256 x 256
-    // schedule wins once its tiles fill the co-resident pairs; below that,
-    // one-CTA tiles give more CTAs: 128 x 256 while those fill the pairs'
-    // count and K is short (from K = 8192 the pair's faster mainloop wins
-    // back its idle SMs), else 128 x 128.
-    const int workers = multiprocessor_count() / 2;
+    // Measured on B200 (CUDA-graph replays, warm L2):
+    // * M <= 32: one CTA per tile staging 32 rows of A (more B in flight per
+    //   SM; the problem is bound by reading B): 128 x 256 tiles when they
+    //   fill the SMs' pairs count, else 128 x 128 with split K on long K;
+    // * the CTA-pair 256 x 256 schedule once its tiles fill the co-resident
+    //   pairs;
+    // * below that, one CTA per 128 x 256 tile while those fill the pairs'
+    //   count and K is short (from K = 4096 the pair's faster mainloop wins
+    //   back its idle SMs), else one CTA per 128 x 128 tile, split K on long K.
+    const int sms = multiprocessor_count();
+    const int workers = sms / 2;
+    kmcts_gemm_config small = *cfg;
+    small.cluster_m = 1;
+    if (M > 0 && M <= 32) {
+        small.tile_m = 32;
+        if ((N + 255) / 256 >= workers) {
+            small.tile_n = 256;
+            small.tile_k = 64;
+            small.stages = 5;
+        } else {
+            small.tile_n = 128;
+            small.tile_k = 128;
+            small.stages = 4;
+        }
+        small.k_splits = choose_splits((N + small.tile_n - 1) / small.tile_n, K, sms);
+        if (tcgen05_legal(small, M, N, K, b_layout, nullptr, 0) == KMCTS_OK) {
+            *cfg = small;
+            return KMCTS_OK;
+        }
+        small = *cfg;
+        small.cluster_m = 1;
+    }
     const long long pair_tiles = static_cast<long long>((M + 255) / 256) * ((N + 255) / 256);
     if (pair_tiles >= workers) return KMCTS_OK;
-    kmcts_gemm_config small = *cfg;
     small.tile_m = 128;
-    small.cluster_m = 1;
     const long long wide_tiles = static_cast<long long>((M + 127) / 128) * ((N + 255) / 256);
     if (wide_tiles >= workers) {
         if (K >= 4096) return KMCTS_OK;
@@ -108,25 +156,7 @@ int kmcts_select_config(int M, int N, int K, int b_layout, kmcts_gemm_config* cf
         small.tile_n = 128;
         small.tile_k = 128;
         small.stages = 3;
-        // Few 128 x 128 tiles over a long K (skinny M or N): split K so the
-        // operand streams run through more SMs.  Splits minimise
-        // waves x (K blocks per unit + 2), the 2 standing for a unit's fixed
-        // cost (fill, epilogue, partial store), with units of at least 16 K
-        // blocks (measured: splitting K = 1024 or 2048 loses).
-        const int sms = multiprocessor_count();
-        const long long tiles = static_cast<long long>((M + 127) / 128) * ((N + 127) / 128);
-        const int num_kb = (K + 127) / 128;
-        if (tiles > 0 && tiles < sms && num_kb >= 32) {
-            double best = 0.0;
-            for (int splits = 1; splits <= 16 && splits <= num_kb / 16; ++splits) {
-                const long long waves = (tiles * splits + sms - 1) / sms;
-                const double cost = static_cast<double>(waves) * (static_cast<double>(num_kb) / splits + 2.0);
-                if (splits == 1 || cost < best) {
-                    best = cost;
-                    small.k_splits = splits;
-                }
-            }
-        }
+        small.k_splits = choose_splits(static_cast<long long>((M + 127) / 128) * ((N + 127) / 128), K, sms);
     }
     if (tcgen05_legal(small, M, N, K, b_layout, nullptr, 0) == KMCTS_OK) *cfg = small;
     return KMCTS_OK;

@@ -38,9 +38,14 @@ using namespace gemm;
 constexpr int kBM = 128;
 constexpr int kMaxDevices = 64;
 
-template <int BN, int BK, int STAGES, bool B_MN>
+// AR: rows of A staged per tile.  128 normally; 32 for skinny GEMMs (M <= 32):
+// the MMA still computes 128 rows, but rows 32-127 read whatever follows A's
+// 32 rows in the stage and are never stored, and the freed shared memory
+// holds more B stages in flight.
+template <int BN, int BK, int STAGES, bool B_MN, int AR = kBM>
 struct Layout {
-    static constexpr int kABytes = kBM * BK * 2;
+    static constexpr int kAHalf = AR * 128;  // one 64-wide K half of A
+    static constexpr int kABytes = AR * BK * 2;
     static constexpr int kBBytes = BN * BK * 2;
     static constexpr int kStageBytes = kABytes + kBBytes;
     static constexpr int kStagingOffset = STAGES * kStageBytes;
@@ -50,6 +55,9 @@ struct Layout {
     static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "BN must be 64..256, step 64");
     static_assert(BK == 64 || BK == 128, "BK must be 64 or 128");
     static_assert(kSmemBytes <= kMaxSmem, "shared memory budget exceeded");
+    static_assert(AR == kBM || AR == 32, "A is staged as 128 or 32 rows");
+    // The MMA reads 128 rows (16 KB) from each A half: that must stay inside the stage.
+    static_assert(AR == kBM || (BK / 64 - 1) * kAHalf + kBM * 128 <= kStageBytes, "A over-read leaves the stage");
 };
 
 // Split K: unit u is K range s = u % splits of tile u / splits.  Partials are
@@ -82,13 +90,13 @@ __device__ __forceinline__ int arrive_counted(unsigned long long* counter, int e
     }
 }
 
-template <int BN, int BK, int STAGES, bool B_MN>
+template <int BN, int BK, int STAGES, bool B_MN, int AR>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_tcgen05(const __grid_constant__ CUtensorMap map_a,
                       const __grid_constant__ CUtensorMap map_b,
                       const __grid_constant__ CUtensorMap map_c, int M, int N, int K, int group,
                       uint64_t limit_ns, int* status, const SplitK sk) {
-    using L = Layout<BN, BK, STAGES, B_MN>;
+    using L = Layout<BN, BK, STAGES, B_MN, AR>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~uintptr_t(1023));
@@ -164,7 +172,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int kh = 0; kh < BK / 64; ++kh) {
                         const int k0 = kb * BK + kh * 64;
-                        ptx::tma_load_2d(sa + kh * (kBM * 128), &map_a, &full[stage], k0, m0);
+                        ptx::tma_load_2d(sa + kh * L::kAHalf, &map_a, &full[stage], k0, m0);
                         if constexpr (B_MN) {
 #pragma unroll
                             for (int nb = 0; nb < BN / 64; ++nb) {
@@ -224,8 +232,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int kk = 0; kk < BK / 16; ++kk) {
                         const int kh = kk / 4;  // which 64-wide K half of the stage
                         const int kq = kk % 4;  // 16-element step inside it
-                        const uint64_t adesc =
-                            ptx::make_sw128_desc(sa + kh * (kBM * 128) + kq * 32, 16, 1024);
+                        const uint64_t adesc = ptx::make_sw128_desc(sa + kh * L::kAHalf + kq * 32, 16, 1024);
                         uint64_t bdesc;
                         if constexpr (B_MN) {
                             bdesc = ptx::make_sw128_desc(sb + kh * (BN / 64) * 8192 + kq * 2048,
@@ -272,8 +279,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             ptx::tc_fence_after();
             const uint32_t row_addr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                                       static_cast<uint32_t>(acc * BN);
-            if (splits > 1 && m0 + quarter * 32 >= M) {
-                // Split K, and none of this warp's rows exist: nothing to store.
+            if (m0 + quarter * 32 >= M) {
+                // None of this warp's rows exist: nothing to store.
                 ptx::tc_fence_before();
                 __syncwarp();
                 if (lane == 0) ptx::mbar_arrive(&tmem_empty[acc]);
@@ -385,12 +392,12 @@ int resolve_splits(int M, int N, int K, int requested, cudaStream_t stream, Spli
     return splits;
 }
 
-template <int BN, int BK, int STAGES, bool B_MN>
+template <int BN, int BK, int STAGES, bool B_MN, int AR>
 int launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, int M,
                    int N, int K, int group, bool persistent, int k_splits, uint64_t limit_ns,
                    cudaStream_t stream, int* status) {
-    using L = Layout<BN, BK, STAGES, B_MN>;
-    auto kernel = gemm_bf16_tcgen05<BN, BK, STAGES, B_MN>;
+    using L = Layout<BN, BK, STAGES, B_MN, AR>;
+    auto kernel = gemm_bf16_tcgen05<BN, BK, STAGES, B_MN, AR>;
     // The shared-memory opt-in is per device; set it once on each.
     static std::mutex mu;
     static bool configured[kMaxDevices] = {};
@@ -421,11 +428,12 @@ using Launcher = int (*)(const CUtensorMap&, const CUtensorMap&, const CUtensorM
                          int, int, bool, int, uint64_t, cudaStream_t, int*);
 
 struct Variant {
-    int bn, bk, stages, b_mn;
+    int bn, bk, stages, b_mn, ar;
     Launcher fn;
 };
 
-#define KMCTS_VARIANT(BN, BK, ST, MN) {BN, BK, ST, MN, &launch_variant<BN, BK, ST, MN>}
+#define KMCTS_VARIANT(BN, BK, ST, MN) {BN, BK, ST, MN, kBM, &launch_variant<BN, BK, ST, MN, kBM>}
+#define KMCTS_SKINNY(BN, BK, ST, MN) {BN, BK, ST, MN, 32, &launch_variant<BN, BK, ST, MN, 32>}
 
 // The compiled 1-CTA schedule space: every (tile_n, tile_k, stages) of the
 // sweep grid that fits 227 KB (stages*(128+BN)*BK*2 + 32 KB staging + 2 KB),
@@ -441,12 +449,16 @@ const Variant kVariants[] = {
     KMCTS_VARIANT(256, 128, 2, false), KMCTS_VARIANT(256, 128, 2, true),
     KMCTS_VARIANT(192, 64, 4, false), KMCTS_VARIANT(192, 64, 4, true),
     KMCTS_VARIANT(64, 64, 6, false),  KMCTS_VARIANT(64, 64, 6, true),
+    // tile_m 32 (M <= 32): A staged as 32 rows, more B stages in flight.
+    KMCTS_SKINNY(256, 64, 5, false),  KMCTS_SKINNY(256, 64, 5, true),
+    KMCTS_SKINNY(128, 64, 9, false),  KMCTS_SKINNY(128, 64, 9, true),
+    KMCTS_SKINNY(128, 128, 4, false), KMCTS_SKINNY(128, 128, 4, true),
 };
 
 const Variant* find_variant(const kmcts_gemm_config& cfg, int b_layout) {
     for (const Variant& v : kVariants) {
         if (v.bn == cfg.tile_n && v.bk == cfg.tile_k && v.stages == cfg.stages &&
-            v.b_mn == (b_layout == KMCTS_B_ROW ? 1 : 0)) {
+            v.b_mn == (b_layout == KMCTS_B_ROW ? 1 : 0) && v.ar == (cfg.tile_m == 32 ? 32 : kBM)) {
             return &v;
         }
     }
@@ -461,6 +473,7 @@ void put_reason(char* why, int len, const char* text) {
 }
 
 bool is_pair(const kmcts_gemm_config& cfg) { return cfg.tile_m == 256; }
+bool is_one_cta(const kmcts_gemm_config& cfg) { return cfg.tile_m == kBM || cfg.tile_m == 32; }
 
 }  // namespace
 
@@ -468,8 +481,8 @@ int64_t tcgen05_smem_bytes(const kmcts_gemm_config& cfg, int b_layout) {
     (void)b_layout;
     if (cfg.tile_n <= 0 || cfg.tile_k <= 0 || cfg.stages <= 0) return 0;
     if (cfg.tile_m == 256) return pair_smem_bytes(cfg.tile_n, cfg.tile_k, cfg.stages);
-    if (cfg.tile_m != kBM) return 0;
-    return static_cast<int64_t>(cfg.stages) * (kBM + cfg.tile_n) * cfg.tile_k * 2 +
+    if (cfg.tile_m != kBM && cfg.tile_m != 32) return 0;
+    return static_cast<int64_t>(cfg.stages) * (cfg.tile_m + cfg.tile_n) * cfg.tile_k * 2 +
            kEpilogueWarps * 2 * kStagingBytes + kSmemReserve;
 }
 
@@ -491,8 +504,8 @@ int tcgen05_legal(const kmcts_gemm_config& cfg, int M, int N, int K, int b_layou
         put_reason(why, len, "k_splits must be >= 0");
         return KMCTS_EINVAL;
     }
-    if (cfg.k_splits > 1 && cfg.tile_m != kBM) {
-        put_reason(why, len, "split K runs on one-CTA schedules (tile_m 128)");
+    if (cfg.k_splits > 1 && !is_one_cta(cfg)) {
+        put_reason(why, len, "split K runs on one-CTA schedules (tile_m 128 or 32)");
         return KMCTS_ENOTSUP;
     }
     if (cfg.cluster_m < 1 || cfg.cluster_n < 1) {
@@ -505,9 +518,13 @@ int tcgen05_legal(const kmcts_gemm_config& cfg, int M, int N, int K, int b_layou
                    "which this library never issues");
         return KMCTS_ENOTSUP;
     }
-    if (cfg.tile_m == kBM) {
+    if (is_one_cta(cfg)) {
         if (cfg.cluster_m != 1) {
-            put_reason(why, len, "tile_m 128 runs one CTA per tile (cluster 1x1)");
+            put_reason(why, len, "tile_m 128 and 32 run one CTA per tile (cluster 1x1)");
+            return KMCTS_ENOTSUP;
+        }
+        if (cfg.tile_m == 32 && M > 32) {
+            put_reason(why, len, "tile_m 32 stages 32 rows of A: it takes M <= 32");
             return KMCTS_ENOTSUP;
         }
     } else if (cfg.tile_m == 256) {
@@ -520,7 +537,7 @@ int tcgen05_legal(const kmcts_gemm_config& cfg, int M, int N, int K, int b_layou
             return KMCTS_ENOTSUP;
         }
     } else {
-        put_reason(why, len, "tile_m must be 128 (one CTA) or 256 (CTA pair)");
+        put_reason(why, len, "tile_m must be 128 or 32 (one CTA) or 256 (CTA pair)");
         return KMCTS_ENOTSUP;
     }
     const int64_t smem = tcgen05_smem_bytes(cfg, b_layout);
@@ -563,7 +580,7 @@ int launch_tcgen05(const void* A, const void* B, void* C, int M, int N, int K, i
     // Each CTA stages 128 rows of A, and BN (one CTA) or BN/2 (pair) of B.
     const uint32_t b_rows = pair ? cfg.tile_n / 2 : cfg.tile_n;
     CUtensorMap ma, mb, mb_half, mc;
-    bool ok = encode_tensor_map_2d(&ma, A, K, M, static_cast<uint64_t>(K) * 2, 64, kBM);
+    bool ok = encode_tensor_map_2d(&ma, A, K, M, static_cast<uint64_t>(K) * 2, 64, cfg.tile_m == 32 ? 32 : kBM);
     if (b_layout == KMCTS_B_COL) {
         ok = ok && encode_tensor_map_2d(&mb, B, K, N, static_cast<uint64_t>(K) * 2, 64, b_rows);
         // Half-width units of a pair stage b_rows / 2 columns of B.

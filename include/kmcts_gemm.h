@@ -67,11 +67,12 @@ extern "C" {
 
 /* Kernel schedule.  Zero-initialise and call kmcts_default_config() first. */
 typedef struct kmcts_gemm_config {
-    int32_t tile_m;       /* 128: one CTA per tile; 256: one CTA pair per tile */
+    int32_t tile_m;       /* 128: one CTA per tile; 256: one CTA pair per tile;
+                             32: one CTA per tile staging 32 rows of A (M <= 32) */
     int32_t tile_n;       /* tile columns: 64, 128, 192, 256 (one CTA); 128, 256 (pair) */
     int32_t tile_k;       /* K per pipeline stage: 64 or 128 */
     int32_t stages;       /* shared-memory pipeline depth: 2..6 */
-    int32_t cluster_m;    /* 1 with tile_m 128; 2 with tile_m 256 (tcgen05 cta_group::2) */
+    int32_t cluster_m;    /* 1 with tile_m 128 or 32; 2 with tile_m 256 (tcgen05 cta_group::2) */
     int32_t cluster_n;    /* must be 1: no TMA multicast is used */
     int32_t persistent;   /* 1: one CTA per SM loops over tiles; 0: one CTA per tile */
     int32_t raster_group; /* M-tiles per raster group (L2 locality), >= 1 */
@@ -82,7 +83,7 @@ typedef struct kmcts_gemm_config {
     int32_t reserved;     /* zero */
 } kmcts_gemm_config;
 
-/* Split K (tile_m 128).  With k_splits = S > 1 each output tile runs as S
+/* Split K (tile_m 128 or 32).  With k_splits = S > 1 each output tile runs as S
  * units over consecutive K ranges, so a shape with few tiles (skinny M or N)
  * still streams its operands through every SM.  Each unit stores its FP32
  * partial in a per-stream library workspace and counts itself on the tile's
@@ -98,10 +99,11 @@ typedef struct kmcts_gemm_config {
  * x 128, 3-stage schedule that is fastest at 4096^3). Returns KMCTS_OK. */
 int kmcts_default_config(kmcts_gemm_config* cfg);
 
-/* Fills *cfg with the schedule a NULL cfg selects for this shape: the default
- * when its 256 x 256 pair tiles fill the co-resident CTA pairs; else one CTA
- * per 128 x 256 tile while those fill them (the default again from K = 4096),
- * else one CTA per 128 x 128 tile.  Every
+/* Fills *cfg with the schedule a NULL cfg selects for this shape: for M <= 32,
+ * one CTA per tile staging 32 rows of A (tile_m 32); else the default when its
+ * 256 x 256 pair tiles fill the co-resident CTA pairs; else one CTA per
+ * 128 x 256 tile while those fill them (the default again from K = 4096),
+ * else one CTA per 128 x 128 tile.  Few tiles over a long K get split K.  Every
  * schedule gives results within the parity criterion and bit-exact ones on
  * integer inputs.  Returns KMCTS_OK or KMCTS_EINVAL. */
 int kmcts_select_config(int M, int N, int K, int b_layout, kmcts_gemm_config* cfg);

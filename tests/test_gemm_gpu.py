@@ -433,7 +433,7 @@ def test_split_k_concurrent_streams_and_selection(cuda_device):
     """Skinny shapes select split K; two streams use separate workspaces."""
     m, n, k = 16, 4096, 8192
     sel = _native.select_config(m, n, k, _native.B_COL)
-    assert sel.tile_m == 128 and sel.k_splits > 1
+    assert sel.tile_m == 32 and sel.k_splits > 1
     x_a, x_b = oracle.integer_inputs(m, n, k, seed=1)
     y_a, y_b = oracle.integer_inputs(m, n, k, seed=2)
     ex = oracle.torch_bits(oracle.torch_reference(x_a, x_b))
@@ -450,3 +450,20 @@ def test_split_k_concurrent_streams_and_selection(cuda_device):
     for cx, cy in outs:
         np.testing.assert_array_equal(bits_of(cx), ex)
         np.testing.assert_array_equal(bits_of(cy), ey)
+
+
+SKINNY = [(256, 64, 5), (128, 64, 9), (128, 128, 4)]
+
+
+@pytest.mark.parametrize("layout", ["col", "row"])
+@pytest.mark.parametrize("tile_n,tile_k,stages", SKINNY)
+@pytest.mark.parametrize("shape,splits", [((1, 520, 1032), 1), ((16, 1024, 2048), 3), ((32, 264, 4096), 8),
+                                          ((7, 2048, 512), 1)])
+def test_skinny_a_rows_integer_exact(cuda_device, layout, tile_n, tile_k, stages, shape, splits):
+    """tile_m 32 stages 32 rows of A; the MMA's other 96 rows are discarded."""
+    m, n, k = shape
+    a_t, b_t = oracle.integer_inputs(m, n, k, seed=m + splits)
+    expect = oracle.torch_bits(oracle.torch_reference(a_t, b_t))
+    c = run(a_t.cuda(), b_for(layout, b_t.cuda()), layout, kernel=_native.KERNEL_TCGEN05, tile_m=32, cluster_m=1,
+            tile_n=tile_n, tile_k=tile_k, stages=stages, k_splits=splits)
+    np.testing.assert_array_equal(bits_of(c), expect)

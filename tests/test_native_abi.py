@@ -44,9 +44,20 @@ def test_version_and_default_config():
     assert km.config_legal(cfg, 4096, 4096, 4096) == (0, "ok")
 
 
+def test_skinny_a_rows_take_at_most_32_rows():
+    cfg = km.make_config(tile_m=32, cluster_m=1, tile_n=256, tile_k=64, stages=5)
+    assert km.config_legal(cfg, 32, 4096, 4096, km.B_ROW)[0] == 0
+    code, why = km.config_legal(cfg, 33, 4096, 4096, km.B_ROW)
+    assert code == _native.KMCTS_ENOTSUP and "M <= 32" in why
+    assert km.config_legal(km.make_config(tile_m=32, cluster_m=2), 16, 4096, 4096)[0] == _native.KMCTS_ENOTSUP
+
+
 def test_select_config_splits_k_for_skinny_shapes():
     cfg = km.select_config(16, 8192, 8192, km.B_ROW)
-    assert (cfg.tile_m, cfg.tile_n, cfg.k_splits) == (128, 128, 2)  # 64 tiles -> 128 units
+    assert (cfg.tile_m, cfg.tile_n, cfg.k_splits) == (32, 128, 2)  # 64 tiles -> 128 units
+    wide = km.select_config(8, 28672, 8192, km.B_ROW)
+    assert (wide.tile_m, wide.tile_n, wide.k_splits) == (32, 256, 0)  # 112 tiles: no split
+    assert km.select_config(64, 8192, 8192, km.B_ROW).tile_m == 128
     assert km.select_config(512, 512, 8192, km.B_ROW).k_splits == 4
     assert km.select_config(1024, 1024, 1024, km.B_ROW).k_splits == 0  # short K: no split
     assert km.select_config(4096, 4096, 4096, km.B_ROW).k_splits == 0
@@ -69,6 +80,7 @@ def test_select_config_splits_k_for_skinny_shapes():
         # N not a multiple of 8: no tensor-core schedule is legal; the default
         # stays and AUTO launches go to the SIMT kernel.
         ((256, 250, 256), (256, 256, 128, 3, 2)),
+        ((16, 250, 256), (256, 256, 128, 3, 2)),
     ],
 )
 def test_select_config_by_shape(shape, expect):
