@@ -2,6 +2,7 @@
 
     python -m kernel_mcts_b200.profile_gemm --M 4096 --N 4096 --K 4096 \
         --b-layout row --launches 3
+    python -m kernel_mcts_b200.profile_gemm --M 16 --N 8192 --K 8192 --select
 
 Prints one JSON line with the CUDA-event time of each launch.  Inputs are
 N(0,1) BF16 from a seeded generator on the device; nothing else runs on the
@@ -28,15 +29,19 @@ def main() -> None:
     p.add_argument("--b-layout", choices=("col", "row"), default="row")
     p.add_argument("--launches", type=int, default=3)
     p.add_argument("--kernel", choices=("auto", "tcgen05", "simt"), default="tcgen05")
-    for name in ("tile_m", "tile_n", "tile_k", "stages", "cluster_m", "persistent", "raster_group"):
+    fields = ("tile_m", "tile_n", "tile_k", "stages", "cluster_m", "persistent", "raster_group", "k_splits", "flags")
+    for name in fields:
         p.add_argument(f"--{name.replace('_', '-')}", type=int, default=None)
+    p.add_argument("--select", action="store_true", help="start from the library's schedule for the shape")
     args = p.parse_args()
 
-    overrides = {name: getattr(args, name) for name in ("tile_m", "tile_n", "tile_k", "stages", "cluster_m", "persistent", "raster_group")
-                 if getattr(args, name) is not None}
+    overrides = {name: getattr(args, name) for name in fields if getattr(args, name) is not None}
     overrides["kernel"] = {"auto": _native.KERNEL_AUTO, "tcgen05": _native.KERNEL_TCGEN05,
                            "simt": _native.KERNEL_SIMT}[args.kernel]
-    cfg = _native.make_config(**overrides)
+    layout = _native.B_ROW if args.b_layout == "row" else _native.B_COL
+    cfg = _native.select_config(args.M, args.N, args.K, layout) if args.select else _native.default_config()
+    for name, value in overrides.items():
+        setattr(cfg, name, int(value))
     device = torch.device("cuda", 0)
     g = torch.Generator(device=device).manual_seed(0)
     a = torch.randn((args.M, args.K), generator=g, device=device).to(torch.bfloat16)
