@@ -49,7 +49,9 @@ struct Layout {
     static constexpr int kBBytes = BN * BK * 2;
     static constexpr int kStageBytes = kABytes + kBBytes;
     static constexpr int kStagingOffset = STAGES * kStageBytes;
-    static constexpr int kBarrierOffset = kStagingOffset + kEpilogueWarps * 2 * kStagingBytes;
+    // With 32 rows of A only the warp of TMEM lanes 0-31 ever stores C.
+    static constexpr int kStagingWarps = AR == kBM ? kEpilogueWarps : 1;
+    static constexpr int kBarrierOffset = kStagingOffset + kStagingWarps * 2 * kStagingBytes;
     static constexpr int kSmemBytes = kBarrierOffset + kSmemReserve;
     static constexpr uint32_t kTmemCols = tmem_columns_for(2 * BN);
     static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "BN must be 64..256, step 64");
@@ -260,7 +262,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ------------------------------------------------------------ epilogue
         const int quarter = warp % 4;  // TMEM lanes this warp may access
         const int e = warp - 2;
-        uint8_t* staging = smem + L::kStagingOffset + e * 2 * kStagingBytes;
+        uint8_t* staging = smem + L::kStagingOffset + (L::kStagingWarps == 1 ? 0 : e) * 2 * kStagingBytes;
         int local = 0;
         int chunk_count = 0;
         for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++local) {
@@ -449,7 +451,8 @@ const Variant kVariants[] = {
     KMCTS_VARIANT(256, 128, 2, false), KMCTS_VARIANT(256, 128, 2, true),
     KMCTS_VARIANT(192, 64, 4, false), KMCTS_VARIANT(192, 64, 4, true),
     KMCTS_VARIANT(64, 64, 6, false),  KMCTS_VARIANT(64, 64, 6, true),
-    // tile_m 32 (M <= 32): A staged as 32 rows, more B stages in flight.
+    // tile_m 32 (M <= 32): A staged as 32 rows and one warp's epilogue
+    // staging, so more B stages are in flight.
     KMCTS_SKINNY(256, 64, 5, false),  KMCTS_SKINNY(256, 64, 5, true),
     KMCTS_SKINNY(128, 64, 9, false),  KMCTS_SKINNY(128, 64, 9, true),
     KMCTS_SKINNY(128, 128, 4, false), KMCTS_SKINNY(128, 128, 4, true),
@@ -483,7 +486,7 @@ int64_t tcgen05_smem_bytes(const kmcts_gemm_config& cfg, int b_layout) {
     if (cfg.tile_m == 256) return pair_smem_bytes(cfg.tile_n, cfg.tile_k, cfg.stages);
     if (cfg.tile_m != kBM && cfg.tile_m != 32) return 0;
     return static_cast<int64_t>(cfg.stages) * (cfg.tile_m + cfg.tile_n) * cfg.tile_k * 2 +
-           kEpilogueWarps * 2 * kStagingBytes + kSmemReserve;
+           (cfg.tile_m == 32 ? 1 : kEpilogueWarps) * 2 * kStagingBytes + kSmemReserve;
 }
 
 int tcgen05_legal(const kmcts_gemm_config& cfg, int M, int N, int K, int b_layout, char* why,

@@ -71,7 +71,7 @@ typedef struct kmcts_gemm_config {
                              32: one CTA per tile staging 32 rows of A (M <= 32) */
     int32_t tile_n;       /* tile columns: 64, 128, 192, 256 (one CTA); 128, 256 (pair) */
     int32_t tile_k;       /* K per pipeline stage: 64 or 128 */
-    int32_t stages;       /* shared-memory pipeline depth: 2..6 */
+    int32_t stages;       /* shared-memory pipeline depth: 2..6 (9 for some tile_m 32 schedules) */
     int32_t cluster_m;    /* 1 with tile_m 128 or 32; 2 with tile_m 256 (tcgen05 cta_group::2) */
     int32_t cluster_n;    /* must be 1: no TMA multicast is used */
     int32_t persistent;   /* 1: one CTA per SM loops over tiles; 0: one CTA per tile */
