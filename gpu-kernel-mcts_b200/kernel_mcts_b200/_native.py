@@ -63,6 +63,7 @@ EXPORTED_SYMBOLS = (
     "kmcts_compare_workspace_bytes",
     "kmcts_bf16_compare",
     "kmcts_launch_count",
+    "kmcts_time_gemm",
     "kmcts_gemm_plan_query",
     "kmcts_bf16_compare_noalloc",
     "kmcts_generate_inputs",
@@ -215,6 +216,9 @@ def load() -> ctypes.CDLL:
         lib.kmcts_selftest_bounded_wait.restype = i32
         lib.kmcts_launch_count.argtypes = []
         lib.kmcts_launch_count.restype = i64
+        lib.kmcts_time_gemm.argtypes = [vp, vp, vp, i32, i32, i32, i32, ctypes.POINTER(GemmConfig), vp, vp, i32, i32,
+                                        vp, ctypes.c_size_t, ctypes.POINTER(ctypes.c_float)]
+        lib.kmcts_time_gemm.restype = i32
         _lib = lib
         return lib
 

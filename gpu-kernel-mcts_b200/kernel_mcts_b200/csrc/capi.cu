@@ -166,6 +166,52 @@ const char* kmcts_version(void) { return "kmcts_gemm_sm100 0.1.0 (sm_100a tcgen0
 
 int64_t kmcts_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
+int kmcts_time_gemm(const void* A, const void* B, void* C, int M, int N, int K, int b_layout,
+                    const kmcts_gemm_config* cfg, void* stream, int* device_status, int warmups,
+                    int measurements, void* flush, size_t flush_bytes, float* timings_us) {
+    if (warmups < 0 || measurements < 1 || !timings_us || !device_status || (flush_bytes && !flush))
+        return KMCTS_EINVAL;
+    cudaStream_t s = as_stream(stream);
+    for (int i = 0; i < warmups; ++i) {
+        const int rc = kmcts_bf16_gemm_ex(A, B, C, M, N, K, b_layout, cfg, stream, device_status);
+        if (rc != KMCTS_OK) return rc;
+    }
+    if (cudaStreamSynchronize(s) != cudaSuccess) return KMCTS_ESYNC;
+    cudaEvent_t start = nullptr, stop = nullptr;
+    if (cudaEventCreate(&start) != cudaSuccess || cudaEventCreate(&stop) != cudaSuccess) {
+        if (start) cudaEventDestroy(start);
+        return KMCTS_EHANDLE;
+    }
+    int rc = KMCTS_OK;
+    for (int i = 0; i < measurements && rc == KMCTS_OK; ++i) {
+        if (flush && cudaMemsetAsync(flush, i & 0xff, flush_bytes, s) != cudaSuccess) {
+            rc = KMCTS_ESYNC;
+            break;
+        }
+        if (cudaEventRecord(start, s) != cudaSuccess) {
+            rc = KMCTS_ESYNC;
+            break;
+        }
+        rc = kmcts_bf16_gemm_ex(A, B, C, M, N, K, b_layout, cfg, stream, device_status);
+        if (rc != KMCTS_OK) break;
+        float ms = 0.0f;
+        if (cudaEventRecord(stop, s) != cudaSuccess || cudaEventSynchronize(stop) != cudaSuccess ||
+            cudaEventElapsedTime(&ms, start, stop) != cudaSuccess) {
+            rc = KMCTS_ESYNC;
+            break;
+        }
+        timings_us[i] = ms * 1000.0f;
+    }
+    cudaEventDestroy(start);
+    cudaEventDestroy(stop);
+    if (rc != KMCTS_OK) return rc;
+    int status = 0;
+    if (cudaMemcpyAsync(&status, device_status, sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+        cudaStreamSynchronize(s) != cudaSuccess)
+        return KMCTS_ESYNC;
+    return status == 0 ? KMCTS_OK : KMCTS_ETIMEOUT;
+}
+
 int64_t kmcts_config_smem_bytes(const kmcts_gemm_config* cfg, int b_layout) {
     if (!cfg) return 0;
     return tcgen05_smem_bytes(*cfg, b_layout);

@@ -127,6 +127,19 @@ class PreparedGemm:
         if rc != 0:
             _native.check(rc, "kmcts_bf16_gemm_ex")
 
+    def time(self, warmups: int, measurements: int, flush: torch.Tensor | None = None) -> list[float]:
+        """The reference harness's benchmark protocol, run by the library:
+        warm-ups, one synchronise, then one event pair and synchronise per
+        launch (``kmcts_time_gemm``).  Needs a status tensor.  Returns µs."""
+        if self._args[-1] is None:
+            raise ValueError("timing needs a status tensor")
+        out = (ctypes.c_float * measurements)()
+        flush_args = (ctypes.c_void_p(flush.data_ptr()), flush.numel() * flush.element_size()) if flush is not None \
+            else (None, 0)
+        rc = _native.load().kmcts_time_gemm(*self._args, warmups, measurements, *flush_args, out)
+        _native.check(rc, "kmcts_time_gemm")
+        return [float(v) for v in out]
+
 
 def bf16_gemm_sync(a: torch.Tensor, b_nk: torch.Tensor, out: torch.Tensor) -> int:
     """The drop-in entry point (column-major B, default stream, synchronising).

@@ -183,25 +183,18 @@ class InProcessSm100Backend:
 
     def _benchmark_shape(self, artifact: ScheduleArtifact, workload: WorkloadContract, dimensions) -> BenchmarkResult:
         torch = self.torch
-        stream = torch.cuda.current_stream(self.device)
         if self.flush_l2 and self._flush is None:
             self._flush = torch.empty(512 << 20, dtype=torch.uint8, device=self.device)
-        for _ in range(self.warmup_count):
-            self._launch(artifact, workload, dimensions)
-        torch.cuda.synchronize(self.device)
-        timings = []
         prepared = self._prepared(artifact, workload, dimensions)
-        events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-                  for _ in range(self.measurement_count)]
-        for i, (start, stop) in enumerate(events):
-            if self._flush is not None:
-                self._flush.fill_(i & 0xFF)
-            start.record(stream)
-            prepared.launch()
-            stop.record(stream)
-            stop.synchronize()
-            timings.append(start.elapsed_time(stop) * 1e3)
-        self._check_status()
+        # The harness protocol, looped in the library: no interpreter work
+        # between a start event and its launch.
+        try:
+            timings = prepared.time(self.warmup_count, self.measurement_count, self._flush)
+        except _native.KmctsError as error:
+            if error.code == _native.KMCTS_ETIMEOUT:
+                self._status.zero_()
+                raise CandidateLaunchError(f"device-side wait gave up ({error})") from error
+            raise CandidateLaunchError(str(error)) from error
         return BenchmarkResult(
             timings_us=tuple(timings), median_us=statistics.median(timings), warmup_count=self.warmup_count,
             mean_us=statistics.fmean(timings), stddev_us=statistics.pstdev(timings), min_us=min(timings),

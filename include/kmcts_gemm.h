@@ -253,6 +253,19 @@ int kmcts_selftest_bounded_wait(int64_t limit_ns, int arrive, void* stream, int*
  * points).  Lets callers count GPU launches inside a timed region. */
 int64_t kmcts_launch_count(void);
 
+/* Times kmcts_bf16_gemm_ex with the reference harness's benchmark protocol
+ * (src/kernel_mcts/benchmarks/kernels/bf16_gemm_harness.cu:177-215):
+ * `warmups` launches, one synchronise, then `measurements` x (event record,
+ * launch, event record, event synchronise), writing each launch's time in
+ * microseconds to timings_us[0..measurements).  If flush is not NULL,
+ * flush_bytes of it are overwritten before every timed launch, outside the
+ * events (an L2 flush).  Synchronous.  Returns KMCTS_OK, the launch's error,
+ * KMCTS_ESYNC, or KMCTS_ETIMEOUT when device_status (required) reports a
+ * bounded wait that gave up. */
+int kmcts_time_gemm(const void* A, const void* B, void* C, int M, int N, int K, int b_layout,
+                    const kmcts_gemm_config* cfg, void* stream, int* device_status, int warmups,
+                    int measurements, void* flush, size_t flush_bytes, float* timings_us);
+
 #ifdef __cplusplus
 }
 #endif

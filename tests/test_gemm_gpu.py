@@ -467,3 +467,21 @@ def test_skinny_a_rows_integer_exact(cuda_device, layout, tile_n, tile_k, stages
     c = run(a_t.cuda(), b_for(layout, b_t.cuda()), layout, kernel=_native.KERNEL_TCGEN05, tile_m=32, cluster_m=1,
             tile_n=tile_n, tile_k=tile_k, stages=stages, k_splits=splits)
     np.testing.assert_array_equal(bits_of(c), expect)
+
+
+def test_library_timing_loop_matches_the_protocol(cuda_device):
+    """kmcts_time_gemm: warm-ups, then one event pair per launch; the times are
+    positive and the GEMM's result is the same as a plain launch's."""
+    m = n = k = 1024
+    a_t, b_t = oracle.integer_inputs(m, n, k, seed=3)
+    a, b = a_t.cuda(), b_t.cuda()
+    c = torch.empty((m, n), dtype=torch.bfloat16, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    launches = _native.launch_count()
+    prepared = kg.PreparedGemm(a, b, c, config=_native.make_config(), status=status)
+    times = prepared.time(3, 7)
+    assert len(times) == 7 and all(t > 0 for t in times)
+    assert _native.launch_count() - launches == 10
+    flush = torch.empty(64 << 20, dtype=torch.uint8, device="cuda")
+    assert len(prepared.time(0, 2, flush)) == 2
+    np.testing.assert_array_equal(bits_of(c), oracle.torch_bits(oracle.torch_reference(a_t, b_t)))
