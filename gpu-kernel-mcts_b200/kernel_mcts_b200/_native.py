@@ -64,6 +64,7 @@ EXPORTED_SYMBOLS = (
     "kmcts_bf16_compare",
     "kmcts_launch_count",
     "kmcts_time_gemm",
+    "kmcts_bf16_gemm_host",
     "kmcts_gemm_plan_query",
     "kmcts_bf16_compare_noalloc",
     "kmcts_generate_inputs",
@@ -219,6 +220,9 @@ def load() -> ctypes.CDLL:
         lib.kmcts_time_gemm.argtypes = [vp, vp, vp, i32, i32, i32, i32, ctypes.POINTER(GemmConfig), vp, vp, i32, i32,
                                         vp, ctypes.c_size_t, ctypes.POINTER(ctypes.c_float)]
         lib.kmcts_time_gemm.restype = i32
+        lib.kmcts_bf16_gemm_host.argtypes = [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, ctypes.POINTER(GemmConfig),
+                                             i32, vp, vp]
+        lib.kmcts_bf16_gemm_host.restype = i32
         _lib = lib
         return lib
 

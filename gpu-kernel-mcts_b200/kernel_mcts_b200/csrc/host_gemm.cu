@@ -1,0 +1,106 @@
+// C = A·B for operands in host memory: the copies over PCIe and the GEMM
+// overlap.  B goes to the device first; A then follows in row blocks, and each
+// block's GEMM starts as soon as its rows have landed, while the next block is
+// still in flight; each block's C rows go back while later blocks compute.
+// Host-to-device copies run on one internal stream, device-to-host copies on
+// another (the two directions of the link), the GEMMs on the caller's stream,
+// ordered by events; the caller's stream waits for the last copy back, so the
+// call is asynchronous on `stream` like every other entry point.
+#include <mutex>
+
+#include "kmcts_internal.h"
+
+namespace kmcts {
+namespace {
+
+constexpr int kMaxDevices = 64;
+
+struct CopyStreams {
+    cudaStream_t in = nullptr, out = nullptr;
+};
+
+bool copy_streams(CopyStreams* out) {
+    static std::mutex mu;
+    static CopyStreams streams[kMaxDevices];
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kMaxDevices) return false;
+    std::lock_guard<std::mutex> lock(mu);
+    CopyStreams& s = streams[device];
+    if (!s.in) {
+        if (cudaStreamCreateWithFlags(&s.in, cudaStreamNonBlocking) != cudaSuccess) return false;
+        if (cudaStreamCreateWithFlags(&s.out, cudaStreamNonBlocking) != cudaSuccess) {
+            cudaStreamDestroy(s.in);
+            s.in = nullptr;
+            return false;
+        }
+    }
+    *out = s;
+    return true;
+}
+
+}  // namespace
+}  // namespace kmcts
+
+using namespace kmcts;
+
+extern "C" int kmcts_bf16_gemm_host(const void* A_host, const void* B_host, void* C_host, void* A_dev, void* B_dev,
+                                    void* C_dev, int M, int N, int K, int b_layout, const kmcts_gemm_config* cfg,
+                                    int chunks, void* stream, int* device_status) {
+    if (M < 0 || N < 0 || K < 0 || (b_layout != KMCTS_B_COL && b_layout != KMCTS_B_ROW)) return KMCTS_EINVAL;
+    if (M == 0 || N == 0) return KMCTS_OK;
+    if (!A_host || !B_host || !C_host || !A_dev || !B_dev || !C_dev) return KMCTS_EINVAL;
+    if (chunks <= 0) chunks = 8;
+    const int rows = (((M + chunks - 1) / chunks) + 127) / 128 * 128;  // whole 128-row tiles per block
+    chunks = (M + rows - 1) / rows;
+    CopyStreams cs;
+    if (!copy_streams(&cs)) return KMCTS_EHANDLE;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const size_t a_row = static_cast<size_t>(K) * 2, c_row = static_cast<size_t>(N) * 2;
+    int rc = KMCTS_OK;
+    cudaEvent_t start = nullptr, done_out = nullptr;
+    const unsigned flags = cudaEventDisableTiming;
+    if (cudaEventCreateWithFlags(&start, flags) != cudaSuccess || cudaEventCreateWithFlags(&done_out, flags) != cudaSuccess)
+        rc = KMCTS_EHANDLE;
+    // The copies start after the work already queued on the caller's stream.
+    if (rc == KMCTS_OK && (cudaEventRecord(start, s) != cudaSuccess || cudaStreamWaitEvent(cs.in, start, 0) != cudaSuccess ||
+                           cudaStreamWaitEvent(cs.out, start, 0) != cudaSuccess))
+        rc = KMCTS_ESYNC;
+    if (rc == KMCTS_OK &&
+        cudaMemcpyAsync(B_dev, B_host, static_cast<size_t>(K) * N * 2, cudaMemcpyHostToDevice, cs.in) != cudaSuccess)
+        rc = KMCTS_ESYNC;
+    for (int i = 0; i < chunks && rc == KMCTS_OK; ++i) {
+        const int r0 = i * rows;
+        const int mi = M - r0 < rows ? M - r0 : rows;
+        cudaEvent_t landed = nullptr, computed = nullptr;
+        if (cudaEventCreateWithFlags(&landed, flags) != cudaSuccess ||
+            cudaEventCreateWithFlags(&computed, flags) != cudaSuccess) {
+            if (landed) cudaEventDestroy(landed);
+            rc = KMCTS_EHANDLE;
+            break;
+        }
+        const char* a_src = static_cast<const char*>(A_host) + r0 * a_row;
+        char* a_dst = static_cast<char*>(A_dev) + r0 * a_row;
+        char* c_dev = static_cast<char*>(C_dev) + r0 * c_row;
+        char* c_dst = static_cast<char*>(C_host) + r0 * c_row;
+        if (K > 0 && cudaMemcpyAsync(a_dst, a_src, mi * a_row, cudaMemcpyHostToDevice, cs.in) != cudaSuccess)
+            rc = KMCTS_ESYNC;
+        if (rc == KMCTS_OK && (cudaEventRecord(landed, cs.in) != cudaSuccess || cudaStreamWaitEvent(s, landed, 0) != cudaSuccess))
+            rc = KMCTS_ESYNC;
+        if (rc == KMCTS_OK) rc = kmcts_bf16_gemm_ex(a_dst, B_dev, c_dev, mi, N, K, b_layout, cfg, s, device_status);
+        if (rc == KMCTS_OK && (cudaEventRecord(computed, s) != cudaSuccess ||
+                               cudaStreamWaitEvent(cs.out, computed, 0) != cudaSuccess ||
+                               cudaMemcpyAsync(c_dst, c_dev, mi * c_row, cudaMemcpyDeviceToHost, cs.out) != cudaSuccess))
+            rc = KMCTS_ESYNC;
+        cudaEventDestroy(landed);  // released once the recorded work completes
+        cudaEventDestroy(computed);
+    }
+    // The caller's stream ends with the last copy back (also on an error
+    // part-way, so nothing outlives the call unordered).
+    if (done_out) {
+        if (cudaEventRecord(done_out, cs.out) != cudaSuccess || cudaStreamWaitEvent(s, done_out, 0) != cudaSuccess)
+            rc = rc == KMCTS_OK ? KMCTS_ESYNC : rc;
+        cudaEventDestroy(done_out);
+    }
+    if (start) cudaEventDestroy(start);
+    return rc;
+}

@@ -141,6 +141,42 @@ class PreparedGemm:
         return [float(v) for v in out]
 
 
+def bf16_gemm_host(
+    a_host: torch.Tensor,
+    b_host: torch.Tensor,
+    c_host: torch.Tensor,
+    a_dev: torch.Tensor,
+    b_dev: torch.Tensor,
+    c_dev: torch.Tensor,
+    *,
+    b_layout: str | int = "col",
+    config: GemmConfig | None = None,
+    chunks: int = 0,
+    stream: torch.cuda.Stream | None = None,
+    status: torch.Tensor | None = None,
+) -> None:
+    """C = A·B with A, B, C in (pinned) host tensors, through the caller's
+    device tensors of the same shapes; copies and GEMM blocks overlap
+    (``kmcts_bf16_gemm_host``).  Asynchronous on ``stream``."""
+    code = layout_code(b_layout)
+    m, n, k = gemm_shapes(a_host, b_host, code)
+    for name, t in (("A", a_host), ("B", b_host), ("C", c_host)):
+        if t.is_cuda or t.dtype != torch.bfloat16 or not t.is_contiguous():
+            raise ValueError(f"{name} host tensor must be a contiguous bfloat16 CPU tensor")
+    if tuple(c_host.shape) != (m, n):
+        raise ValueError(f"C must have shape {(m, n)}")
+    _check_operand("A", a_dev, (m, k))
+    _check_operand("B", b_dev, (n, k) if code == B_COL else (k, n))
+    _check_operand("C", c_dev, (m, n))
+    if stream is None:
+        stream = torch.cuda.current_stream(a_dev.device)
+    rc = _native.load().kmcts_bf16_gemm_host(
+        a_host.data_ptr(), b_host.data_ptr(), c_host.data_ptr(), a_dev.data_ptr(), b_dev.data_ptr(),
+        c_dev.data_ptr(), m, n, k, code, ctypes.byref(config) if config is not None else None, chunks,
+        stream.cuda_stream, status.data_ptr() if status is not None else None)
+    _native.check(rc, "kmcts_bf16_gemm_host")
+
+
 def bf16_gemm_sync(a: torch.Tensor, b_nk: torch.Tensor, out: torch.Tensor) -> int:
     """The drop-in entry point (column-major B, default stream, synchronising).
 
@@ -225,6 +261,7 @@ __all__ = [
     "KmctsError",
     "PreparedGemm",
     "bf16_gemm",
+    "bf16_gemm_host",
     "bf16_gemm_sync",
     "compare",
     "gemm_shapes",

@@ -253,6 +253,20 @@ int kmcts_selftest_bounded_wait(int64_t limit_ns, int arrive, void* stream, int*
  * points).  Lets callers count GPU launches inside a timed region. */
 int64_t kmcts_launch_count(void);
 
+/* C = A·B with A, B and C in host memory (page-locked, or the copies do not
+ * overlap), through device buffers the caller owns: A_dev [M,K], B_dev (as
+ * b_layout), C_dev [M,N].  No counterpart in the reference, whose harness
+ * copies inputs and results around the timed region.  B is copied first,
+ * then A in `chunks` row blocks (<= 0: 8; whole 128-row tiles per block):
+ * each block's GEMM starts when its rows have landed and its C rows go back
+ * while later blocks compute, so both copy directions and the GEMMs overlap.
+ * Internal copy streams wait for the work already on `stream`, and `stream`
+ * waits for the last copy back: asynchronous on `stream`, complete when it
+ * is.  cfg as for kmcts_bf16_gemm_ex (per block). */
+int kmcts_bf16_gemm_host(const void* A_host, const void* B_host, void* C_host, void* A_dev, void* B_dev,
+                         void* C_dev, int M, int N, int K, int b_layout, const kmcts_gemm_config* cfg,
+                         int chunks, void* stream, int* device_status);
+
 /* Times kmcts_bf16_gemm_ex with the reference harness's benchmark protocol
  * (src/kernel_mcts/benchmarks/kernels/bf16_gemm_harness.cu:177-215):
  * `warmups` launches, one synchronise, then `measurements` x (event record,

@@ -485,3 +485,25 @@ def test_library_timing_loop_matches_the_protocol(cuda_device):
     flush = torch.empty(64 << 20, dtype=torch.uint8, device="cuda")
     assert len(prepared.time(0, 2, flush)) == 2
     np.testing.assert_array_equal(bits_of(c), oracle.torch_bits(oracle.torch_reference(a_t, b_t)))
+
+
+@pytest.mark.parametrize("layout", ["col", "row"])
+@pytest.mark.parametrize("shape,chunks", [((1000, 520, 264), 3), ((4096, 1024, 512), 0), ((64, 256, 128), 8)])
+def test_host_buffer_gemm_overlapped_copies(cuda_device, layout, shape, chunks):
+    """kmcts_bf16_gemm_host: pinned host operands, device buffers, row blocks
+    whose copies and GEMMs overlap; the host C is exact on integer inputs."""
+    m, n, k = shape
+    a_t, b_t = oracle.integer_inputs(m, n, k, seed=m % 7)
+    b_host = (b_t if layout == "col" else b_t.T.contiguous()).pin_memory()
+    a_host = a_t.pin_memory()
+    c_host = torch.empty((m, n), dtype=torch.bfloat16).pin_memory()
+    a_dev = torch.empty_like(a_host, device="cuda")
+    b_dev = torch.empty_like(b_host, device="cuda")
+    c_dev = torch.empty((m, n), dtype=torch.bfloat16, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    stream = torch.cuda.Stream()
+    kg.bf16_gemm_host(a_host, b_host, c_host, a_dev, b_dev, c_dev, b_layout=layout, chunks=chunks,
+                      stream=stream, status=status)
+    stream.synchronize()
+    assert int(status.item()) == 0
+    np.testing.assert_array_equal(oracle.torch_bits(c_host), oracle.torch_bits(oracle.torch_reference(a_t, b_t)))
