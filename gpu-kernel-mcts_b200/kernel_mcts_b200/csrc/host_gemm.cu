@@ -49,7 +49,7 @@ extern "C" int kmcts_bf16_gemm_host(const void* A_host, const void* B_host, void
     if (M < 0 || N < 0 || K < 0 || (b_layout != KMCTS_B_COL && b_layout != KMCTS_B_ROW)) return KMCTS_EINVAL;
     if (M == 0 || N == 0) return KMCTS_OK;
     if (!A_host || !B_host || !C_host || !A_dev || !B_dev || !C_dev) return KMCTS_EINVAL;
-    if (chunks <= 0) chunks = 8;
+    if (chunks <= 0) chunks = 4;  // measured at 4096^3: 4 blocks 1.58 ms, 2 1.65, 8 1.61, 16 1.71, 1 1.93
     const int rows = (((M + chunks - 1) / chunks) + 127) / 128 * 128;  // whole 128-row tiles per block
     chunks = (M + rows - 1) / rows;
     CopyStreams cs;

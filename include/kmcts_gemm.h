@@ -257,7 +257,7 @@ int64_t kmcts_launch_count(void);
  * overlap), through device buffers the caller owns: A_dev [M,K], B_dev (as
  * b_layout), C_dev [M,N].  No counterpart in the reference, whose harness
  * copies inputs and results around the timed region.  B is copied first,
- * then A in `chunks` row blocks (<= 0: 8; whole 128-row tiles per block):
+ * then A in `chunks` row blocks (<= 0: 4; whole 128-row tiles per block):
  * each block's GEMM starts when its rows have landed and its C rows go back
  * while later blocks compute, so both copy directions and the GEMMs overlap.
  * Internal copy streams wait for the work already on `stream`, and `stream`
