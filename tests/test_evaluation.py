@@ -223,3 +223,200 @@ def test_backend_plugs_into_the_reference_evaluator(tmp_path):
     result = evaluator.evaluate(ref_domain.KernelProgram(ROOT_SOURCE), ref_workload)
     assert result.status.value == "VALID", result
     assert result.reward == pytest.approx(math.log(100.0 / 11.0))
+
+
+def test_reference_sequential_loop_runs_on_the_b200_backend(tmp_path):
+    """The reference's own sequential refinement loop
+    (src/kernel_mcts/sequential.py:77-288) runs unchanged with its own
+    BackendKernelEvaluator over CudaSm100Backend (fake runner: no GPU, no
+    nvcc, no ncu) and a scripted generator: it evaluates, profiles and
+    accepts candidates, and the best node is the fastest one."""
+    if not REFERENCE_SRC.exists():
+        pytest.skip("reference source tree not present")
+    sys.path.insert(0, str(REFERENCE_SRC))
+    try:
+        from kernel_mcts import domain as ref_domain
+        from kernel_mcts.evaluation import BackendKernelEvaluator as RefEvaluator
+        from kernel_mcts.evaluation import EvaluationContext as RefContext
+        from kernel_mcts.generation import GenerationResult
+        from kernel_mcts.sequential import SequentialConfig, run_sequential_loop
+    except Exception as error:  # the reference needs packages this image may lack
+        pytest.skip(f"reference sequential loop not importable: {error}")
+    finally:
+        sys.path.remove(str(REFERENCE_SRC))
+    import json
+
+    from kernel_mcts_b200.profiling import resolve_metric_set
+    from test_backend import FakeRunner, LAUNCHER_SOURCE, ROOT_SOURCE, make_backend
+
+    class Runner(FakeRunner):
+        """Compiles each candidate into distinct executable bytes (its source)."""
+
+        def __call__(self, command, *, timeout, env):
+            out = super().__call__(command, timeout=timeout, env=env)
+            command = list(command)
+            if "-o" in command and command[0].endswith("nvcc"):
+                source = next(c for c in command if c.endswith("candidate.cu"))
+                Path(command[command.index("-o") + 1]).write_bytes(Path(source).read_bytes())
+            return out
+
+    runner = Runner()
+    metrics = resolve_metric_set("lightweight_v1", "sm_100a").metrics
+    runner.ncu_stdout = "\n".join(['"ID","Kernel Name","Metric Name","Metric Unit","Metric Value"'] +
+                                  [f'"0","bf16_gemm_launch","{m}","u","{i + 1}"' for i, m in enumerate(metrics)])
+    backend = make_backend(tmp_path, runner)
+    # The root times 11 us; each candidate the generator proposes is faster.
+    speeds = iter([11.0, 8.0, 6.0, 5.0])
+    real_execute = backend._execute
+
+    def execute(artifact, workload, mode, dimensions=None):
+        if mode == "benchmark" and "candidate" in " ".join(artifact.extra_args):
+            t = next(speeds, 5.0)
+            runner.benchmark_stdout = json.dumps({"status": "ok", "timings_us": [t, t, t]})
+        return real_execute(artifact, workload, mode, dimensions)
+
+    backend._execute = execute
+    ref_workload = ref_domain.WorkloadContract(
+        benchmark_id="bf16_gemm_4096_b200", operation="gemm", dtype="bfloat16",
+        shapes=(ref_domain.ShapeCase({"M": 4096, "N": 4096, "K": 4096}, 1.0),), rtol=0.02, atol=0.02,
+        metadata=dict(BF16_GEMM_4096_B200.metadata),
+    )
+    evaluator = RefEvaluator(backend=backend, root_benchmark=ref_domain.BenchmarkResult((11.0,), 11.0),
+                             context=RefContext("w", "m", {}, {}))
+    root = evaluator.evaluate(ref_domain.KernelProgram(ROOT_SOURCE), ref_workload)
+    assert root.status.value == "VALID", root
+
+    class Generator:
+        def __init__(self):
+            self.calls = 0
+
+        def generate(self, request):
+            self.calls += 1
+            source = LAUNCHER_SOURCE + f"\nstatic const int kCandidate = {self.calls};\n"
+            return GenerationResult(f"g{self.calls}", source, ref_domain.KernelProgram(source), f"h{self.calls}")
+
+    class Trace:
+        def __init__(self):
+            self.events = []
+
+        def emit(self, kind, payload):
+            self.events.append(kind)
+
+        def start_run(self, *args, **kwargs):
+            pass
+
+        def store_compiler_artifact(self, sha256, content):
+            pass
+
+        def get_node_dataflow(self, node_id):
+            return None
+
+    trace = Trace()
+    result = run_sequential_loop(
+        root_evaluation=root, workload=ref_workload, hardware={"gpu": "B200"}, generator=Generator(),
+        evaluator=evaluator, profiler=evaluator, trace=trace, generation_budget=3,
+        config=SequentialConfig(compiler_detail="none", dataflow_view="none"),
+    )
+    assert result.generations == 3 and result.accepted_depth >= 1
+    assert result.best.evaluation.benchmark.median_us == 5.0
+    assert result.profile_calls >= 2  # the root and accepted candidates were profiled through ncu
+    assert trace.events[0] == "run_started" and trace.events[-1] == "run_completed"
+    assert "new_global_best" in trace.events
+
+
+def _reference_search_setup(tmp_path):
+    """The reference's evaluator over CudaSm100Backend with a fake runner whose
+    candidates get faster one by one, plus a scripted generator."""
+    sys.path.insert(0, str(REFERENCE_SRC))
+    try:
+        from kernel_mcts import domain as ref_domain
+        from kernel_mcts.evaluation import BackendKernelEvaluator as RefEvaluator
+        from kernel_mcts.evaluation import EvaluationContext as RefContext
+        from kernel_mcts.generation import GenerationResult
+    finally:
+        sys.path.remove(str(REFERENCE_SRC))
+    import json
+
+    from kernel_mcts_b200.profiling import resolve_metric_set
+    from test_backend import FakeRunner, LAUNCHER_SOURCE, ROOT_SOURCE, make_backend
+
+    class Runner(FakeRunner):
+        def __call__(self, command, *, timeout, env):
+            out = super().__call__(command, timeout=timeout, env=env)
+            command = list(command)
+            if "-o" in command and command[0].endswith("nvcc"):
+                source = next(c for c in command if c.endswith("candidate.cu"))
+                Path(command[command.index("-o") + 1]).write_bytes(Path(source).read_bytes())
+            return out
+
+    runner = Runner()
+    metrics = resolve_metric_set("lightweight_v1", "sm_100a").metrics
+    runner.ncu_stdout = "\n".join(['"ID","Kernel Name","Metric Name","Metric Unit","Metric Value"'] +
+                                   [f'"0","bf16_gemm_launch","{m}","u","{i + 1}"' for i, m in enumerate(metrics)])
+    backend = make_backend(tmp_path, runner)
+    times = iter([11.0] + [10.0 - 0.5 * i for i in range(40)])
+    real_execute = backend._execute
+
+    def execute(artifact, workload, mode, dimensions=None):
+        if mode == "benchmark":
+            t = next(times)
+            runner.benchmark_stdout = json.dumps({"status": "ok", "timings_us": [t, t, t]})
+        return real_execute(artifact, workload, mode, dimensions)
+
+    backend._execute = execute
+    workload = ref_domain.WorkloadContract(
+        benchmark_id="bf16_gemm_4096_b200", operation="gemm", dtype="bfloat16",
+        shapes=(ref_domain.ShapeCase({"M": 4096, "N": 4096, "K": 4096}, 1.0),), rtol=0.02, atol=0.02,
+        metadata=dict(BF16_GEMM_4096_B200.metadata),
+    )
+    evaluator = RefEvaluator(backend=backend, root_benchmark=ref_domain.BenchmarkResult((11.0,), 11.0),
+                             context=RefContext("w", "m", {}, {}))
+    root = evaluator.evaluate(ref_domain.KernelProgram(ROOT_SOURCE), workload)
+
+    class Generator:
+        def __init__(self):
+            self.calls = 0
+
+        def generate(self, request):
+            self.calls += 1
+            source = LAUNCHER_SOURCE + f"\nstatic const int kCandidate = {self.calls};\n"
+            return GenerationResult(f"g{self.calls}", source, ref_domain.KernelProgram(source), f"h{self.calls}")
+
+    return ref_domain, evaluator, root, workload, Generator()
+
+
+def test_reference_mcts_runs_on_the_b200_backend_with_pool_drift_probes(tmp_path):
+    """The reference's MCTS (src/kernel_mcts/search/mcts.py) runs unchanged over
+    its own evaluator on CudaSm100Backend, with PoolDriftMonitor (here over the
+    same evaluator) as its measurement-drift probe."""
+    if not REFERENCE_SRC.exists():
+        pytest.skip("reference source tree not present")
+    try:
+        ref_domain, evaluator, root, workload, generator = _reference_search_setup(tmp_path)
+        sys.path.insert(0, str(REFERENCE_SRC))
+        from kernel_mcts.budget import GenerationBudget
+        from kernel_mcts.search.mcts import MCTS, MCTSConfig
+    except Exception as error:  # the reference needs packages this image may lack
+        pytest.skip(f"reference MCTS not importable: {error}")
+    finally:
+        if str(REFERENCE_SRC) in sys.path:
+            sys.path.remove(str(REFERENCE_SRC))
+    from kernel_mcts_b200.autotune import PoolDriftMonitor
+
+    class UniformPriors:
+        name = "uniform"
+        counts_toward_b_prior = False
+
+        def get_priors(self, program, workload, strategies, profile):
+            return {s.id: 1.0 / len(strategies) for s in strategies}
+
+    strategies = [ref_domain.Strategy(f"s{i}", f"strategy {i}", {"cuda_cpp": f"try {i}"}) for i in range(3)]
+    drift = PoolDriftMonitor(evaluator)
+    search = MCTS(strategies=strategies, workload=workload, generator=generator, evaluator=evaluator,
+                  prior_provider=UniformPriors(), budget=GenerationBudget(5), hardware={"gpu": "B200"},
+                  config=MCTSConfig(measurement_drift_interval=1), seed=1, profiler=evaluator,
+                  drift_monitor=drift)
+    assert root.status.value == "VALID"
+    result = search.run(root)
+    assert result.best.reward > root.reward  # a faster candidate was found and kept
+    assert generator.calls == 5 and drift.calls == result.drift_probe_calls >= 1
