@@ -69,6 +69,21 @@ class WorkloadContract:
 
 
 @dataclass(frozen=True, slots=True)
+class Strategy:
+    """A search strategy: an id, a description and one prompt per backend."""
+
+    id: str
+    description: str
+    prompts: Mapping[str, str]
+
+    def prompt_for(self, backend: str) -> str:
+        try:
+            return self.prompts[backend]
+        except KeyError as error:
+            raise ValueError(f"strategy {self.id!r} has no prompt for {backend!r}") from error
+
+
+@dataclass(frozen=True, slots=True)
 class KernelProgram:
     source: str
     backend: str = "cuda_cpp"
