@@ -286,7 +286,8 @@ class CudaSm100Backend:
         resolved = cfg.as_dict()
         args = tuple(
             f"--{name.replace('_', '-')}={resolved[name]}"
-            for name in ("tile_m", "cluster_m", "tile_n", "tile_k", "stages", "persistent", "raster_group", "k_splits")
+            for name in ("tile_m", "cluster_m", "cluster_n", "tile_n", "tile_k", "stages", "persistent", "raster_group",
+                         "k_splits")
         ) + ("--kernel=tcgen05",)
         digest = hashlib.sha256()
         digest.update(harness.read_bytes())

@@ -34,11 +34,11 @@ struct TileCoord {
 
 // Grouped rasterisation: tiles walk `group` M-blocks down a column strip
 // before moving right, so concurrently running CTAs share A and B panels in L2.
-__device__ __forceinline__ TileCoord tile_coord(int t, int num_m, int num_n, int group) {
+__host__ __device__ __forceinline__ TileCoord tile_coord(int t, int num_m, int num_n, int group) {
     const int per_group = group * num_n;
     const int g = t / per_group;
     const int first_m = g * group;
-    const int rows = min(num_m - first_m, group);
+    const int rows = num_m - first_m < group ? num_m - first_m : group;
     const int r = t - g * per_group;
     return {first_m + r % rows, r / rows};
 }

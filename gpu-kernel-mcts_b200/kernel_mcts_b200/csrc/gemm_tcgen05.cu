@@ -31,6 +31,23 @@ namespace kmcts {
 
 __device__ int g_default_status;
 
+int* default_status_ptr() {
+    // Device code of other translation units cannot name this symbol (the
+    // library is built without relocatable device code), so launches there
+    // get its address from here; one address per device.
+    static std::mutex mu;
+    static int* cached[64] = {};
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= 64) return nullptr;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!cached[device]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_default_status) != cudaSuccess) return nullptr;
+        cached[device] = static_cast<int*>(p);
+    }
+    return cached[device];
+}
+
 namespace {
 
 using namespace gemm;
@@ -515,10 +532,14 @@ int tcgen05_legal(const kmcts_gemm_config& cfg, int M, int N, int K, int b_layou
         put_reason(why, len, "cluster dimensions must be positive");
         return KMCTS_EINVAL;
     }
-    if (cfg.cluster_n != 1) {
+    if (cfg.cluster_n != 1 && !(cfg.cluster_n == 2 && cfg.tile_m == 256)) {
         put_reason(why, len,
-                   "cluster_n > 1 only pays with a TMA multicast of A across the cluster, "
-                   "which this library never issues");
+                   "cluster_n 2 takes tile_m 256 (two CTA pairs sharing A); one-CTA schedules and larger "
+                   "clusters would need a TMA multicast, which this library never issues");
+        return KMCTS_ENOTSUP;
+    }
+    if (cfg.cluster_n == 2 && (cfg.tile_n != 256 || cfg.tile_k != 128 || cfg.stages != 3)) {
+        put_reason(why, len, "cluster_n 2 is compiled for tile_n 256, tile_k 128, 3 stages");
         return KMCTS_ENOTSUP;
     }
     if (is_one_cta(cfg)) {
@@ -548,7 +569,7 @@ int tcgen05_legal(const kmcts_gemm_config& cfg, int M, int N, int K, int b_layou
         put_reason(why, len, "shared memory per CTA exceeds 227 KB");
         return KMCTS_ESMEM;
     }
-    const bool compiled = is_pair(cfg) ? pair_variant_exists(cfg.tile_n, cfg.tile_k, cfg.stages, b_layout)
+    const bool compiled = is_pair(cfg) ? pair_variant_exists(cfg, b_layout)
                                        : find_variant(cfg, b_layout) != nullptr;
     if (!compiled) {
         put_reason(why, len, "schedule (tile_m, tile_n, tile_k, stages) is not compiled in");
@@ -610,7 +631,7 @@ int launch_allgather_tcgen05(const void* A, const void* B_shard, void* const* C_
         N_total < 0 || K < 0 || N_total % num_ranks != 0)
         return KMCTS_EINVAL;
     const int n_shard = N_total / num_ranks;
-    if (n_shard % 256 != 0 || !is_pair(cfg)) return KMCTS_ENOTSUP;
+    if (n_shard % 256 != 0 || !is_pair(cfg) || cfg.cluster_n != 1) return KMCTS_ENOTSUP;
     int rc = tcgen05_legal(cfg, M, n_shard, K, b_layout, nullptr, 0);
     if (rc != KMCTS_OK) return rc;
     void* own = C_ranks[rank];

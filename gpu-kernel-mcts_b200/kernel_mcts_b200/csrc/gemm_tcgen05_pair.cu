@@ -27,8 +27,6 @@
 
 namespace kmcts {
 
-extern __device__ int g_default_status;
-
 namespace {
 
 using namespace gemm;
@@ -171,6 +169,47 @@ __device__ __forceinline__ Unit schedule_unit(const Schedule& s, int i, const Ta
     return out;
 }
 
+// Slot schedule (cluster_n 2).  The grid is cut into slots of four CTAs
+// (blocks 4s .. 4s + 3); slot s walks super tiles of 256 rows x 2 BN columns
+// round-robin, and pair p of the slot (blocks 4s + 2p, 4s + 2p + 1) computes
+// the BN-wide half p.  A super tile whose second half lies past N runs as two
+// BN/2-wide halves of its one tile.  The last partial wave splits like
+// kTailSplitN: each of its super tiles becomes two units on two slots, unit h
+// covering tile 2 n + h as two BN/2-wide halves; a unit with no tile is
+// dropped.  Both pairs of a slot always run the same rows of A over the same
+// K blocks, which is what lets a 4-CTA cluster share A.
+__device__ __forceinline__ Schedule make_slot_schedule(int M, int N, int K, int BN, int BK, int group,
+                                                       int full_tiles, int slot, int slots, const TailSplit& tail) {
+    Schedule s = make_schedule(M, N, K, 2 * BN, BK, group, full_tiles, slot, slots, tail);
+    if (s.n_tail > 0 && (slot & 1)) {
+        const TileCoord tc = tile_coord(full_tiles + slot / 2, s.num_m, s.num_n, group);
+        if (2 * tc.n_blk + 1 >= (N + BN - 1) / BN) s.n_tail = 0;
+    }
+    return s;
+}
+
+template <int BN>
+__device__ __forceinline__ Unit slot_unit(const Schedule& s, int i, int pair, int N) {
+    Unit out = {0, 0, BN, 0, s.num_kb, -1};
+    const int tiles_n = (N + BN - 1) / BN;
+    if (i < s.n_full) {
+        const TileCoord tc = tile_coord(s.cluster + i * s.clusters, s.num_m, s.num_n, s.group);
+        out.m_blk = tc.m_blk;
+        if (2 * tc.n_blk + 1 < tiles_n) {
+            out.n0 = (2 * tc.n_blk + pair) * BN;
+        } else {
+            out.width = BN / 2;
+            out.n0 = 2 * tc.n_blk * BN + pair * (BN / 2);
+        }
+    } else {
+        const TileCoord tc = tile_coord(s.full_tiles + s.cluster / 2, s.num_m, s.num_n, s.group);
+        out.m_blk = tc.m_blk;
+        out.width = BN / 2;
+        out.n0 = (2 * tc.n_blk + (s.cluster & 1)) * BN + pair * (BN / 2);
+    }
+    return out;
+}
+
 // Chunk c (32 rows x 64 FP32) of the partial at a range boundary for (CTA
 // rank, lane quarter), stored as 16 float4 groups interleaved across the 32
 // lanes, so that every warp-wide store and load is coalesced.
@@ -184,8 +223,15 @@ __device__ __forceinline__ size_t flag_index(int boundary, int rank, int quarter
     return (static_cast<size_t>(boundary) * 2 + rank) * 4 + quarter;
 }
 
-template <int BN, int BK, int STAGES, bool B_MN, bool ALLGATHER>
-__global__ void __launch_bounds__(kThreads, 1)
+// Threads of a pair kernel: the slot schedule adds two warps that exchange A
+// inside a 4-CTA cluster (warp 6 sends, warp 7 relays what arrived).
+template <bool SLOTS>
+constexpr int pair_threads() {
+    return SLOTS ? kThreads + 64 : kThreads;
+}
+
+template <int BN, int BK, int STAGES, bool B_MN, bool ALLGATHER, bool SLOTS>
+__global__ void __launch_bounds__(pair_threads<SLOTS>(), 1)
     gemm_bf16_tcgen05_pair(const __grid_constant__ CUtensorMap map_a,
                            const __grid_constant__ CUtensorMap map_b,
                            const __grid_constant__ CUtensorMap map_b_half,
@@ -202,26 +248,52 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* tmem_empty = tmem_full + 2;
     uint64_t* drain = tmem_empty + 2;
     uint64_t* partial_full = drain + 1;  // one per epilogue warp: partial landed in shared memory
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(partial_full + kEpilogueWarps);
+    uint64_t* landed = partial_full + kEpilogueWarps;  // 4-CTA cluster: this CTA's K half of A landed
+    uint64_t* fwd_in = landed + STAGES;                // 4-CTA cluster: the partner's K half of A landed
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fwd_in + STAGES);
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
     volatile int* no_abort = abort + 1;
 
-    if (status == nullptr) status = &g_default_status;
     // A warp's rows of a stream-K partial (BN/64 chunks of 32 x 64 FP32) are
     // staged in the pipeline buffers when those hold all four warps' rows.
     constexpr uint32_t kPartialWarpBytes = (BN / 64) * 32 * 64 * 4;
     constexpr bool kStagePartial = L::kStagingOffset >= kEpilogueWarps * static_cast<int>(kPartialWarpBytes);
     const int warp = threadIdx.x / 32;
     const int lane = threadIdx.x % 32;
-    const uint32_t rank = ptx::cluster_ctarank();
+    // The pair is cluster ranks {2q, 2q + 1} (tcgen05 pairs CTAs whose ranks
+    // differ in bit 0); rank 2q leads it.  A 4-CTA cluster (slot schedule)
+    // holds two pairs, and CTA r shares its rows of A with CTA r ^ 2.
+    const uint32_t cta_rank = ptx::cluster_ctarank();
+    const uint32_t rank = cta_rank & 1u;
+    const uint32_t pair_base = cta_rank & ~1u;
+    const uint32_t partner = cta_rank ^ 2u;
     const bool leader = rank == 0;
-    const Schedule sched = make_schedule(M, N, K, BN, BK, group, full_tiles, blockIdx.x / 2, gridDim.x / 2, tail);
-    const int num_units = sched.count();
+    bool quad = false;
+    if constexpr (SLOTS) quad = ptx::cluster_nctarank() == 4;
+    const int pair_id = SLOTS ? static_cast<int>((blockIdx.x >> 1) & 1u) : 0;
+    const uint16_t pair_mask = static_cast<uint16_t>(0x3u << pair_base);
+    const uint16_t stage_mask = quad ? static_cast<uint16_t>(0xF) : pair_mask;
+    const Schedule sched =
+        SLOTS ? make_slot_schedule(M, N, K, BN, BK, group, full_tiles, blockIdx.x / 4, gridDim.x / 4, tail)
+              : make_schedule(M, N, K, BN, BK, group, full_tiles, blockIdx.x / 2, gridDim.x / 2, tail);
+    auto unit_at = [&](int u) { return SLOTS ? slot_unit<BN>(sched, u, pair_id, N) : schedule_unit<BN>(sched, u, tail); };
+    // Slots assume clusters of consecutive blocks (4s .. 4s + 3, or 2t, 2t + 1
+    // when the launch fell back to pairs); anything else computes nothing and
+    // reports KMCTS_EGEMM.
+    bool layout_ok = true;
+    if constexpr (SLOTS) layout_ok = (blockIdx.x & (quad ? 3u : 1u)) == cta_rank;
+    const int num_units = layout_ok ? sched.count() : 0;
 
     if (threadIdx.x == 0) {
+        if (!layout_ok) atomicCAS(status, 0, KMCTS_EGEMM);
+        // 4-CTA cluster: the leader's full barrier also takes its own A half
+        // (warp 6) and the non-leader's relay (warp 7); every empty barrier
+        // both pairs' UMMA commits.
         for (int s = 0; s < STAGES; ++s) {
-            ptx::mbar_init(&full[s], 1);
-            ptx::mbar_init(&empty[s], 1);
+            ptx::mbar_init(&full[s], quad ? 3 : 1);
+            ptx::mbar_init(&empty[s], quad ? 2 : 1);
+            ptx::mbar_init(&landed[s], 1);
+            ptx::mbar_init(&fwd_in[s], 1);
         }
         for (int a = 0; a < 2; ++a) {
             ptx::mbar_init(&tmem_full[a], 1);
@@ -257,11 +329,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t issued = 0, issued_phase = 0;
             bool ok = true;
             for (int u = 0; u < num_units && ok; ++u) {
-                const Unit w = schedule_unit<BN>(sched, u, tail);
+                const Unit w = unit_at(u);
                 const int m0 = w.m_blk * 256 + static_cast<int>(rank) * 128;
                 const int b_cols = w.width / 2;  // B columns this CTA stages
                 const int nb0 = w.n0 + static_cast<int>(rank) * b_cols;
-                const uint32_t unit_bytes = 2u * (L::kABytes + b_cols * BK * 2);
+                // The leader posts the pair's bytes on its full barrier: both
+                // CTAs' B; and both CTAs' A, or in a 4-CTA cluster the A half
+                // its partner copies in.
+                const uint32_t unit_bytes = 2u * b_cols * BK * 2 + (quad ? L::kABytes / 2 : 2u * L::kABytes);
                 const CUtensorMap* mb = w.width == BN ? &map_b : &map_b_half;
                 for (int kb = w.kb0; kb < w.kb1; ++kb) {
                     if (!ptx::mbar_wait(&empty[stage], phase ^ 1u, limit_ns, abort)) {
@@ -272,11 +347,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                     uint8_t* sa = smem + stage * L::kStageBytes;
                     uint8_t* sb = sa + L::kABytes;
                     if (leader) ptx::mbar_arrive_expect_tx(&full[stage], unit_bytes);
-                    const uint32_t bar = ptx::mapa_shared(ptx::smem_addr(&full[stage]), 0);
+                    const uint32_t bar = ptx::mapa_shared(ptx::smem_addr(&full[stage]), pair_base);
 #pragma unroll
                     for (int kh = 0; kh < BK / 64; ++kh) {
                         const int k0 = kb * BK + kh * 64;
-                        ptx::tma_load_2d_pair(sa + kh * (128 * 128), &map_a, bar, k0, m0);
+                        if (!quad) {
+                            ptx::tma_load_2d_pair(sa + kh * (128 * 128), &map_a, bar, k0, m0);
+                        } else if (kh == pair_id) {
+                            // This CTA's K half of its A rows; warp 6 copies
+                            // it to the partner once it lands.
+                            ptx::mbar_arrive_expect_tx(&landed[stage], 128 * 128);
+                            ptx::tma_load_2d(sa + kh * (128 * 128), &map_a, &landed[stage], k0, m0);
+                        }
                         if constexpr (B_MN) {
                             for (int nb = 0; nb < b_cols / 64; ++nb) {
                                 ptx::tma_load_2d_pair(sb + (kh * (L::kHalfN / 64) + nb) * 8192, &map_b, bar,
@@ -294,14 +376,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
             }
-            // Drain (leader): its full barriers count both CTAs' bytes.
-            if (leader) {
-                for (int s = 0; s < STAGES; ++s) {
-                    if ((issued & (1u << s)) &&
-                        !ptx::mbar_wait(&full[s], (issued_phase >> s) & 1u, drain_limit(limit_ns), no_abort)) {
-                        record_failure(status, abort, kRoleDrain);
-                    }
-                }
+            // Drain (leader): its full barriers count both CTAs' bytes.  In
+            // a 4-CTA cluster every CTA also waits for its own A loads.
+            for (int s = 0; s < STAGES; ++s) {
+                if (!(issued & (1u << s))) continue;
+                const uint32_t par = (issued_phase >> s) & 1u;
+                if (leader && !ptx::mbar_wait(&full[s], par, drain_limit(limit_ns), no_abort))
+                    record_failure(status, abort, kRoleDrain);
+                if (quad && !ptx::mbar_wait(&landed[s], par, drain_limit(limit_ns), no_abort))
+                    record_failure(status, abort, kRoleDrain);
             }
         }
     } else if (warp == 1) {
@@ -314,7 +397,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             int local = 0;
             bool ok = true;
             for (int u = 0; u < num_units && ok; ++u, ++local) {
-                const Unit w = schedule_unit<BN>(sched, u, tail);
+                const Unit w = unit_at(u);
                 const uint32_t idesc = w.width == BN ? idesc_full : idesc_half;
                 const int acc = local & 1;
                 const uint32_t acc_phase = (local >> 1) & 1;
@@ -346,15 +429,88 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                         ptx::umma_bf16_pair(d_tmem, adesc, bdesc, idesc, (kb != w.kb0 || kk != 0) ? 1u : 0u);
                     }
-                    ptx::umma_commit_pair(&empty[stage], 0x3);
+                    ptx::umma_commit_pair(&empty[stage], stage_mask);
                     if (++stage == STAGES) {
                         stage = 0;
                         phase ^= 1u;
                     }
                 }
-                if (ok) ptx::umma_commit_pair(&tmem_full[acc], 0x3);
+                if (ok) ptx::umma_commit_pair(&tmem_full[acc], pair_mask);
             }
-            ptx::umma_commit_pair(drain, 0x3);
+            ptx::umma_commit_pair(drain, pair_mask);
+        }
+        __syncwarp();
+    } else if (warp >= 2 + kEpilogueWarps) {
+        // ---------------------------------------- A exchange (4-CTA cluster)
+        // CTA x and CTA x ^ 2 (same rank in the two pairs) stage the same 128
+        // rows of A; each loads one 64-deep K half per stage and copies it
+        // into the other's same stage.  Leaders receive into their full
+        // barrier (the producer's expected bytes include it); non-leaders
+        // receive into fwd_in, and warp 7 relays "both halves here" to the
+        // leader.  A copy into the partner's stage is safe once this CTA's
+        // producer has loaded that stage: it loaded only after both pairs'
+        // UMMAs released it, here and (same UMMAs) in the partner.  This
+        // CTA's source half is free again once both pairs' UMMAs release the
+        // stage: the partner pair's UMMAs read the copy, so it has landed.
+        if (quad && lane == 0 && warp == 2 + kEpilogueWarps) {
+            // Outgoing: copy each landed half to the partner.
+            constexpr uint32_t kHalfBytes = 128 * 128;
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            for (int u = 0; u < num_units && ok; ++u) {
+                const Unit w = unit_at(u);
+                for (int kb = w.kb0; kb < w.kb1; ++kb) {
+                    uint8_t* half = smem + stage * L::kStageBytes + pair_id * kHalfBytes;
+                    if (!ptx::mbar_wait(&landed[stage], phase, limit_ns, abort)) {
+                        record_failure(status, abort, kRoleProducer);
+                        ok = false;
+                        break;
+                    }
+                    uint64_t* dst_bar = leader ? &full[stage] : &fwd_in[stage];
+                    ptx::bulk_copy_to_cta(ptx::mapa_shared(ptx::smem_addr(half), partner), half, kHalfBytes,
+                                          ptx::mapa_shared(ptx::smem_addr(dst_bar), partner));
+                    if (leader) ptx::mbar_arrive(&full[stage]);  // the leader's own half is here
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+        } else if (quad && !leader && lane == 0) {
+            // Incoming (non-leader): once the partner's half and this CTA's
+            // own half have landed, one arrival on the leader's full barrier.
+            constexpr uint32_t kHalfBytes = 128 * 128;
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t armed = 0, armed_phase = 0;  // incoming copies expected and not yet seen
+            bool ok = true;
+            for (int u = 0; u < num_units && ok; ++u) {
+                const Unit w = unit_at(u);
+                for (int kb = w.kb0; kb < w.kb1; ++kb) {
+                    ptx::mbar_arrive_expect_tx(&fwd_in[stage], kHalfBytes);
+                    armed |= 1u << stage;
+                    armed_phase = (armed_phase & ~(1u << stage)) | (phase << stage);
+                    if (!ptx::mbar_wait(&fwd_in[stage], phase, limit_ns, abort) ||
+                        !ptx::mbar_wait(&landed[stage], phase, limit_ns, abort)) {
+                        record_failure(status, abort, kRoleProducer);
+                        ok = false;
+                        break;
+                    }
+                    armed &= ~(1u << stage);
+                    ptx::mbar_arrive_cluster_relaxed(ptx::mapa_shared(ptx::smem_addr(&full[stage]), pair_base));
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            // Drain: no copy into this CTA may still be in flight at exit.
+            for (int s = 0; s < STAGES; ++s) {
+                if ((armed & (1u << s)) &&
+                    !ptx::mbar_wait(&fwd_in[s], (armed_phase >> s) & 1u, drain_limit(limit_ns), no_abort))
+                    record_failure(status, abort, kRoleDrain);
+            }
         }
         __syncwarp();
     } else {
@@ -364,7 +520,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         int local = 0;
         int chunk_count = 0;
         for (int u = 0; u < num_units; ++u, ++local) {
-            const Unit w = schedule_unit<BN>(sched, u, tail);
+            const Unit w = unit_at(u);
             const int m0 = w.m_blk * 256 + static_cast<int>(rank) * 128;
             const int n0 = w.n0;
             const int chunks = w.width / 64;
@@ -427,7 +583,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (c == chunks - 1) {
                     ptx::tc_fence_before();
                     __syncwarp();
-                    if (lane == 0) ptx::mbar_arrive_cluster(ptx::mapa_shared(ptx::smem_addr(&tmem_empty[acc]), 0));
+                    if (lane == 0) ptx::mbar_arrive_cluster(ptx::mapa_shared(ptx::smem_addr(&tmem_empty[acc]), pair_base));
                 }
                 if (split) {
                     float4* part = partial_chunk<BN>(tail, w.boundary, static_cast<int>(rank), quarter, c);
@@ -520,10 +676,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 constexpr int kMaxDevices = 64;
 
 // Co-resident CTA pairs of a pair kernel on the current device (cached).
-template <int BN, int BK, int STAGES, bool B_MN, bool ALLGATHER = false>
+template <int BN, int BK, int STAGES, bool B_MN, bool ALLGATHER = false, bool SLOTS = false>
 int pair_workers(int device) {
     using L = PairLayout<BN, BK, STAGES, B_MN>;
-    auto kernel = gemm_bf16_tcgen05_pair<BN, BK, STAGES, B_MN, ALLGATHER>;
+    auto kernel = gemm_bf16_tcgen05_pair<BN, BK, STAGES, B_MN, ALLGATHER, SLOTS>;
     static std::mutex mu;
     static int max_clusters[kMaxDevices] = {};
     std::lock_guard<std::mutex> lock(mu);
@@ -537,7 +693,7 @@ int pair_workers(int device) {
         attr[0].val.clusterDim.y = 1;
         attr[0].val.clusterDim.z = 1;
         config.gridDim = dim3(2 * (multiprocessor_count() / 2), 1, 1);
-        config.blockDim = dim3(kThreads, 1, 1);
+        config.blockDim = dim3(pair_threads<SLOTS>(), 1, 1);
         config.dynamicSmemBytes = L::kSmemBytes;
         config.attrs = attr;
         config.numAttrs = 1;
@@ -611,13 +767,56 @@ kmcts_gemm_plan make_pair_plan(int M, int N, int K, int workers, bool persistent
     return plan;
 }
 
-template <int BN, int BK, int STAGES, bool B_MN, bool ALLGATHER = false>
-int plan_pair_variant(int M, int N, int K, bool persistent, int tail, kmcts_gemm_plan* out) {
+// Slot schedule (cluster_n 2): `slots` groups of four CTAs, each walking
+// super tiles of 256 x 2 BN; the last partial wave splits as in the pair
+// plan (stream-K requests take the N split).  Host copy of the kernel's
+// make_slot_schedule.
+template <int BN, int BK>
+kmcts_gemm_plan make_slot_plan(int M, int N, int K, int slots, bool persistent, int tail, int group, int64_t smem) {
+    kmcts_gemm_plan plan = {};
+    plan.kernel = 2;
+    plan.cluster_size = 4;
+    plan.workers = slots;
+    const int num_m = (M + 255) / 256, num_sn = (N + 2 * BN - 1) / (2 * BN), tiles_n = (N + BN - 1) / BN;
+    plan.tiles = num_m * num_sn;
+    plan.full_tiles = plan.tiles;
+    plan.units = plan.tiles;
+    int used = plan.tiles;
+    if (persistent) {
+        used = plan.tiles < slots ? plan.tiles : slots;
+        const int rem = plan.tiles % slots;
+        if (rem != 0 && tail != KMCTS_TAIL_NONE && 2 * rem <= slots) {
+            plan.tail_split = KMCTS_TAIL_SPLIT_N;
+            plan.full_tiles = plan.tiles - rem;
+            plan.tail_clusters = 2 * rem;
+            plan.tail_segments = 1;
+            // Two units per tail super tile, one when it holds a single tile.
+            plan.units = plan.full_tiles;
+            for (int t = plan.full_tiles; t < plan.tiles; ++t)
+                plan.units += 2 * tile_coord(t, num_m, num_sn, group).n_blk + 1 < tiles_n ? 2 : 1;
+            used = 2 * rem > used ? 2 * rem : used;
+        }
+    }
+    plan.ctas = 4 * used;
+    plan.smem_bytes = static_cast<int32_t>(smem);
+    plan.k_splits = 1;
+    return plan;
+}
+
+template <int BN, int BK, int STAGES, bool B_MN, bool ALLGATHER = false, bool SLOTS = false>
+int plan_pair_variant(int M, int N, int K, bool persistent, int tail, int group, kmcts_gemm_plan* out) {
     int device = 0;
     if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kMaxDevices) return KMCTS_EHANDLE;
-    const int workers = pair_workers<BN, BK, STAGES, B_MN, ALLGATHER>(device);
+    const int workers = pair_workers<BN, BK, STAGES, B_MN, ALLGATHER, SLOTS>(device);
     if (workers <= 0) return KMCTS_EGEMM;
-    *out = make_pair_plan<BN, BK>(M, N, K, workers, persistent, tail, PairLayout<BN, BK, STAGES, B_MN>::kSmemBytes);
+    constexpr int64_t smem = PairLayout<BN, BK, STAGES, B_MN>::kSmemBytes;
+    if constexpr (SLOTS) {
+        if (workers < 2) return KMCTS_EGEMM;
+        *out = make_slot_plan<BN, BK>(M, N, K, workers / 2, persistent, tail, group, smem);
+    } else {
+        (void)group;
+        *out = make_pair_plan<BN, BK>(M, N, K, workers, persistent, tail, smem);
+    }
     return KMCTS_OK;
 }
 
@@ -642,64 +841,80 @@ bool tail_workspace(cudaStream_t stream, int boundaries, TailSplit* out) {
     return true;
 }
 
-template <int BN, int BK, int STAGES, bool B_MN, bool ALLGATHER = false>
+template <int BN, int BK, int STAGES, bool B_MN, bool ALLGATHER = false, bool SLOTS = false>
 int launch_pair_variant_peers(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb_half,
                               const CUtensorMap& mc, int M, int N, int K, int group, bool persistent, int tail_req,
                               uint64_t limit_ns, cudaStream_t stream, int* status, const PeerOutputs& peers) {
     using L = PairLayout<BN, BK, STAGES, B_MN>;
+    if (status == nullptr) status = default_status_ptr();
+    if (status == nullptr) return KMCTS_EGEMM;
     kmcts_gemm_plan plan;
-    int rc = plan_pair_variant<BN, BK, STAGES, B_MN, ALLGATHER>(M, N, K, persistent, tail_req, &plan);
+    int rc = plan_pair_variant<BN, BK, STAGES, B_MN, ALLGATHER, SLOTS>(M, N, K, persistent, tail_req, group, &plan);
     if (rc != KMCTS_OK) return rc;
     TailSplit tail = {};
     if (plan.tail_split == KMCTS_TAIL_STREAM_K && !tail_workspace(stream, plan.tail_clusters, &tail)) {
         // No workspace: the bit-identical N split (or whole tiles) instead.
-        rc = plan_pair_variant<BN, BK, STAGES, B_MN, ALLGATHER>(M, N, K, persistent, KMCTS_TAIL_SPLIT_N, &plan);
+        rc = plan_pair_variant<BN, BK, STAGES, B_MN, ALLGATHER, SLOTS>(M, N, K, persistent, KMCTS_TAIL_SPLIT_N,
+                                                                       group, &plan);
         if (rc != KMCTS_OK) return rc;
     }
     tail.mode = plan.tail_split == KMCTS_TAIL_STREAM_K ? kTailStreamK
                 : plan.tail_split == KMCTS_TAIL_SPLIT_N ? kTailSplitN
                                                         : kTailWhole;
     cudaLaunchConfig_t config = {};
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    // Slots: 4-CTA clusters where the GPCs hold them, pairs on the SMs left
+    // over (the kernel reads which it got from %cluster_nctarank).
+    attr[1].id = cudaLaunchAttributePreferredClusterDimension;
+    attr[1].val.preferredClusterDim.x = 4;
+    attr[1].val.preferredClusterDim.y = 1;
+    attr[1].val.preferredClusterDim.z = 1;
     config.gridDim = dim3(plan.ctas, 1, 1);
-    config.blockDim = dim3(kThreads, 1, 1);
+    config.blockDim = dim3(pair_threads<SLOTS>(), 1, 1);
     config.dynamicSmemBytes = L::kSmemBytes;
     config.stream = stream;
     config.attrs = attr;
-    config.numAttrs = 1;
-    const cudaError_t err = cudaLaunchKernelEx(&config, gemm_bf16_tcgen05_pair<BN, BK, STAGES, B_MN, ALLGATHER>,
-                                               ma, mb, mb_half, mc, M, N, K, group, plan.full_tiles, limit_ns,
-                                               status, peers, tail);
+    config.numAttrs = SLOTS ? 2 : 1;
+    const cudaError_t err =
+        cudaLaunchKernelEx(&config, gemm_bf16_tcgen05_pair<BN, BK, STAGES, B_MN, ALLGATHER, SLOTS>, ma, mb, mb_half,
+                           mc, M, N, K, group, plan.full_tiles, limit_ns, status, peers, tail);
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return err == cudaSuccess ? KMCTS_OK : KMCTS_EGEMM;
 }
 
-template <int BN, int BK, int STAGES, bool B_MN>
+template <int BN, int BK, int STAGES, bool B_MN, bool SLOTS>
 int launch_pair_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb_half,
                         const CUtensorMap& mc, int M, int N, int K, int group, bool persistent, int tail_req,
                         uint64_t limit_ns, cudaStream_t stream, int* status) {
     const PeerOutputs none = {};
-    return launch_pair_variant_peers<BN, BK, STAGES, B_MN, false>(ma, mb, mb_half, mc, M, N, K, group, persistent,
-                                                                  tail_req, limit_ns, stream, status, none);
+    return launch_pair_variant_peers<BN, BK, STAGES, B_MN, false, SLOTS>(
+        ma, mb, mb_half, mc, M, N, K, group, persistent, tail_req, limit_ns, stream, status, none);
+}
+
+template <int BN, int BK, int STAGES, bool B_MN, bool SLOTS>
+int plan_variant(int M, int N, int K, bool persistent, int tail, int group, kmcts_gemm_plan* out) {
+    return plan_pair_variant<BN, BK, STAGES, B_MN, false, SLOTS>(M, N, K, persistent, tail, group, out);
 }
 
 using PairLauncher = int (*)(const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, int,
                              int, int, int, bool, int, uint64_t, cudaStream_t, int*);
 
-using PairPlanner = int (*)(int, int, int, bool, int, kmcts_gemm_plan*);
+using PairPlanner = int (*)(int, int, int, bool, int, int, kmcts_gemm_plan*);
 
 struct PairVariant {
-    int bn, bk, stages, b_mn;
+    int bn, bk, stages, b_mn, slots;
     PairLauncher fn;
     PairPlanner plan;
 };
 
 #define KMCTS_PAIR(BN, BK, ST, MN) \
-    {BN, BK, ST, MN, &launch_pair_variant<BN, BK, ST, MN>, &plan_pair_variant<BN, BK, ST, MN>}
+    {BN, BK, ST, MN, 0, &launch_pair_variant<BN, BK, ST, MN, false>, &plan_variant<BN, BK, ST, MN, false>}
+#define KMCTS_SLOTS(BN, BK, ST, MN) \
+    {BN, BK, ST, MN, 1, &launch_pair_variant<BN, BK, ST, MN, true>, &plan_variant<BN, BK, ST, MN, true>}
 
 // Every pair schedule of the sweep grid that fits 227 KB:
 // stages * (128 + BN/2) * BK * 2 + 32 KB staging + 2 KB.
@@ -712,16 +927,28 @@ const PairVariant kPairVariants[] = {
     KMCTS_PAIR(256, 64, 6, true),   KMCTS_PAIR(256, 128, 3, true),  KMCTS_PAIR(128, 64, 3, true),
     KMCTS_PAIR(128, 64, 4, true),   KMCTS_PAIR(128, 64, 5, true),   KMCTS_PAIR(128, 64, 6, true),
     KMCTS_PAIR(128, 128, 3, true),  KMCTS_PAIR(128, 128, 4, true),
+    // cluster_n 2: two pairs per slot sharing A (BK 128: one 64-deep K half each).
+    KMCTS_SLOTS(256, 128, 3, false), KMCTS_SLOTS(256, 128, 3, true),
 };
 
 }  // namespace
 
-bool pair_variant_exists(int bn, int bk, int stages, int b_layout) {
+namespace {
+
+const PairVariant* find_pair_variant(const kmcts_gemm_config& cfg, int b_layout) {
     const int mn = b_layout == KMCTS_B_ROW ? 1 : 0;
+    const int slots = cfg.cluster_n == 2 ? 1 : 0;
     for (const PairVariant& v : kPairVariants) {
-        if (v.bn == bn && v.bk == bk && v.stages == stages && v.b_mn == mn) return true;
+        if (v.bn == cfg.tile_n && v.bk == cfg.tile_k && v.stages == cfg.stages && v.b_mn == mn && v.slots == slots)
+            return &v;
     }
-    return false;
+    return nullptr;
+}
+
+}  // namespace
+
+bool pair_variant_exists(const kmcts_gemm_config& cfg, int b_layout) {
+    return find_pair_variant(cfg, b_layout) != nullptr;
 }
 
 int64_t pair_smem_bytes(int bn, int bk, int stages) {
@@ -730,13 +957,9 @@ int64_t pair_smem_bytes(int bn, int bk, int stages) {
 }
 
 int plan_pair(const kmcts_gemm_config& cfg, int M, int N, int K, int b_layout, kmcts_gemm_plan* out) {
-    const int mn = b_layout == KMCTS_B_ROW ? 1 : 0;
-    for (const PairVariant& v : kPairVariants) {
-        if (v.bn == cfg.tile_n && v.bk == cfg.tile_k && v.stages == cfg.stages && v.b_mn == mn) {
-            return v.plan(M, N, K, cfg.persistent != 0, requested_tail(cfg.flags), out);
-        }
-    }
-    return KMCTS_ENOTSUP;
+    const PairVariant* v = find_pair_variant(cfg, b_layout);
+    if (!v) return KMCTS_ENOTSUP;
+    return v->plan(M, N, K, cfg.persistent != 0, requested_tail(cfg.flags), cfg.raster_group, out);
 }
 
 int launch_pair_allgather(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb_half,
@@ -768,14 +991,10 @@ int launch_pair_allgather(const CUtensorMap& ma, const CUtensorMap& mb, const CU
 int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb_half, const CUtensorMap& mc,
                 int M, int N, int K, int b_layout, const kmcts_gemm_config& cfg, uint64_t limit_ns,
                 cudaStream_t stream, int* status) {
-    const int mn = b_layout == KMCTS_B_ROW ? 1 : 0;
-    for (const PairVariant& v : kPairVariants) {
-        if (v.bn == cfg.tile_n && v.bk == cfg.tile_k && v.stages == cfg.stages && v.b_mn == mn) {
-            return v.fn(ma, mb, mb_half, mc, M, N, K, cfg.raster_group, cfg.persistent != 0,
-                        requested_tail(cfg.flags), limit_ns, stream, status);
-        }
-    }
-    return KMCTS_ENOTSUP;
+    const PairVariant* v = find_pair_variant(cfg, b_layout);
+    if (!v) return KMCTS_ENOTSUP;
+    return v->fn(ma, mb, mb_half, mc, M, N, K, cfg.raster_group, cfg.persistent != 0, requested_tail(cfg.flags),
+                 limit_ns, stream, status);
 }
 
 }  // namespace kmcts

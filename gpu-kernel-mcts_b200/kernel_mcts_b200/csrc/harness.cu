@@ -10,7 +10,7 @@
 //
 // Additive flags: --b-layout=col|row, --inputs=uniform|randn|int,
 // --kernel=auto|tcgen05|simt|candidate|cublas|cutlass_sm80, --k-splits, --tile-m
-// --cluster-m --tile-n --tile-k --stages --persistent --raster-group --flags
+// --cluster-m --cluster-n --tile-n --tile-k --stages --persistent --raster-group --flags
 // --wait-limit-ns, --flush-l2=0|1.  cublas and cutlass_sm80 are the vendor
 // baseline columns (src/kernel_mcts/vendor_baselines.py), timed under the
 // same protocol as the library kernel.
@@ -207,6 +207,7 @@ int main(int argc, char** argv) {
     kmcts_select_config(l.M, l.N, l.K, l.b_layout, &l.cfg);  // explicit schedule flags override it
     l.cfg.tile_m = static_cast<int>(int_arg(argc, argv, "tile-m", l.cfg.tile_m));
     l.cfg.cluster_m = static_cast<int>(int_arg(argc, argv, "cluster-m", l.cfg.cluster_m));
+    l.cfg.cluster_n = static_cast<int>(int_arg(argc, argv, "cluster-n", l.cfg.cluster_n));
     l.cfg.flags = static_cast<int>(int_arg(argc, argv, "flags", l.cfg.flags));
     l.cfg.tile_n = static_cast<int>(int_arg(argc, argv, "tile-n", l.cfg.tile_n));
     l.cfg.tile_k = static_cast<int>(int_arg(argc, argv, "tile-k", l.cfg.tile_k));

@@ -34,6 +34,10 @@ int64_t tcgen05_smem_bytes(const kmcts_gemm_config& cfg, int b_layout);
 int launch_simt(const void* A, const void* B, void* C, int M, int N, int K, int b_layout,
                 cudaStream_t stream);
 
+// Device address of the library's default status word (for kernels launched
+// with no status pointer), or nullptr if it cannot be had.
+int* default_status_ptr();
+
 // Reads and clears the library's default device status word.
 int take_default_status(cudaStream_t stream, int* value);
 
@@ -48,7 +52,7 @@ constexpr int kWorkspaceStreamK = 0, kWorkspaceSplitK = 1;
 bool stream_workspace(cudaStream_t stream, int user, size_t bytes, void** ptr, int* epoch);
 
 // CTA-pair (cta_group::2) kernels, gemm_tcgen05_pair.cu.
-bool pair_variant_exists(int bn, int bk, int stages, int b_layout);
+bool pair_variant_exists(const kmcts_gemm_config& cfg, int b_layout);
 int64_t pair_smem_bytes(int bn, int bk, int stages);
 int plan_pair(const kmcts_gemm_config& cfg, int M, int N, int K, int b_layout, kmcts_gemm_plan* out);
 int launch_pair_allgather(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb_half,

@@ -219,6 +219,13 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
     return r;
 }
 
+// CTAs in this CTA's cluster (with a preferred cluster size, either size).
+__device__ __forceinline__ uint32_t cluster_nctarank() {
+    uint32_t n;
+    asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(n));
+    return n;
+}
+
 // Address of the same shared-memory offset in CTA `rank` of the cluster.
 __device__ __forceinline__ uint32_t mapa_shared(uint32_t smem_byte_addr, uint32_t rank) {
     uint32_t out;
@@ -236,6 +243,13 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
+// Arrive on an mbarrier of any CTA of the cluster without ordering this
+// thread's earlier memory accesses: for a barrier that only reports that
+// asynchronous copies (already waited for) have landed.
+__device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
 // 2-D tiled load into this CTA's shared memory whose completion is counted
 // on an mbarrier that may live in the peer CTA (`bar_cluster_addr`).
 __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t bar_cluster_addr,
@@ -244,6 +258,19 @@ __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* m
         "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
         " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_addr(dst)),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster_addr), "r"(c0), "r"(c1)
+        : "memory");
+}
+
+// Bulk copy of `bytes` (a multiple of 16, both addresses 16-byte aligned)
+// from this CTA's shared memory into another CTA's of the cluster
+// (`dst_cluster_addr`), completion counted in bytes on an mbarrier in the
+// destination CTA (`bar_cluster_addr`).  One destination, no multicast.
+__device__ __forceinline__ void bulk_copy_to_cta(uint32_t dst_cluster_addr, const void* src, uint32_t bytes,
+                                                 uint32_t bar_cluster_addr) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            dst_cluster_addr),
+        "r"(smem_addr(src)), "r"(bytes), "r"(bar_cluster_addr)
         : "memory");
 }
 

@@ -73,7 +73,9 @@ typedef struct kmcts_gemm_config {
     int32_t tile_k;       /* K per pipeline stage: 64 or 128 */
     int32_t stages;       /* shared-memory pipeline depth: 2..6 (9 for some tile_m 32 schedules) */
     int32_t cluster_m;    /* 1 with tile_m 128 or 32; 2 with tile_m 256 (tcgen05 cta_group::2) */
-    int32_t cluster_n;    /* must be 1: no TMA multicast is used */
+    int32_t cluster_n;    /* 1; or 2 with tile_m 256, tile_n 256, tile_k 128, 3 stages: two CTA
+                             pairs per 4-CTA cluster share A over distributed shared memory
+                             (no TMA multicast); bit-identical to cluster_n 1, and slower */
     int32_t persistent;   /* 1: one CTA per SM loops over tiles; 0: one CTA per tile */
     int32_t raster_group; /* M-tiles per raster group (L2 locality), >= 1 */
     int32_t kernel;       /* KMCTS_KERNEL_* */

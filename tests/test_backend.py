@@ -207,7 +207,9 @@ def test_schedule_programs_select_prebuilt_kernels_without_nvcc(tmp_path):
     too_big = backend.compile(schedule_program(tile_m=256, cluster_m=2, tile_n=256, tile_k=128, stages=6),
                               BF16_GEMM_4096_B200)
     assert not too_big.success and "shared memory" in too_big.stderr
-    multicast = backend.compile(schedule_program(tile_m=256, cluster_m=2, cluster_n=2), BF16_GEMM_4096_B200)
+    quad = backend.compile(schedule_program(tile_m=256, cluster_m=2, cluster_n=2), BF16_GEMM_4096_B200)
+    assert quad.success and "--cluster-n=2" in quad.artifact.extra_args
+    multicast = backend.compile(schedule_program(tile_m=128, cluster_m=1, cluster_n=2), BF16_GEMM_4096_B200)
     assert not multicast.success and "multicast" in multicast.stderr
     with pytest.raises(ValueError):
         backend.normalize_program(KernelProgram('{"warp_size": 7}', "kmcts_sm100"))

@@ -200,6 +200,45 @@ def test_cta_pair_n_split_tail_changes_no_bit(cuda_device, layout, shape):
     assert torch.equal(split.view(torch.int16), whole.view(torch.int16))
 
 
+# The default pair schedule, the one the slot schedule (cluster_n 2) is compiled for.
+PAIR_128K = dict(kernel=_native.KERNEL_TCGEN05, tile_m=256, cluster_m=2, tile_n=256, tile_k=128, stages=3)
+
+
+@pytest.mark.parametrize("layout", ["col", "row"])
+@pytest.mark.parametrize("shape", [(256, 256, 256), (300, 264, 136), (1234, 2312, 1000), (512, 768, 512),
+                                   (4096, 4096, 4096), (2048, 1280, 2048), (4096, 4160, 512), (3072, 5120, 1024)])
+def test_slot_schedule_bit_identical_to_pairs(cuda_device, layout, shape):
+    """cluster_n 2: two CTA pairs of a 4-CTA cluster share their rows of A
+    (each CTA loads one K half and copies it to the other pair over
+    distributed shared memory).  Every output is the same full-K UMMA chain
+    as on the pair schedule, so N(0,1) results are bit-identical; the shapes
+    cover ragged edges, a super tile holding one tile, and the split tail."""
+    m, n, k = shape
+    a_t, b_t = oracle.randn_inputs(m, n, k, seed=3, b_layout=layout)
+    a, b = a_t.cuda(), b_t.cuda()
+    slots = run(a, b, layout, cluster_n=2, **PAIR_128K)
+    pair = run(a, b, layout, **PAIR_128K)
+    assert torch.equal(slots.view(torch.int16), pair.view(torch.int16))
+
+
+def test_slot_schedule_integer_exact_and_plan(cuda_device):
+    """The slot schedule on integer inputs matches the oracle bit for bit; its
+    plan is groups of four CTAs (4-CTA clusters where they fit, pairs on the
+    SMs left over) walking 256 x 512 super tiles."""
+    m, n, k = 1000, 1288, 520
+    a, b_nk = oracle.integer_inputs(m, n, k, seed=11)
+    expect = oracle.root_gemm(bits_of(a), bits_of(b_nk))
+    c = run(a.cuda(), b_nk.cuda(), "col", cluster_n=2, **PAIR_128K)
+    np.testing.assert_array_equal(bits_of(c), expect)
+    plan = plan_of(4096, 4096, 4096, cluster_n=2, **PAIR_128K)
+    pair = plan_of(4096, 4096, 4096, **PAIR_128K)
+    assert plan["cluster_size"] == 4 and plan["workers"] == pair["workers"] // 2
+    assert plan["tiles"] == 16 * 8 and plan["ctas"] % 4 == 0
+    rem = plan["tiles"] % plan["workers"]
+    if rem and 2 * rem <= plan["workers"]:
+        assert plan["tail_split"] == _native.TAIL_SPLIT_N and plan["units"] == plan["tiles"] - rem + 2 * rem
+
+
 SK = _native.FLAG_TAIL_STREAM_K
 
 

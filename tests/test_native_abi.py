@@ -96,7 +96,10 @@ def test_select_config_by_shape(shape, expect):
         ({"tile_m": 128, "cluster_m": 1, "tile_n": 256, "tile_k": 64, "stages": 5}, (4096, 4096, 4096), _native.KMCTS_ESMEM),
         ({"tile_m": 256, "cluster_m": 1}, (4096, 4096, 4096), _native.KMCTS_ENOTSUP),
         ({"tile_m": 128, "cluster_m": 2}, (4096, 4096, 4096), _native.KMCTS_ENOTSUP),
-        ({"cluster_n": 2}, (4096, 4096, 4096), _native.KMCTS_ENOTSUP),
+        ({"cluster_n": 2}, (4096, 4096, 4096), _native.KMCTS_OK),  # two pairs per 4-CTA cluster sharing A
+        ({"cluster_n": 2, "tile_k": 64, "stages": 6}, (4096, 4096, 4096), _native.KMCTS_ENOTSUP),
+        ({"cluster_n": 2, "tile_m": 128, "cluster_m": 1}, (4096, 4096, 4096), _native.KMCTS_ENOTSUP),
+        ({"cluster_n": 4}, (4096, 4096, 4096), _native.KMCTS_ENOTSUP),
         ({"tile_k": 128, "stages": 4}, (4096, 4096, 4096), _native.KMCTS_ESMEM),
         ({"tile_n": 192}, (4096, 4096, 4096), _native.KMCTS_ENOTSUP),
         ({}, (4096, 4096, 4100), _native.KMCTS_ENOTSUP),  # K not a multiple of 8

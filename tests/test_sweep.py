@@ -39,7 +39,12 @@ def test_grid_is_the_96_point_baseline_grid():
 def test_static_legality_rejects_what_cannot_run():
     w = BF16_GEMM_4096_RANDN
     assert static_reasons(DEFAULT_SCHEDULE, w) == []
-    assert "multicast" in static_reasons({**DEFAULT_SCHEDULE, "cluster_n": 2}, w)[0]
+    # cluster 2x2: two CTA pairs sharing A over distributed shared memory,
+    # compiled for the default tile only; one-CTA 2x2 would need a multicast
+    assert static_reasons({**DEFAULT_SCHEDULE, "cluster_n": 2}, w) == []
+    assert "cluster_n 2" in static_reasons({**DEFAULT_SCHEDULE, "cluster_n": 2, "tile_k": 64, "stages": 6}, w)[0]
+    assert "multicast" in static_reasons({"tile_m": 128, "tile_n": 256, "tile_k": 64, "stages": 4, "cluster_m": 1,
+                                          "cluster_n": 2}, w)[0]
     assert "shared memory" in static_reasons({**DEFAULT_SCHEDULE, "stages": 6}, w)[0]
     assert static_reasons({"tile_m": 128, "tile_n": 256, "tile_k": 64, "stages": 4, "cluster_m": 1,
                            "cluster_n": 1}, w) == []
@@ -52,7 +57,7 @@ def test_report_schema_charging_and_best():
     assert report["candidate_count"] == 96
     statuses = [t["status"] for t in report["trials"]]
     legal = [t for t in report["trials"] if t["status"] != "STATICALLY_REJECTED"]
-    assert len(fake.calls) == len(legal) == report["b_tune"] == 18
+    assert len(fake.calls) == len(legal) == report["b_tune"] == 19
     assert statuses.count("FAILED") == 1
     rejected = [t for t in report["trials"] if t["status"] == "STATICALLY_REJECTED"]
     assert all(not t["charged_to_b_tune"] and t["reasons"] for t in rejected)
@@ -62,5 +67,5 @@ def test_report_schema_charging_and_best():
     assert report["best"]["schedule"]["tile_m"] == 256 and report["best"]["schedule"]["tile_k"] == 128
     assert report["default"]["schedule"] == {**DEFAULT_SCHEDULE}
     assert report["comparison"]["best_latency_ratio_vs_cublas"] == report["best"]["median_us"] / 95.0
-    assert report["status"] == "ok" and report["evaluations"] == 18
-    assert run_schedule_sweep(FakeEvaluator(), BF16_GEMM_4096_RANDN, cublas, repeat=3)["evaluations"] == 54
+    assert report["status"] == "ok" and report["evaluations"] == 19
+    assert run_schedule_sweep(FakeEvaluator(), BF16_GEMM_4096_RANDN, cublas, repeat=3)["evaluations"] == 57
