@@ -18,6 +18,9 @@
 //   warps 2-5  epilogue in both CTAs: drain this CTA's 128 accumulator rows
 //              from TMEM, round to BF16, TMA-store; then arrive (remotely for
 //              the peer) on the leader's accumulator-empty barrier.
+// The slot schedule (cluster_n 2, 256 threads) runs two such pairs in a 4-CTA
+// cluster that share their rows of A: warps 6 and 7 exchange K halves of A
+// between the pairs over distributed shared memory (see "A exchange" below).
 // Every wait is bounded; see gemm_tcgen05.cu for the failure protocol.
 #include <cstring>
 #include <mutex>

@@ -256,15 +256,20 @@ int kmcts_selftest_bounded_wait(int64_t limit_ns, int arrive, void* stream, int*
 int64_t kmcts_launch_count(void);
 
 /* C = A·B with A, B and C in host memory (page-locked, or the copies do not
- * overlap), through device buffers the caller owns: A_dev [M,K], B_dev (as
- * b_layout), C_dev [M,N].  No counterpart in the reference, whose harness
- * copies inputs and results around the timed region.  B is copied first,
- * then A in `chunks` row blocks (<= 0: 4; whole 128-row tiles per block):
- * each block's GEMM starts when its rows have landed and its C rows go back
- * while later blocks compute, so both copy directions and the GEMMs overlap.
- * Internal copy streams wait for the work already on `stream`, and `stream`
- * waits for the last copy back: asynchronous on `stream`, complete when it
- * is.  cfg as for kmcts_bf16_gemm_ex (per block). */
+ * overlap), through device scratch buffers the caller owns, as large as A
+ * [M,K], B (K x N) and C [M,N]; their contents afterwards are unspecified
+ * (B and C blocks are kept as dense sub-matrices).  No counterpart in the
+ * reference, whose harness copies inputs and results around the timed
+ * region.  A goes over in `chunks` row blocks (<= 0: 4; whole 128-row tiles)
+ * and B in `chunks` column blocks (whole 256-column tiles; one block when
+ * N < 512), alternating; each C block is computed once its A and B blocks
+ * have landed and goes back at once, so both copy directions and the GEMMs
+ * overlap.  Every block runs one schedule: cfg, or for a NULL cfg the one
+ * kmcts_select_config picks for the whole problem, so C is bit-identical to
+ * kmcts_bf16_gemm_ex on the whole problem with that schedule (except with
+ * KMCTS_FLAG_TAIL_STREAM_K, whose splits depend on the shape).  Internal
+ * copy streams wait for the work already on `stream`, and `stream` waits for
+ * the last copy back: asynchronous on `stream`, complete when it is. */
 int kmcts_bf16_gemm_host(const void* A_host, const void* B_host, void* C_host, void* A_dev, void* B_dev,
                          void* C_dev, int M, int N, int K, int b_layout, const kmcts_gemm_config* cfg,
                          int chunks, void* stream, int* device_status);
