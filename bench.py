@@ -71,7 +71,7 @@ def profiled_traffic() -> float | None:
     for line in path.read_text().splitlines():
         if line.startswith("traffic_bytes_per_launch:"):
             try:
-                return float(line.split(":", 1)[1].strip())
+                return float(line.split(":", 1)[1].split()[0])
             except ValueError:
                 return None
     return None
@@ -96,35 +96,55 @@ class ClockSampler:
         self.samples: list[tuple[float, int, float]] = []
         self.max_mhz: float | None = None
         self.error: str | None = None
+        self._handle = None
+        self._nvml = None
         self._stop = threading.Event()
+        self._first = threading.Event()
         self._thread = threading.Thread(target=self._run, daemon=True)
 
+    def _sample(self) -> None:
+        nvml, handle = self._nvml, self._handle
+        sm = float(nvml.nvmlDeviceGetClockInfo(handle, nvml.NVML_CLOCK_SM))
+        reasons = int(nvml.nvmlDeviceGetCurrentClocksEventReasons(handle))
+        power = nvml.nvmlDeviceGetPowerUsage(handle) / 1000.0
+        self.samples.append((sm, reasons, power))
+
     def _run(self) -> None:
+        try:
+            while True:  # at least one sample, then every ~2 ms until stopped
+                self._sample()
+                self._first.set()
+                if self._stop.wait(0.002):
+                    break
+            self._sample()  # and one as the region ends
+        except Exception as error:  # NVML refused mid-run: report it, do not fail the bench
+            self.error = f"{type(error).__name__}: {error}"
+        finally:
+            self._first.set()
+
+    def __enter__(self):
+        # NVML is opened here, before the timed region: its first call can take
+        # longer than a short region lasts.
         try:
             import pynvml
 
             pynvml.nvmlInit()
             visible = os.environ.get("CUDA_VISIBLE_DEVICES")
             index = int(visible.split(",")[self.device_index]) if visible else self.device_index
-            handle = pynvml.nvmlDeviceGetHandleByIndex(index)
-            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(handle, pynvml.NVML_CLOCK_SM))
-            while not self._stop.is_set():
-                sm = float(pynvml.nvmlDeviceGetClockInfo(handle, pynvml.NVML_CLOCK_SM))
-                reasons = int(pynvml.nvmlDeviceGetCurrentClocksEventReasons(handle))
-                power = pynvml.nvmlDeviceGetPowerUsage(handle) / 1000.0
-                self.samples.append((sm, reasons, power))
-                time.sleep(0.002)
+            self._handle = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self._nvml = pynvml
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(self._handle, pynvml.NVML_CLOCK_SM))
         except Exception as error:  # NVML missing or refused: report it, do not fail the bench
             self.error = f"{type(error).__name__}: {error}"
-
-    def __enter__(self):
+            return self
         self._thread.start()
-        time.sleep(0.05)
+        self._first.wait(timeout=5.0)
         return self
 
     def __exit__(self, *exc) -> None:
         self._stop.set()
-        self._thread.join(timeout=10)
+        if self._thread.is_alive():
+            self._thread.join(timeout=10)
 
     def summary(self) -> dict:
         if not self.samples:
