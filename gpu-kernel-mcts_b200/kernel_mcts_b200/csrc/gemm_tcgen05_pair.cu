@@ -242,6 +242,8 @@ __global__ void __launch_bounds__(pair_threads<SLOTS>(), 1)
                            int full_tiles, uint64_t limit_ns, int* status,
                            const __grid_constant__ PeerOutputs peers, const TailSplit tail) {
     using L = PairLayout<BN, BK, STAGES, B_MN>;
+    // The A exchange splits each stage's A into its two 64-deep K halves.
+    static_assert(!SLOTS || (BK == 128 && !ALLGATHER), "the slot schedule is built for BK 128, plain GEMM");
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~uintptr_t(1023));
