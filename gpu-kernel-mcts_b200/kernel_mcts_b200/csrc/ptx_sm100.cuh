@@ -238,9 +238,15 @@ __device__ __forceinline__ void cluster_sync() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
-// Arrive on an mbarrier given by its shared::cluster address (any CTA of the cluster).
+// Arrive on an mbarrier given by its shared::cluster address (any CTA of the
+// cluster), with the default semantics (release at CTA scope).  Used to hand
+// TMEM accumulators back to the UMMA issuer: the tcgen05.fence::before /
+// after_thread_sync pair around the barrier orders the TMEM reads before the
+// next UMMA, so no cluster-scope release is needed, and one costs about half a
+// microsecond per arrival (measured: 8192^2 x 128 took 48.8 us with it, 37.9
+// without).
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
 // Arrive on an mbarrier of any CTA of the cluster without ordering this
