@@ -103,8 +103,8 @@ int kmcts_default_config(kmcts_gemm_config* cfg);
 
 /* Fills *cfg with the schedule a NULL cfg selects for this shape: for M <= 32,
  * one CTA per tile staging 32 rows of A (tile_m 32); else the default when its
- * 256 x 256 pair tiles fill the co-resident CTA pairs (with five 64-deep stages
- * when K <= 512); else one CTA per
+ * 256 x 256 pair tiles fill the co-resident CTA pairs (with 64-deep stages when
+ * K <= 768); else one CTA per
  * 128 x 256 tile while those fill them (the default again from K = 4096),
  * else one CTA per 128 x 128 tile.  Few tiles over a long K get split K.  Every
  * schedule gives results within the parity criterion and bit-exact ones on

@@ -70,10 +70,12 @@ def test_select_config_splits_k_for_skinny_shapes():
         # 256 pair tiles >= 74 co-resident pairs (148 SMs assumed without a GPU): the default.
         ((4096, 4096, 4096), (256, 256, 128, 3, 2)),
         ((2048, 4096, 2048), (256, 256, 128, 3, 2)),
-        # K <= 512 (at most four 128-deep blocks): 64-deep stages, five of them.
-        ((8192, 8192, 512), (256, 256, 64, 5, 2)),
-        ((16384, 4096, 384), (256, 256, 64, 5, 2)),
-        ((8192, 8192, 768), (256, 256, 128, 3, 2)),
+        # K <= 768: 64-deep stages, six of them (five for K <= 256).
+        ((8192, 8192, 512), (256, 256, 64, 6, 2)),
+        ((16384, 4096, 384), (256, 256, 64, 6, 2)),
+        ((8192, 8192, 768), (256, 256, 64, 6, 2)),
+        ((8192, 8192, 256), (256, 256, 64, 5, 2)),
+        ((8192, 8192, 1024), (256, 256, 128, 3, 2)),
         # 64 pair tiles, 128 one-CTA 128x256 tiles: one CTA per 128x256 tile.
         ((2048, 2048, 2048), (128, 256, 64, 4, 1)),
         # ... unless K is long: the pair's mainloop wins back its idle SMs.
