@@ -523,8 +523,9 @@ def run_ours(args: argparse.Namespace) -> None:
         hc = torch.empty((M, N), dtype=torch.bfloat16).pin_memory()
 
         def end_to_end():
-            # The public host-buffer call: B, then A in row blocks whose GEMMs
-            # and copies back overlap the rest of the copies in.
+            # The public host-buffer call: A row blocks and B column blocks
+            # alternate on the link; each C block's GEMM and copy back overlap
+            # the rest of the copies in.
             kg.bf16_gemm_host(ha, hb, hc, a, b, c, b_layout=layout, stream=stream, status=status)
 
         with torch.cuda.stream(stream):

@@ -555,8 +555,9 @@ def test_library_timing_loop_matches_the_protocol(cuda_device):
 @pytest.mark.parametrize("layout", ["col", "row"])
 @pytest.mark.parametrize("shape,chunks", [((1000, 520, 264), 3), ((4096, 1024, 512), 0), ((64, 256, 128), 8)])
 def test_host_buffer_gemm_overlapped_copies(cuda_device, layout, shape, chunks):
-    """kmcts_bf16_gemm_host: pinned host operands, device buffers, row blocks
-    whose copies and GEMMs overlap; the host C is exact on integer inputs."""
+    """kmcts_bf16_gemm_host: pinned host operands, device scratch buffers, A
+    row blocks and B column blocks whose copies and block GEMMs overlap; the
+    host C is exact on integer inputs."""
     m, n, k = shape
     a_t, b_t = oracle.integer_inputs(m, n, k, seed=m % 7)
     b_host = (b_t if layout == "col" else b_t.T.contiguous()).pin_memory()
