@@ -158,10 +158,12 @@ extern "C" int kmcts_bf16_gemm_host(const void* A_host, const void* B_host, void
             }
         }
     }
-    // The caller's stream ends with the last copy back (also on an error
-    // part-way, so nothing outlives the call unordered).
+    // The caller's stream ends after the last copy in each direction (also on
+    // an error part-way, when a copy in may have no GEMM after it), so nothing
+    // outlives the call unordered.
     if (done_out) {
-        if (cudaEventRecord(done_out, cs.out) != cudaSuccess || cudaStreamWaitEvent(s, done_out, 0) != cudaSuccess)
+        if (cudaEventRecord(done_out, cs.out) != cudaSuccess || cudaStreamWaitEvent(s, done_out, 0) != cudaSuccess ||
+            cudaEventRecord(done_out, cs.in) != cudaSuccess || cudaStreamWaitEvent(s, done_out, 0) != cudaSuccess)
             rc = rc == KMCTS_OK ? KMCTS_ESYNC : rc;
         cudaEventDestroy(done_out);
     }
