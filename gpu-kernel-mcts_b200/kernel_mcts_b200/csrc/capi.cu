@@ -86,24 +86,22 @@ int kmcts_default_config(kmcts_gemm_config* cfg) {
 
 namespace {
 
-// K splits for `tiles` one-CTA tiles over K: minimise
-// waves x (128-deep K blocks per unit + 2), the 2 standing for a unit's
-// fixed cost (fill, epilogue, partial store), with units of at least 16 K
-// blocks (measured: splitting K = 1024 or 2048 loses).  0 = no split.
+// K splits for `tiles` one-CTA tiles over K: as many as keep every unit in
+// one wave (SMs / tiles), at most 16 (the last unit to arrive reads every
+// split's FP32 partial), and at least sixteen 128-deep K blocks per unit.
+// Measured on B200 (L2 flushed): the best split count fills one wave and no
+// more, e.g. 4096 x 512 x 16384 (128 tiles) 77 us unsplit against 89 with two
+// splits and 148 with eight; 2048 x 256 x 8192 (32 tiles) 27.8 us with four
+// against 40 unsplit and 39.9 with eight; 128 x 128 x 65536 (one tile) best at
+// 16 (46 us; 52 at 8, 59 at 32); shorter units lose (512 x 512 x 8192: 24.8 us
+// with four splits, 26.6 with eight).  0 = no split.
 int choose_splits(long long tiles, int K, int sms) {
     const int num_kb = (K + 127) / 128;
     if (tiles <= 0 || tiles >= sms || num_kb < 32) return 0;
-    int chosen = 0;
-    double best = 0.0;
-    for (int splits = 1; splits <= 16 && splits <= num_kb / 16; ++splits) {
-        const long long waves = (tiles * splits + sms - 1) / sms;
-        const double cost = static_cast<double>(waves) * (static_cast<double>(num_kb) / splits + 2.0);
-        if (splits == 1 || cost < best) {
-            best = cost;
-            chosen = splits == 1 ? 0 : splits;
-        }
-    }
-    return chosen;
+    long long splits = sms / tiles;
+    if (splits > 16) splits = 16;
+    if (splits > num_kb / 16) splits = num_kb / 16;
+    return splits >= 2 ? static_cast<int>(splits) : 0;
 }
 
 }  // namespace

@@ -62,6 +62,10 @@ def test_select_config_splits_k_for_skinny_shapes():
     assert km.select_config(1024, 1024, 1024, km.B_ROW).k_splits == 0  # short K: no split
     assert km.select_config(4096, 4096, 4096, km.B_ROW).k_splits == 0
     assert km.select_config(256, 256, 256, km.B_ROW).k_splits == 0  # K too short to split
+    # 128 tiles already fill most of the SMs: splitting would add waves and partials.
+    assert km.select_config(4096, 512, 16384, km.B_ROW).k_splits == 0
+    assert km.select_config(2048, 256, 8192, km.B_ROW).k_splits == 4  # 32 tiles -> 128 units, one wave
+    assert km.select_config(128, 128, 65536, km.B_ROW).k_splits == 16  # one tile: at most 16 splits
 
 
 @pytest.mark.parametrize(
