@@ -114,7 +114,8 @@ int kmcts_select_config(int M, int N, int K, int b_layout, kmcts_gemm_config* cf
     //   SM; the problem is bound by reading B): 128 x 256 tiles when they
     //   fill the SMs' pairs count, else 128 x 128 with split K on long K;
     // * the CTA-pair 256 x 256 schedule once its tiles fill the co-resident
-    //   pairs (with 64-deep stages when K <= 768);
+    //   pairs (with 64-deep stages when K <= 768), or, split in two along K,
+    //   when two units per tile fill three quarters of them and K >= 8192;
     // * below that, one CTA per 128 x 256 tile while those fill the pairs'
     //   count and K is short (from K = 4096 the pair's faster mainloop wins
     //   back its idle SMs), else one CTA per 128 x 128 tile, split K on long K.
@@ -151,6 +152,18 @@ int kmcts_select_config(int M, int N, int K, int b_layout, kmcts_gemm_config* cf
             cfg->tile_k = 64;
             cfg->stages = K <= 256 ? 5 : 6;
         }
+        return KMCTS_OK;
+    }
+    // Two K splits of the pair tiles fill at least three quarters of the pairs
+    // and K is long enough to carry the 256 KB FP32 partial of each unit
+    // (measured: 4096 x 512 x 16384 68.2 us against 76.5 for one-CTA tiles,
+    // 256 x 8192 x 8192 49.0 against 52.4; at K = 4096, or with four splits,
+    // one-CTA tiles win).  Not for M <= 128, where a 256-row pair tile would
+    // be mostly empty.
+    if (M > 128 && 2 * pair_tiles <= workers && 8 * pair_tiles >= 3 * workers && K >= 8192) {
+        cfg->tile_k = 64;
+        cfg->stages = 6;
+        cfg->k_splits = 2;
         return KMCTS_OK;
     }
     small.tile_m = 128;

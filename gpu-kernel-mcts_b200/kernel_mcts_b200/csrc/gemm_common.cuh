@@ -88,6 +88,21 @@ __device__ __forceinline__ void store_chunk(const CUtensorMap* map_c, uint8_t* s
     ++chunk_count;
 }
 
+// Split K: counts one arrival on an epoch-tagged counter (epoch << 32 |
+// units arrived) and returns how many units arrived before this one in this
+// launch.  A counter left by an earlier launch counts as zero.
+__device__ __forceinline__ int arrive_counted(unsigned long long* counter, int epoch) {
+    const unsigned long long tag = static_cast<unsigned long long>(static_cast<unsigned>(epoch)) << 32;
+    unsigned long long old = *reinterpret_cast<volatile unsigned long long*>(counter);
+    while (true) {
+        const bool same = (old >> 32) == static_cast<unsigned>(epoch);
+        const unsigned long long next = same ? old + 1 : (tag | 1ull);
+        const unsigned long long seen = atomicCAS(counter, old, next);
+        if (seen == old) return same ? static_cast<int>(old & 0xffffffffull) : 0;
+        old = seen;  // another unit arrived in between: retry on its value
+    }
+}
+
 constexpr uint32_t tmem_columns_for(int cols) {
     return cols <= 32 ? 32 : cols <= 64 ? 64 : cols <= 128 ? 128 : cols <= 256 ? 256 : 512;
 }

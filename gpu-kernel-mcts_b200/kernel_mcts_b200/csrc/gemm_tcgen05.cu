@@ -95,20 +95,6 @@ __device__ __forceinline__ float4* split_chunk(const SplitK& sk, int tile, int s
     return reinterpret_cast<float4*>(sk.partials + block * 32 * 64);
 }
 
-// Counts one arrival on an epoch-tagged counter; returns how many units
-// arrived before this one in this launch.
-__device__ __forceinline__ int arrive_counted(unsigned long long* counter, int epoch) {
-    const unsigned long long tag = static_cast<unsigned long long>(static_cast<unsigned>(epoch)) << 32;
-    unsigned long long old = *reinterpret_cast<volatile unsigned long long*>(counter);
-    while (true) {
-        const bool same = (old >> 32) == static_cast<unsigned>(epoch);
-        const unsigned long long next = same ? old + 1 : (tag | 1ull);
-        const unsigned long long seen = atomicCAS(counter, old, next);
-        if (seen == old) return same ? static_cast<int>(old & 0xffffffffull) : 0;
-        old = seen;  // another unit arrived in between: retry on its value
-    }
-}
-
 template <int BN, int BK, int STAGES, bool B_MN, int AR>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_tcgen05(const __grid_constant__ CUtensorMap map_a,
@@ -524,8 +510,8 @@ int tcgen05_legal(const kmcts_gemm_config& cfg, int M, int N, int K, int b_layou
         put_reason(why, len, "k_splits must be >= 0");
         return KMCTS_EINVAL;
     }
-    if (cfg.k_splits > 1 && !is_one_cta(cfg)) {
-        put_reason(why, len, "split K runs on one-CTA schedules (tile_m 128 or 32)");
+    if (cfg.k_splits > 1 && !is_one_cta(cfg) && !(is_pair(cfg) && cfg.cluster_n == 1)) {
+        put_reason(why, len, "split K runs on one-CTA schedules (tile_m 128 or 32) and CTA pairs (cluster 2x1)");
         return KMCTS_ENOTSUP;
     }
     if (cfg.cluster_m < 1 || cfg.cluster_n < 1) {

@@ -86,12 +86,23 @@ struct PeerOutputs {
 //                 so a half unit takes about 3/4 of a whole tile's time.
 // Flags carry the launch's epoch (a per-workspace host counter), so values
 // left by an earlier failed launch are never taken for this launch's.
-constexpr int kTailWhole = 0, kTailSplitN = 1, kTailStreamK = 2;
+//
+// kSplitK (k_splits = S > 1, few tiles over a long K) is not a tail mode: every
+// tile runs as S units over consecutive K ranges, dealt round-robin like whole
+// tiles (full_tiles then counts units).  Each unit stores both CTAs' FP32 rows
+// in the workspace and counts itself per (CTA rank, lane quarter) on the
+// tile's epoch-tagged counter; the unit that arrives last adds the S partials
+// in split order and writes C, as the one-CTA kernel's split K does.  Nothing
+// waits.
+constexpr int kTailWhole = 0, kTailSplitN = 1, kTailStreamK = 2, kSplitK = 3;
 
 struct TailSplit {
-    float* partials;  // [boundary][CTA rank][quarter][BN/64 chunks][16 float4][32 lanes]
+    float* partials;  // stream-K: [boundary][CTA rank][quarter][BN/64 chunks][16 float4][32 lanes];
+                      // split K: [tile][split][CTA rank][quarter][BN/64 chunks][16 float4][32 lanes]
     int* ready;       // [boundary][CTA rank][quarter]
     int* arrivals;    // [boundary][CTA rank][quarter]
+    unsigned long long* counters;  // split K: [tile][CTA rank][quarter], epoch << 32 | units arrived
+    int splits;                    // split K: K ranges per tile
     int epoch;
     int mode;
 };
@@ -99,6 +110,7 @@ struct TailSplit {
 struct Unit {
     int m_blk, n0, width, kb0, kb1;
     int boundary;  // stream-K: the range boundary splitting this tile, else -1
+    int tile, split;  // split K: the tile and its K range, else -1
 };
 
 // Stream-K ranges: cluster c owns K blocks [lo(c), lo(c + 1)) of the
@@ -149,9 +161,16 @@ __device__ __forceinline__ Schedule make_schedule(int M, int N, int K, int BN, i
 
 template <int BN>
 __device__ __forceinline__ Unit schedule_unit(const Schedule& s, int i, const TailSplit& tail) {
-    Unit out = {0, 0, BN, 0, s.num_kb, -1};
+    Unit out = {0, 0, BN, 0, s.num_kb, -1, -1, -1};
     int t, half_n = 0;
-    if (i < s.n_full) {
+    if (tail.mode == kSplitK) {
+        const int u = s.cluster + i * s.clusters;
+        t = u / tail.splits;
+        out.tile = t;
+        out.split = u % tail.splits;
+        out.kb0 = out.split * s.num_kb / tail.splits;
+        out.kb1 = (out.split + 1) * s.num_kb / tail.splits;
+    } else if (i < s.n_full) {
         t = s.cluster + i * s.clusters;
     } else if (tail.mode == kTailSplitN) {
         t = s.full_tiles + s.cluster / 2;
@@ -193,7 +212,7 @@ __device__ __forceinline__ Schedule make_slot_schedule(int M, int N, int K, int 
 
 template <int BN>
 __device__ __forceinline__ Unit slot_unit(const Schedule& s, int i, int pair, int N) {
-    Unit out = {0, 0, BN, 0, s.num_kb, -1};
+    Unit out = {0, 0, BN, 0, s.num_kb, -1, -1, -1};
     const int tiles_n = (N + BN - 1) / BN;
     if (i < s.n_full) {
         const TileCoord tc = tile_coord(s.cluster + i * s.clusters, s.num_m, s.num_n, s.group);
@@ -224,6 +243,16 @@ __device__ __forceinline__ float4* partial_chunk(const TailSplit& tail, int boun
 
 __device__ __forceinline__ size_t flag_index(int boundary, int rank, int quarter) {
     return (static_cast<size_t>(boundary) * 2 + rank) * 4 + quarter;
+}
+
+// Chunk c of split `split`'s partial of `tile` for (CTA rank, lane quarter),
+// in the same interleaved layout as partial_chunk.
+template <int BN>
+__device__ __forceinline__ float4* split_partial_chunk(const TailSplit& tail, int tile, int split, int rank,
+                                                       int quarter, int c) {
+    const size_t chunk =
+        (((static_cast<size_t>(tile) * tail.splits + split) * 2 + rank) * 4 + quarter) * (BN / 64) + c;
+    return reinterpret_cast<float4*>(tail.partials + chunk * 32 * 64);
 }
 
 // Threads of a pair kernel: the slot schedule adds two warps that exchange A
@@ -590,6 +619,22 @@ __global__ void __launch_bounds__(pair_threads<SLOTS>(), 1)
                     __syncwarp();
                     if (lane == 0) ptx::mbar_arrive_cluster(ptx::mapa_shared(ptx::smem_addr(&tmem_empty[acc]), pair_base));
                 }
+                if (w.split >= 0) {
+                    // Split K: store this K range's FP32 rows; the tile's last
+                    // unit to arrive writes C after the loop.
+                    float4* part = split_partial_chunk<BN>(tail, w.tile, w.split, static_cast<int>(rank), quarter, c);
+#pragma unroll
+                    for (int q = 0; q < 8; ++q)
+                        __stcg(part + q * 32 + lane,
+                               make_float4(__uint_as_float(lo[4 * q]), __uint_as_float(lo[4 * q + 1]),
+                                           __uint_as_float(lo[4 * q + 2]), __uint_as_float(lo[4 * q + 3])));
+#pragma unroll
+                    for (int q = 0; q < 8; ++q)
+                        __stcg(part + (8 + q) * 32 + lane,
+                               make_float4(__uint_as_float(hi[4 * q]), __uint_as_float(hi[4 * q + 1]),
+                                           __uint_as_float(hi[4 * q + 2]), __uint_as_float(hi[4 * q + 3])));
+                    continue;
+                }
                 if (split) {
                     float4* part = partial_chunk<BN>(tail, w.boundary, static_cast<int>(rank), quarter, c);
                     if (!second) {
@@ -631,6 +676,52 @@ __global__ void __launch_bounds__(pair_threads<SLOTS>(), 1)
                 // chunk also goes to every peer's C (TMA stores over NVLink).
                 store_chunk(&map_c, staging, chunk_count, lo, hi, lane, peers.col_offset + n0 + c * 64,
                             m0 + quarter * 32, ALLGATHER ? peers.map : nullptr, ALLGATHER ? peers.count : 0);
+            }
+            if (w.split >= 0) {
+                // Publish this warp's rows of the partial, then count the
+                // unit; the tile's last unit sums every split in split order.
+                __threadfence();
+                __syncwarp();
+                unsigned long long* counter =
+                    tail.counters + (static_cast<size_t>(w.tile) * 2 + rank) * 4 + quarter;
+                int order = 0;
+                if (lane == 0) order = arrive_counted(counter, tail.epoch);
+                if (__shfl_sync(0xffffffffu, order, 0) == tail.splits - 1) {
+                    __threadfence();
+#pragma unroll 1
+                    for (int c = 0; c < chunks; ++c) {
+                        float sum[64];
+#pragma unroll 1
+                        for (int j = 0; j < tail.splits; ++j) {
+                            const float4* part = split_partial_chunk<BN>(tail, w.tile, j, static_cast<int>(rank), quarter, c);
+#pragma unroll
+                            for (int q = 0; q < 16; ++q) {
+                                const float4 f = __ldcg(part + q * 32 + lane);
+                                if (j == 0) {
+                                    sum[4 * q] = f.x;
+                                    sum[4 * q + 1] = f.y;
+                                    sum[4 * q + 2] = f.z;
+                                    sum[4 * q + 3] = f.w;
+                                } else {
+                                    sum[4 * q] += f.x;
+                                    sum[4 * q + 1] += f.y;
+                                    sum[4 * q + 2] += f.z;
+                                    sum[4 * q + 3] += f.w;
+                                }
+                            }
+                        }
+                        uint32_t lo[32], hi[32];
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) {
+                            lo[e] = __float_as_uint(sum[e]);
+                            hi[e] = __float_as_uint(sum[32 + e]);
+                        }
+                        store_chunk(&map_c, staging, chunk_count, lo, hi, lane, peers.col_offset + n0 + c * 64,
+                                    m0 + quarter * 32, ALLGATHER ? peers.map : nullptr, ALLGATHER ? peers.count : 0);
+                    }
+                    __syncwarp();
+                    if (lane == 0) *counter = 0ull;  // every unit of the tile has arrived: clear for replays
+                }
             }
             if (split) {
                 __syncwarp();
@@ -734,7 +825,8 @@ int stream_k_units(long long total, int num_kb, int p) {
 // The launch shape: how many pairs run, which tiles run whole, and how the
 // tiles of the last partial wave are shared.
 template <int BN, int BK>
-kmcts_gemm_plan make_pair_plan(int M, int N, int K, int workers, bool persistent, int tail, int64_t smem) {
+kmcts_gemm_plan make_pair_plan(int M, int N, int K, int workers, bool persistent, int tail, int k_splits,
+                               int64_t smem) {
     kmcts_gemm_plan plan = {};
     plan.kernel = 2;
     plan.cluster_size = 2;
@@ -742,6 +834,20 @@ kmcts_gemm_plan make_pair_plan(int M, int N, int K, int workers, bool persistent
     plan.tiles = ((M + 255) / 256) * ((N + BN - 1) / BN);
     plan.full_tiles = plan.tiles;
     plan.units = plan.tiles;
+    plan.k_splits = 1;
+    const int num_kb_all = (K + BK - 1) / BK;
+    const int splits = k_splits < num_kb_all ? k_splits : num_kb_all;
+    if (splits > 1) {
+        // Split K: every tile as `splits` K ranges, dealt like whole tiles;
+        // full_tiles counts the units.
+        plan.k_splits = splits;
+        plan.units = plan.tiles * splits;
+        plan.full_tiles = plan.units;
+        const int clusters = persistent && plan.units > workers ? workers : plan.units;
+        plan.ctas = 2 * clusters;
+        plan.smem_bytes = static_cast<int32_t>(smem);
+        return plan;
+    }
     int clusters = plan.tiles;
     if (persistent) {
         clusters = plan.tiles < workers ? plan.tiles : workers;
@@ -768,7 +874,6 @@ kmcts_gemm_plan make_pair_plan(int M, int N, int K, int workers, bool persistent
     }
     plan.ctas = 2 * clusters;
     plan.smem_bytes = static_cast<int32_t>(smem);
-    plan.k_splits = 1;
     return plan;
 }
 
@@ -809,7 +914,7 @@ kmcts_gemm_plan make_slot_plan(int M, int N, int K, int slots, bool persistent, 
 }
 
 template <int BN, int BK, int STAGES, bool B_MN, bool ALLGATHER = false, bool SLOTS = false>
-int plan_pair_variant(int M, int N, int K, bool persistent, int tail, int group, kmcts_gemm_plan* out) {
+int plan_pair_variant(int M, int N, int K, bool persistent, int tail, int group, int k_splits, kmcts_gemm_plan* out) {
     int device = 0;
     if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kMaxDevices) return KMCTS_EHANDLE;
     const int workers = pair_workers<BN, BK, STAGES, B_MN, ALLGATHER, SLOTS>(device);
@@ -817,10 +922,11 @@ int plan_pair_variant(int M, int N, int K, bool persistent, int tail, int group,
     constexpr int64_t smem = PairLayout<BN, BK, STAGES, B_MN>::kSmemBytes;
     if constexpr (SLOTS) {
         if (workers < 2) return KMCTS_EGEMM;
+        (void)k_splits;
         *out = make_slot_plan<BN, BK>(M, N, K, workers / 2, persistent, tail, group, smem);
     } else {
         (void)group;
-        *out = make_pair_plan<BN, BK>(M, N, K, workers, persistent, tail, smem);
+        *out = make_pair_plan<BN, BK>(M, N, K, workers, persistent, tail, ALLGATHER ? 0 : k_splits, smem);
     }
     return KMCTS_OK;
 }
@@ -846,26 +952,50 @@ bool tail_workspace(cudaStream_t stream, int boundaries, TailSplit* out) {
     return true;
 }
 
+// Split K: the FP32 partials of every (tile, split) and the tiles' counters,
+// in the stream's split-K workspace.
+template <int BN>
+bool split_workspace(cudaStream_t stream, int tiles, int splits, TailSplit* out) {
+    const size_t counter_bytes = static_cast<size_t>(tiles) * 2 * 4 * sizeof(unsigned long long);
+    const size_t partial_bytes = static_cast<size_t>(tiles) * splits * 2 * 4 * (BN / 64) * 32 * 64 * sizeof(float);
+    void* base = nullptr;
+    int epoch = 0;
+    if (!stream_workspace(stream, kWorkspaceSplitK, counter_bytes + partial_bytes, &base, &epoch)) return false;
+    out->counters = static_cast<unsigned long long*>(base);
+    out->partials = reinterpret_cast<float*>(static_cast<char*>(base) + counter_bytes);
+    out->splits = splits;
+    out->epoch = epoch;
+    return true;
+}
+
 template <int BN, int BK, int STAGES, bool B_MN, bool ALLGATHER = false, bool SLOTS = false>
 int launch_pair_variant_peers(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb_half,
                               const CUtensorMap& mc, int M, int N, int K, int group, bool persistent, int tail_req,
-                              uint64_t limit_ns, cudaStream_t stream, int* status, const PeerOutputs& peers) {
+                              int k_splits, uint64_t limit_ns, cudaStream_t stream, int* status,
+                              const PeerOutputs& peers) {
     using L = PairLayout<BN, BK, STAGES, B_MN>;
     if (status == nullptr) status = default_status_ptr();
     if (status == nullptr) return KMCTS_EGEMM;
     kmcts_gemm_plan plan;
-    int rc = plan_pair_variant<BN, BK, STAGES, B_MN, ALLGATHER, SLOTS>(M, N, K, persistent, tail_req, group, &plan);
+    int rc = plan_pair_variant<BN, BK, STAGES, B_MN, ALLGATHER, SLOTS>(M, N, K, persistent, tail_req, group, k_splits,
+                                                                       &plan);
     if (rc != KMCTS_OK) return rc;
     TailSplit tail = {};
+    if (plan.k_splits > 1 && !split_workspace<BN>(stream, plan.tiles, plan.k_splits, &tail)) {
+        // No workspace (out of memory, or growth under graph capture): unsplit.
+        rc = plan_pair_variant<BN, BK, STAGES, B_MN, ALLGATHER, SLOTS>(M, N, K, persistent, tail_req, group, 0, &plan);
+        if (rc != KMCTS_OK) return rc;
+    }
     if (plan.tail_split == KMCTS_TAIL_STREAM_K && !tail_workspace(stream, plan.tail_clusters, &tail)) {
         // No workspace: the bit-identical N split (or whole tiles) instead.
         rc = plan_pair_variant<BN, BK, STAGES, B_MN, ALLGATHER, SLOTS>(M, N, K, persistent, KMCTS_TAIL_SPLIT_N,
-                                                                       group, &plan);
+                                                                       group, 0, &plan);
         if (rc != KMCTS_OK) return rc;
     }
-    tail.mode = plan.tail_split == KMCTS_TAIL_STREAM_K ? kTailStreamK
-                : plan.tail_split == KMCTS_TAIL_SPLIT_N ? kTailSplitN
-                                                        : kTailWhole;
+    tail.mode = plan.k_splits > 1                           ? kSplitK
+                : plan.tail_split == KMCTS_TAIL_STREAM_K ? kTailStreamK
+                : plan.tail_split == KMCTS_TAIL_SPLIT_N  ? kTailSplitN
+                                                         : kTailWhole;
     cudaLaunchConfig_t config = {};
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -894,21 +1024,21 @@ int launch_pair_variant_peers(const CUtensorMap& ma, const CUtensorMap& mb, cons
 template <int BN, int BK, int STAGES, bool B_MN, bool SLOTS>
 int launch_pair_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb_half,
                         const CUtensorMap& mc, int M, int N, int K, int group, bool persistent, int tail_req,
-                        uint64_t limit_ns, cudaStream_t stream, int* status) {
+                        int k_splits, uint64_t limit_ns, cudaStream_t stream, int* status) {
     const PeerOutputs none = {};
     return launch_pair_variant_peers<BN, BK, STAGES, B_MN, false, SLOTS>(
-        ma, mb, mb_half, mc, M, N, K, group, persistent, tail_req, limit_ns, stream, status, none);
+        ma, mb, mb_half, mc, M, N, K, group, persistent, tail_req, k_splits, limit_ns, stream, status, none);
 }
 
 template <int BN, int BK, int STAGES, bool B_MN, bool SLOTS>
-int plan_variant(int M, int N, int K, bool persistent, int tail, int group, kmcts_gemm_plan* out) {
-    return plan_pair_variant<BN, BK, STAGES, B_MN, false, SLOTS>(M, N, K, persistent, tail, group, out);
+int plan_variant(int M, int N, int K, bool persistent, int tail, int group, int k_splits, kmcts_gemm_plan* out) {
+    return plan_pair_variant<BN, BK, STAGES, B_MN, false, SLOTS>(M, N, K, persistent, tail, group, k_splits, out);
 }
 
 using PairLauncher = int (*)(const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, int,
-                             int, int, int, bool, int, uint64_t, cudaStream_t, int*);
+                             int, int, int, bool, int, int, uint64_t, cudaStream_t, int*);
 
-using PairPlanner = int (*)(int, int, int, bool, int, int, kmcts_gemm_plan*);
+using PairPlanner = int (*)(int, int, int, bool, int, int, int, kmcts_gemm_plan*);
 
 struct PairVariant {
     int bn, bk, stages, b_mn, slots;
@@ -964,7 +1094,7 @@ int64_t pair_smem_bytes(int bn, int bk, int stages) {
 int plan_pair(const kmcts_gemm_config& cfg, int M, int N, int K, int b_layout, kmcts_gemm_plan* out) {
     const PairVariant* v = find_pair_variant(cfg, b_layout);
     if (!v) return KMCTS_ENOTSUP;
-    return v->plan(M, N, K, cfg.persistent != 0, requested_tail(cfg.flags), cfg.raster_group, out);
+    return v->plan(M, N, K, cfg.persistent != 0, requested_tail(cfg.flags), cfg.raster_group, cfg.k_splits, out);
 }
 
 int launch_pair_allgather(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb_half,
@@ -986,11 +1116,11 @@ int launch_pair_allgather(const CUtensorMap& ma, const CUtensorMap& mb, const CU
     const int split = requested_tail(cfg.flags) == KMCTS_TAIL_NONE ? KMCTS_TAIL_NONE : KMCTS_TAIL_SPLIT_N;
     if (b_layout == KMCTS_B_ROW)
         return launch_pair_variant_peers<256, 128, 3, true, true>(ma, mb, mb_half, mc, M, N_shard, K,
-                                                                  cfg.raster_group, cfg.persistent != 0, split,
+                                                                  cfg.raster_group, cfg.persistent != 0, split, 0,
                                                                   limit_ns, stream, status, peers);
     return launch_pair_variant_peers<256, 128, 3, false, true>(ma, mb, mb_half, mc, M, N_shard, K, cfg.raster_group,
-                                                               cfg.persistent != 0, split, limit_ns, stream, status,
-                                                               peers);
+                                                               cfg.persistent != 0, split, 0, limit_ns, stream,
+                                                               status, peers);
 }
 
 int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb_half, const CUtensorMap& mc,
@@ -999,7 +1129,7 @@ int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap&
     const PairVariant* v = find_pair_variant(cfg, b_layout);
     if (!v) return KMCTS_ENOTSUP;
     return v->fn(ma, mb, mb_half, mc, M, N, K, cfg.raster_group, cfg.persistent != 0, requested_tail(cfg.flags),
-                 limit_ns, stream, status);
+                 cfg.k_splits, limit_ns, stream, status);
 }
 
 }  // namespace kmcts

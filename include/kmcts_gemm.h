@@ -81,11 +81,13 @@ typedef struct kmcts_gemm_config {
     int32_t kernel;       /* KMCTS_KERNEL_* */
     int32_t flags;        /* KMCTS_FLAG_* bits */
     int64_t wait_limit_ns; /* bound on each device-side wait; 0 = 2 s default */
-    int32_t k_splits;     /* one-CTA schedules: K ranges per tile (0 or 1 = none); see below */
+    int32_t k_splits;     /* one-CTA schedules and CTA pairs (cluster 2x1): K ranges per tile
+                             (0 or 1 = none); see below */
     int32_t reserved;     /* zero */
 } kmcts_gemm_config;
 
-/* Split K (tile_m 128 or 32).  With k_splits = S > 1 each output tile runs as S
+/* Split K (tile_m 128 or 32, and tile_m 256 pairs in clusters of two; it takes
+ * precedence over the pairs' tail splits).  With k_splits = S > 1 each output tile runs as S
  * units over consecutive K ranges, so a shape with few tiles (skinny M or N)
  * still streams its operands through every SM.  Each unit stores its FP32
  * partial in a per-stream library workspace and counts itself on the tile's
@@ -104,7 +106,8 @@ int kmcts_default_config(kmcts_gemm_config* cfg);
 /* Fills *cfg with the schedule a NULL cfg selects for this shape: for M <= 32,
  * one CTA per tile staging 32 rows of A (tile_m 32); else the default when its
  * 256 x 256 pair tiles fill the co-resident CTA pairs (with 64-deep stages when
- * K <= 768); else one CTA per
+ * K <= 768), or in two K splits when those fill three quarters of them and
+ * K >= 8192; else one CTA per
  * 128 x 256 tile while those fill them (the default again from K = 4096),
  * else one CTA per 128 x 128 tile.  Few tiles over a long K get split K.  Every
  * schedule gives results within the parity criterion and bit-exact ones on
@@ -150,7 +153,7 @@ typedef struct kmcts_gemm_plan {
     int32_t tail_split;   /* KMCTS_TAIL_*: how the tiles after full_tiles split */
     int32_t tail_clusters; /* pairs that share the tiles after full_tiles */
     int32_t tail_segments; /* most units one tile runs as (2 when split) */
-    int32_t k_splits;     /* one-CTA split K: K ranges per tile (1 = none) */
+    int32_t k_splits;     /* split K: K ranges per tile (1 = none) */
 } kmcts_gemm_plan;
 
 /* Fills *out with the launch shape kmcts_bf16_gemm_ex would use for this

@@ -494,6 +494,39 @@ def test_split_k_randn_within_criterion_and_deterministic(cuda_device, layout):
     assert report["passed"] and report["max_ulp_where_ref_ge_0.5"] <= 1, report
 
 
+@pytest.mark.parametrize("layout", ["col", "row"])
+@pytest.mark.parametrize("tile_k,stages", [(128, 3), (64, 6)])
+@pytest.mark.parametrize("shape,splits", [((512, 520, 2048), 3), ((300, 264, 1032), 4), ((256, 256, 4096), 16),
+                                          ((1024, 1024, 1024), 2)])
+def test_cta_pair_split_k_integer_inputs_bit_exact(cuda_device, layout, tile_k, stages, shape, splits):
+    """Split K on the CTA pair: each unit's FP32 rows of both CTAs go to the
+    workspace and the tile's last unit adds them in split order; integer
+    inputs stay exact (ragged tiles, empty second CTAs included)."""
+    m, n, k = shape
+    cfg = dict(kernel=_native.KERNEL_TCGEN05, tile_m=256, cluster_m=2, tile_n=256, tile_k=tile_k, stages=stages)
+    plan = plan_of(m, n, k, layout, k_splits=splits, **cfg)
+    want = min(splits, -(-k // tile_k))
+    assert plan["k_splits"] == want and plan["units"] == plan["tiles"] * want and plan["tail_split"] == _native.TAIL_NONE
+    a_t, b_t = oracle.integer_inputs(m, n, k, seed=splits)
+    expect = oracle.torch_bits(oracle.torch_reference(a_t, b_t))
+    c = run(a_t.cuda(), b_for(layout, b_t.cuda()), layout, k_splits=splits, **cfg)
+    np.testing.assert_array_equal(bits_of(c), expect)
+
+
+@pytest.mark.parametrize("layout", ["col", "row"])
+def test_cta_pair_split_k_randn_within_criterion_and_deterministic(cuda_device, layout):
+    m, n, k = 512, 1024, 8192
+    a_t, b_t = oracle.randn_inputs(m, n, k, seed=8, b_layout=layout)
+    a, b = a_t.cuda(), b_t.cuda()
+    c = run(a, b, layout, k_splits=4, **PAIR_128K)
+    again = run(a, b, layout, k_splits=4, **PAIR_128K)
+    assert torch.equal(c.view(torch.int16), again.view(torch.int16))  # fixed split order
+    whole = run(a, b, layout, **PAIR_128K)
+    ref64, mag = oracle.fp64_reference(a_t, b_t, layout)
+    report = oracle.parity_report(bits_of(c), bits_of(whole), ref64, mag, k)
+    assert report["passed"] and report["max_ulp_where_ref_ge_0.5"] <= 1, report
+
+
 def test_split_k_concurrent_streams_and_selection(cuda_device):
     """Skinny shapes select split K; two streams use separate workspaces."""
     m, n, k = 16, 4096, 8192

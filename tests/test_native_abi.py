@@ -62,8 +62,12 @@ def test_select_config_splits_k_for_skinny_shapes():
     assert km.select_config(1024, 1024, 1024, km.B_ROW).k_splits == 0  # short K: no split
     assert km.select_config(4096, 4096, 4096, km.B_ROW).k_splits == 0
     assert km.select_config(256, 256, 256, km.B_ROW).k_splits == 0  # K too short to split
-    # 128 tiles already fill most of the SMs: splitting would add waves and partials.
-    assert km.select_config(4096, 512, 16384, km.B_ROW).k_splits == 0
+    # 32 pair tiles over a long K: the pair schedule in two K splits.
+    pair_split = km.select_config(4096, 512, 16384, km.B_ROW)
+    assert (pair_split.tile_m, pair_split.tile_k, pair_split.stages, pair_split.k_splits) == (256, 64, 6, 2)
+    assert km.select_config(256, 8192, 8192, km.B_ROW).k_splits == 2
+    # ... not at K = 4096: one CTA per 128 x 256 tile.
+    assert km.select_config(2048, 1024, 4096, km.B_ROW).tile_m == 128
     assert km.select_config(2048, 256, 8192, km.B_ROW).k_splits == 4  # 32 tiles -> 128 units, one wave
     assert km.select_config(128, 128, 65536, km.B_ROW).k_splits == 16  # one tile: at most 16 splits
 
