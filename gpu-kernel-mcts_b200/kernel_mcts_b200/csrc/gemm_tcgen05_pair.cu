@@ -159,11 +159,11 @@ __device__ __forceinline__ Schedule make_schedule(int M, int N, int K, int BN, i
     return s;
 }
 
-template <int BN>
+template <int BN, bool SPLITK>
 __device__ __forceinline__ Unit schedule_unit(const Schedule& s, int i, const TailSplit& tail) {
     Unit out = {0, 0, BN, 0, s.num_kb, -1, -1, -1};
     int t, half_n = 0;
-    if (tail.mode == kSplitK) {
+    if (SPLITK) {
         const int u = s.cluster + i * s.clusters;
         t = u / tail.splits;
         out.tile = t;
@@ -262,7 +262,10 @@ constexpr int pair_threads() {
     return SLOTS ? kThreads + 64 : kThreads;
 }
 
-template <int BN, int BK, int STAGES, bool B_MN, bool ALLGATHER, bool SLOTS>
+// SPLITK instantiations run the split-K schedule (tail.mode kSplitK) and
+// nothing else; the others never see it, so their code is the same as
+// without split K.
+template <int BN, int BK, int STAGES, bool B_MN, bool ALLGATHER, bool SLOTS, bool SPLITK>
 __global__ void __launch_bounds__(pair_threads<SLOTS>(), 1)
     gemm_bf16_tcgen05_pair(const __grid_constant__ CUtensorMap map_a,
                            const __grid_constant__ CUtensorMap map_b,
@@ -273,6 +276,7 @@ __global__ void __launch_bounds__(pair_threads<SLOTS>(), 1)
     using L = PairLayout<BN, BK, STAGES, B_MN>;
     // The A exchange splits each stage's A into its two 64-deep K halves.
     static_assert(!SLOTS || (BK == 128 && !ALLGATHER), "the slot schedule is built for BK 128, plain GEMM");
+    static_assert(!SPLITK || (!SLOTS && !ALLGATHER), "split K is built for the plain pair schedule");
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~uintptr_t(1023));
@@ -310,7 +314,9 @@ __global__ void __launch_bounds__(pair_threads<SLOTS>(), 1)
     const Schedule sched =
         SLOTS ? make_slot_schedule(M, N, K, BN, BK, group, full_tiles, blockIdx.x / 4, gridDim.x / 4, tail)
               : make_schedule(M, N, K, BN, BK, group, full_tiles, blockIdx.x / 2, gridDim.x / 2, tail);
-    auto unit_at = [&](int u) { return SLOTS ? slot_unit<BN>(sched, u, pair_id, N) : schedule_unit<BN>(sched, u, tail); };
+    auto unit_at = [&](int u) {
+        return SLOTS ? slot_unit<BN>(sched, u, pair_id, N) : schedule_unit<BN, SPLITK>(sched, u, tail);
+    };
     // Slots assume clusters of consecutive blocks (4s .. 4s + 3, or 2t, 2t + 1
     // when the launch fell back to pairs); anything else computes nothing and
     // reports KMCTS_EGEMM.
@@ -619,7 +625,7 @@ __global__ void __launch_bounds__(pair_threads<SLOTS>(), 1)
                     __syncwarp();
                     if (lane == 0) ptx::mbar_arrive_cluster(ptx::mapa_shared(ptx::smem_addr(&tmem_empty[acc]), pair_base));
                 }
-                if (w.split >= 0) {
+                if (SPLITK) {
                     // Split K: store this K range's FP32 rows; the tile's last
                     // unit to arrive writes C after the loop.
                     float4* part = split_partial_chunk<BN>(tail, w.tile, w.split, static_cast<int>(rank), quarter, c);
@@ -677,7 +683,7 @@ __global__ void __launch_bounds__(pair_threads<SLOTS>(), 1)
                 store_chunk(&map_c, staging, chunk_count, lo, hi, lane, peers.col_offset + n0 + c * 64,
                             m0 + quarter * 32, ALLGATHER ? peers.map : nullptr, ALLGATHER ? peers.count : 0);
             }
-            if (w.split >= 0) {
+            if (SPLITK) {
                 // Publish this warp's rows of the partial, then count the
                 // unit; the tile's last unit sums every split in split order.
                 __threadfence();
@@ -775,7 +781,7 @@ constexpr int kMaxDevices = 64;
 template <int BN, int BK, int STAGES, bool B_MN, bool ALLGATHER = false, bool SLOTS = false>
 int pair_workers(int device) {
     using L = PairLayout<BN, BK, STAGES, B_MN>;
-    auto kernel = gemm_bf16_tcgen05_pair<BN, BK, STAGES, B_MN, ALLGATHER, SLOTS>;
+    auto kernel = gemm_bf16_tcgen05_pair<BN, BK, STAGES, B_MN, ALLGATHER, SLOTS, false>;
     static std::mutex mu;
     static int max_clusters[kMaxDevices] = {};
     std::lock_guard<std::mutex> lock(mu);
@@ -968,6 +974,25 @@ bool split_workspace(cudaStream_t stream, int tiles, int splits, TailSplit* out)
     return true;
 }
 
+// The split-K instantiation's shared-memory opt-in (per device, once); its
+// occupancy is the plain one's (same shared memory and block).
+template <int BN, int BK, int STAGES, bool B_MN>
+bool split_smem_configured() {
+    static std::mutex mu;
+    static bool done[kMaxDevices] = {};
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kMaxDevices) return false;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!done[device]) {
+        if (cudaFuncSetAttribute(gemm_bf16_tcgen05_pair<BN, BK, STAGES, B_MN, false, false, true>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 PairLayout<BN, BK, STAGES, B_MN>::kSmemBytes) != cudaSuccess)
+            return false;
+        done[device] = true;
+    }
+    return true;
+}
+
 template <int BN, int BK, int STAGES, bool B_MN, bool ALLGATHER = false, bool SLOTS = false>
 int launch_pair_variant_peers(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb_half,
                               const CUtensorMap& mc, int M, int N, int K, int group, bool persistent, int tail_req,
@@ -1014,9 +1039,19 @@ int launch_pair_variant_peers(const CUtensorMap& ma, const CUtensorMap& mb, cons
     config.stream = stream;
     config.attrs = attr;
     config.numAttrs = SLOTS ? 2 : 1;
-    const cudaError_t err =
-        cudaLaunchKernelEx(&config, gemm_bf16_tcgen05_pair<BN, BK, STAGES, B_MN, ALLGATHER, SLOTS>, ma, mb, mb_half,
-                           mc, M, N, K, group, plan.full_tiles, limit_ns, status, peers, tail);
+    cudaError_t err;
+    if constexpr (!SLOTS && !ALLGATHER) {
+        if (tail.mode == kSplitK) {
+            auto split_kernel = gemm_bf16_tcgen05_pair<BN, BK, STAGES, B_MN, false, false, true>;
+            if (!split_smem_configured<BN, BK, STAGES, B_MN>()) return KMCTS_EGEMM;
+            err = cudaLaunchKernelEx(&config, split_kernel, ma, mb, mb_half, mc, M, N, K, group, plan.full_tiles,
+                                     limit_ns, status, peers, tail);
+            g_launches.fetch_add(1, std::memory_order_relaxed);
+            return err == cudaSuccess ? KMCTS_OK : KMCTS_EGEMM;
+        }
+    }
+    err = cudaLaunchKernelEx(&config, gemm_bf16_tcgen05_pair<BN, BK, STAGES, B_MN, ALLGATHER, SLOTS, false>, ma, mb,
+                             mb_half, mc, M, N, K, group, plan.full_tiles, limit_ns, status, peers, tail);
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return err == cudaSuccess ? KMCTS_OK : KMCTS_EGEMM;
 }
