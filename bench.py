@@ -397,10 +397,16 @@ def sharded_gemm(device, world: int, local_rank: int, steps: int = 5, warmup: in
     """8192x28672x8192, N(0, 0.02^2) BF16, B and C sharded by
     N columns over the ranks.  The fused kernel (GEMM + all-gather of C over
     NVLink peer stores) against the same GEMM followed by NCCL all_gather and
-    a re-layout; aggregate TFLOP/s = 2MNK / max-over-ranks median time."""
+    a re-layout; aggregate TFLOP/s = 2MNK / max-over-ranks median time.
+
+    Outside the timed region every rank checks its full C, on the first and
+    last 256 rows (the first and last row tiles) and all columns, bit for bit
+    against the single-GPU kernel run on those rows of the whole problem;
+    ``bit_identical`` is the AND over ranks and paths."""
     import torch
     import torch.distributed as dist
 
+    from kernel_mcts_b200 import gemm as kg
     from kernel_mcts_b200.sharded import ShardedGemm
 
     m, n, k = 8192, 28672, 8192
@@ -409,12 +415,17 @@ def sharded_gemm(device, world: int, local_rank: int, steps: int = 5, warmup: in
         if not dist.is_initialized():
             dist.init_process_group("gloo", init_method="tcp://127.0.0.1:29555", rank=0, world_size=1)
             dist_owned = True
-    g = torch.Generator(device=device).manual_seed(0)
+    g = torch.Generator(device=device).manual_seed(0)  # the same A and B on every rank
     a = (torch.randn((m, k), generator=g, device=device) * 0.02).to(torch.bfloat16)
+    b_full = (torch.randn((k, n), generator=g, device=device) * 0.02).to(torch.bfloat16)
     sg = ShardedGemm(m, n, k, b_layout="row")
-    b_shard = (torch.randn((k, sg.shard_width), generator=g, device=device) * 0.02).to(torch.bfloat16)
+    b_shard = b_full[:, sg.col0:sg.col1].contiguous()
+    rows = torch.cat([torch.arange(0, 256, device=device), torch.arange(m - 256, m, device=device)])
+    single = kg.bf16_gemm(a[rows].contiguous(), b_full, b_layout="row", config=sg.config)
+    torch.cuda.synchronize(device)
     stream = torch.cuda.current_stream(device)
     out = {"workload": "8192x28672x8192 N(0,0.02) bf16, B/C sharded by N", "gpus": world}
+    identical = True
     try:
         for name, fn in (("fused", sg.run), ("nccl", sg.run_nccl)):
             if world == 1 and name == "nccl":
@@ -438,6 +449,17 @@ def sharded_gemm(device, world: int, local_rank: int, steps: int = 5, warmup: in
                 dist.all_reduce(med, op=dist.ReduceOp.MAX)
             out[f"{name}_median_us"] = float(med.item())
             out[f"{name}_tflops"] = 2.0 * m * n * k / (float(med.item()) * 1e-6) / 1e12
+            # Untimed: this rank's full C (every rank's columns) on the sampled
+            # rows against the single-GPU kernel; AND over ranks.
+            same = torch.tensor([1 if torch.equal(sg.c[rows].view(torch.int16), single.view(torch.int16)) else 0],
+                                dtype=torch.int32, device=device)
+            if world > 1:
+                dist.all_reduce(same, op=dist.ReduceOp.MIN)
+            out[f"{name}_bit_identical"] = bool(same.item())
+            identical = identical and bool(same.item())
+        out["bit_identical"] = identical
+        out["bit_identity_check"] = ("every rank's full C, rows [0,256) and [8192-256,8192), all 28672 columns, "
+                                     "against the single-GPU kernel on those rows of the whole problem")
     finally:
         sg.close()
         if world == 1 and dist_owned:
@@ -561,7 +583,8 @@ def run_ours(args: argparse.Namespace) -> None:
 
     if rank == 0:
         peaks, peaks_kind = load_peaks()
-        achieved = FLOPS / (mean_ours * 1e-6) / 1e12
+        # Same median launch time as `value` (per GPU), so frac = value / (N * peak).
+        achieved = FLOPS / (med_ours * 1e-6) / 1e12
         peak = float(peaks["bf16_tflops"])
         value = world * FLOPS / (med_ours * 1e-6) / 1e12
         cpu = None
@@ -614,6 +637,8 @@ def run_ours(args: argparse.Namespace) -> None:
                 "traffic": profiled_traffic(),
                 "peak_source": f"{peaks_kind} bf16_tflops (burst; kernel timed alone)",
                 "algorithmic_flops_per_launch": FLOPS,
+                "launch_time": "median of the event-timed launches (as value)",
+                "achieved_from_mean": FLOPS / (mean_ours * 1e-6) / 1e12,
             },
             "cpu_baseline": cpu,
             "e2e": e2e,

@@ -126,9 +126,9 @@ int compare_bf16_device(const void* C, const void* reference, int64_t count, dou
 // Some callers cannot call cudaMalloc at the moment they want a correctness
 // check: a worker in the middle of an evaluation whose memory budget is fully
 // owned by another allocator (a framework caching allocator that must see
-// every device allocation), code running while a stream is being captured
-// (where cudaMalloc is not permitted), or an embedding host whose only device
-// memory is the inputs and outputs it already passes in.  For them the
+// every device allocation, or it may run the device out of memory), or an
+// embedding host whose only device memory is the inputs and outputs it
+// already passes in.  For them the
 // comparison's scratch (its reduction accumulators) lives in this file-scope
 // device array instead of a caller-provided workspace.  Every GPU that loads
 // the library holds these bytes until the process exits.

@@ -100,7 +100,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_tcgen05(const __grid_constant__ CUtensorMap map_a,
                       const __grid_constant__ CUtensorMap map_b,
                       const __grid_constant__ CUtensorMap map_c, int M, int N, int K, int group,
-                      uint64_t limit_ns, int* status, const SplitK sk) {
+                      uint64_t limit_ns, int* status, const SplitK sk, int b_evict_first) {
     using L = Layout<BN, BK, STAGES, B_MN, AR>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -159,6 +159,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t phase = 0;
             uint32_t issued = 0, issued_phase = 0;
             bool ok = true;
+            // B read once (one M tile): its lines go first when L2 needs room.
+            const uint64_t b_policy = b_evict_first ? ptx::policy_evict_first() : 0ull;
             for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
                 const int t = u / splits, s = u % splits;
                 const TileCoord tc = tile_coord(t, num_m, num_n, group);
@@ -181,11 +183,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if constexpr (B_MN) {
 #pragma unroll
                             for (int nb = 0; nb < BN / 64; ++nb) {
-                                ptx::tma_load_2d(sb + (kh * (BN / 64) + nb) * 8192, &map_b,
-                                                 &full[stage], n0 + nb * 64, k0);
+                                uint8_t* dst = sb + (kh * (BN / 64) + nb) * 8192;
+                                if (b_evict_first)
+                                    ptx::tma_load_2d_hint(dst, &map_b, &full[stage], n0 + nb * 64, k0, b_policy);
+                                else
+                                    ptx::tma_load_2d(dst, &map_b, &full[stage], n0 + nb * 64, k0);
                             }
                         } else {
-                            ptx::tma_load_2d(sb + kh * (BN * 128), &map_b, &full[stage], k0, n0);
+                            if (b_evict_first)
+                                ptx::tma_load_2d_hint(sb + kh * (BN * 128), &map_b, &full[stage], k0, n0, b_policy);
+                            else
+                                ptx::tma_load_2d(sb + kh * (BN * 128), &map_b, &full[stage], k0, n0);
                         }
                     }
                     issued |= 1u << stage;
@@ -399,8 +407,8 @@ int resolve_splits(int M, int N, int K, int requested, cudaStream_t stream, Spli
 
 template <int BN, int BK, int STAGES, bool B_MN, int AR>
 int launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, int M,
-                   int N, int K, int group, bool persistent, int k_splits, uint64_t limit_ns,
-                   cudaStream_t stream, int* status) {
+                   int N, int K, int group, bool persistent, int k_splits, bool b_evict_first,
+                   uint64_t limit_ns, cudaStream_t stream, int* status) {
     using L = Layout<BN, BK, STAGES, B_MN, AR>;
     auto kernel = gemm_bf16_tcgen05<BN, BK, STAGES, B_MN, AR>;
     // The shared-memory opt-in is per device; set it once on each.
@@ -424,13 +432,13 @@ int launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorM
     int grid = units;
     if (persistent) grid = units < multiprocessor_count() ? units : multiprocessor_count();
     kernel<<<grid, kThreads, L::kSmemBytes, stream>>>(ma, mb, mc, M, N, K, group, limit_ns,
-                                                      status, sk);
+                                                      status, sk, b_evict_first ? 1 : 0);
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return cudaGetLastError() == cudaSuccess ? KMCTS_OK : KMCTS_EGEMM;
 }
 
 using Launcher = int (*)(const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, int, int,
-                         int, int, bool, int, uint64_t, cudaStream_t, int*);
+                         int, int, bool, int, bool, uint64_t, cudaStream_t, int*);
 
 struct Variant {
     int bn, bk, stages, b_mn, ar;
@@ -606,8 +614,8 @@ int launch_tcgen05(const void* A, const void* B, void* C, int M, int N, int K, i
         cfg.wait_limit_ns > 0 ? static_cast<uint64_t>(cfg.wait_limit_ns) : kDefaultWaitNs;
     if (pair) return launch_pair(ma, mb, mb_half, mc, M, N, K, b_layout, cfg, limit, stream, device_status);
     const Variant* v = find_variant(cfg, b_layout);
-    return v->fn(ma, mb, mc, M, N, K, cfg.raster_group, cfg.persistent != 0, cfg.k_splits, limit, stream,
-                 device_status);
+    return v->fn(ma, mb, mc, M, N, K, cfg.raster_group, cfg.persistent != 0, cfg.k_splits,
+                 (cfg.flags & KMCTS_FLAG_B_EVICT_FIRST) != 0, limit, stream, device_status);
 }
 
 int launch_allgather_tcgen05(const void* A, const void* B_shard, void* const* C_ranks, int num_ranks, int rank,

@@ -1,9 +1,11 @@
 """Evaluation-contract data types.
 
-Field names and enum values are the reference's wire contract
+This module restates the reference's domain types
 (src/kernel_mcts/domain.py:8-135, serialised by serialization.py:24-79): the
-MCTS, sequential, autotune and profiling callers read these names, so they
-stay identical.  The classes themselves are written for this package.
+same enums and frozen dataclasses, field for field, with the same validation.
+They are the wire contract that the MCTS, sequential, autotune and profiling
+callers read, so names, values and field order are kept as the reference has
+them; only the layout of the source differs.
 """
 
 from __future__ import annotations

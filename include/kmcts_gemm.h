@@ -60,6 +60,12 @@ extern "C" {
 #define KMCTS_FLAG_NO_TAIL_SPLIT 1
 #define KMCTS_FLAG_TAIL_SPLIT_N 2  /* the default; kept for explicit requests */
 #define KMCTS_FLAG_TAIL_STREAM_K 4
+/* One-CTA schedules (tile_m 128 or 32): B's loads carry an L2 evict-first
+ * policy.  For shapes whose M fits one tile row B is read exactly once, and
+ * streaming it through L2 at normal priority would push out everything else
+ * there (dirty lines cost a DRAM write-back on eviction).  Results are
+ * unchanged; only the cache policy differs. */
+#define KMCTS_FLAG_B_EVICT_FIRST 8
 
 #define KMCTS_TAIL_NONE 0     /* kmcts_gemm_plan.tail_split: every tile whole */
 #define KMCTS_TAIL_SPLIT_N 1  /* last wave as half-width units */
@@ -97,7 +103,11 @@ typedef struct kmcts_gemm_config {
  * number of K blocks; launches on a stream under CUDA-graph capture before its
  * workspace is large enough run unsplit.  Workspaces are never freed, so a
  * graph that captured one stays valid; graphs captured on one stream share
- * that stream's workspace and must not replay concurrently. */
+ * that stream's workspace and must not replay concurrently.  Every direct
+ * launch tags the counters with a new epoch, but a graph replays the epoch it
+ * captured: after a replay that reported KMCTS_ETIMEOUT, capture the graph
+ * again before replaying it (the failed launch may have left arrivals counted
+ * under that epoch). */
 
 /* Fills *cfg with the tuned default schedule for B200 (the CTA-pair 256 x 256
  * x 128, 3-stage schedule that is fastest at 4096^3). Returns KMCTS_OK. */
@@ -109,7 +119,8 @@ int kmcts_default_config(kmcts_gemm_config* cfg);
  * K <= 768), or in two K splits when those fill three quarters of them and
  * K >= 8192; else one CTA per
  * 128 x 256 tile while those fill them (the default again from K = 4096),
- * else one CTA per 128 x 128 tile.  Few tiles over a long K get split K.  Every
+ * else one CTA per 128 x 128 tile.  Few tiles over a long K get split K; one-CTA
+ * schedules for M <= 128 (one tile row) add KMCTS_FLAG_B_EVICT_FIRST.  Every
  * schedule gives results within the parity criterion and bit-exact ones on
  * integer inputs.  Returns KMCTS_OK or KMCTS_EINVAL. */
 int kmcts_select_config(int M, int N, int K, int b_layout, kmcts_gemm_config* cfg);
@@ -230,9 +241,11 @@ int kmcts_bf16_compare(const void* C, const void* reference, int64_t count, doub
 
 /* No counterpart in the reference.  kmcts_bf16_compare without a workspace
  * argument, for callers that cannot allocate device memory when they check a
- * result: a worker whose device memory is owned by another allocator, code
- * running while a stream is being captured (cudaMalloc is not permitted
- * there), or a host that only holds the tensors it passes in.  The scratch is
+ * result: a worker whose device memory is all owned by another allocator (a
+ * framework's caching allocator that must account for every byte, so a
+ * cudaMalloc behind its back could push it out of memory), or a host
+ * application that embeds this library and hands it only the tensors it
+ * passes in, with no allocation rights of its own.  The scratch is
  * a file-scope device array of KMCTS_NOALLOC_SCRATCH_BYTES (256 bytes) that
  * every GPU loading this library keeps until the process exits; the
  * comparison needs that much for any `count`, and a call needing more would

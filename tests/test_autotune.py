@@ -125,7 +125,8 @@ def test_schedule_programs_tune_schedule_fields():
 
 
 def test_trial_order_matches_the_reference_autotuner():
-    ref_root = Path("/root/reference/src")
+    from reference_tree import REFERENCE_SRC as ref_root
+
     if not ref_root.exists():
         pytest.skip("reference source tree not present")
     sys.path.insert(0, str(ref_root))

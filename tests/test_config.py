@@ -14,7 +14,7 @@ from kernel_mcts_b200.config import B200_WORKLOAD, SM100_STRATEGIES, load_data, 
 from kernel_mcts_b200.domain import KernelProgram
 from kernel_mcts_b200.workloads import BF16_GEMM_4096_B200
 
-REFERENCE_SRC = Path("/root/reference/src")
+from reference_tree import REFERENCE_SRC
 
 
 def test_sm100_strategies_load_and_have_cuda_prompts():

@@ -195,7 +195,7 @@ def test_evaluation_round_trips_through_wire_json():
     assert back.benchmark.median_us == result.benchmark.median_us
 
 
-REFERENCE_SRC = Path("/root/reference/src")
+from reference_tree import REFERENCE_SRC  # noqa: E402
 
 
 @pytest.mark.skipif(not (REFERENCE_SRC / "kernel_mcts" / "evaluation.py").exists(),

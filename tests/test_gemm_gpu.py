@@ -343,26 +343,62 @@ def test_tcgen05_4096_integer_bit_exact_and_matches_cublas(cuda_device):
     assert kg.compare(c_row, ref).ulp_hist[0] == n * n
 
 
-def test_tcgen05_4096_randn_within_one_ulp_or_bound(cuda_device):
-    """4096^3 N(0,1) BF16 inputs, seed 0."""
+@pytest.mark.parametrize("layout", ["row", "col"])
+def test_config1_256_randn_seed0_against_the_reference_cpu_path(cuda_device, layout):
+    """BASELINE config 1 exactly: M = N = K = 256, A and B N(0,1) from seed 0
+    (CPU generator, B generated row-major [K, N] as the config states) cast to
+    BF16, against the reference's CPU-runnable check
+    torch.matmul(a.float(), b.float().T).to(bfloat16)
+    (src/kernel_mcts/cute_independent_tma.py:1030-1032) and the FP64 bound.
+    Both B layouts carry the same matrix; every tcgen05 schedule (the NULL-config
+    selection, the CTA-pair default, a one-CTA schedule) gives the same bits."""
+    n = 256
+    a_t, b_kn = oracle.randn_inputs(n, n, n, seed=0, b_layout="row")
+    ref32 = oracle.torch_bits(oracle.torch_reference(a_t, b_kn, "row"))
+    ref64, mag = oracle.fp64_reference(a_t, b_kn, "row")
+    b_dev = b_kn.cuda() if layout == "row" else b_kn.T.contiguous().cuda()
+    schedules = {
+        "select": None,
+        "pair": dict(kernel=_native.KERNEL_TCGEN05),
+        "one_cta": dict(kernel=_native.KERNEL_TCGEN05, tile_m=128, cluster_m=1, tile_n=256, tile_k=64, stages=4),
+    }
+    outputs = {}
+    for name, cfg in schedules.items():
+        c = run(a_t.cuda(), b_dev, layout) if cfg is None else run(a_t.cuda(), b_dev, layout, **cfg)
+        bits = bits_of(c)
+        report = oracle.parity_report(bits, ref32, ref64, mag, n)
+        assert report["passed"] and report["max_ulp_where_ref_ge_0.5"] <= 1, (name, report)
+        assert oracle.harness_check(bits, ref32)["success"], name
+        outputs[name] = bits
+    np.testing.assert_array_equal(outputs["pair"], outputs["select"])
+    np.testing.assert_array_equal(outputs["one_cta"], outputs["select"])
+
+
+@pytest.mark.parametrize("layout", ["row", "col"])
+def test_tcgen05_4096_randn_within_one_ulp_or_bound(cuda_device, layout):
+    """4096^3 N(0,1) BF16 inputs, seed 0, in the bench's
+    layout (row-major B, generated as [K, N]) and the reference contract's
+    (column-major B, generated as [N, K])."""
     n = 4096
-    a_t, b_t = oracle.randn_inputs(n, n, n, seed=0)
-    c = run(a_t.cuda(), b_t.cuda(), "col")
-    ref32 = oracle.torch_bits(oracle.torch_reference(a_t, b_t))
-    ref64, mag = oracle.fp64_reference(a_t, b_t)
+    a_t, b_t = oracle.randn_inputs(n, n, n, seed=0, b_layout=layout)
+    c = run(a_t.cuda(), b_t.cuda(), layout)
+    ref32 = oracle.torch_bits(oracle.torch_reference(a_t, b_t, layout))
+    ref64, mag = oracle.fp64_reference(a_t, b_t, layout)
     report = oracle.parity_report(bits_of(c), ref32, ref64, mag, n)
     assert report["passed"], report
     # Where |ref| >= 0.5 the FP32 reordering error (~K^0.5 * 2^-24 * |partial
     # sums|) is far below half a BF16 ulp, so those elements sit within 1 ulp.
     d = oracle.ulp_distance(bits_of(c), ref32)
     assert int(d[np.abs(ref64) >= 0.5].max()) <= 1
+    assert oracle.harness_check(bits_of(c), ref32)["success"]
     # Same-run cuBLAS (tensor cores, FP32 accumulate, the same K order per
     # output) gives the same bits.
-    cublas = oracle.torch_bits(torch.matmul(a_t.cuda(), b_t.cuda().T))
+    b_torch = b_t.cuda().T if layout == "col" else b_t.cuda()
+    cublas = oracle.torch_bits(torch.matmul(a_t.cuda(), b_torch))
     np.testing.assert_array_equal(bits_of(c), cublas)
     # The stream-K tail sums two FP32 chains in its cut tiles: within 1 ulp of
     # cuBLAS wherever |ref| >= 0.5, and within the criterion everywhere.
-    sk = bits_of(run(a_t.cuda(), b_t.cuda(), "col", flags=SK))
+    sk = bits_of(run(a_t.cuda(), b_t.cuda(), layout, flags=SK))
     assert int(oracle.ulp_distance(sk, cublas)[np.abs(ref64) >= 0.5].max()) <= 1
     assert oracle.parity_report(sk, cublas, ref64, mag, n)["passed"]
 
@@ -391,6 +427,19 @@ def test_config4_full_size_integer_exact_and_randn_matches_cublas(cuda_device):
     assert cmp.success and cmp.n_nonfinite == 0 and sum(cmp.ulp_hist[2:]) == 0, cmp  # none beyond 1 ulp
     c_row = run(a, b_nk.T.contiguous(), "row")
     assert torch.equal(c_row.view(torch.int16), c_col.view(torch.int16))
+    # A row sample against the CPU oracle: the first and last 32 rows (the
+    # first and last row tiles), all 28,672 columns, checked against the
+    # reference's CPU path torch.matmul(a.float(), b.float().T).bfloat16()
+    # and the FP64 bound.
+    rows = torch.cat([torch.arange(0, 32), torch.arange(m - 32, m)])
+    a_rows = a[rows.cuda()].cpu()
+    b_cpu = b_nk.cpu()
+    ref32 = oracle.torch_bits(oracle.torch_reference(a_rows, b_cpu))
+    ref64, mag = oracle.fp64_reference(a_rows, b_cpu)
+    sample = bits_of(c_col[rows.cuda()])
+    report = oracle.parity_report(sample, ref32, ref64, mag, k)
+    assert report["passed"] and report["max_ulp_where_ref_ge_2^-6"] <= 1, report
+    assert oracle.harness_check(sample, ref32)["success"]
 
 
 # ------------------------------------------------------------- ABI details
@@ -514,6 +563,25 @@ def test_cta_pair_split_k_integer_inputs_bit_exact(cuda_device, layout, tile_k, 
 
 
 @pytest.mark.parametrize("layout", ["col", "row"])
+def test_cta_pair_split_k_persistent_round_robin_bit_exact(cuda_device, layout):
+    """More split units than co-resident pairs: each persistent pair runs
+    several split units in turn, alternating TMEM accumulators and staging
+    buffers between them, with the last arriver of each tile reducing.
+    Integer inputs are exact, and a second launch repeats every bit."""
+    m, n, k, splits = 2048, 2048, 8192, 4
+    cfg = dict(PAIR_128K, persistent=1)
+    plan = plan_of(m, n, k, layout, k_splits=splits, **cfg)
+    assert plan["units"] == plan["tiles"] * splits and plan["units"] > plan["ctas"] // 2, plan
+    a_t, b_t = oracle.integer_inputs(m, n, k, seed=11)
+    expect = oracle.torch_bits(oracle.torch_reference(a_t, b_t))
+    a, b = a_t.cuda(), b_for(layout, b_t.cuda())
+    first = run(a, b, layout, k_splits=splits, **cfg)
+    second = run(a, b, layout, k_splits=splits, **cfg)
+    np.testing.assert_array_equal(bits_of(first), expect)
+    assert torch.equal(first.view(torch.int16), second.view(torch.int16))
+
+
+@pytest.mark.parametrize("layout", ["col", "row"])
 def test_cta_pair_split_k_randn_within_criterion_and_deterministic(cuda_device, layout):
     m, n, k = 512, 1024, 8192
     a_t, b_t = oracle.randn_inputs(m, n, k, seed=8, b_layout=layout)
@@ -558,13 +626,35 @@ SKINNY = [(256, 64, 5), (128, 64, 9), (128, 128, 4)]
 @pytest.mark.parametrize("shape,splits", [((1, 520, 1032), 1), ((16, 1024, 2048), 3), ((32, 264, 4096), 8),
                                           ((7, 2048, 512), 1)])
 def test_skinny_a_rows_integer_exact(cuda_device, layout, tile_n, tile_k, stages, shape, splits):
-    """tile_m 32 stages 32 rows of A; the MMA's other 96 rows are discarded."""
+    """tile_m 32 stages 32 rows of A; the MMA's other 96 rows are discarded.
+    The evict-first cache policy on B's loads changes no bit."""
     m, n, k = shape
     a_t, b_t = oracle.integer_inputs(m, n, k, seed=m + splits)
     expect = oracle.torch_bits(oracle.torch_reference(a_t, b_t))
-    c = run(a_t.cuda(), b_for(layout, b_t.cuda()), layout, kernel=_native.KERNEL_TCGEN05, tile_m=32, cluster_m=1,
-            tile_n=tile_n, tile_k=tile_k, stages=stages, k_splits=splits)
+    for flags in (0, _native.FLAG_B_EVICT_FIRST):
+        c = run(a_t.cuda(), b_for(layout, b_t.cuda()), layout, kernel=_native.KERNEL_TCGEN05, tile_m=32,
+                cluster_m=1, tile_n=tile_n, tile_k=tile_k, stages=stages, k_splits=splits, flags=flags)
+        np.testing.assert_array_equal(bits_of(c), expect)
+
+
+@pytest.mark.parametrize("layout", ["col", "row"])
+@pytest.mark.parametrize("shape", [(16, 8192, 8192), (128, 16384, 4096), (100, 1000, 2048)])
+def test_skinny_selection_streams_b_evict_first_same_bits(cuda_device, layout, shape):
+    """The NULL-config selection for one-tile-row shapes sets the evict-first
+    policy; its results equal the same schedule without it, bit for bit, and
+    are exact on integer inputs."""
+    m, n, k = shape
+    sel = _native.select_config(m, n, k, _native.B_ROW if layout == "row" else _native.B_COL)
+    assert sel.flags & _native.FLAG_B_EVICT_FIRST and sel.tile_m in (32, 128)
+    a_t, b_t = oracle.integer_inputs(m, n, k, seed=5)
+    expect = oracle.torch_bits(oracle.torch_reference(a_t, b_t))
+    a, b = a_t.cuda(), b_for(layout, b_t.cuda())
+    c = run(a, b, layout)  # NULL config
     np.testing.assert_array_equal(bits_of(c), expect)
+    plain = {name: getattr(sel, name) for name, _ in sel._fields_}
+    plain["flags"] &= ~_native.FLAG_B_EVICT_FIRST
+    c_plain = run(a, b, layout, **plain)
+    assert torch.equal(c.view(torch.int16), c_plain.view(torch.int16))
 
 
 def test_library_timing_loop_matches_the_protocol(cuda_device):

@@ -1,10 +1,11 @@
 """The allocation-free comparison entry point, kmcts_bf16_compare_noalloc.
 
 It exists for callers that cannot allocate device memory when they check a
-result (a worker whose device memory belongs to another allocator, code
-running during stream capture, a host holding only its own tensors): its
-scratch is a static device array inside the library instead of a workspace
-the caller passes.  This file is named so pytest collects it last.
+result: a worker whose device memory all belongs to another allocator that
+must account for every byte, or a host application that embeds the library
+and hands it only the tensors it passes in.  Its scratch is a static device
+array inside the library instead of a workspace the caller passes.  This file
+is named so pytest collects it last.
 """
 
 from __future__ import annotations
@@ -62,6 +63,11 @@ def test_noalloc_compare_matches_workspace_compare_on_two_calls(cuda_device):
         assert got.n_nonfinite == expect.n_nonfinite
         assert tuple(got.ulp_hist) == expect.ulp_hist
         assert got.max_ulp == expect.max_ulp
+        # And against the CPU restatement of the reference harness's check.
+        host = oracle.harness_check(c_bits, ref_bits, rtol=0.02, atol=0.02)
+        assert bool(got.success) == host["success"]
+        assert got.maximum_error == pytest.approx(host["maximum_error"], rel=1e-12, abs=0.0)
+        assert got.mean_error == pytest.approx(host["mean_error"], rel=1e-9, abs=0.0)
 
 
 def test_noalloc_compare_rejects_bad_arguments(cuda_device):
