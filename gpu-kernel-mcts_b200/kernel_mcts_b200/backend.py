@@ -46,7 +46,7 @@ from .evaluation import (
     CandidateTimeoutError,
     EvaluationInfrastructureError,
 )
-from .profiling import ProfileParseError, parse_ncu_csv, resolve_metric_set
+from .profiling import ProfileParseError, metrics_missing_from_query, parse_ncu_csv, resolve_metric_set
 
 CANDIDATE_BACKEND = "cuda_cpp"
 SCHEDULE_BACKEND = "kmcts_sm100"
@@ -255,6 +255,7 @@ class CudaSm100Backend:
         self.config = config
         self._runner = runner or run_command
         self._compiler_output: dict[str, str] = {}
+        self._validated_metric_sets: set[str] = set()
 
     # -------------------------------------------------------------- compile
 
@@ -468,21 +469,50 @@ class CudaSm100Backend:
         return {"backend": self.name, "architecture": self.config.architecture, "abi": artifact.abi,
                 "schedule_args": list(artifact.extra_args)}
 
+    def profile_target_command(self, artifact: Sm100Artifact, workload: WorkloadContract) -> list[str]:
+        """The harness command a lightweight profile runs under ncu: one
+        benchmark launch, no warm-ups (as src/kernel_mcts/cuda_backend.py:345-368)."""
+        command = self._command(artifact, workload, "benchmark")
+        return [command[0], *[arg for arg in command[1:] if not arg.startswith(("--warmups=", "--measurements="))],
+                "--warmups=0", "--measurements=1"]
+
+    def validate_metric_set(self, definition) -> None:
+        """Checks once per metric set that this GPU's ncu offers every metric
+        in it (``ncu --query-metrics-mode all --devices 0``, the device the
+        harness runs on), as src/kernel_mcts/cuda_backend.py:413-461 does for
+        non-default sets.  Raises EvaluationInfrastructureError naming what is
+        missing."""
+        if definition.id == "lightweight_v1" or definition.id in self._validated_metric_sets:
+            return
+        command = [_resolve_tool(self.config.ncu), "--query-metrics-mode", "all", "--devices", "0"]
+        try:
+            result = self._runner(command, timeout=self.config.profile_timeout_seconds,
+                                  env=self.config.subprocess_environment)
+        except (OSError, subprocess.TimeoutExpired) as error:
+            raise EvaluationInfrastructureError("Nsight Compute metric validation could not be completed") from error
+        if result.returncode != 0:
+            raise EvaluationInfrastructureError(
+                "Nsight Compute metric validation failed: " + _bounded(result.stderr + result.stdout, 2000))
+        missing = metrics_missing_from_query(definition, f"{result.stdout}\n{result.stderr}")
+        if missing:
+            preview = ", ".join(missing[:8]) + (", ..." if len(missing) > 8 else "")
+            raise EvaluationInfrastructureError(
+                f"Nsight Compute metric set {definition.id!r} is unavailable; missing: {preview}")
+        self._validated_metric_sets.add(definition.id)
+
     def lightweight_profile(self, artifact: Sm100Artifact, workload: WorkloadContract,
                             metric_set: str = "lightweight_v1") -> Mapping[str, object]:
         try:
             definition = resolve_metric_set(metric_set, self.config.architecture)
         except ValueError as error:
             raise EvaluationInfrastructureError(str(error)) from error
+        self.validate_metric_set(definition)
         command = [
             _resolve_tool(self.config.ncu), "--csv", "--page", "raw", "--log-file", "stdout",
             "--clock-control", "none", "--kernel-name-base", "function",
             "--kernel-name", f"regex:{definition.kernel_regex(artifact.abi)}",
             "--launch-count", "1", "--metrics", ",".join(definition.metrics),
-            *self._command(artifact, workload, "benchmark")[:1],
-            *[arg for arg in self._command(artifact, workload, "benchmark")[1:]
-              if not arg.startswith(("--warmups=", "--measurements="))],
-            "--warmups=0", "--measurements=1",
+            *self.profile_target_command(artifact, workload),
         ]
         try:
             result = self._runner(command, timeout=self.config.profile_timeout_seconds,

@@ -17,7 +17,9 @@ Failure handling (host side only; nothing here touches a GPU):
 
 ``evaluate_many`` keeps the KernelEvaluator call shape
 (src/kernel_mcts/interfaces.py:8-9) for a batch; ``evaluate`` is the single
-call, so MCTS runs unchanged on top.
+call, so MCTS runs unchanged on top.  ``lightweight_profile`` keeps the
+NodeProfiler call shape: the worker that evaluated a program profiles it,
+from the compiled artifact it still holds.
 """
 
 from __future__ import annotations
@@ -59,10 +61,25 @@ def _worker_main(slot: int, device: str, spec: WorkerSpec, jobs: "mp.Queue", res
         results.put(("startup_error", slot, None, traceback.format_exc()))
         return
     results.put(("ready", slot, None, None))
+    # This worker's latest result per (program source, workload id): a later
+    # profile request for that evaluation needs its compiled artifact.
+    evaluated: dict[tuple[str, str], EvaluationResult] = {}
     while True:
         item = jobs.get()
         if item is None:
             return
+        if item[0] == "profile":
+            _, job_id, program_value, workload_value, metric_set = item
+            workload = deserialize_workload(workload_value)
+            evaluation = evaluated.get((program_value["source"], workload.benchmark_id))
+            try:
+                if evaluation is None:
+                    raise LookupError("this worker holds no evaluation of that program and workload")
+                profile = dict(evaluator.lightweight_profile(evaluation, workload, metric_set))
+                results.put(("profiled", slot, job_id, profile))
+            except Exception as error:
+                results.put(("profile_error", slot, job_id, (type(error).__name__, str(error)[-2000:])))
+            continue
         if item[0] == "prepare":
             # Warm this worker for a workload (inputs, references) before timing starts.
             try:
@@ -78,6 +95,7 @@ def _worker_main(slot: int, device: str, spec: WorkerSpec, jobs: "mp.Queue", res
         workload = deserialize_workload(workload_value)
         try:
             evaluation = evaluator.evaluate(program, workload)
+            evaluated[(program.source, workload.benchmark_id)] = evaluation
             results.put(("result", slot, job_id, serialize_evaluation(evaluation)))
         except Exception:
             results.put(("error", slot, job_id, traceback.format_exc()))
@@ -116,6 +134,8 @@ class EvaluationPool:
         self._ctx = mp.get_context("spawn")
         self._results = self._ctx.Queue()
         self._workers: list[_Worker] = []
+        self._ran_on: dict[tuple[str, str], int] = {}  # (source, workload id) -> slot that evaluated it
+        self._profile_jobs = 0
         self.restarts = 0
         for slot, device in enumerate(self.devices):
             self._workers.append(self._start(slot, device))
@@ -222,6 +242,8 @@ class EvaluationPool:
                 if out[job] is None:
                     out[job] = (deserialize_evaluation(payload) if kind == "result"
                                 else _infrastructure_failure(programs[job], f"worker raised:\n{payload}"))
+                    if kind == "result":
+                        self._ran_on[(programs[job].source, workload.benchmark_id)] = slot
                     done += 1
             elif kind == "startup_error":
                 w = self._workers[slot]
@@ -243,8 +265,53 @@ class EvaluationPool:
                             programs[job], f"worker on device {w.device} died {attempts[job]} time(s)")
                         done += 1
                 self.restarts += 1
+                self._ran_on = {key: s for key, s in self._ran_on.items() if s != w.slot}
                 self._workers[w.slot] = self._start(w.slot, w.device)
         return [r for r in out if r is not None]
+
+
+    def lightweight_profile(self, evaluation: EvaluationResult, workload: WorkloadContract,
+                            metric_set: str = "lightweight_v1", timeout_seconds: float = 900.0) -> Mapping[str, Any]:
+        """Profiles a valid evaluation this pool ran, on the worker that ran it
+        (it holds the compiled artifact).  Raises EvaluationInfrastructureError
+        when that worker has been restarted since, or profiling fails there."""
+        from .evaluation import EvaluationInfrastructureError
+
+        if evaluation.status != ProposalStatus.VALID or evaluation.program is None:
+            raise ValueError("only valid evaluations can be profiled")
+        slot = self._ran_on.get((evaluation.program.source, workload.benchmark_id))
+        if slot is None:
+            raise EvaluationInfrastructureError("no worker of this pool holds that evaluation")
+        w = self._workers[slot]
+        if not w.process.is_alive():
+            raise EvaluationInfrastructureError("the worker that ran the evaluation has exited")
+        self._profile_jobs += 1
+        job = -self._profile_jobs  # negative ids never collide with evaluation jobs
+        program = evaluation.program
+        w.jobs.put(("profile", job, {"source": program.source, "backend": program.backend},
+                    serialize_workload(workload), metric_set))
+        deadline = time.monotonic() + timeout_seconds
+        while True:
+            try:
+                kind, got_slot, got_job, payload = self._results.get(timeout=0.5)
+            except queue.Empty:
+                if not w.process.is_alive():
+                    self._ran_on = {key: s for key, s in self._ran_on.items() if s != slot}
+                    self.restarts += 1
+                    self._workers[slot] = self._start(slot, w.device)
+                    raise EvaluationInfrastructureError("the worker died while profiling") from None
+                if time.monotonic() > deadline:
+                    raise EvaluationInfrastructureError("profiling did not finish in time") from None
+                continue
+            if kind == "ready":
+                self._workers[got_slot].ready = True
+            elif got_slot == slot and got_job == job:
+                if kind == "profiled":
+                    return payload
+                error_type, message = payload
+                if error_type == "EvaluationInfrastructureError":
+                    raise EvaluationInfrastructureError(message)
+                raise RuntimeError(f"{error_type}: {message}")
 
 
 def _infrastructure_failure(program: KernelProgram, reason: str) -> EvaluationResult:

@@ -33,6 +33,8 @@ def main() -> None:
     for name in fields:
         p.add_argument(f"--{name.replace('_', '-')}", type=int, default=None)
     p.add_argument("--select", action="store_true", help="start from the library's schedule for the shape")
+    p.add_argument("--cublas", action="store_true",
+                   help="after this library's launches, the same number of torch.matmul (cuBLAS) launches")
     args = p.parse_args()
 
     overrides = {name: getattr(args, name) for name in fields if getattr(args, name) is not None}
@@ -60,12 +62,24 @@ def main() -> None:
         times.append(start.elapsed_time(stop) * 1e3)
     if int(status.item()) != 0:
         raise SystemExit(f"device status {int(status.item()):#x}")
+    cublas_times = []
+    if args.cublas:
+        b_op = b if args.b_layout == "row" else b.T
+        ref = torch.empty_like(c)
+        for _ in range(args.launches):
+            start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record(stream)
+            torch.matmul(a, b_op, out=ref)
+            stop.record(stream)
+            stop.synchronize()
+            cublas_times.append(start.elapsed_time(stop) * 1e3)
     flops = 2.0 * args.M * args.N * args.K
     layout_code = _native.B_ROW if args.b_layout == "row" else _native.B_COL
     plan = _native.plan(cfg, args.M, args.N, args.K, layout_code)
     print(json.dumps({"config": cfg.as_dict(), "plan": plan, "shape": [args.M, args.N, args.K], "b_layout": args.b_layout,
                       "times_us": times, "median_us": statistics.median(times),
-                      "tflops": flops / (statistics.median(times) * 1e-6) / 1e12}))
+                      "tflops": flops / (statistics.median(times) * 1e-6) / 1e12,
+                      "cublas_times_us": cublas_times}))
 
 
 if __name__ == "__main__":

@@ -94,6 +94,18 @@ _METRIC_SETS = {
 
 PROFILE_METRIC_SET_IDS = ("lightweight_v1", "sm100_v1")
 
+# Launch attributes that ncu collects but does not list among queryable
+# metrics (the reference exempts the same one, src/kernel_mcts/profiling.py:22-24).
+NCU_QUERY_VALIDATION_EXEMPT_METRICS = frozenset({"launch__registers_per_thread"})
+
+
+def metrics_missing_from_query(definition: "ProfileMetricSet", query_output: str) -> list[str]:
+    """Metrics of ``definition`` that ``ncu --query-metrics-mode all`` output
+    does not list (the check of src/kernel_mcts/cuda_backend.py:413-461:
+    every token containing "__" is an available metric name)."""
+    available = {token.strip(" ,:\"'") for token in query_output.split() if "__" in token}
+    return [m for m in definition.metrics if m not in available and m not in NCU_QUERY_VALIDATION_EXEMPT_METRICS]
+
 
 def resolve_metric_set(metric_set_id: str, architecture: str) -> ProfileMetricSet:
     definition = _METRIC_SETS.get((metric_set_id, architecture)) or _METRIC_SETS.get((metric_set_id, "*"))

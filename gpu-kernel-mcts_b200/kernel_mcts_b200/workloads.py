@@ -10,7 +10,7 @@ launch as a limitation, docs/local-autotuning.md:175-177).
 
 from __future__ import annotations
 
-from .domain import ShapeCase, WorkloadContract
+from .domain import KernelProgram, ShapeCase, WorkloadContract
 
 _TENSORS_COL = {
     "A": {"shape": ["M", "K"], "layout": "row_major"},
@@ -110,3 +110,29 @@ BF16_GEMM_MIX_RANDN = multi_shape_gemm_workload(
 
 ALL_WORKLOADS = (BF16_GEMM_4096_B200, BF16_GEMM_256_RANDN, BF16_GEMM_4096_RANDN, BF16_GEMM_4096_INT,
                  BF16_GEMM_MIX_RANDN)
+
+
+# The root program a worker calibrates against when no other is named: a
+# host-launcher candidate running the library's CUDA-core kernel, which keeps
+# the reference root's arithmetic (one FP32 accumulator per output, one FMA
+# per k in order, src/kernel_mcts/benchmarks/kernels/bf16_gemm_root.cu:8-44).
+SIMT_ROOT_LAUNCHER = r"""
+#include <cuda_runtime.h>
+#include "kmcts_gemm.h"
+extern "C" int bf16_gemm_launch(const void* A, const void* B, void* C, int M, int N, int K, cudaStream_t s) {
+    kmcts_gemm_config cfg;
+    kmcts_default_config(&cfg);
+    cfg.kernel = KMCTS_KERNEL_SIMT;
+    return kmcts_bf16_gemm_ex(A, B, C, M, N, K, KMCTS_B_COL, &cfg, s, nullptr);
+}
+"""
+
+
+def root_program(path: str | None = None) -> KernelProgram:
+    """The worker's root program: the candidate source at ``path`` (for
+    instance the reference's own bf16_gemm_root.cu), else the CUDA-core
+    launcher above."""
+    if path:
+        with open(path, encoding="utf-8") as handle:
+            return KernelProgram(handle.read(), "cuda_cpp")
+    return KernelProgram(SIMT_ROOT_LAUNCHER, "cuda_cpp")

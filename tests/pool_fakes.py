@@ -38,3 +38,13 @@ class FakeEvaluator:
 
 def make(device_index: int, *, marker_dir: str, delay: float = 0.0) -> FakeEvaluator:
     return FakeEvaluator(device_index, marker_dir, delay)
+
+
+def _profile(self, evaluation, workload, metric_set="lightweight_v1"):
+    """Profiles only what this worker evaluated: the lookup the real
+    evaluator needs for its compiled artifact."""
+    return {"metric_set": metric_set, "profiler": "fake", "pid": os.getpid(),
+            "visible_devices": os.environ.get("CUDA_VISIBLE_DEVICES"), "source": evaluation.program.source}
+
+
+FakeEvaluator.lightweight_profile = _profile

@@ -26,7 +26,7 @@ from kernel_mcts_b200.evaluation import (
     CandidateTimeoutError,
     EvaluationInfrastructureError,
 )
-from kernel_mcts_b200.profiling import SM100_V1_METRICS, parse_ncu_csv
+from kernel_mcts_b200.profiling import LIGHTWEIGHT_V1_METRICS, SM100_V1_METRICS, parse_ncu_csv
 from kernel_mcts_b200.workloads import (
     BF16_GEMM_4096_B200,
     BF16_GEMM_4096_RANDN,
@@ -316,3 +316,77 @@ def test_multi_shape_reward_through_the_evaluator(tmp_path):
     result = evaluator.evaluate(schedule_program(tile_m=256, cluster_m=2, tile_n=256, tile_k=128, stages=3), MIX)
     assert result.status.value == "VALID", result
     assert result.reward == pytest.approx(0.75 * math.log(2.0) + 0.25 * math.log(1.0))
+
+
+# ------------------------------------------------------- profile metric sets
+
+
+def _query_listing(metrics):
+    rows = ["Metric Name  Metric Type  Metric Unit  Metric Description"]
+    rows += [f"{m}  Counter  byte  something" for m in metrics]
+    return "\n".join(rows)
+
+
+def _wide_csv(metrics):
+    return (",".join(f'"{m}"' for m in metrics) + "\n" + ",".join('"u"' for _ in metrics) + "\n"
+            + ",".join(f'"{i + 1}"' for i, _ in enumerate(metrics)))
+
+
+def test_sm100_metric_set_is_validated_against_ncu_before_profiling(tmp_path):
+    """As src/kernel_mcts/cuda_backend.py:413-461: a non-default metric set is
+    checked against `ncu --query-metrics-mode all` once, and a set the GPU's
+    ncu does not offer is refused with the missing names."""
+    from kernel_mcts_b200.evaluation import EvaluationInfrastructureError
+
+    class QueryRunner(FakeRunner):
+        def __init__(self, listing):
+            super().__init__()
+            self.listing = listing
+
+        def __call__(self, command, *, timeout, env):
+            if command[0].endswith("ncu") and "--query-metrics-mode" in command:
+                self.calls.append((list(command), timeout, dict(env)))
+                return subprocess.CompletedProcess(command, 0, self.listing, "")
+            return super().__call__(command, timeout=timeout, env=env)
+
+    artifact = Sm100Artifact("id", tmp_path / "exe", abi="schedule")
+    # One metric missing (the exempt launch attribute does not count).
+    partial = [m for m in SM100_V1_METRICS if m not in ("launch__registers_per_thread", "dram__bytes_read.sum")]
+    runner = QueryRunner(_query_listing(partial))
+    with pytest.raises(EvaluationInfrastructureError, match="dram__bytes_read.sum"):
+        make_backend(tmp_path, runner).lightweight_profile(artifact, BF16_GEMM_4096_B200, "sm100_v1")
+    assert not any("--metrics" in c[0] for c in runner.calls)  # refused before profiling
+    # Complete listing: validated once, then profiled; the second call skips the query.
+    runner = QueryRunner(_query_listing([m for m in SM100_V1_METRICS if m != "launch__registers_per_thread"]))
+    runner.ncu_stdout = _wide_csv(SM100_V1_METRICS)
+    backend = make_backend(tmp_path, runner)
+    for _ in range(2):
+        profile = backend.lightweight_profile(artifact, BF16_GEMM_4096_B200, "sm100_v1")
+        assert profile["metric_set"] == "sm100_v1"
+        assert profile["summary"]["tensor_pipe_active_pct_of_elapsed"] == 3.0
+    queries = [c[0] for c in runner.calls if "--query-metrics-mode" in c[0]]
+    assert queries == [["/opt/cuda/bin/ncu", "--query-metrics-mode", "all", "--devices", "0"]]
+    profiled = [c[0] for c in runner.calls if "--metrics" in c[0]]
+    assert len(profiled) == 2 and "--clock-control" in profiled[0] and "none" in profiled[0]
+    # The default set is never queried (the reference skips it too).
+    runner = QueryRunner("")
+    runner.ncu_stdout = _wide_csv(LIGHTWEIGHT_V1_METRICS)
+    make_backend(tmp_path, runner).lightweight_profile(artifact, BF16_GEMM_4096_B200, "lightweight_v1")
+    assert not any("--query-metrics-mode" in c[0] for c in runner.calls)
+
+
+def test_sm100_metric_set_is_offered_by_this_ncu_for_b200():
+    """The installed ncu lists every sm100_v1 metric for the B200 chip (gb100);
+    `--chips` answers without a GPU."""
+    import shutil
+
+    from kernel_mcts_b200.profiling import metrics_missing_from_query, resolve_metric_set
+
+    ncu = shutil.which("ncu") or "/usr/local/cuda/bin/ncu"
+    if not Path(ncu).exists():
+        pytest.skip("ncu not installed")
+    out = subprocess.run([ncu, "--query-metrics-mode", "all", "--chips", "gb100"], capture_output=True, text=True,
+                         timeout=300)
+    assert out.returncode == 0, out.stderr[-2000:]
+    for metric_set in ("sm100_v1", "lightweight_v1"):
+        assert metrics_missing_from_query(resolve_metric_set(metric_set, "sm_100a"), out.stdout) == []

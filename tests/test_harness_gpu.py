@@ -206,3 +206,27 @@ def test_pool_autotuner_on_one_gpu(tmp_path):
     assert statuses <= {ProposalStatus.VALID, ProposalStatus.INVALID}, statuses
     assert any(t.evaluation.status == ProposalStatus.VALID for t in result.trials)
     assert result.best is not None and result.best.reward >= baseline.reward
+
+
+def test_sm100_metric_set_profiles_a_schedule_on_b200(backend):
+    """The worker's /profile path on a B200: the sm100_v1 metric set is
+    validated against this GPU's ncu (--query-metrics-mode all), then one
+    launch of a 256^3 schedule program is profiled through
+    lightweight_profile (one kernel, one launch, --clock-control none).  The
+    same harness command runs once without ncu first and must exit 0."""
+    import shutil
+
+    if shutil.which("ncu") is None:
+        pytest.skip("ncu not installed")
+    workload = gemm_workload("bf16_gemm_256_profile", 256, 256, 256)
+    compiled = backend.compile(schedule_program(tile_m=256, cluster_m=2, tile_n=256, tile_k=128, stages=3), workload)
+    assert compiled.success, compiled.stderr
+    target = backend.profile_target_command(compiled.artifact, workload)
+    plain = subprocess.run(target, capture_output=True, text=True, timeout=120,
+                           env=dict(backend.config.subprocess_environment))
+    assert plain.returncode == 0, plain.stdout[-2000:] + plain.stderr[-2000:]
+    profile = backend.lightweight_profile(compiled.artifact, workload, "sm100_v1")
+    assert profile["metric_set"] == "sm100_v1" and profile["profiler"] == "ncu"
+    summary = profile["summary"]
+    assert summary["tensor_pipe_active_pct_of_elapsed"] > 0.0
+    assert summary["duration"] > 0.0 and summary["sm_cycles_active"] > 0.0
