@@ -344,53 +344,97 @@ def skinny_gemms(device, stream, flush, steps: int = 20) -> dict:
             "timing": "per-launch CUDA events, L2 flushed, interleaved with cuBLAS, medians", "shapes": rows}
 
 
-def evaluation_throughput(device, world: int, local_rank: int, a_cpu, b_cpu, layout: str, repeat: int) -> dict:
-    """Candidate-evaluation throughput, one evaluator per GPU (this rank's).
-    Every legal point of the 96-point schedule grid is evaluated ``repeat``
-    times through the tier-0 evaluator: compile (static legality), correctness
-    against cuBLAS, and the harness timing protocol (10 warm-ups, 30 event-timed
-    launches).  Inputs and the reference are prepared before the clock starts.
-    evals/sec = all ranks' evaluations / the slowest rank's wall time."""
+def evaluation_throughput(device, world: int, local_rank: int, layout: str, repeat: int) -> dict:
+    """the 96-point schedule sweep, one evaluator per GPU
+    (this rank's), reported as src/kernel_mcts/cute_tuning.py:136-226 reports
+    it: every point's static legality first (rejections are recorded with
+    their reasons and not charged to b_tune), then every legal point compiled
+    (for a prebuilt schedule: legality and kernel selection, no nvcc),
+    correctness-checked against cuBLAS and timed with the harness protocol
+    (10 warm-ups, 30 event-timed launches); best, default and their ratios to
+    this run's cuBLAS median.  The legal points run ``repeat`` times so the
+    batch keeps the GPU busy; evals/sec = all ranks' evaluations / the slowest
+    rank's wall time."""
     import torch
     import torch.distributed as dist
 
-    from kernel_mcts_b200.domain import BenchmarkResult, ProposalStatus
+    from kernel_mcts_b200.domain import BenchmarkResult
     from kernel_mcts_b200.evaluation import BackendKernelEvaluator, EvaluationContext
     from kernel_mcts_b200.inprocess import InProcessSm100Backend
-    from kernel_mcts_b200.sweep import schedule_grid, static_reasons
-    from kernel_mcts_b200.backend import schedule_program
+    from kernel_mcts_b200.sweep import run_schedule_sweep, schedule_grid
     from kernel_mcts_b200.workloads import gemm_workload
 
     workload = gemm_workload("bf16_gemm_4096_randn_b200", M, N, K, b_layout=layout, inputs="randn")
     backend = InProcessSm100Backend(warmup_count=10, measurement_count=30)
     evaluator = BackendKernelEvaluator(backend=backend, root_benchmark=BenchmarkResult((100.0,), 100.0),
                                        context=EvaluationContext(f"rank{local_rank}", "bench", {}, {}))
-    legal = [s for s in schedule_grid() if not static_reasons(s, workload)]
-    programs = [schedule_program(**s) for s in legal] * repeat
     evaluator.prepare(workload)
+    cublas_us = cublas_protocol_median(device, layout, warmups=10, measurements=30)
     if world > 1:
         dist.barrier(device_ids=[local_rank])
     torch.cuda.synchronize(device)
-    start = time.perf_counter()
-    results = [evaluator.evaluate(p, workload) for p in programs]
+    cublas = {"benchmark": {"median_us": cublas_us},
+              "protocol": "torch.matmul under the evaluations' protocol (10 warm-ups, 30 event-timed launches, "
+                          "no L2 flush), on this GPU"}
+    report = run_schedule_sweep(evaluator, workload, cublas, schedules=schedule_grid(96, 0), repeat=repeat)
     torch.cuda.synchronize(device)
-    wall = torch.tensor([time.perf_counter() - start], dtype=torch.float64, device=device)
-    valid = torch.tensor([sum(r.status == ProposalStatus.VALID for r in results)], dtype=torch.float64, device=device)
+    wall = torch.tensor([report["wall_seconds"]], dtype=torch.float64, device=device)
+    valid = torch.tensor([sum(t.get("status") == "VALID" for t in report["trials"]) * repeat],
+                         dtype=torch.float64, device=device)
     if world > 1:
         dist.all_reduce(wall, op=dist.ReduceOp.MAX)
         dist.all_reduce(valid, op=dist.ReduceOp.SUM)
-    total = len(programs) * world
+    total = report["evaluations"] * world
+    rejected: dict[str, int] = {}
+    for trial in report["trials"]:
+        if trial.get("status") == "STATICALLY_REJECTED":
+            for reason in trial["reasons"]:
+                rejected[reason] = rejected.get(reason, 0) + 1
     return {
         "value": total / float(wall.item()),
         "unit": "evaluations/s",
         "evaluations": total,
         "valid": int(valid.item()),
         "wall_s": float(wall.item()),
-        "per_evaluation": "static legality + correctness vs cuBLAS + 10 warm-up and 30 event-timed launches",
-        "schedules": len(legal),
+        "per_evaluation": "compile (static legality + kernel selection: prebuilt schedules run no nvcc) + "
+                          "correctness vs cuBLAS + 10 warm-up and 30 event-timed launches",
+        "grid_points": report["candidate_count"],
+        "legal": report["b_tune"],
+        "statically_rejected": report["candidate_count"] - report["b_tune"],
+        "rejection_reasons": rejected,
+        "best": report["best"],
+        "default": report["default"],
+        "comparison": report["comparison"],
+        "cublas_median_us": cublas_us,
         "repeat": repeat,
         "gpus": world,
     }
+
+
+def cublas_protocol_median(device, layout: str, warmups: int, measurements: int) -> float:
+    """Same-run cuBLAS (torch.matmul) at 4096^3 N(0,1) under the evaluation
+    protocol of kmcts_time_gemm: warm-ups, one synchronise, then per launch an
+    event pair and a synchronise.  Median in microseconds."""
+    import torch
+
+    g = torch.Generator(device=device).manual_seed(1)
+    a = torch.randn((M, K), generator=g, device=device).to(torch.bfloat16)
+    b = torch.randn((K, N) if layout == "row" else (N, K), generator=g, device=device).to(torch.bfloat16)
+    b_op = b if layout == "row" else b.T
+    c = torch.empty((M, N), dtype=torch.bfloat16, device=device)
+    stream = torch.cuda.current_stream(device)
+    for _ in range(warmups):
+        torch.matmul(a, b_op, out=c)
+    torch.cuda.synchronize(device)
+    times = []
+    for _ in range(measurements):
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        torch.matmul(a, b_op, out=c)
+        stop.record(stream)
+        stop.synchronize()
+        times.append(start.elapsed_time(stop) * 1e3)
+    return statistics.median(times)
 
 
 def sharded_gemm(device, world: int, local_rank: int, steps: int = 5, warmup: int = 2) -> dict:
@@ -576,7 +620,7 @@ def run_ours(args: argparse.Namespace) -> None:
 
     evaluations = None
     if not args.no_evals:
-        evaluations = evaluation_throughput(device, world, local_rank, a_cpu, b_cpu, layout, repeat=args.eval_repeat)
+        evaluations = evaluation_throughput(device, world, local_rank, layout, args.eval_repeat)
     sharded = None
     if not args.no_sharded:
         sharded = sharded_gemm(device, world, local_rank)

@@ -45,6 +45,7 @@ FLAG_NO_TAIL_SPLIT = 1
 FLAG_TAIL_SPLIT_N = 2
 FLAG_TAIL_STREAM_K = 4
 FLAG_B_EVICT_FIRST = 8
+FLAG_SWAP_AB = 16
 
 TAIL_NONE = 0
 TAIL_SPLIT_N = 1

@@ -31,8 +31,8 @@ HARNESS = LIB_DIR / "kmcts_bf16_eval"
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON_FLAGS = ["-std=c++17", "-O3", "-lineinfo", *ARCH_FLAGS, f"-I{INCLUDE}", f"-I{CSRC}"]
 
-LIBRARY_SOURCES = ("gemm_tcgen05.cu", "gemm_tcgen05_pair.cu", "gemm_simt.cu", "compare.cu", "capi.cu", "ipc.cu", "selftest.cu",
-                   "workspace.cu", "host_gemm.cu")
+LIBRARY_SOURCES = ("gemm_tcgen05.cu", "gemm_tcgen05_pair.cu", "gemm_tcgen05_stream.cu", "gemm_simt.cu", "compare.cu",
+                   "capi.cu", "ipc.cu", "selftest.cu", "workspace.cu", "host_gemm.cu")
 HEADERS = ("ptx_sm100.cuh", "gemm_common.cuh", "kmcts_internal.h")
 
 

@@ -467,6 +467,7 @@ const Variant kVariants[] = {
     KMCTS_SKINNY(256, 64, 5, false),  KMCTS_SKINNY(256, 64, 5, true),
     KMCTS_SKINNY(128, 64, 9, false),  KMCTS_SKINNY(128, 64, 9, true),
     KMCTS_SKINNY(128, 128, 4, false), KMCTS_SKINNY(128, 128, 4, true),
+    KMCTS_SKINNY(64, 128, 8, false),  KMCTS_SKINNY(64, 128, 8, true),
 };
 
 const Variant* find_variant(const kmcts_gemm_config& cfg, int b_layout) {
@@ -491,9 +492,12 @@ bool is_one_cta(const kmcts_gemm_config& cfg) { return cfg.tile_m == kBM || cfg.
 
 }  // namespace
 
+bool is_swapped(const kmcts_gemm_config& cfg) { return (cfg.flags & KMCTS_FLAG_SWAP_AB) != 0; }
+
 int64_t tcgen05_smem_bytes(const kmcts_gemm_config& cfg, int b_layout) {
     (void)b_layout;
     if (cfg.tile_n <= 0 || cfg.tile_k <= 0 || cfg.stages <= 0) return 0;
+    if (is_swapped(cfg)) return cfg.tile_m == 32 ? stream_smem_bytes(cfg.tile_k, cfg.stages) : 0;
     if (cfg.tile_m == 256) return pair_smem_bytes(cfg.tile_n, cfg.tile_k, cfg.stages);
     if (cfg.tile_m != kBM && cfg.tile_m != 32) return 0;
     return static_cast<int64_t>(cfg.stages) * (cfg.tile_m + cfg.tile_n) * cfg.tile_k * 2 +
@@ -517,6 +521,31 @@ int tcgen05_legal(const kmcts_gemm_config& cfg, int M, int N, int K, int b_layou
     if (cfg.k_splits < 0) {
         put_reason(why, len, "k_splits must be >= 0");
         return KMCTS_EINVAL;
+    }
+    if (is_swapped(cfg)) {
+        if (cfg.tile_m != 32 || cfg.cluster_m != 1 || cfg.cluster_n != 1 || cfg.tile_n != 128) {
+            put_reason(why, len, "the swapped schedule takes tile_m 32, tile_n 128 and a 1x1 cluster");
+            return KMCTS_ENOTSUP;
+        }
+        if (M > 32) {
+            put_reason(why, len, "the swapped schedule puts A's rows in the MMA's N: it takes M <= 32");
+            return KMCTS_ENOTSUP;
+        }
+        const int64_t smem = tcgen05_smem_bytes(cfg, b_layout);
+        if (smem <= 0 || smem > kMaxSmem) {
+            put_reason(why, len, "shared memory per CTA exceeds 227 KB");
+            return KMCTS_ESMEM;
+        }
+        if (!stream_variant_exists(cfg, b_layout)) {
+            put_reason(why, len, "the swapped schedule is compiled for tile_k 64 x 10 stages and 128 x 5");
+            return KMCTS_ENOTSUP;
+        }
+        if (K % 8 != 0 || N % 8 != 0) {
+            put_reason(why, len, "TMA needs K and N to be multiples of 8");
+            return KMCTS_ENOTSUP;
+        }
+        put_reason(why, len, "ok");
+        return KMCTS_OK;
     }
     if (cfg.k_splits > 1 && !is_one_cta(cfg) && !(is_pair(cfg) && cfg.cluster_n == 1)) {
         put_reason(why, len, "split K runs on one-CTA schedules (tile_m 128 or 32) and CTA pairs (cluster 2x1)");
@@ -594,6 +623,13 @@ int launch_tcgen05(const void* A, const void* B, void* C, int M, int N, int K, i
                    ? KMCTS_OK
                    : KMCTS_EGEMM;
     }
+    if (is_swapped(cfg)) {
+        const uint64_t limit =
+            cfg.wait_limit_ns > 0 ? static_cast<uint64_t>(cfg.wait_limit_ns) : kDefaultWaitNs;
+        int* status = device_status ? device_status : default_status_ptr();
+        if (status == nullptr) return KMCTS_EHANDLE;
+        return launch_stream(A, B, C, M, N, K, b_layout, cfg, limit, stream, status);
+    }
     const bool pair = is_pair(cfg);
     // Each CTA stages 128 rows of A, and BN (one CTA) or BN/2 (pair) of B.
     const uint32_t b_rows = pair ? cfg.tile_n / 2 : cfg.tile_n;
@@ -662,6 +698,7 @@ int plan_tcgen05(const kmcts_gemm_config& cfg, int M, int N, int K, int b_layout
     const int rc = tcgen05_legal(cfg, M, N, K, b_layout, nullptr, 0);
     if (rc != KMCTS_OK) return rc;
     if (is_pair(cfg)) return plan_pair(cfg, M, N, K, b_layout, out);
+    if (is_swapped(cfg)) return plan_stream(cfg, M, N, K, out);
     kmcts_gemm_plan plan = {};
     plan.kernel = 1;
     plan.cluster_size = 1;

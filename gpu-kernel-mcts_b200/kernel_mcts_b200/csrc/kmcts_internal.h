@@ -51,6 +51,13 @@ int multiprocessor_count();
 constexpr int kWorkspaceStreamK = 0, kWorkspaceSplitK = 1;
 bool stream_workspace(cudaStream_t stream, int user, size_t bytes, void** ptr, int* epoch);
 
+// Streamed skinny kernel (C^T = B^T A^T, M <= 32), gemm_tcgen05_stream.cu.
+bool stream_variant_exists(const kmcts_gemm_config& cfg, int b_layout);
+int64_t stream_smem_bytes(int bk, int stages);
+int plan_stream(const kmcts_gemm_config& cfg, int M, int N, int K, kmcts_gemm_plan* out);
+int launch_stream(const void* A, const void* B, void* C, int M, int N, int K, int b_layout,
+                  const kmcts_gemm_config& cfg, uint64_t limit_ns, cudaStream_t stream, int* device_status);
+
 // CTA-pair (cta_group::2) kernels, gemm_tcgen05_pair.cu.
 bool pair_variant_exists(const kmcts_gemm_config& cfg, int b_layout);
 int64_t pair_smem_bytes(int bn, int bk, int stages);

@@ -357,6 +357,12 @@ __host__ __device__ constexpr uint32_t make_idesc_bf16(int m, int n, bool b_mn_m
            (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
 }
 
+// The same with the A operand's major-ness chosen too (bit 15: 0 = K-major,
+// 1 = MN-major).
+__host__ __device__ constexpr uint32_t make_idesc_bf16_ab(int m, int n, bool a_mn_major, bool b_mn_major) {
+    return make_idesc_bf16(m, n, b_mn_major) | ((a_mn_major ? 1u : 0u) << 15);
+}
+
 // Shared-memory matrix descriptor for a 128-byte-swizzled operand.
 //   bits 0-13 start address >> 4; 16-29 leading byte offset >> 4;
 //   32-45 stride byte offset >> 4; 46-47 version (1 on sm_100);

@@ -66,6 +66,17 @@ extern "C" {
  * there (dirty lines cost a DRAM write-back on eviction).  Results are
  * unchanged; only the cache policy differs. */
 #define KMCTS_FLAG_B_EVICT_FIRST 8
+/* tile_m 32 (M <= 32), tile_n 128, tile_k 64 with 10 stages or 128 with 5:
+ * the operands swap roles, C^T = B^T * A^T, so B's 128-column tiles are the
+ * MMA's 128 rows and A's M rows its N (16 or 32): no tensor work is padding.
+ * The (tile, K block) pairs are cut into one contiguous range per SM (at
+ * least four K blocks each); a tile cut by range boundaries is summed from
+ * FP32 partials in a per-stream library workspace, in range order, by the
+ * range that finishes it last (deterministic; exact on integer inputs,
+ * within the parity bound otherwise).  B's loads are evict-first; k_splits
+ * is ignored.  Without a workspace (growth under graph capture) each CTA
+ * takes one whole tile. */
+#define KMCTS_FLAG_SWAP_AB 16
 
 #define KMCTS_TAIL_NONE 0     /* kmcts_gemm_plan.tail_split: every tile whole */
 #define KMCTS_TAIL_SPLIT_N 1  /* last wave as half-width units */

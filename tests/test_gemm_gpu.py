@@ -717,3 +717,56 @@ def test_host_buffer_gemm_bit_identical_to_device_call(cuda_device, layout, shap
     torch.cuda.synchronize()
     assert int(status.item()) == 0
     assert torch.equal(c_host.view(torch.int16), device.cpu().view(torch.int16))
+
+
+# ------------------------------------------------------- swapped skinny path
+
+SWAP = dict(kernel=_native.KERNEL_TCGEN05, tile_m=32, cluster_m=1, tile_n=128, flags=_native.FLAG_SWAP_AB)
+
+
+@pytest.mark.parametrize("layout", ["col", "row"])
+@pytest.mark.parametrize("tile_k,stages", [(64, 10), (128, 5)])
+@pytest.mark.parametrize("shape", [(1, 520, 1032), (7, 2048, 512), (16, 1024, 2048), (17, 264, 4096),
+                                   (32, 8192, 1024), (16, 128, 8192), (3, 136, 8)])
+def test_swapped_skinny_schedule_integer_exact(cuda_device, layout, tile_k, stages, shape):
+    """C^T = B^T A^T with every SM streaming a contiguous range of (tile, K
+    block) pairs; cut tiles are summed from FP32 partials.  Integer inputs are
+    exact whatever the cuts (ragged N and K, one tile over many ranges, M from
+    1 to 32), and a second launch repeats every bit (the counters reset)."""
+    m, n, k = shape
+    cfg = dict(SWAP, tile_k=tile_k, stages=stages)
+    plan = plan_of(m, n, k, layout, **cfg)
+    assert plan["kernel"] == 3 and plan["tiles"] == -(-n // 128) and plan["units"] >= plan["tiles"]
+    a_t, b_t = oracle.integer_inputs(m, n, k, seed=m + k)
+    expect = oracle.torch_bits(oracle.torch_reference(a_t, b_t))
+    a, b = a_t.cuda(), b_for(layout, b_t.cuda())
+    first = run(a, b, layout, **cfg)
+    np.testing.assert_array_equal(bits_of(first), expect)
+    second = run(a, b, layout, **cfg)
+    assert torch.equal(first.view(torch.int16), second.view(torch.int16))
+
+
+@pytest.mark.parametrize("layout", ["row", "col"])
+def test_swapped_skinny_randn_within_criterion_deterministic_and_concurrent(cuda_device, layout):
+    """16 x 8192 x 8192 N(0,1): within the parity criterion against the
+    reference's CPU path and the FP64 bound; bit-identical across launches
+    and across two streams running at once (separate workspaces)."""
+    m, n, k = 16, 8192, 8192
+    a_t, b_t = oracle.randn_inputs(m, n, k, seed=3, b_layout=layout)
+    a, b = a_t.cuda(), b_t.cuda()
+    cfg = _native.make_config(**SWAP, tile_k=64, stages=10)
+    c = run(a, b, layout, **cfg.as_dict())
+    ref32 = oracle.torch_bits(oracle.torch_reference(a_t, b_t, layout))
+    ref64, mag = oracle.fp64_reference(a_t, b_t, layout)
+    report = oracle.parity_report(bits_of(c), ref32, ref64, mag, k)
+    assert report["passed"] and report["max_ulp_where_ref_ge_0.5"] <= 1, report
+    assert oracle.harness_check(bits_of(c), ref32)["success"]
+    s1, s2 = torch.cuda.Stream(), torch.cuda.Stream()
+    status = torch.zeros(2, dtype=torch.int32, device="cuda")
+    outs = [(kg.bf16_gemm(a, b, b_layout=layout, config=cfg, stream=s1, status=status[0:1]),
+             kg.bf16_gemm(a, b, b_layout=layout, config=cfg, stream=s2, status=status[1:2])) for _ in range(3)]
+    torch.cuda.synchronize()
+    assert status.tolist() == [0, 0]
+    for x, y in outs:
+        assert torch.equal(x.view(torch.int16), c.view(torch.int16))
+        assert torch.equal(y.view(torch.int16), c.view(torch.int16))
