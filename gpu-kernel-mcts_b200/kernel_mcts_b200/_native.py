@@ -44,12 +44,14 @@ KERNEL_SIMT = 2
 FLAG_NO_TAIL_SPLIT = 1
 FLAG_TAIL_SPLIT_N = 2
 FLAG_TAIL_STREAM_K = 4
+FLAG_TAIL_SPLIT_K = 32
 FLAG_B_EVICT_FIRST = 8
 FLAG_SWAP_AB = 16
 
 TAIL_NONE = 0
 TAIL_SPLIT_N = 1
 TAIL_STREAM_K = 2
+TAIL_SPLIT_K = 3
 
 INPUTS = {"uniform": 0, "randn": 1, "int": 2}
 

@@ -94,7 +94,17 @@ struct PeerOutputs {
 // tile's epoch-tagged counter; the unit that arrives last adds the S partials
 // in split order and writes C, as the one-CTA kernel's split K does.  Nothing
 // waits.
-constexpr int kTailWhole = 0, kTailSplitN = 1, kTailStreamK = 2, kSplitK = 3;
+//
+// kTailSplitK   (opt-in; 2 rem <= W, BN 256) each of the last rem tiles as its
+//               two K halves on two clusters (c and c ^ 1).  Each half-unit
+//               stores its FP32 values of the other's BN/2 columns in the
+//               tile's partial slot and raises its ready flag, then waits
+//               (bounded) for the other's flag, adds the other's values to
+//               its own for its BN/2 columns, rounds once and stores C.  Both
+//               units raise their flag before waiting, and both are the last
+//               units of co-resident clusters with the same number of whole
+//               tiles before them, so each wait is for work already running.
+constexpr int kTailWhole = 0, kTailSplitN = 1, kTailStreamK = 2, kSplitK = 3, kTailSplitK = 4;
 
 struct TailSplit {
     float* partials;  // stream-K: [boundary][CTA rank][quarter][BN/64 chunks][16 float4][32 lanes];
@@ -149,7 +159,7 @@ __device__ __forceinline__ Schedule make_schedule(int M, int N, int K, int BN, i
     s.g0 = s.g1 = 0;
     const int rest = s.num_m * s.num_n - full_tiles;
     s.total = static_cast<long long>(rest) * s.num_kb;
-    if (rest > 0 && tail.mode == kTailSplitN) {
+    if (rest > 0 && (tail.mode == kTailSplitN || tail.mode == kTailSplitK)) {
         s.n_tail = cluster < 2 * rest ? 1 : 0;
     } else if (rest > 0 && tail.mode == kTailStreamK) {
         s.g0 = sk_lo(cluster, s.total, clusters);
@@ -176,6 +186,13 @@ __device__ __forceinline__ Unit schedule_unit(const Schedule& s, int i, const Ta
         t = s.full_tiles + s.cluster / 2;
         half_n = s.cluster & 1;
         out.width = BN / 2;
+    } else if (tail.mode == kTailSplitK) {
+        // K half (cluster & 1) of tail tile cluster / 2.
+        t = s.full_tiles + s.cluster / 2;
+        out.tile = s.cluster / 2;
+        out.split = s.cluster & 1;
+        out.kb0 = out.split * (s.num_kb / 2);
+        out.kb1 = out.split ? s.num_kb : s.num_kb / 2;
     } else {
         const long long tt = s.g0 / s.num_kb + (i - s.n_full);
         const long long first_g = tt * s.num_kb;
@@ -614,6 +631,86 @@ __global__ void __launch_bounds__(pair_threads<SLOTS>(), 1)
             ptx::tc_fence_after();
             const uint32_t row_addr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                                       static_cast<uint32_t>(acc * BN);
+            if constexpr (!SPLITK && !ALLGATHER && !SLOTS) {
+                if (tail.mode == kTailSplitK && w.split >= 0) {
+                    // K-half exchange: give the partner this half's FP32 values
+                    // of its chunks, then add the partner's to this half's
+                    // chunks and store them.
+                    const int h = w.split;
+                    const int half_chunks = chunks / 2;
+                    const int give0 = (1 - h) * half_chunks, keep0 = h * half_chunks;
+                    int* my_ready = tail.ready + flag_index(2 * w.tile + h, static_cast<int>(rank), quarter);
+                    int* peer_ready = tail.ready + flag_index(2 * w.tile + 1 - h, static_cast<int>(rank), quarter);
+#pragma unroll 1
+                    for (int c = give0; c < give0 + half_chunks; ++c) {
+                        uint32_t lo[32], hi[32];
+                        ptx::tmem_ld_32x32b_x32(row_addr + c * 64, lo);
+                        ptx::tmem_ld_32x32b_x32(row_addr + c * 64 + 32, hi);
+                        ptx::tmem_wait_ld();
+                        float4* part = partial_chunk<BN>(tail, w.tile, static_cast<int>(rank), quarter, c);
+#pragma unroll
+                        for (int q = 0; q < 8; ++q)
+                            __stcg(part + q * 32 + lane,
+                                   make_float4(__uint_as_float(lo[4 * q]), __uint_as_float(lo[4 * q + 1]),
+                                               __uint_as_float(lo[4 * q + 2]), __uint_as_float(lo[4 * q + 3])));
+#pragma unroll
+                        for (int q = 0; q < 8; ++q)
+                            __stcg(part + (8 + q) * 32 + lane,
+                                   make_float4(__uint_as_float(hi[4 * q]), __uint_as_float(hi[4 * q + 1]),
+                                               __uint_as_float(hi[4 * q + 2]), __uint_as_float(hi[4 * q + 3])));
+                    }
+                    __threadfence();
+                    __syncwarp();
+                    if (lane == 0) ptx::st_release_gpu(my_ready, tail.epoch);
+                    // Wait (bounded) for the partner's values of this half's chunks.
+                    bool got = true;
+                    const uint64_t start = ptx::global_timer_ns();
+                    while (ptx::ld_acquire_gpu(peer_ready) != tail.epoch) {
+                        if (*abort || ptx::global_timer_ns() - start > limit_ns) {
+                            got = false;
+                            break;
+                        }
+                    }
+                    if (!__all_sync(0xffffffffu, got)) {
+                        if (lane == 0) record_failure(status, abort, kRoleEpilogue);
+                        break;
+                    }
+#pragma unroll 1
+                    for (int c = keep0; c < keep0 + half_chunks; ++c) {
+                        uint32_t lo[32], hi[32];
+                        ptx::tmem_ld_32x32b_x32(row_addr + c * 64, lo);
+                        ptx::tmem_ld_32x32b_x32(row_addr + c * 64 + 32, hi);
+                        ptx::tmem_wait_ld();
+                        if (c == keep0 + half_chunks - 1) {
+                            ptx::tc_fence_before();
+                            __syncwarp();
+                            if (lane == 0)
+                                ptx::mbar_arrive_cluster(ptx::mapa_shared(ptx::smem_addr(&tmem_empty[acc]), pair_base));
+                        }
+                        const float4* part = partial_chunk<BN>(tail, w.tile, static_cast<int>(rank), quarter, c);
+                        float4 p[16];  // all of the chunk's loads in flight at once
+#pragma unroll
+                        for (int q = 0; q < 16; ++q) p[q] = __ldcg(part + q * 32 + lane);
+#pragma unroll
+                        for (int q = 0; q < 8; ++q) {
+                            lo[4 * q] = __float_as_uint(__uint_as_float(lo[4 * q]) + p[q].x);
+                            lo[4 * q + 1] = __float_as_uint(__uint_as_float(lo[4 * q + 1]) + p[q].y);
+                            lo[4 * q + 2] = __float_as_uint(__uint_as_float(lo[4 * q + 2]) + p[q].z);
+                            lo[4 * q + 3] = __float_as_uint(__uint_as_float(lo[4 * q + 3]) + p[q].w);
+                            hi[4 * q] = __float_as_uint(__uint_as_float(hi[4 * q]) + p[8 + q].x);
+                            hi[4 * q + 1] = __float_as_uint(__uint_as_float(hi[4 * q + 1]) + p[8 + q].y);
+                            hi[4 * q + 2] = __float_as_uint(__uint_as_float(hi[4 * q + 2]) + p[8 + q].z);
+                            hi[4 * q + 3] = __float_as_uint(__uint_as_float(hi[4 * q + 3]) + p[8 + q].w);
+                        }
+                        store_chunk(&map_c, staging, chunk_count, lo, hi, lane, n0 + c * 64, m0 + quarter * 32);
+                    }
+                    // The partner's values are consumed: clear its flag, so a
+                    // replay of this very launch (same epoch) starts clean.
+                    __syncwarp();
+                    if (lane == 0) *peer_ready = 0;
+                    continue;
+                }
+            }
 #pragma unroll 1
             for (int c = 0; c < chunks; ++c) {
                 uint32_t lo[32], hi[32];
@@ -814,6 +911,7 @@ int pair_workers(int device) {
 int requested_tail(int flags) {
     if (flags & KMCTS_FLAG_NO_TAIL_SPLIT) return KMCTS_TAIL_NONE;
     if (flags & KMCTS_FLAG_TAIL_STREAM_K) return KMCTS_TAIL_STREAM_K;
+    if (flags & KMCTS_FLAG_TAIL_SPLIT_K) return KMCTS_TAIL_SPLIT_K;
     return KMCTS_TAIL_SPLIT_N;
 }
 
@@ -868,6 +966,14 @@ kmcts_gemm_plan make_pair_plan(int M, int N, int K, int workers, bool persistent
             const long long total = static_cast<long long>(plan.tiles - plan.full_tiles) * num_kb;
             plan.units = plan.full_tiles + stream_k_units(total, num_kb, workers);
             clusters = workers;
+        } else if (rem != 0 && tail == KMCTS_TAIL_SPLIT_K && BN == 256 && 2 * rem <= workers && num_kb >= 2) {
+            // Each tail tile as its two K halves on two clusters.
+            plan.tail_split = KMCTS_TAIL_SPLIT_K;
+            plan.tail_clusters = 2 * rem;
+            plan.tail_segments = 2;
+            plan.full_tiles = plan.tiles - rem;
+            plan.units = plan.full_tiles + 2 * rem;
+            clusters = plan.units < workers ? plan.units : workers;
         } else if (rem != 0 && tail != KMCTS_TAIL_NONE && BN == 256 && 2 * rem <= workers) {
             // Half-width units: BN/2 must be whole 64-column TMA boxes per CTA.
             plan.tail_split = KMCTS_TAIL_SPLIT_N;
@@ -1017,8 +1123,15 @@ int launch_pair_variant_peers(const CUtensorMap& ma, const CUtensorMap& mb, cons
                                                                        group, 0, &plan);
         if (rc != KMCTS_OK) return rc;
     }
+    if (plan.tail_split == KMCTS_TAIL_SPLIT_K && !tail_workspace(stream, plan.tail_clusters, &tail)) {
+        // No workspace: the N split, bit-identical to whole tiles.
+        rc = plan_pair_variant<BN, BK, STAGES, B_MN, ALLGATHER, SLOTS>(M, N, K, persistent, KMCTS_TAIL_SPLIT_N,
+                                                                       group, 0, &plan);
+        if (rc != KMCTS_OK) return rc;
+    }
     tail.mode = plan.k_splits > 1                           ? kSplitK
                 : plan.tail_split == KMCTS_TAIL_STREAM_K ? kTailStreamK
+                : plan.tail_split == KMCTS_TAIL_SPLIT_K  ? kTailSplitK
                 : plan.tail_split == KMCTS_TAIL_SPLIT_N  ? kTailSplitN
                                                          : kTailWhole;
     cudaLaunchConfig_t config = {};

@@ -60,6 +60,14 @@ extern "C" {
 #define KMCTS_FLAG_NO_TAIL_SPLIT 1
 #define KMCTS_FLAG_TAIL_SPLIT_N 2  /* the default; kept for explicit requests */
 #define KMCTS_FLAG_TAIL_STREAM_K 4
+/* CTA pairs, tile_n 256, 2R <= W: each of the last R tiles runs as its two K
+ * halves on two pairs.  When both halves are done each pair sends the other
+ * its FP32 values of the other's 128 columns (through the per-stream
+ * workspace) and writes its own 128 columns of C: each output is the FP32 sum
+ * of the two K halves, rounded once (the same bits whichever pair adds).
+ * Deterministic; exact on integer inputs, within the parity bound otherwise.
+ * Without a workspace (growth under graph capture) the N split runs. */
+#define KMCTS_FLAG_TAIL_SPLIT_K 32
 /* One-CTA schedules (tile_m 128 or 32): B's loads carry an L2 evict-first
  * policy.  For shapes whose M fits one tile row B is read exactly once, and
  * streaming it through L2 at normal priority would push out everything else
@@ -81,6 +89,7 @@ extern "C" {
 #define KMCTS_TAIL_NONE 0     /* kmcts_gemm_plan.tail_split: every tile whole */
 #define KMCTS_TAIL_SPLIT_N 1  /* last wave as half-width units */
 #define KMCTS_TAIL_STREAM_K 2 /* last W + R tiles as stream-K ranges */
+#define KMCTS_TAIL_SPLIT_K 3  /* last R tiles as two K halves exchanging FP32 halves */
 
 /* Kernel schedule.  Zero-initialise and call kmcts_default_config() first. */
 typedef struct kmcts_gemm_config {

@@ -770,3 +770,66 @@ def test_swapped_skinny_randn_within_criterion_deterministic_and_concurrent(cuda
     for x, y in outs:
         assert torch.equal(x.view(torch.int16), c.view(torch.int16))
         assert torch.equal(y.view(torch.int16), c.view(torch.int16))
+
+
+# --------------------------------------------------- K-half exchange tail
+
+KX = _native.FLAG_TAIL_SPLIT_K
+
+
+@pytest.mark.parametrize("layout", ["col", "row"])
+@pytest.mark.parametrize("shape,cfg", [
+    ((4096, 4096, 4096), {}),                          # 3 W + 34 tiles
+    ((3072, 5120, 1024), {}),                          # 3 W + 18
+    ((1024, 2048, 512), {}),                           # 32 tiles < W: every tile split
+    ((1000, 1800, 1000), {}),                          # ragged M, N, K (32 tiles)
+    ((4096, 4096, 2048), dict(tile_k=64, stages=6)),
+])
+def test_k_half_exchange_tail_integer_exact_and_repeatable(cuda_device, layout, shape, cfg):
+    """The last wave's tiles as two K halves on two pairs, each writing the
+    FP32 sum for its 128 columns after swapping partials: integer inputs
+    stay exact, and repeated launches (same stream workspace, new epochs)
+    repeat every bit."""
+    m, n, k = shape
+    base = dict(PAIR_128K, **cfg)
+    plan = plan_of(m, n, k, layout, flags=KX, **base)
+    w = plan["workers"]
+    rem = plan["tiles"] % w
+    assert plan["tail_split"] == _native.TAIL_SPLIT_K and 2 * rem <= w, plan
+    assert plan["units"] == plan["tiles"] - rem + 2 * rem and plan["tail_segments"] == 2
+    a_t, b_t = oracle.integer_inputs(m, n, k, seed=13)
+    expect = oracle.torch_bits(oracle.torch_reference(a_t, b_t))
+    a, b = a_t.cuda(), b_for(layout, b_t.cuda())
+    first = run(a, b, layout, flags=KX, **base)
+    np.testing.assert_array_equal(bits_of(first), expect)
+    for _ in range(2):
+        again = run(a, b, layout, flags=KX, **base)
+        assert torch.equal(first.view(torch.int16), again.view(torch.int16))
+
+
+@pytest.mark.parametrize("layout", ["row", "col"])
+def test_k_half_exchange_tail_randn_within_criterion(cuda_device, layout):
+    """4096^3 N(0,1) with the K-half exchange tail: within the parity
+    criterion against the FP64 product on the last row band (where the
+    exchanged tiles lie), within 1 ulp of the unsplit kernel wherever
+    |C| >= 0.5, deterministic across launches and concurrent streams."""
+    m = n = k = 4096
+    a_t, b_t = oracle.randn_inputs(m, n, k, seed=0, b_layout=layout)
+    a, b = a_t.cuda(), b_t.cuda()
+    cfg = _native.make_config(flags=KX)
+    c = run(a, b, layout, flags=KX)
+    whole = run(a, b, layout, flags=_native.FLAG_NO_TAIL_SPLIT)
+    assert kg.compare(c, whole).success
+    sub = slice(m - 512, m)
+    ref64, mag = oracle.fp64_reference(a_t[sub], b_t, layout)
+    report = oracle.parity_report(bits_of(c)[sub], bits_of(whole)[sub], ref64, mag, k)
+    assert report["passed"] and report["max_ulp_where_ref_ge_0.5"] <= 1, report
+    s1, s2 = torch.cuda.Stream(), torch.cuda.Stream()
+    status = torch.zeros(2, dtype=torch.int32, device="cuda")
+    outs = [(kg.bf16_gemm(a, b, b_layout=layout, config=cfg, stream=s1, status=status[0:1]),
+             kg.bf16_gemm(a, b, b_layout=layout, config=cfg, stream=s2, status=status[1:2])) for _ in range(3)]
+    torch.cuda.synchronize()
+    assert status.tolist() == [0, 0]
+    for x, y in outs:
+        assert torch.equal(x.view(torch.int16), c.view(torch.int16))
+        assert torch.equal(y.view(torch.int16), c.view(torch.int16))
