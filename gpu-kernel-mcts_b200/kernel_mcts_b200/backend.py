@@ -33,6 +33,7 @@ import re
 import shutil
 import statistics
 import subprocess
+import threading
 import time
 from dataclasses import dataclass, field
 from pathlib import Path
@@ -86,6 +87,10 @@ class CudaSm100Config:
     device_index: int = 0
     flush_l2: bool = False
     subprocess_environment: Mapping[str, str] = field(default_factory=_default_env)
+    # Where candidate builds are cached (by source, ABI, harness and library);
+    # None: under artifact_root.  Backends that share it (a host compile pool
+    # and the GPU workers) build each candidate once.
+    candidate_cache: Path | None = None
 
     def __post_init__(self) -> None:
         if min(self.compile_timeout_seconds, self.execution_timeout_seconds, self.profile_timeout_seconds) <= 0:
@@ -298,11 +303,9 @@ class CudaSm100Backend:
         return Sm100CompilationResult(True, artifact, "", "", time.monotonic() - started,
                                       compiler_context={"schedule": schedule, "smem_bytes": _native.config_smem_bytes(cfg, layout)})
 
-    def _compile_candidate(self, program: KernelProgram, workload: WorkloadContract) -> Sm100CompilationResult:
-        try:
-            abi = detect_candidate_abi(program.source)
-        except ValueError as error:
-            return Sm100CompilationResult(False, None, "", str(error), 0.0)
+    def candidate_key(self, program: KernelProgram) -> tuple[str, str]:
+        """(ABI, cache key) of a candidate source's build."""
+        abi = detect_candidate_abi(program.source)
         library = native_build.build_library()
         harness_src = native_build.CSRC / "harness.cu"
         key = hashlib.sha256(
@@ -310,38 +313,112 @@ class CudaSm100Backend:
                         hashlib.sha256(harness_src.read_bytes()).hexdigest(),
                         hashlib.sha256(library.read_bytes()).hexdigest()]).encode()
         ).hexdigest()[:32]
-        artifact_dir = Path(self.config.artifact_root) / f"cand-{key}"
+        return abi, key
+
+    def _cache_root(self) -> Path:
+        return Path(self.config.candidate_cache or self.config.artifact_root)
+
+    def _harness_object(self, abi: str) -> tuple[Path | None, str]:
+        """The harness compiled once per ABI (relocatable device code), so a
+        candidate build compiles only the candidate and links.  Returns the
+        object, or None and the compiler output on failure."""
+        harness_src = native_build.CSRC / "harness.cu"
+        digest = hashlib.sha256(harness_src.read_bytes() + (native_build.INCLUDE / "kmcts_gemm.h").read_bytes()
+                                + abi.encode() + self.config.architecture.encode()).hexdigest()[:24]
+        obj = self._cache_root() / f"harness-{abi}-{digest}.o"
+        if obj.exists():
+            return obj, ""
+        obj.parent.mkdir(parents=True, exist_ok=True)
+        tmp = obj.with_name(f"{obj.name}.{os.getpid()}.{threading.get_ident()}.tmp")
+        command = [
+            _resolve_tool(self.config.nvcc), "-gencode", "arch=compute_100a,code=sm_100a", "-std=c++17", "-O3",
+            "-rdc=true", "-DKMCTS_CANDIDATE_ROOT" if abi == "root" else "-DKMCTS_CANDIDATE_LAUNCHER",
+            f"-I{native_build.INCLUDE}", "-c", str(harness_src), "-o", str(tmp),
+        ]
+        completed = self._runner(command, timeout=self.config.compile_timeout_seconds,
+                                 env=self.config.subprocess_environment)
+        if completed.returncode != 0 or not tmp.exists():
+            return None, f"{completed.stdout}\n{completed.stderr}"
+        os.replace(tmp, obj)  # atomic: concurrent builders leave one complete object
+        return obj, ""
+
+    def _compile_candidate(self, program: KernelProgram, workload: WorkloadContract) -> Sm100CompilationResult:
+        """nvcc build of a candidate source against the evaluation harness
+        (src/kernel_mcts/cuda_backend.py:129-208 builds candidate and harness
+        in one nvcc call; here the harness is compiled once per ABI and each
+        candidate is compiled alone, -rdc, and linked to it).  Builds are
+        cached on disk by key, with their compiler output, so another
+        process sharing ``candidate_cache`` reuses them."""
+        try:
+            abi, key = self.candidate_key(program)
+        except ValueError as error:
+            return Sm100CompilationResult(False, None, "", str(error), 0.0)
+        artifact_dir = self._cache_root() / f"cand-{key}"
         executable = artifact_dir / "evaluate"
+        log = artifact_dir / "compile.log"
         started = time.monotonic()
-        if executable.exists() and key in self._compiler_output:
-            output = self._compiler_output[key]
+        if executable.exists() and (key in self._compiler_output or log.exists()):
+            output = self._compiler_output.get(key)
+            if output is None:
+                output = log.read_text(encoding="utf-8", errors="replace")
+                self._compiler_output[key] = output
             return self._compiled(executable, abi, "", output, time.monotonic() - started)
         artifact_dir.mkdir(parents=True, exist_ok=True)
-        candidate = artifact_dir / "candidate.cu"
-        candidate.write_text(program.source, encoding="utf-8")
-        command = [
-            _resolve_tool(self.config.nvcc),
-            "-gencode", "arch=compute_100a,code=sm_100a",
-            "-std=c++17", "-O3", "-rdc=true", "-Xptxas=-v",
-            "-DKMCTS_CANDIDATE_ROOT" if abi == "root" else "-DKMCTS_CANDIDATE_LAUNCHER",
-            f"-I{native_build.INCLUDE}",
-            str(candidate), str(harness_src),
-            f"-L{native_build.LIB_DIR}", "-lkmcts_gemm_sm100", "-lcublas",
-            "-Xlinker", f"-rpath={native_build.LIB_DIR}",
-            "-o", str(executable),
-        ]
         try:
-            completed = self._runner(command, timeout=self.config.compile_timeout_seconds,
-                                     env=self.config.subprocess_environment)
+            harness_obj, harness_output = self._harness_object(abi)
         except subprocess.TimeoutExpired as error:
             return Sm100CompilationResult(False, None, _bounded(_text(error.stdout)), _bounded(_text(error.stderr)),
                                           time.monotonic() - started, True)
         except OSError as error:
             raise EvaluationInfrastructureError("CUDA compiler could not be executed") from error
+        if harness_obj is None:
+            raise EvaluationInfrastructureError("the evaluation harness failed to compile: "
+                                                + _bounded(harness_output, 2000))
+        tag = f"{os.getpid()}.{threading.get_ident()}"
+        candidate = artifact_dir / f"candidate.{tag}.cu"
+        candidate.write_text(program.source, encoding="utf-8")
+        candidate_obj = artifact_dir / f"candidate.{tag}.o"
+        tmp_executable = artifact_dir / f"evaluate.{tag}.tmp"
+        arch = ["-gencode", "arch=compute_100a,code=sm_100a"]
+        compile_command = [
+            _resolve_tool(self.config.nvcc), *arch, "-std=c++17", "-O3", "-rdc=true", "-Xptxas=-v",
+            "-DKMCTS_CANDIDATE_ROOT" if abi == "root" else "-DKMCTS_CANDIDATE_LAUNCHER",
+            f"-I{native_build.INCLUDE}", "-c", str(candidate), "-o", str(candidate_obj),
+        ]
+        link_command = [
+            _resolve_tool(self.config.nvcc), *arch, "-rdc=true", str(candidate_obj), str(harness_obj),
+            f"-L{native_build.LIB_DIR}", "-lkmcts_gemm_sm100", "-lcublas",
+            "-Xlinker", f"-rpath={native_build.LIB_DIR}",
+            "-o", str(tmp_executable),
+        ]
+        try:
+            completed = self._runner(compile_command, timeout=self.config.compile_timeout_seconds,
+                                     env=self.config.subprocess_environment)
+            if completed.returncode == 0:
+                linked = self._runner(link_command, timeout=self.config.compile_timeout_seconds,
+                                      env=self.config.subprocess_environment)
+                if linked.returncode != 0:
+                    completed = subprocess.CompletedProcess(link_command, linked.returncode,
+                                                            completed.stdout + linked.stdout,
+                                                            completed.stderr + linked.stderr)
+        except subprocess.TimeoutExpired as error:
+            return Sm100CompilationResult(False, None, _bounded(_text(error.stdout)), _bounded(_text(error.stderr)),
+                                          time.monotonic() - started, True)
+        except OSError as error:
+            raise EvaluationInfrastructureError("CUDA compiler could not be executed") from error
+        finally:
+            for leftover in (candidate_obj,):
+                try:
+                    leftover.unlink()
+                except OSError:
+                    pass
         duration = time.monotonic() - started
-        if completed.returncode != 0:
+        if completed.returncode != 0 or not tmp_executable.exists():
             return Sm100CompilationResult(False, None, _bounded(completed.stdout), _bounded(completed.stderr), duration)
         output = f"{completed.stdout}\n{completed.stderr}"
+        os.replace(candidate, artifact_dir / "candidate.cu")
+        os.replace(tmp_executable, executable)  # atomic: a concurrent builder's copy is equivalent
+        log.write_text(output, encoding="utf-8")
         self._compiler_output[key] = output
         return self._compiled(executable, abi, _bounded(completed.stdout), output, duration)
 

@@ -15,6 +15,12 @@ Failure handling (host side only; nothing here touches a GPU):
   INFRASTRUCTURE_FAILURE result, as an infrastructure retry in the reference
   would report it (src/kernel_mcts/orchestration.py:256-272).
 
+A ``HostCompilePool`` builds candidate sources with nvcc on host cores ahead
+of the GPU workers: ``evaluate_many(..., compile_ahead=pool)`` submits every
+candidate's build at once and hands a candidate to a GPU only when its build
+is done, so the GPU evaluates candidate i while nvcc builds i+1, i+2, ...;
+the workers find the builds in the shared candidate cache.
+
 ``evaluate_many`` keeps the KernelEvaluator call shape
 (src/kernel_mcts/interfaces.py:8-9) for a batch; ``evaluate`` is the single
 call, so MCTS runs unchanged on top.  ``lightweight_profile`` keeps the
@@ -215,22 +221,39 @@ class EvaluationPool:
     def evaluate(self, program: KernelProgram, workload: WorkloadContract) -> EvaluationResult:
         return self.evaluate_many([program], workload)[0]
 
-    def evaluate_many(self, programs: Sequence[KernelProgram], workload: WorkloadContract) -> list[EvaluationResult]:
+    def evaluate_many(self, programs: Sequence[KernelProgram], workload: WorkloadContract, *,
+                      compile_ahead: "HostCompilePool | None" = None) -> list[EvaluationResult]:
         workload_value = serialize_workload(workload)
+        builds = ([compile_ahead.submit(p, workload) for p in programs] if compile_ahead is not None
+                  else [None] * len(programs))
         pending = list(range(len(programs)))[::-1]  # pop() takes the lowest index first
         attempts = [0] * len(programs)
         out: list[EvaluationResult | None] = [None] * len(programs)
         done = 0
+
+        def next_job() -> int | None:
+            # The lowest pending job whose build (if any) has finished.
+            for position in range(len(pending) - 1, -1, -1):
+                build = builds[pending[position]]
+                if build is None or build.done():
+                    return pending.pop(position)
+            return None
+
         while done < len(programs):
             for w in self._workers:
                 if w.job is None and w.ready and pending:
-                    job = pending.pop()
+                    job = next_job()
+                    if job is None:
+                        break
                     attempts[job] += 1
                     p = programs[job]
                     w.jobs.put((job, {"source": p.source, "backend": p.backend}, workload_value))
                     w.job, w.started_at = job, time.monotonic()
             try:
-                kind, slot, job, payload = self._results.get(timeout=0.5)
+                # Short waits while builds are still running, so a finished
+                # build reaches an idle GPU at once.
+                waiting_builds = any(builds[j] is not None and not builds[j].done() for j in pending)
+                kind, slot, job, payload = self._results.get(timeout=0.02 if waiting_builds else 0.5)
             except queue.Empty:
                 kind = None
             if kind == "ready":
@@ -314,6 +337,48 @@ class EvaluationPool:
                 raise RuntimeError(f"{error_type}: {message}")
 
 
+class HostCompilePool:
+    """nvcc builds of candidate sources on host cores, into the candidate
+    cache the GPU workers read (``CudaSm100Config.candidate_cache``).
+    Schedule programs need no build and get no job."""
+
+    def __init__(self, artifact_root: str | os.PathLike, *, jobs: int | None = None, runner: Any = None) -> None:
+        from concurrent.futures import ThreadPoolExecutor
+        from pathlib import Path
+
+        from .backend import CudaSm100Backend, CudaSm100Config
+
+        root = Path(artifact_root)
+        self.backend = CudaSm100Backend(CudaSm100Config(artifact_root=root / "host-compile",
+                                                        candidate_cache=candidate_cache(root)), runner=runner)
+        self.jobs = jobs or max(1, (os.cpu_count() or 2) - 1)
+        self._executor = ThreadPoolExecutor(max_workers=self.jobs, thread_name_prefix="kmcts-nvcc")
+
+    def submit(self, program: KernelProgram, workload: WorkloadContract):
+        from .backend import CANDIDATE_BACKEND
+
+        if program.backend != CANDIDATE_BACKEND:
+            return None
+        return self._executor.submit(self.backend.compile, program, workload)
+
+    def close(self) -> None:
+        self._executor.shutdown(wait=True)
+
+    def __enter__(self) -> "HostCompilePool":
+        return self
+
+    def __exit__(self, *exc) -> None:
+        self.close()
+
+
+def candidate_cache(artifact_root: str | os.PathLike):
+    """The candidate build cache shared by a host compile pool and the GPU
+    workers under one artifact root."""
+    from pathlib import Path
+
+    return Path(artifact_root) / "candidates"
+
+
 def _infrastructure_failure(program: KernelProgram, reason: str) -> EvaluationResult:
     return EvaluationResult(status=ProposalStatus.INFRASTRUCTURE_FAILURE, program=program,
                             metadata={"error_type": "WorkerFailure", "reason": reason[-2000:]})
@@ -338,7 +403,8 @@ def sm100_evaluator(device_index: int, *, artifact_root: str, root_us: float, wa
 
     subprocess_backend = CudaSm100Backend(CudaSm100Config(
         artifact_root=Path(artifact_root) / f"gpu{device_index}", warmup_count=warmup_count,
-        measurement_count=measurement_count, device_index=device_index, flush_l2=flush_l2))
+        measurement_count=measurement_count, device_index=device_index, flush_l2=flush_l2,
+        candidate_cache=candidate_cache(artifact_root)))
     local = (InProcessSm100Backend(warmup_count=warmup_count, measurement_count=measurement_count,
                                    flush_l2=flush_l2, device_index=device_index) if inprocess else None)
     backend = HybridSm100Backend(subprocess_backend, local)
@@ -346,3 +412,63 @@ def sm100_evaluator(device_index: int, *, artifact_root: str, root_us: float, wa
                                 {"launcher": "kmcts_bf16_gemm_ex"}, {"gpu": "B200", "arch": "sm_100a"})
     return BackendKernelEvaluator(backend=backend, root_benchmark=BenchmarkResult((root_us,), root_us),
                                   context=context)
+
+
+# ------------------------------------------------------------ measurement
+
+
+def candidate_sources(count: int) -> list[KernelProgram]:
+    """``count`` distinct host-launcher candidates (each runs the library's
+    GEMM with its own raster group, so each is a separate build)."""
+    template = (
+        "#include <cuda_runtime.h>\n#include \"kmcts_gemm.h\"\n"
+        "extern \"C\" int bf16_gemm_launch(const void* A, const void* B, void* C, int M, int N, int K,\n"
+        "                                cudaStream_t s) {{\n"
+        "    kmcts_gemm_config cfg;\n    kmcts_default_config(&cfg);\n    cfg.raster_group = {group};\n"
+        "    return kmcts_bf16_gemm_ex(A, B, C, M, N, K, KMCTS_B_COL, &cfg, s, nullptr);\n}}\n")
+    return [KernelProgram(template.format(group=1 + i), "cuda_cpp") for i in range(count)]
+
+
+def _measure(argv: Sequence[str] | None = None) -> None:
+    """Candidate-source evaluations per second through the pool, with and
+    without the host compile pool ahead of it (fresh build caches each)."""
+    import argparse
+    import json
+    import tempfile
+
+    from .workloads import gemm_workload
+
+    p = argparse.ArgumentParser(description=_measure.__doc__.split("\n")[0])
+    p.add_argument("--devices", default="0")
+    p.add_argument("--candidates", type=int, default=8)
+    p.add_argument("--M", type=int, default=4096)
+    p.add_argument("--N", type=int, default=4096)
+    p.add_argument("--K", type=int, default=4096)
+    p.add_argument("--jobs", type=int, default=None, help="host compile threads")
+    args = p.parse_args(argv)
+    devices = [d for d in args.devices.split(",") if d]
+    workload = gemm_workload(f"bf16_gemm_{args.M}x{args.N}x{args.K}_b200", args.M, args.N, args.K)
+    programs = candidate_sources(args.candidates)
+    report: dict[str, Any] = {"candidates": len(programs), "devices": devices, "shape": [args.M, args.N, args.K]}
+    for mode in ("worker_compiles", "compile_ahead"):
+        with tempfile.TemporaryDirectory(prefix="kmcts-candidates-") as root:
+            spec = WorkerSpec("kernel_mcts_b200.pool:sm100_evaluator", {"artifact_root": root, "root_us": 100.0})
+            with EvaluationPool(devices, spec) as pool:
+                pool.prepare(workload)
+                compiler = HostCompilePool(root, jobs=args.jobs) if mode == "compile_ahead" else None
+                started = time.monotonic()
+                try:
+                    results = pool.evaluate_many(programs, workload, compile_ahead=compiler)
+                finally:
+                    if compiler is not None:
+                        compiler.close()
+                wall = time.monotonic() - started
+        valid = sum(r.status == ProposalStatus.VALID for r in results)
+        report[mode] = {"wall_s": wall, "evaluations_per_second": len(programs) / wall, "valid": valid,
+                        "host_compile_threads": (args.jobs or max(1, (os.cpu_count() or 2) - 1))
+                        if mode == "compile_ahead" else 0}
+    print(json.dumps(report))
+
+
+if __name__ == "__main__":
+    _measure()

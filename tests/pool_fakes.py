@@ -27,12 +27,13 @@ class FakeEvaluator:
                 os._exit(3)
         if "RAISE" in source:
             raise RuntimeError("backend exploded")
+        started = time.time()
         time.sleep(float(source.split("sleep=")[1].split(";")[0]) if "sleep=" in source else self.delay)
         return EvaluationResult(
             status=ProposalStatus.VALID, program=program, state_key=f"key-{source}", reward=1.0,
             benchmark=BenchmarkResult((1.0,), 1.0),
             metadata={"pid": os.getpid(), "visible_devices": os.environ.get("CUDA_VISIBLE_DEVICES"),
-                      "device_index": self.device_index},
+                      "device_index": self.device_index, "started": started},
         )
 
 

@@ -71,11 +71,15 @@ class FakeRunner:
         command = list(command)
         self.calls.append((command, timeout, dict(env)))
         if "-o" in command and command[0].endswith("nvcc"):
-            if self.timeout_stage == "compile":
+            # The candidate's own compile step is the one a test makes fail;
+            # the harness object and the link always succeed here.
+            candidate = "-c" in command and any(Path(part).name.startswith("candidate.") for part in command)
+            if self.timeout_stage == "compile" and candidate:
                 raise subprocess.TimeoutExpired(command, timeout)
-            if self.compile_returncode == 0:
+            returncode = self.compile_returncode if candidate else 0
+            if returncode == 0:
                 Path(command[command.index("-o") + 1]).write_bytes(b"executable bytes")
-            return subprocess.CompletedProcess(command, self.compile_returncode, "", self.compile_stderr)
+            return subprocess.CompletedProcess(command, returncode, "", self.compile_stderr if candidate else "")
         if command[0].endswith("nvidia-smi"):
             return subprocess.CompletedProcess(command, 0, "40, 1965, 3996, 500.0, 1000.0, P0, 99, 20, 0x0000000000000000\n", "")
         if command[0].endswith("ncu"):
@@ -96,15 +100,23 @@ def make_backend(tmp_path, runner, **changes) -> CudaSm100Backend:
 
 
 def test_candidate_compile_command_targets_sm100a_and_links_the_library(tmp_path):
+    """The harness is compiled once per ABI (relocatable device code); each
+    candidate is compiled alone with ptxas resource output, then linked to it
+    and to the library."""
     runner = FakeRunner()
     result = make_backend(tmp_path, runner).compile(KernelProgram(ROOT_SOURCE), BF16_GEMM_4096_B200)
     assert result.success and result.artifact is not None
-    command, timeout, env = runner.calls[0]
+    harness, compile_step, link = (c[0] for c in runner.calls[:3])
+    assert "-c" in harness and any(p.endswith("harness.cu") for p in harness)
+    assert "-DKMCTS_CANDIDATE_ROOT" in harness and "-rdc=true" in harness
+    command, timeout, env = runner.calls[1]
     assert command[0] == "/opt/cuda/bin/nvcc"
-    assert "arch=compute_100a,code=sm_100a" in command
-    assert "-DKMCTS_CANDIDATE_ROOT" in command and "-rdc=true" in command and "-Xptxas=-v" in command
-    assert "-lkmcts_gemm_sm100" in command and "-lcublas" in command
-    assert not any("--keep" in part for part in command)  # no PTX kept: nothing reads it
+    for step in (harness, compile_step, link):
+        assert "arch=compute_100a,code=sm_100a" in step
+        assert not any("--keep" in part for part in step)  # no PTX kept: nothing reads it
+    assert "-c" in compile_step and "-rdc=true" in compile_step and "-Xptxas=-v" in compile_step
+    assert "-lkmcts_gemm_sm100" in link and "-lcublas" in link and "-rdc=true" in link
+    assert any(p.startswith(str(tmp_path / "harness-root-")) for p in link)
     assert set(env) <= {"PATH", "LANG", "LC_ALL", "LD_LIBRARY_PATH", "CUDA_VISIBLE_DEVICES", "HOME"}
     assert result.compiler_context["ptxas"] == [
         {"function": "bf16_gemm_root", "stack_bytes": 0, "spill_store_bytes": 0, "spill_load_bytes": 0,
@@ -112,10 +124,28 @@ def test_candidate_compile_command_targets_sm100a_and_links_the_library(tmp_path
     ]
 
 
+def test_candidate_builds_are_cached_on_disk_across_backends(tmp_path):
+    """A backend sharing the candidate cache (another process, e.g. a host
+    compile pool ahead of the GPU workers) reuses a build and its compiler
+    output; the harness object is built once per ABI."""
+    first = FakeRunner()
+    built = make_backend(tmp_path / "a", first, candidate_cache=tmp_path / "cache").compile(
+        KernelProgram(ROOT_SOURCE), BF16_GEMM_4096_B200)
+    second = FakeRunner()
+    reused = make_backend(tmp_path / "b", second, candidate_cache=tmp_path / "cache").compile(
+        KernelProgram(ROOT_SOURCE + "\n// a comment only"), BF16_GEMM_4096_B200)
+    assert built.success and reused.success and second.calls == []
+    assert reused.artifact.executable == built.artifact.executable
+    assert reused.compiler_context["ptxas"] == built.compiler_context["ptxas"]
+    other = make_backend(tmp_path / "b", second, candidate_cache=tmp_path / "cache").compile(
+        KernelProgram(ROOT_SOURCE.replace("int K) {}", "int K) { (void)M; }")), BF16_GEMM_4096_B200)
+    assert other.success and len(second.calls) == 2  # compile + link; the harness object is reused
+
+
 def test_launcher_abi_is_detected_and_compiled_with_its_macro(tmp_path):
     runner = FakeRunner()
     make_backend(tmp_path, runner).compile(KernelProgram(LAUNCHER_SOURCE), BF16_GEMM_4096_B200)
-    assert "-DKMCTS_CANDIDATE_LAUNCHER" in runner.calls[0][0]
+    assert "-DKMCTS_CANDIDATE_LAUNCHER" in runner.calls[0][0] and "-DKMCTS_CANDIDATE_LAUNCHER" in runner.calls[1][0]
     assert detect_candidate_abi(LAUNCHER_SOURCE) == "launcher"
     assert detect_candidate_abi("// bf16_gemm_launch(\n" + ROOT_SOURCE) == "root"  # comments ignored
     with pytest.raises(ValueError):

@@ -256,8 +256,10 @@ def test_reference_sequential_loop_runs_on_the_b200_backend(tmp_path):
             out = super().__call__(command, timeout=timeout, env=env)
             command = list(command)
             if "-o" in command and command[0].endswith("nvcc"):
-                source = next(c for c in command if c.endswith("candidate.cu"))
-                Path(command[command.index("-o") + 1]).write_bytes(Path(source).read_bytes())
+                # Compile: the object is the source; link: the executable is the object.
+                inputs = [c for c in command if Path(c).name.startswith("candidate.") and c.endswith((".cu", ".o"))]
+                if inputs:
+                    Path(command[command.index("-o") + 1]).write_bytes(Path(inputs[0]).read_bytes())
             return out
 
     runner = Runner()
@@ -345,8 +347,10 @@ def _reference_search_setup(tmp_path):
             out = super().__call__(command, timeout=timeout, env=env)
             command = list(command)
             if "-o" in command and command[0].endswith("nvcc"):
-                source = next(c for c in command if c.endswith("candidate.cu"))
-                Path(command[command.index("-o") + 1]).write_bytes(Path(source).read_bytes())
+                # Compile: the object is the source; link: the executable is the object.
+                inputs = [c for c in command if Path(c).name.startswith("candidate.") and c.endswith((".cu", ".o"))]
+                if inputs:
+                    Path(command[command.index("-o") + 1]).write_bytes(Path(inputs[0]).read_bytes())
             return out
 
     runner = Runner()

@@ -84,3 +84,41 @@ def test_prepare_reaches_every_worker(tmp_path):
     with EvaluationPool([0, 1, 2], spec(tmp_path)) as pool:
         pool.prepare(WORKLOAD)  # fake evaluators have no prepare hook: a no-op ack per worker
         assert pool.evaluate(KernelProgram("x"), WORKLOAD).status == ProposalStatus.VALID
+
+
+def test_host_compile_pool_builds_ahead_of_the_gpu_workers(tmp_path):
+    """Candidate sources are built on host threads while the (fake) GPU
+    worker evaluates: no candidate reaches a worker before its build is done,
+    and builds overlap evaluations (serialised, build + evaluation would take
+    4 x (0.3 + 0.2) s)."""
+    from test_backend import FakeRunner
+
+    from kernel_mcts_b200.pool import HostCompilePool
+
+    class SlowNvcc(FakeRunner):
+        def __init__(self):
+            super().__init__()
+            self.finished: dict[str, float] = {}
+
+        def __call__(self, command, *, timeout, env):
+            out = super().__call__(command, timeout=timeout, env=env)
+            if command[0].endswith("nvcc") and "-c" in command:
+                source = next((c for c in command if c.endswith(".cu") and "candidate." in c), None)
+                if source is not None:
+                    time.sleep(0.3)
+                    text = open(source).read()
+                    self.finished[text.split("sleep=")[1].split(";")[0] + text.split("#")[-1].strip()] = time.time()
+            return out
+
+    runner = SlowNvcc()
+    programs = [KernelProgram(f"// sleep=0.2;\nextern \"C\" __global__ void bf16_gemm_root() {{}}\n#{i}",
+                              "cuda_cpp") for i in range(4)]
+    with EvaluationPool([0], spec(tmp_path)) as pool, HostCompilePool(tmp_path, jobs=4, runner=runner) as builds:
+        start = time.time()
+        results = pool.evaluate_many(programs, WORKLOAD, compile_ahead=builds)
+        wall = time.time() - start
+    assert [r.status for r in results] == [ProposalStatus.VALID] * 4
+    assert len(runner.finished) == 4
+    for i, r in enumerate(results):
+        assert r.metadata["started"] >= runner.finished[f"0.2{i}"] - 0.05  # built before it ran
+    assert wall < 1.7, wall
