@@ -31,12 +31,14 @@ from . import _native
 from . import build as native_build
 from .backend import (
     SCHEDULE_BACKEND,
+    SCHEDULE_FIELDS,
     CudaSm100Backend,
     Sm100CompilationResult,
     Sm100CorrectnessResult,
     merge_benchmarks,
     merge_correctness,
     schedule_from_source,
+    schedule_program,
     shape_mnk,
 )
 from .domain import BenchmarkResult, KernelProgram, WorkloadContract
@@ -253,4 +255,13 @@ class HybridSm100Backend:
         return self._for_artifact(artifact).evaluation_metadata(artifact)
 
     def lightweight_profile(self, artifact, workload, metric_set="lightweight_v1"):
-        return self._for_artifact(artifact).lightweight_profile(artifact, workload, metric_set)
+        # A schedule evaluated in process is profiled as the same schedule run
+        # by the harness executable under ncu (one kernel, one launch).
+        if isinstance(artifact, ScheduleArtifact):
+            schedule = {k: v for k, v in artifact.schedule.items() if k in SCHEDULE_FIELDS}
+            compiled = self.subprocess_backend.compile(schedule_program(**schedule), workload)
+            if not compiled.success or compiled.artifact is None:
+                raise EvaluationInfrastructureError("the schedule could not be prepared for profiling: "
+                                                    + compiled.stderr[-2000:])
+            artifact = compiled.artifact
+        return self.subprocess_backend.lightweight_profile(artifact, workload, metric_set)

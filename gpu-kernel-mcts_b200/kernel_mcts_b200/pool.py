@@ -334,7 +334,9 @@ class EvaluationPool:
                 error_type, message = payload
                 if error_type == "EvaluationInfrastructureError":
                     raise EvaluationInfrastructureError(message)
-                raise RuntimeError(f"{error_type}: {message}")
+                # Any other failure in the worker is an infrastructure failure
+                # to the caller; keep its type in the diagnostic.
+                raise EvaluationInfrastructureError(f"{error_type}: {message}")
 
 
 class HostCompilePool:

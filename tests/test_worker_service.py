@@ -329,3 +329,29 @@ def test_reference_worker_application_over_the_sm100_backend(tmp_path):
     profile = app.handle("POST", "/profile", AUTH,
                          json.dumps({"evaluation_id": "r1", "profile_level": "lightweight"}).encode())
     assert profile.status == 200 and profile.payload["metric_set"] == "lightweight_v1"
+
+
+def test_in_process_schedule_profiles_through_the_harness(tmp_path):
+    """A schedule evaluated in process (its artifact carries the resolved
+    config, launch fields included) is profiled as the same schedule run by
+    the harness under ncu."""
+    from test_backend import FakeRunner, _wide_csv, make_backend
+
+    from kernel_mcts_b200 import _native
+    from kernel_mcts_b200.inprocess import HybridSm100Backend, ScheduleArtifact
+    from kernel_mcts_b200.profiling import SM100_V1_METRICS
+
+    class Query(FakeRunner):
+        def __call__(self, command, *, timeout, env):
+            if command[0].endswith("ncu") and "--query-metrics-mode" in command:
+                return __import__("subprocess").CompletedProcess(command, 0, "\n".join(SM100_V1_METRICS), "")
+            return super().__call__(command, timeout=timeout, env=env)
+
+    runner = Query()
+    runner.ncu_stdout = _wide_csv(SM100_V1_METRICS)
+    hybrid = HybridSm100Backend(make_backend(tmp_path, runner), None)
+    resolved = _native.make_config(tile_m=256, cluster_m=2, tile_n=256, tile_k=128, stages=3).as_dict()
+    profile = hybrid.lightweight_profile(ScheduleArtifact("id", resolved), WORKLOAD, "sm100_v1")
+    assert profile["metric_set"] == "sm100_v1"
+    profiled = [c[0] for c in runner.calls if "--metrics" in c[0]]
+    assert len(profiled) == 1 and "--tile-m=256" in profiled[0] and "--kernel=tcgen05" in profiled[0]
