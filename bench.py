@@ -440,8 +440,10 @@ def cublas_protocol_median(device, layout: str, warmups: int, measurements: int)
 def sharded_gemm(device, world: int, local_rank: int, steps: int = 5, warmup: int = 2) -> dict:
     """8192x28672x8192, N(0, 0.02^2) BF16, B and C sharded by
     N columns over the ranks.  The fused kernel (GEMM + all-gather of C over
-    NVLink peer stores) against the same GEMM followed by NCCL all_gather and
-    a re-layout; aggregate TFLOP/s = 2MNK / max-over-ranks median time.
+    NVLink peer stores), the copy-engine all-gather (row-block GEMMs whose
+    finished rows the copy engines send to every rank's C) and the same GEMM
+    followed by NCCL all_gather and a re-layout; aggregate TFLOP/s = 2MNK /
+    max-over-ranks median time.
 
     Outside the timed region every rank checks its full C, on the first and
     last 256 rows (the first and last row tiles) and all columns, bit for bit
@@ -471,8 +473,8 @@ def sharded_gemm(device, world: int, local_rank: int, steps: int = 5, warmup: in
     out = {"workload": "8192x28672x8192 N(0,0.02) bf16, B/C sharded by N", "gpus": world}
     identical = True
     try:
-        for name, fn in (("fused", sg.run), ("nccl", sg.run_nccl)):
-            if world == 1 and name == "nccl":
+        for name, fn in (("fused", sg.run), ("copy_engines", sg.run_copy_engines), ("nccl", sg.run_nccl)):
+            if world == 1 and name != "fused":
                 continue
             for _ in range(warmup):
                 fn(a, b_shard)

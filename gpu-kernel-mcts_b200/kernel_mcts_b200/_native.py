@@ -75,6 +75,7 @@ EXPORTED_SYMBOLS = (
     "kmcts_ipc_export",
     "kmcts_ipc_import",
     "kmcts_ipc_close",
+    "kmcts_copy_2d",
     "kmcts_bf16_gemm_allgather",
     "kmcts_selftest_bounded_wait",
 )
@@ -214,6 +215,9 @@ def load() -> ctypes.CDLL:
         lib.kmcts_ipc_import.restype = i32
         lib.kmcts_ipc_close.argtypes = [vp]
         lib.kmcts_ipc_close.restype = i32
+        sz = ctypes.c_size_t
+        lib.kmcts_copy_2d.argtypes = [vp, sz, vp, sz, sz, sz, vp]
+        lib.kmcts_copy_2d.restype = i32
         lib.kmcts_bf16_gemm_allgather.argtypes = [vp, vp, vp, i32, i32, i32, i32, i32, i32,
                                                   ctypes.POINTER(GemmConfig), vp, vp]
         lib.kmcts_bf16_gemm_allgather.restype = i32

@@ -86,4 +86,16 @@ int kmcts_ipc_close(void* device_ptr) {
     return KMCTS_OK;
 }
 
+int kmcts_copy_2d(void* dst, size_t dst_pitch, const void* src, size_t src_pitch, size_t width_bytes,
+                  size_t height, void* stream) {
+    if (!dst || !src || width_bytes > dst_pitch || width_bytes > src_pitch) return KMCTS_EINVAL;
+    if (width_bytes == 0 || height == 0) return KMCTS_OK;
+    if (cudaMemcpy2DAsync(dst, dst_pitch, src, src_pitch, width_bytes, height, cudaMemcpyDeviceToDevice,
+                          static_cast<cudaStream_t>(stream)) != cudaSuccess) {
+        cudaGetLastError();
+        return KMCTS_ESYNC;
+    }
+    return KMCTS_OK;
+}
+
 }  // extern "C"

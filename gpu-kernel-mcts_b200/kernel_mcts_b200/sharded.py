@@ -8,11 +8,17 @@ ranks (one process per GPU).  Rank r owns columns [r·N/G, (r+1)·N/G).
   TMA store, its peers' by plain stores through CUDA-IPC-mapped pointers over
   NVLink.  The all-gather of C overlaps the GEMM tile by tile, with no
   collective library call, no multicast objects and no NVLS.
+* ``ShardedGemm.run_copy_engines`` moves the all-gather off the SMs: the
+  shard's GEMM runs as row blocks into a local buffer (each block a whole
+  number of near-full waves of CTA pairs), and as each block finishes, one
+  stream per destination copies its rows into that rank's C with
+  ``kmcts_copy_2d`` (cudaMemcpy2DAsync into IPC-mapped peer memory: the copy
+  engines drive NVLink while the SMs compute the next block).
 * ``ShardedGemm.run_nccl`` is the baseline: the same GEMM into a local shard,
   ``all_gather_into_tensor`` over NCCL, then the column-block-to-row-major
   copy.
 
-Both leave C bit-identical to the single-GPU kernel on the full problem
+All three leave C bit-identical to the single-GPU kernel on the full problem
 under the N tail split (the default here): shard widths are whole
 256-column tiles, so every output element has the same K-ordered
 accumulation.
@@ -112,6 +118,7 @@ class ShardedGemm:
         self._c_array = (ctypes.c_void_p * self.world)(*self.c_ptrs)
         self._shard = None  # NCCL baseline buffers, made on first use
         self._gathered = None
+        self._ce = None  # copy-engine path: streams and events, made on first use
 
     @property
     def shard_width(self) -> int:
@@ -128,6 +135,61 @@ class ShardedGemm:
             self.rank, self.m, self.n, self.k, self.layout, ctypes.byref(self.config),
             ctypes.c_void_p(stream.cuda_stream), ctypes.c_void_p(self.status.data_ptr()))
         _native.check(rc, "kmcts_bf16_gemm_allgather")
+
+    def row_blocks(self) -> list[tuple[int, int]]:
+        """Row ranges of the copy-engine path: each range's 256 x 256 pair
+        tiles fill the co-resident pairs' waves as fully as possible (the
+        last range may be shorter), with at least four ranges so the copies
+        start early."""
+        workers = int(_native.plan(self.config, self.m, self.shard_width, self.k, self.layout)["workers"]) or 74
+        num_m = -(-self.m // 256)
+        tiles_n = -(-self.shard_width // 256)
+        best, best_eff = 1, -1.0
+        for per in range(1, num_m + 1):
+            if -(-num_m // per) < min(4, num_m):
+                break
+            tiles = per * tiles_n
+            eff = tiles / (-(-tiles // workers) * workers)
+            if eff > best_eff + 1e-9:
+                best, best_eff = per, eff
+        rows = best * 256
+        return [(r0, min(self.m, r0 + rows)) for r0 in range(0, self.m, rows)]
+
+    def run_copy_engines(self, a: torch.Tensor, b_shard: torch.Tensor, stream: torch.cuda.Stream | None = None) -> None:
+        """GEMM of the shard in row blocks; each finished block copied into
+        every rank's C (own and peers') by the copy engines, one stream per
+        destination.  Asynchronous: call ``finish()`` before reading C."""
+        from . import gemm as kg
+
+        stream = stream or torch.cuda.current_stream(self.device)
+        if self._shard is None:
+            self._shard = torch.empty((self.m, self.shard_width), dtype=torch.bfloat16, device=self.device)
+        if self._ce is None:
+            blocks = self.row_blocks()
+            self._ce = {
+                "blocks": blocks,
+                "streams": [torch.cuda.Stream(self.device) for _ in range(self.world)],
+                "events": [torch.cuda.Event() for _ in blocks],
+                "done": [torch.cuda.Event() for _ in range(self.world)],
+            }
+        lib = _native.load()
+        ce = self._ce
+        w = self.shard_width
+        pitch = self.n * 2
+        for (r0, r1), event in zip(ce["blocks"], ce["events"]):
+            kg.bf16_gemm(a[r0:r1], b_shard, out=self._shard[r0:r1], b_layout=self.layout, config=self.config,
+                         stream=stream, status=self.status)
+            event.record(stream)
+            for dest, copy_stream in enumerate(ce["streams"]):
+                copy_stream.wait_event(event)
+                dst = self.c_ptrs[dest] + (r0 * self.n + self.col0) * 2
+                rc = lib.kmcts_copy_2d(ctypes.c_void_p(dst), pitch,
+                                       ctypes.c_void_p(self._shard.data_ptr() + r0 * w * 2), w * 2, w * 2, r1 - r0,
+                                       ctypes.c_void_p(copy_stream.cuda_stream))
+                _native.check(rc, "kmcts_copy_2d")
+        for done, copy_stream in zip(ce["done"], ce["streams"]):
+            done.record(copy_stream)
+            stream.wait_event(done)
 
     def run_nccl(self, a: torch.Tensor, b_shard: torch.Tensor, stream: torch.cuda.Stream | None = None) -> None:
         """Baseline: local GEMM, NCCL all-gather, column-block -> row-major copy."""
@@ -192,14 +254,14 @@ def _main(argv: Sequence[str] | None = None) -> None:
     try:
         if args.check:
             full = kg.bf16_gemm(a, b_full, b_layout=args.b_layout, config=sg.config)
-            for name, fn in (("fused", sg.run), ("nccl", sg.run_nccl)):
+            for name, fn in (("fused", sg.run), ("copy_engines", sg.run_copy_engines), ("nccl", sg.run_nccl)):
                 sg.c.zero_()
                 dist.barrier(device_ids=[local_rank])
                 fn(a, b_shard)
                 sg.finish()
                 out[f"{name}_bit_identical"] = bool(torch.equal(sg.c.view(torch.int16), full.view(torch.int16)))
         stream = torch.cuda.current_stream(device)
-        for name, fn in (("fused", sg.run), ("nccl", sg.run_nccl)):
+        for name, fn in (("fused", sg.run), ("copy_engines", sg.run_copy_engines), ("nccl", sg.run_nccl)):
             for _ in range(args.warmup):
                 fn(a, b_shard)
                 sg.finish()

@@ -208,6 +208,16 @@ int kmcts_ipc_import(const uint8_t* handle, void** device_ptr_out);
 /* Unmaps an imported allocation. */
 int kmcts_ipc_close(void* device_ptr);
 
+/* No counterpart in the reference.  Copies `height` rows of `width_bytes`
+ * bytes between device buffers (row pitches in bytes) on `stream`, with
+ * cudaMemcpy2DAsync: into an IPC-imported peer buffer the GPU's copy engines
+ * move the rows over NVLink while the SMs keep computing.  The copy-engine
+ * all-gather of the N-sharded GEMM uses it to send finished row blocks of a
+ * rank's C columns to every peer's C.  Asynchronous; KMCTS_ESYNC if the copy
+ * cannot be queued. */
+int kmcts_copy_2d(void* dst, size_t dst_pitch, const void* src, size_t src_pitch, size_t width_bytes,
+                  size_t height, void* stream);
+
 /* C_ranks[r] is rank r's full C (this rank's own buffer at index `rank`,
  * IPC-imported peer buffers elsewhere).  B_shard is this rank's columns:
  * [N/G, K] row-major for KMCTS_B_COL, [K, N/G] row-major for KMCTS_B_ROW.

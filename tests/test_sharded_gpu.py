@@ -1,6 +1,6 @@
 """The fused N-sharded GEMM + all-gather on 2 GPUs (skipped with fewer): every
 rank's full C is bit-identical to the single-GPU kernel on the full problem,
-for the fused kernel and for the NCCL baseline."""
+for the fused kernel, the copy-engine all-gather and the NCCL baseline."""
 
 from __future__ import annotations
 
@@ -32,3 +32,4 @@ def test_fused_allgather_matches_single_gpu_bit_for_bit(cuda_device, layout):
     line = [l for l in out.stdout.splitlines() if l.startswith("{")][-1]
     result = json.loads(line)
     assert result["fused_bit_identical"] and result["nccl_bit_identical"], result
+    assert result["copy_engines_bit_identical"], result
