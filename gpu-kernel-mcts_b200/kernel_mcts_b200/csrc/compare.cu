@@ -8,6 +8,7 @@
 // arrays (HBM-bound: 4 bytes read per element) instead of a 16.8 M-element
 // host loop after two device-to-host copies.
 #include <cuda_bf16.h>
+#include <cudaTypedefs.h>
 
 #include <cstring>
 #include <mutex>
@@ -138,25 +139,48 @@ namespace {
 constexpr size_t kNoAllocScratchBytes = KMCTS_NOALLOC_SCRATCH_BYTES;
 static __device__ __align__(256) unsigned char g_compare_scratch[kNoAllocScratchBytes];
 
+PFN_cuCtxGetCurrent_v4000 current_context_fn() {
+    static std::once_flag once;
+    static PFN_cuCtxGetCurrent_v4000 fn = nullptr;
+    std::call_once(once, [] {
+        void* entry = nullptr;
+        cudaDriverEntryPointQueryResult query;
+        if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &entry, 4000, cudaEnableDefault, &query) ==
+                cudaSuccess &&
+            query == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(entry);
+    });
+    return fn;
+}
+
 // Device address of g_compare_scratch, looked up once per device with that
-// device current (host code cannot use the symbol itself as a pointer).
+// device current (host code cannot use the symbol itself as a pointer), and
+// looked up again if the device's context has been recreated since (after a
+// cudaDeviceReset the module reloads and the array may move).
 void* noalloc_scratch_address(int* rc) {
     static std::mutex mu;
     static void* address[64] = {};
+    static CUcontext context[64] = {};
     int device = 0;
     if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= 64) {
         *rc = KMCTS_EHANDLE;
         return nullptr;
     }
+    auto get_current = current_context_fn();
+    CUcontext current = nullptr;
+    if (get_current == nullptr || get_current(&current) != CUDA_SUCCESS) current = nullptr;
     std::lock_guard<std::mutex> lock(mu);
-    if (address[device] == nullptr) {
+    if (address[device] == nullptr || context[device] != current) {
         void* ptr = nullptr;
         if (cudaGetSymbolAddress(&ptr, g_compare_scratch) != cudaSuccess || ptr == nullptr) {
             cudaGetLastError();
             *rc = KMCTS_EHANDLE;
             return nullptr;
         }
+        // The lookup made the device's primary context current: remember it.
+        if (get_current == nullptr || get_current(&current) != CUDA_SUCCESS) current = nullptr;
         address[device] = ptr;
+        context[device] = current;
     }
     *rc = KMCTS_OK;
     return address[device];

@@ -89,6 +89,27 @@ def peer_pointers(own_ptr: int, handles: Sequence[bytes], rank: int, opener: Cal
     return [own_ptr if r == rank else opener(h) for r, h in enumerate(handles)]
 
 
+def copy_engine_row_blocks(m: int, shard_width: int, workers: int, min_blocks: int = 4) -> list[tuple[int, int]]:
+    """Row ranges for the copy-engine path: whole 256-row tile rows per range,
+    chosen so each range's 256 x 256 pair tiles fill the ``workers``
+    co-resident pairs' waves as fully as possible (the last range may be
+    shorter), with at least ``min_blocks`` ranges so the first copies start
+    early."""
+    workers = max(1, workers)
+    num_m = -(-m // 256)
+    tiles_n = -(-shard_width // 256)
+    best, best_eff = 1, -1.0
+    for per in range(1, num_m + 1):
+        if -(-num_m // per) < min(min_blocks, num_m):
+            break
+        tiles = per * tiles_n
+        eff = tiles / (-(-tiles // workers) * workers)
+        if eff > best_eff + 1e-9:
+            best, best_eff = per, eff
+    rows = best * 256
+    return [(r0, min(m, r0 + rows)) for r0 in range(0, m, rows)]
+
+
 class ShardedGemm:
     """One rank's view of an N-sharded GEMM of shape (M, N, K)."""
 
@@ -116,8 +137,8 @@ class ShardedGemm:
         handles = exchange_handles(self._ipc.export(self.c.data_ptr()), group)
         self.c_ptrs = peer_pointers(self.c.data_ptr(), handles, self.rank, self._ipc.open)
         self._c_array = (ctypes.c_void_p * self.world)(*self.c_ptrs)
-        self._shard = None  # NCCL baseline buffers, made on first use
-        self._gathered = None
+        self._shard = None  # local shard of C (copy-engine and NCCL paths), made on first use
+        self._gathered = None  # NCCL baseline's gathered shards, made on first use
         self._ce = None  # copy-engine path: streams and events, made on first use
 
     @property
@@ -137,23 +158,9 @@ class ShardedGemm:
         _native.check(rc, "kmcts_bf16_gemm_allgather")
 
     def row_blocks(self) -> list[tuple[int, int]]:
-        """Row ranges of the copy-engine path: each range's 256 x 256 pair
-        tiles fill the co-resident pairs' waves as fully as possible (the
-        last range may be shorter), with at least four ranges so the copies
-        start early."""
-        workers = int(_native.plan(self.config, self.m, self.shard_width, self.k, self.layout)["workers"]) or 74
-        num_m = -(-self.m // 256)
-        tiles_n = -(-self.shard_width // 256)
-        best, best_eff = 1, -1.0
-        for per in range(1, num_m + 1):
-            if -(-num_m // per) < min(4, num_m):
-                break
-            tiles = per * tiles_n
-            eff = tiles / (-(-tiles // workers) * workers)
-            if eff > best_eff + 1e-9:
-                best, best_eff = per, eff
-        rows = best * 256
-        return [(r0, min(self.m, r0 + rows)) for r0 in range(0, self.m, rows)]
+        """Row ranges of the copy-engine path (see copy_engine_row_blocks)."""
+        workers = int(_native.plan(self.config, self.m, self.shard_width, self.k, self.layout)["workers"])
+        return copy_engine_row_blocks(self.m, self.shard_width, workers)
 
     def run_copy_engines(self, a: torch.Tensor, b_shard: torch.Tensor, stream: torch.cuda.Stream | None = None) -> None:
         """GEMM of the shard in row blocks; each finished block copied into
@@ -198,6 +205,7 @@ class ShardedGemm:
         stream = stream or torch.cuda.current_stream(self.device)
         if self._shard is None:
             self._shard = torch.empty((self.m, self.shard_width), dtype=torch.bfloat16, device=self.device)
+        if self._gathered is None:
             self._gathered = torch.empty((self.world, self.m, self.shard_width), dtype=torch.bfloat16,
                                          device=self.device)
         with torch.cuda.stream(stream):

@@ -280,7 +280,8 @@ int kmcts_bf16_compare(const void* C, const void* reference, int64_t count, doub
  * every GPU loading this library keeps until the process exits; the
  * comparison needs that much for any `count`, and a call needing more would
  * return KMCTS_ENOSCRATCH.  The first call on each device looks up the
- * array's device address (cudaGetSymbolAddress), so make that first call
+ * array's device address (cudaGetSymbolAddress; again after the device's
+ * context is recreated, e.g. by cudaDeviceReset), so make that first call
  * before any stream capture.  Each call zeroes the accumulators it uses, but
  * all calls share the one array: calls that overlap on the GPU (different
  * streams or threads) race and corrupt each other's results.  Allocates no

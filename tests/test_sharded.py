@@ -54,3 +54,19 @@ def test_handle_exchange_orders_by_rank_and_opens_only_peers():
         assert p.exitcode == 0
     assert got[0] == ([0, 1], [1000, 5001], [1])
     assert got[1] == ([0, 1], [5000, 1001], [0])
+
+
+def test_copy_engine_row_blocks_fill_waves_and_cover_m():
+    from kernel_mcts_b200.sharded import copy_engine_row_blocks
+
+    # 8 GPUs on config 4: 14 tile columns per rank; 5 tile rows = 70 tiles on 74 pairs.
+    blocks = copy_engine_row_blocks(8192, 3584, 74)
+    assert blocks[0] == (0, 1280) and blocks[-1][1] == 8192 and len(blocks) == 7
+    assert all(b == c for (_, b), (c, _) in zip(blocks, blocks[1:]))
+    # 4 GPUs: 28 tile columns; 5 tile rows = 140 tiles, 0.95 of two waves.
+    assert copy_engine_row_blocks(8192, 7168, 74)[0] == (0, 1280)
+    # At least four blocks whenever there are four tile rows; ragged M covered.
+    small = copy_engine_row_blocks(2048, 2048, 74)
+    assert len(small) >= 4 and small[-1][1] == 2048
+    ragged = copy_engine_row_blocks(1000, 512, 74)
+    assert ragged[0][0] == 0 and ragged[-1][1] == 1000 and all(r1 > r0 for r0, r1 in ragged)
