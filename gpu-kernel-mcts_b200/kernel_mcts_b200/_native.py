@@ -47,6 +47,7 @@ FLAG_TAIL_STREAM_K = 4
 FLAG_TAIL_SPLIT_K = 32
 FLAG_B_EVICT_FIRST = 8
 FLAG_SWAP_AB = 16
+FLAG_SPLIT_CLUSTER = 64
 
 TAIL_NONE = 0
 TAIL_SPLIT_N = 1

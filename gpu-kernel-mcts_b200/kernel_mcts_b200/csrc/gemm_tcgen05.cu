@@ -54,6 +54,7 @@ using namespace gemm;
 
 constexpr int kBM = 128;
 constexpr int kMaxDevices = 64;
+constexpr int kMaxClusterSplits = 8;  // portable cluster size
 
 // AR: rows of A staged per tile.  128 normally; 32 for skinny GEMMs (M <= 32):
 // the MMA still computes 128 rows, but rows 32-127 read whatever follows A's
@@ -82,17 +83,32 @@ struct Layout {
 // Split K: unit u is K range s = u % splits of tile u / splits.  Partials are
 // [tile][split][lane quarter][BN/64 chunks] blocks of 32 rows x 64 FP32, each
 // stored as 16 float4 groups interleaved across the 32 lanes (coalesced).
+//
+// With `cluster` set, the splits of a tile are the CTAs of one cluster
+// (rank = split) and no partial goes through global memory: ranks 1.. store
+// their FP32 values into rank 0's shared memory (same block layout, one slot
+// per sending rank) and arrive on its receive barrier; rank 0 adds them to
+// its own accumulator in split order and writes C.  The sum order is the
+// global path's, so both give the same bits.
 struct SplitK {
     int splits;
     float* partials;
     unsigned long long* counters;  // [tile][lane quarter]: epoch << 32 | units arrived
     int epoch;
+    int cluster;
 };
 
 template <int BN>
 __device__ __forceinline__ float4* split_chunk(const SplitK& sk, int tile, int split, int quarter, int c) {
     const size_t block = ((static_cast<size_t>(tile) * sk.splits + split) * 4 + quarter) * (BN / 64) + c;
     return reinterpret_cast<float4*>(sk.partials + block * 32 * 64);
+}
+
+// Float4 offset of (sending rank's slot, lane quarter, chunk) in rank 0's
+// receive buffer.  `rows` is the rows of A staged per tile (32 or 128).
+template <int BN>
+__device__ __forceinline__ int recv_chunk(int slot, int quarter, int c, int rows) {
+    return ((slot * (rows / 32) + quarter) * (BN / 64) + c) * 16 * 32;
 }
 
 template <int BN, int BK, int STAGES, bool B_MN, int AR>
@@ -110,9 +126,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* tmem_full = empty + STAGES;
     uint64_t* tmem_empty = tmem_full + 2;
     uint64_t* drain = tmem_empty + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    uint64_t* recv_full = drain + 1;  // cluster split K: rank 0 receives the other ranks' values
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(recv_full + 1);
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
     volatile int* no_abort = abort + 1;
+    // Cluster split K's receive buffer: past the barriers (which take well
+    // under 1 KB of the reserve); the launch adds its size to the shared memory.
+    float4* recv = reinterpret_cast<float4*>(smem + L::kBarrierOffset + 1024);
 
     if (status == nullptr) status = &g_default_status;
     const int warp = threadIdx.x / 32;
@@ -134,6 +154,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             ptx::mbar_init(&tmem_empty[a], kEpilogueWarps);
         }
         ptx::mbar_init(drain, 1);
+        // Every lane of every epilogue warp of each sending rank arrives once.
+        ptx::mbar_init(recv_full, sk.cluster ? static_cast<uint32_t>((splits - 1) * kEpilogueWarps * 32) : 1u);
         *abort = 0;
         *no_abort = 0;
         ptx::fence_mbarrier_init();
@@ -149,6 +171,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     ptx::tc_fence_before();
     __syncthreads();
+    if (sk.cluster) ptx::cluster_sync();  // rank 0's receive barrier exists before any rank signals it
     ptx::tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
@@ -276,6 +299,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint8_t* staging = smem + L::kStagingOffset + (L::kStagingWarps == 1 ? 0 : e) * 2 * kStagingBytes;
         int local = 0;
         int chunk_count = 0;
+        // Cluster split K: rank 0's receive buffer and barrier as this CTA
+        // addresses them (the same offsets in every CTA of the launch).
+        const uint32_t recv_remote = sk.cluster ? ptx::mapa_shared(ptx::smem_addr(recv), 0) : 0u;
+        const uint32_t recv_full_remote = sk.cluster ? ptx::mapa_shared(ptx::smem_addr(recv_full), 0) : 0u;
         for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++local) {
             const int t = u / splits, s = u % splits;
             const TileCoord tc = tile_coord(t, num_m, num_n, group);
@@ -283,6 +310,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int n0 = tc.n_blk * BN;
             const int acc = local & 1;
             const uint32_t acc_phase = (local >> 1) & 1;
+            const bool sender = sk.cluster && s != 0;
+            const bool receiver = sk.cluster && s == 0;
             bool ok = ptx::mbar_wait(&tmem_full[acc], acc_phase, limit_ns, abort);
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) {
@@ -297,8 +326,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 ptx::tc_fence_before();
                 __syncwarp();
                 if (lane == 0) ptx::mbar_arrive(&tmem_empty[acc]);
+                if (sender) ptx::mbar_arrive_release_cluster(recv_full_remote);
                 continue;
             }
+            bool received = false;
 #pragma unroll 1
             for (int c = 0; c < BN / 64; ++c) {
                 uint32_t lo[32], hi[32];
@@ -309,6 +340,54 @@ __global__ void __launch_bounds__(kThreads, 1)
                     ptx::tc_fence_before();
                     __syncwarp();
                     if (lane == 0) ptx::mbar_arrive(&tmem_empty[acc]);
+                }
+                if (sender) {
+                    const uint32_t dst = recv_remote + static_cast<uint32_t>(recv_chunk<BN>(s - 1, quarter, c, AR) * 16);
+#pragma unroll
+                    for (int q = 0; q < 8; ++q)
+                        ptx::st_cluster_v4(dst + (q * 32 + lane) * 16, __uint_as_float(lo[4 * q]),
+                                           __uint_as_float(lo[4 * q + 1]), __uint_as_float(lo[4 * q + 2]),
+                                           __uint_as_float(lo[4 * q + 3]));
+#pragma unroll
+                    for (int q = 0; q < 8; ++q)
+                        ptx::st_cluster_v4(dst + ((8 + q) * 32 + lane) * 16, __uint_as_float(hi[4 * q]),
+                                           __uint_as_float(hi[4 * q + 1]), __uint_as_float(hi[4 * q + 2]),
+                                           __uint_as_float(hi[4 * q + 3]));
+                    continue;
+                }
+                if (receiver) {
+                    if (!received) {
+                        bool got = ptx::mbar_wait_cluster(recv_full, 0, limit_ns, abort);
+                        got = __all_sync(0xffffffffu, got);
+                        if (!got) {
+                            if (lane == 0) record_failure(status, abort, kRoleEpilogue);
+                            break;
+                        }
+                        received = true;
+                    }
+                    // Split 0's values, then every other split's, in split order.
+#pragma unroll 1
+                    for (int j = 1; j < splits; ++j) {
+                        const float4* part = recv + recv_chunk<BN>(j - 1, quarter, c, AR);
+#pragma unroll
+                        for (int q = 0; q < 8; ++q) {
+                            const float4 f = part[q * 32 + lane];
+                            lo[4 * q] = __float_as_uint(__uint_as_float(lo[4 * q]) + f.x);
+                            lo[4 * q + 1] = __float_as_uint(__uint_as_float(lo[4 * q + 1]) + f.y);
+                            lo[4 * q + 2] = __float_as_uint(__uint_as_float(lo[4 * q + 2]) + f.z);
+                            lo[4 * q + 3] = __float_as_uint(__uint_as_float(lo[4 * q + 3]) + f.w);
+                        }
+#pragma unroll
+                        for (int q = 0; q < 8; ++q) {
+                            const float4 f = part[(8 + q) * 32 + lane];
+                            hi[4 * q] = __float_as_uint(__uint_as_float(hi[4 * q]) + f.x);
+                            hi[4 * q + 1] = __float_as_uint(__uint_as_float(hi[4 * q + 1]) + f.y);
+                            hi[4 * q + 2] = __float_as_uint(__uint_as_float(hi[4 * q + 2]) + f.z);
+                            hi[4 * q + 3] = __float_as_uint(__uint_as_float(hi[4 * q + 3]) + f.w);
+                        }
+                    }
+                    store_chunk(&map_c, staging, chunk_count, lo, hi, lane, n0 + c * 64, m0 + quarter * 32);
+                    continue;
                 }
                 if (splits > 1) {
                     float4* part = split_chunk<BN>(sk, t, s, quarter, c);
@@ -325,6 +404,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 store_chunk(&map_c, staging, chunk_count, lo, hi, lane, n0 + c * 64, m0 + quarter * 32);
             }
+            if (sender) {
+                // Each lane releases its own stores into rank 0's buffer.
+                ptx::mbar_arrive_release_cluster(recv_full_remote);
+                continue;
+            }
+            if (receiver) continue;
             if (splits > 1) {
                 // Publish this warp's partial rows, then count the unit.  The
                 // unit that arrives last sums every split's rows in split
@@ -376,6 +461,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     ptx::tc_fence_before();
     __syncthreads();
+    // Rank 0 leaves only after every rank's stores into its buffer are done
+    // (also when a bounded wait gave up).
+    if (sk.cluster) ptx::cluster_sync();
     if (warp == 1) {
         ptx::tc_fence_after();
         ptx::tmem_dealloc(tmem_base, L::kTmemCols);
@@ -384,11 +472,30 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // ------------------------------------------------------------------ host side
 
+// Shared memory rank 0 of a cluster split K needs beyond the kernel's own:
+// one slot of FP32 values per other rank.
+int cluster_recv_bytes(int bn, int ar, int splits) {
+    return (splits - 1) * ar * bn * 4;
+}
+
+// K splits of a cluster split K for this launch, or 0 when the workspace
+// path runs: flag off, fewer than 2 or more than 8 splits, receive buffer
+// beyond 227 KB, or (persistent launches) more units than SMs.
+int cluster_splits(int flags, int k_splits, int num_kb, int tiles, bool persistent, int64_t own_smem, int bn,
+                   int ar) {
+    if (!(flags & KMCTS_FLAG_SPLIT_CLUSTER)) return 0;
+    const int s = k_splits < num_kb ? k_splits : num_kb;
+    if (s < 2 || s > kMaxClusterSplits) return 0;
+    if (own_smem + cluster_recv_bytes(bn, ar, s) > kMaxSmem) return 0;
+    if (persistent && static_cast<int64_t>(tiles) * s > multiprocessor_count()) return 0;
+    return s;
+}
+
 // K splits a launch can use: at most one per K block; 1 when the stream's
 // workspace cannot be had (out of memory, or growth under graph capture).
 template <int BN, int BK>
 int resolve_splits(int M, int N, int K, int requested, cudaStream_t stream, SplitK* sk) {
-    *sk = SplitK{1, nullptr, nullptr, 0};
+    *sk = SplitK{1, nullptr, nullptr, 0, 0};
     const int num_kb = (K + BK - 1) / BK;
     int splits = requested < num_kb ? requested : num_kb;
     if (splits <= 1) return 1;
@@ -407,11 +514,13 @@ int resolve_splits(int M, int N, int K, int requested, cudaStream_t stream, Spli
 
 template <int BN, int BK, int STAGES, bool B_MN, int AR>
 int launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, int M,
-                   int N, int K, int group, bool persistent, int k_splits, bool b_evict_first,
+                   int N, int K, int group, bool persistent, int k_splits, int flags,
                    uint64_t limit_ns, cudaStream_t stream, int* status) {
     using L = Layout<BN, BK, STAGES, B_MN, AR>;
     auto kernel = gemm_bf16_tcgen05<BN, BK, STAGES, B_MN, AR>;
-    // The shared-memory opt-in is per device; set it once on each.
+    // The shared-memory opt-in is per device; set it once on each, to the
+    // most any launch of this variant asks for (a cluster split K's receive
+    // buffer comes on top of the variant's own layout).
     static std::mutex mu;
     static bool configured[kMaxDevices] = {};
     int device = 0;
@@ -420,25 +529,50 @@ int launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorM
     {
         std::lock_guard<std::mutex> lock(mu);
         if (!configured[device]) {
-            if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     L::kSmemBytes) != cudaSuccess)
+            if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem) !=
+                cudaSuccess)
                 return KMCTS_EGEMM;
             configured[device] = true;
         }
     }
-    SplitK sk;
-    const int splits = resolve_splits<BN, BK>(M, N, K, k_splits, stream, &sk);
-    const int units = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN) * splits;
+    const int tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
+    const int sms = multiprocessor_count();
+    SplitK sk = {1, nullptr, nullptr, 0, 0};
+    int splits = cluster_splits(flags, k_splits, (K + BK - 1) / BK, tiles, persistent, L::kSmemBytes, BN, AR);
+    int smem = L::kSmemBytes;
+    if (splits > 0) {
+        sk = SplitK{splits, nullptr, nullptr, 0, 1};
+        smem += cluster_recv_bytes(BN, AR, splits);
+    } else splits = resolve_splits<BN, BK>(M, N, K, k_splits, stream, &sk);
+    const int units = tiles * splits;
     int grid = units;
-    if (persistent) grid = units < multiprocessor_count() ? units : multiprocessor_count();
-    kernel<<<grid, kThreads, L::kSmemBytes, stream>>>(ma, mb, mc, M, N, K, group, limit_ns,
-                                                      status, sk, b_evict_first ? 1 : 0);
+    if (persistent && !sk.cluster) grid = units < sms ? units : sms;
+    const int b_evict_first = (flags & KMCTS_FLAG_B_EVICT_FIRST) ? 1 : 0;
+    if (sk.cluster) {
+        cudaLaunchConfig_t lc = {};
+        lc.gridDim = dim3(static_cast<unsigned>(grid));
+        lc.blockDim = dim3(kThreads);
+        lc.dynamicSmemBytes = static_cast<size_t>(smem);
+        lc.stream = stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = static_cast<unsigned>(splits);
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        lc.attrs = attr;
+        lc.numAttrs = 1;
+        if (cudaLaunchKernelEx(&lc, kernel, ma, mb, mc, M, N, K, group, limit_ns, status, sk, b_evict_first) !=
+            cudaSuccess)
+            return KMCTS_EGEMM;
+    } else {
+        kernel<<<grid, kThreads, smem, stream>>>(ma, mb, mc, M, N, K, group, limit_ns, status, sk, b_evict_first);
+    }
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return cudaGetLastError() == cudaSuccess ? KMCTS_OK : KMCTS_EGEMM;
 }
 
 using Launcher = int (*)(const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, int, int,
-                         int, int, bool, int, bool, uint64_t, cudaStream_t, int*);
+                         int, int, bool, int, int, uint64_t, cudaStream_t, int*);
 
 struct Variant {
     int bn, bk, stages, b_mn, ar;
@@ -650,8 +784,8 @@ int launch_tcgen05(const void* A, const void* B, void* C, int M, int N, int K, i
         cfg.wait_limit_ns > 0 ? static_cast<uint64_t>(cfg.wait_limit_ns) : kDefaultWaitNs;
     if (pair) return launch_pair(ma, mb, mb_half, mc, M, N, K, b_layout, cfg, limit, stream, device_status);
     const Variant* v = find_variant(cfg, b_layout);
-    return v->fn(ma, mb, mc, M, N, K, cfg.raster_group, cfg.persistent != 0, cfg.k_splits,
-                 (cfg.flags & KMCTS_FLAG_B_EVICT_FIRST) != 0, limit, stream, device_status);
+    return v->fn(ma, mb, mc, M, N, K, cfg.raster_group, cfg.persistent != 0, cfg.k_splits, cfg.flags, limit,
+                 stream, device_status);
 }
 
 int launch_allgather_tcgen05(const void* A, const void* B_shard, void* const* C_ranks, int num_ranks, int rank,
@@ -711,6 +845,15 @@ int plan_tcgen05(const kmcts_gemm_config& cfg, int M, int N, int K, int b_layout
     plan.units = plan.tiles * plan.k_splits;
     plan.ctas = cfg.persistent ? (plan.units < plan.workers ? plan.units : plan.workers) : plan.units;
     plan.smem_bytes = static_cast<int32_t>(tcgen05_smem_bytes(cfg, b_layout));
+    const int ar = cfg.tile_m == 32 ? 32 : kBM;
+    const int cs = cluster_splits(cfg.flags, cfg.k_splits, num_kb, plan.tiles, cfg.persistent != 0, plan.smem_bytes,
+                                  cfg.tile_n, ar);
+    if (cs > 0) {
+        plan.cluster_size = cs;
+        plan.workers = plan.workers / cs;  // at most: one CTA per SM, whole clusters
+        plan.ctas = plan.units;
+        plan.smem_bytes += cluster_recv_bytes(cfg.tile_n, ar, cs);
+    }
     *out = plan;
     return KMCTS_OK;
 }

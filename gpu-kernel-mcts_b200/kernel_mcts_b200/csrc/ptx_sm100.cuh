@@ -258,6 +258,49 @@ __device__ __forceinline__ void cluster_sync() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
+// 16-byte store into the shared memory of any CTA of the cluster
+// (`cluster_addr` from mapa_shared).
+__device__ __forceinline__ void st_cluster_v4(uint32_t cluster_addr, float a, float b, float c, float d) {
+    asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(cluster_addr), "f"(a), "f"(b), "f"(c),
+                 "f"(d)
+                 : "memory");
+}
+
+// Arrive on an mbarrier of any CTA of the cluster, releasing this thread's
+// earlier writes (its st_cluster_v4 stores included) at cluster scope.
+__device__ __forceinline__ void mbar_arrive_release_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait_acquire_cluster(uint64_t* bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+// mbar_wait with cluster-scope acquire: after it returns true, the writes
+// that other CTAs of the cluster released by their arrives are visible.
+// Bounded like mbar_wait.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, uint64_t limit_ns,
+                                                  volatile int* abort) {
+    if (mbar_try_wait_acquire_cluster(bar, parity)) return true;
+    uint64_t start = global_timer_ns();
+    uint32_t spins = 0;
+    while (!mbar_try_wait_acquire_cluster(bar, parity)) {
+        if ((++spins & 63u) == 0u) {
+            if (*abort) return false;
+            if (global_timer_ns() - start > limit_ns) return false;
+        }
+    }
+    return true;
+}
+
 // Arrive on an mbarrier given by its shared::cluster address (any CTA of the
 // cluster), with the default semantics (release at CTA scope).  Used to hand
 // TMEM accumulators back to the UMMA issuer: the tcgen05.fence::before /

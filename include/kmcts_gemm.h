@@ -85,6 +85,15 @@ extern "C" {
  * is ignored.  Without a workspace (growth under graph capture) each CTA
  * takes one whole tile. */
 #define KMCTS_FLAG_SWAP_AB 16
+/* One-CTA schedules with k_splits 2..8: the K splits of each tile run as one
+ * thread-block cluster (one CTA per split).  The other splits store their
+ * FP32 values into split 0's shared memory, which adds them in split order
+ * and writes C: no partial goes through the workspace, and the sum order,
+ * hence every output bit, is the workspace path's.  It needs
+ * (k_splits - 1) x rows x tile_n x 4 bytes more shared memory (rows = 32 for
+ * tile_m 32, else 128) within 227 KB, and every unit in its own CTA (units
+ * no more than the SMs when persistent); otherwise the workspace path runs. */
+#define KMCTS_FLAG_SPLIT_CLUSTER 64
 
 #define KMCTS_TAIL_NONE 0     /* kmcts_gemm_plan.tail_split: every tile whole */
 #define KMCTS_TAIL_SPLIT_N 1  /* last wave as half-width units */

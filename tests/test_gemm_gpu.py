@@ -638,6 +638,42 @@ def test_skinny_a_rows_integer_exact(cuda_device, layout, tile_n, tile_k, stages
 
 
 @pytest.mark.parametrize("layout", ["col", "row"])
+@pytest.mark.parametrize("tile_m,tile_n,tile_k,stages,shape,splits,cluster", [
+    (32, 128, 128, 4, (16, 1024, 2048), 2, 2),
+    (32, 128, 128, 4, (32, 264, 4096), 4, 4),    # ragged N
+    (32, 128, 64, 9, (7, 2048, 1032), 3, 3),     # ragged K: 17 K blocks over 3 splits
+    (32, 256, 64, 5, (16, 1024, 2048), 2, 2),
+    (128, 128, 64, 4, (100, 520, 1032), 2, 2),   # four lane quarters, ragged M
+    (32, 128, 128, 4, (16, 520, 8192), 8, 1),    # receive buffer over 227 KB: workspace path
+    (32, 128, 128, 4, (16, 1024, 256), 4, 2),    # two K blocks: two splits
+])
+def test_cluster_split_k_same_bits_as_workspace_split_k(cuda_device, layout, tile_m, tile_n, tile_k, stages, shape,
+                                                        splits, cluster):
+    """KMCTS_FLAG_SPLIT_CLUSTER runs a tile's K splits as one cluster that
+    adds them in split 0's shared memory: exact on integer inputs, and on
+    N(0,1) inputs the same bits as the workspace reduction (same sum order),
+    launch after launch."""
+    m, n, k = shape
+    base = dict(kernel=_native.KERNEL_TCGEN05, tile_m=tile_m, cluster_m=1, tile_n=tile_n, tile_k=tile_k,
+                stages=stages, k_splits=splits)
+    flagged = dict(base, flags=_native.FLAG_SPLIT_CLUSTER)
+    plan = plan_of(m, n, k, layout, **flagged)
+    assert plan["cluster_size"] == cluster and plan["units"] == plan["tiles"] * plan["k_splits"], plan
+    assert plan_of(m, n, k, layout, **base)["cluster_size"] == 1
+    a_t, b_t = oracle.integer_inputs(m, n, k, seed=splits + m)
+    expect = oracle.torch_bits(oracle.torch_reference(a_t, b_t))
+    c = run(a_t.cuda(), b_for(layout, b_t.cuda()), layout, **flagged)
+    np.testing.assert_array_equal(bits_of(c), expect)
+    a_t, b_t = oracle.randn_inputs(m, n, k, seed=3, b_layout=layout)
+    a, b = a_t.cuda(), b_t.cuda()
+    workspace = run(a, b, layout, **base)
+    first = run(a, b, layout, **flagged)
+    second = run(a, b, layout, **flagged)
+    assert torch.equal(first.view(torch.int16), workspace.view(torch.int16))
+    assert torch.equal(second.view(torch.int16), workspace.view(torch.int16))
+
+
+@pytest.mark.parametrize("layout", ["col", "row"])
 @pytest.mark.parametrize("shape", [(16, 8192, 8192), (128, 16384, 4096), (100, 1000, 2048)])
 def test_skinny_selection_streams_b_evict_first_same_bits(cuda_device, layout, shape):
     """The NULL-config selection for one-tile-row shapes sets the evict-first
