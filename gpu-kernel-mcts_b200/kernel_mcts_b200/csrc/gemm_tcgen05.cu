@@ -144,6 +144,52 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int splits = sk.splits;
     const int num_units = num_tiles * splits;
 
+    // Producer state, used by thread 0 (warp 0, lane 0) only.
+    int stage_p = 0;
+    uint32_t phase_p = 0;
+    uint32_t issued = 0, issued_phase = 0;
+    int prefilled = 0;  // K blocks of this CTA's first unit issued before the set-up barrier
+    // B read once (one M tile): its lines go first when L2 needs room.
+    const uint64_t b_policy = b_evict_first ? ptx::policy_evict_first() : 0ull;
+    // Waits for the next stage to be free, then TMA-loads K block kb of the
+    // tile at (m0, n0) into it.  False when the wait gave up.
+    auto load_stage = [&](int kb, int m0, int n0) -> bool {
+        if (!ptx::mbar_wait(&empty[stage_p], phase_p ^ 1u, limit_ns, abort)) {
+            record_failure(status, abort, kRoleProducer);
+            return false;
+        }
+        uint8_t* sa = smem + stage_p * L::kStageBytes;
+        uint8_t* sb = sa + L::kABytes;
+        ptx::mbar_arrive_expect_tx(&full[stage_p], L::kStageBytes);
+#pragma unroll
+        for (int kh = 0; kh < BK / 64; ++kh) {
+            const int k0 = kb * BK + kh * 64;
+            ptx::tma_load_2d(sa + kh * L::kAHalf, &map_a, &full[stage_p], k0, m0);
+            if constexpr (B_MN) {
+#pragma unroll
+                for (int nb = 0; nb < BN / 64; ++nb) {
+                    uint8_t* dst = sb + (kh * (BN / 64) + nb) * 8192;
+                    if (b_evict_first)
+                        ptx::tma_load_2d_hint(dst, &map_b, &full[stage_p], n0 + nb * 64, k0, b_policy);
+                    else
+                        ptx::tma_load_2d(dst, &map_b, &full[stage_p], n0 + nb * 64, k0);
+                }
+            } else {
+                if (b_evict_first)
+                    ptx::tma_load_2d_hint(sb + kh * (BN * 128), &map_b, &full[stage_p], k0, n0, b_policy);
+                else
+                    ptx::tma_load_2d(sb + kh * (BN * 128), &map_b, &full[stage_p], k0, n0);
+            }
+        }
+        issued |= 1u << stage_p;
+        issued_phase = (issued_phase & ~(1u << stage_p)) | (phase_p << stage_p);
+        if (++stage_p == STAGES) {
+            stage_p = 0;
+            phase_p ^= 1u;
+        }
+        return true;
+    };
+
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
             ptx::mbar_init(&full[s], 1);
@@ -159,71 +205,48 @@ __global__ void __launch_bounds__(kThreads, 1)
         *abort = 0;
         *no_abort = 0;
         ptx::fence_mbarrier_init();
-    }
-    if (warp == 0 && lane == 0) {
         ptx::prefetch_tensormap(&map_a);
         ptx::prefetch_tensormap(&map_b);
         ptx::prefetch_tensormap(&map_c);
+        // The first unit's first stages go out now, so their descriptor
+        // fetches and DRAM latency overlap the TMEM allocation and the
+        // set-up barrier (the stages are free and only this thread has
+        // used the barriers so far).
+        if (static_cast<int>(blockIdx.x) < num_units) {
+            const int t = blockIdx.x / splits, s = blockIdx.x % splits;
+            const TileCoord tc = tile_coord(t, num_m, num_n, group);
+            const int kb0 = s * num_kb / splits, kb1 = (s + 1) * num_kb / splits;
+            const int n = kb1 - kb0 < STAGES ? kb1 - kb0 : STAGES;
+            while (prefilled < n && load_stage(kb0 + prefilled, tc.m_blk * kBM, tc.n_blk * BN)) ++prefilled;
+        }
     }
     if (warp == 1) {
         ptx::tmem_alloc(tmem_slot, L::kTmemCols);
         ptx::tmem_relinquish();
     }
+    // Cluster split K: every thread arrives on the cluster barrier once rank
+    // 0's receive barrier is initialised; a thread waits on it before its
+    // first access to another CTA (or at the end), so no CTA idles here.
+    if (sk.cluster) ptx::cluster_arrive();
     ptx::tc_fence_before();
     __syncthreads();
-    if (sk.cluster) ptx::cluster_sync();  // rank 0's receive barrier exists before any rank signals it
     ptx::tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
     if (warp == 0) {
         // ------------------------------------------------------------ producer
         if (lane == 0) {
-            int stage = 0;
-            uint32_t phase = 0;
-            uint32_t issued = 0, issued_phase = 0;
-            bool ok = true;
-            // B read once (one M tile): its lines go first when L2 needs room.
-            const uint64_t b_policy = b_evict_first ? ptx::policy_evict_first() : 0ull;
+            bool ok = !*abort;
             for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
                 const int t = u / splits, s = u % splits;
                 const TileCoord tc = tile_coord(t, num_m, num_n, group);
-                const int m0 = tc.m_blk * kBM;
-                const int n0 = tc.n_blk * BN;
                 const int kb1 = (s + 1) * num_kb / splits;
-                for (int kb = s * num_kb / splits; kb < kb1; ++kb) {
-                    if (!ptx::mbar_wait(&empty[stage], phase ^ 1u, limit_ns, abort)) {
-                        record_failure(status, abort, kRoleProducer);
+                int kb = s * num_kb / splits;
+                if (u == static_cast<int>(blockIdx.x)) kb += prefilled;
+                for (; kb < kb1; ++kb) {
+                    if (!load_stage(kb, tc.m_blk * kBM, tc.n_blk * BN)) {
                         ok = false;
                         break;
-                    }
-                    uint8_t* sa = smem + stage * L::kStageBytes;
-                    uint8_t* sb = sa + L::kABytes;
-                    ptx::mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
-#pragma unroll
-                    for (int kh = 0; kh < BK / 64; ++kh) {
-                        const int k0 = kb * BK + kh * 64;
-                        ptx::tma_load_2d(sa + kh * L::kAHalf, &map_a, &full[stage], k0, m0);
-                        if constexpr (B_MN) {
-#pragma unroll
-                            for (int nb = 0; nb < BN / 64; ++nb) {
-                                uint8_t* dst = sb + (kh * (BN / 64) + nb) * 8192;
-                                if (b_evict_first)
-                                    ptx::tma_load_2d_hint(dst, &map_b, &full[stage], n0 + nb * 64, k0, b_policy);
-                                else
-                                    ptx::tma_load_2d(dst, &map_b, &full[stage], n0 + nb * 64, k0);
-                            }
-                        } else {
-                            if (b_evict_first)
-                                ptx::tma_load_2d_hint(sb + kh * (BN * 128), &map_b, &full[stage], k0, n0, b_policy);
-                            else
-                                ptx::tma_load_2d(sb + kh * (BN * 128), &map_b, &full[stage], k0, n0);
-                        }
-                    }
-                    issued |= 1u << stage;
-                    issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
-                    if (++stage == STAGES) {
-                        stage = 0;
-                        phase ^= 1u;
                     }
                 }
             }
@@ -303,6 +326,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         // addresses them (the same offsets in every CTA of the launch).
         const uint32_t recv_remote = sk.cluster ? ptx::mapa_shared(ptx::smem_addr(recv), 0) : 0u;
         const uint32_t recv_full_remote = sk.cluster ? ptx::mapa_shared(ptx::smem_addr(recv_full), 0) : 0u;
+        // Rank 0's receive barrier is initialised (every thread of the
+        // cluster arrived after set-up) before any store or arrive reaches it.
+        if (sk.cluster) ptx::cluster_wait();
+        bool got_recv = false;  // rank 0: the other ranks' values are all here
         for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++local) {
             const int t = u / splits, s = u % splits;
             const TileCoord tc = tile_coord(t, num_m, num_n, group);
@@ -364,6 +391,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             break;
                         }
                         received = true;
+                        got_recv = true;
                     }
                     // Split 0's values, then every other split's, in split order.
 #pragma unroll 1
@@ -457,13 +485,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (lane == 0) ptx::bulk_wait_group_read<0>();  // shared memory must outlive the stores' reads
         __syncwarp();
+        // Rank 0 leaves only after the other ranks' stores into its buffer
+        // are released, also when one of its own waits gave up (a rank that
+        // gave up itself never stores: this wait then ends at its bound).
+        if (sk.cluster && blockIdx.x % splits == 0 && !got_recv)
+            ptx::mbar_wait_cluster(recv_full, 0, drain_limit(limit_ns), no_abort);
     }
 
+    if (sk.cluster && warp < 2) ptx::cluster_wait();  // pairs this thread's arrive after set-up
     ptx::tc_fence_before();
     __syncthreads();
-    // Rank 0 leaves only after every rank's stores into its buffer are done
-    // (also when a bounded wait gave up).
-    if (sk.cluster) ptx::cluster_sync();
     if (warp == 1) {
         ptx::tc_fence_after();
         ptx::tmem_dealloc(tmem_base, L::kTmemCols);
@@ -636,6 +667,15 @@ int64_t tcgen05_smem_bytes(const kmcts_gemm_config& cfg, int b_layout) {
     if (cfg.tile_m != kBM && cfg.tile_m != 32) return 0;
     return static_cast<int64_t>(cfg.stages) * (cfg.tile_m + cfg.tile_n) * cfg.tile_k * 2 +
            (cfg.tile_m == 32 ? 1 : kEpilogueWarps) * 2 * kStagingBytes + kSmemReserve;
+}
+
+int cluster_split_cap(const kmcts_gemm_config& cfg, int b_layout) {
+    if (!is_one_cta(cfg) || is_swapped(cfg) || cfg.tile_n <= 0) return 1;
+    const int64_t own = tcgen05_smem_bytes(cfg, b_layout);
+    const int ar = cfg.tile_m == 32 ? 32 : kBM;
+    int cap = 1;
+    while (cap < kMaxClusterSplits && own + cluster_recv_bytes(cfg.tile_n, ar, cap + 1) <= kMaxSmem) ++cap;
+    return cap;
 }
 
 int tcgen05_legal(const kmcts_gemm_config& cfg, int M, int N, int K, int b_layout, char* why,

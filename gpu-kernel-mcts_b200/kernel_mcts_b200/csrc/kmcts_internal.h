@@ -29,6 +29,10 @@ int launch_tcgen05(const void* A, const void* B, void* C, int M, int N, int K, i
 int tcgen05_legal(const kmcts_gemm_config& cfg, int M, int N, int K, int b_layout, char* why,
                   int len);
 int64_t tcgen05_smem_bytes(const kmcts_gemm_config& cfg, int b_layout);
+// Most K splits a one-CTA schedule can add up as a cluster split K
+// (KMCTS_FLAG_SPLIT_CLUSTER): the receive buffer must fit beside its own
+// shared memory, and a cluster holds at most 8 CTAs.  1 when none fits.
+int cluster_split_cap(const kmcts_gemm_config& cfg, int b_layout);
 
 // CUDA-core path for any shape and alignment.
 int launch_simt(const void* A, const void* B, void* C, int M, int N, int K, int b_layout,

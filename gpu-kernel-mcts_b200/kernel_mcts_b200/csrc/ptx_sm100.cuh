@@ -258,6 +258,17 @@ __device__ __forceinline__ void cluster_sync() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
+// The two halves of a cluster barrier, for threads that arrive early and
+// wait only where they first need the other CTAs (not warp-aligned).  Each
+// thread alternates arrive and wait.
+__device__ __forceinline__ void cluster_arrive() {
+    asm volatile("barrier.cluster.arrive.release;" ::: "memory");
+}
+
+__device__ __forceinline__ void cluster_wait() {
+    asm volatile("barrier.cluster.wait.acquire;" ::: "memory");
+}
+
 // 16-byte store into the shared memory of any CTA of the cluster
 // (`cluster_addr` from mapa_shared).
 __device__ __forceinline__ void st_cluster_v4(uint32_t cluster_addr, float a, float b, float c, float d) {

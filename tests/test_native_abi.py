@@ -55,8 +55,16 @@ def test_skinny_a_rows_take_at_most_32_rows():
 def test_select_config_splits_k_for_skinny_shapes():
     cfg = km.select_config(16, 8192, 8192, km.B_ROW)
     assert (cfg.tile_m, cfg.tile_n, cfg.k_splits) == (32, 128, 2)  # 64 tiles -> 128 units
+    assert cfg.flags & _native.FLAG_SPLIT_CLUSTER  # the two splits add up in shared memory
     wide = km.select_config(8, 28672, 8192, km.B_ROW)
     assert (wide.tile_m, wide.tile_n, wide.k_splits) == (32, 256, 0)  # 112 tiles: no split
+    assert not wide.flags & _native.FLAG_SPLIT_CLUSTER
+    # Narrow N: 64-column tiles; the split count capped at the four whose
+    # FP32 values fit one CTA's shared memory beside its stages.
+    narrow = km.select_config(16, 2048, 16384, km.B_ROW)
+    assert (narrow.tile_m, narrow.tile_n, narrow.tile_k, narrow.stages, narrow.k_splits) == (32, 64, 128, 8, 4)
+    assert narrow.flags & _native.FLAG_SPLIT_CLUSTER
+    assert km.select_config(16, 4096, 8192, km.B_ROW).k_splits == 4  # 32 tiles of 128 columns
     assert km.select_config(64, 8192, 8192, km.B_ROW).tile_m == 128
     assert km.select_config(512, 512, 8192, km.B_ROW).k_splits == 4
     assert km.select_config(1024, 1024, 1024, km.B_ROW).k_splits == 0  # short K: no split
