@@ -148,7 +148,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     int stage_p = 0;
     uint32_t phase_p = 0;
     uint32_t issued = 0, issued_phase = 0;
-    int prefilled = 0;  // K blocks of this CTA's first unit issued before the set-up barrier
     // B read once (one M tile): its lines go first when L2 needs room.
     const uint64_t b_policy = b_evict_first ? ptx::policy_evict_first() : 0ull;
     // Waits for the next stage to be free, then TMA-loads K block kb of the
@@ -208,22 +207,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         ptx::prefetch_tensormap(&map_a);
         ptx::prefetch_tensormap(&map_b);
         ptx::prefetch_tensormap(&map_c);
-        // The first unit's first stages go out now, so their descriptor
-        // fetches and DRAM latency overlap the TMEM allocation and the
-        // set-up barrier (the stages are free and only this thread has
-        // used the barriers so far).
-        if (static_cast<int>(blockIdx.x) < num_units) {
-            const int t = blockIdx.x / splits, s = blockIdx.x % splits;
-            const TileCoord tc = tile_coord(t, num_m, num_n, group);
-            const int kb0 = s * num_kb / splits, kb1 = (s + 1) * num_kb / splits;
-            const int n = kb1 - kb0 < STAGES ? kb1 - kb0 : STAGES;
-            while (prefilled < n && load_stage(kb0 + prefilled, tc.m_blk * kBM, tc.n_blk * BN)) ++prefilled;
-        }
     }
     if (warp == 1) {
         ptx::tmem_alloc(tmem_slot, L::kTmemCols);
         ptx::tmem_relinquish();
     }
+    __syncwarp();  // every warp meets the CTA barrier converged
     // Cluster split K: every thread arrives on the cluster barrier once rank
     // 0's receive barrier is initialised; a thread waits on it before its
     // first access to another CTA (or at the end), so no CTA idles here.
@@ -236,14 +225,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 0) {
         // ------------------------------------------------------------ producer
         if (lane == 0) {
-            bool ok = !*abort;
+            bool ok = true;
             for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
                 const int t = u / splits, s = u % splits;
                 const TileCoord tc = tile_coord(t, num_m, num_n, group);
                 const int kb1 = (s + 1) * num_kb / splits;
-                int kb = s * num_kb / splits;
-                if (u == static_cast<int>(blockIdx.x)) kb += prefilled;
-                for (; kb < kb1; ++kb) {
+                for (int kb = s * num_kb / splits; kb < kb1; ++kb) {
                     if (!load_stage(kb, tc.m_blk * kBM, tc.n_blk * BN)) {
                         ok = false;
                         break;
@@ -259,6 +246,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
         }
+        __syncwarp();  // lanes 1-31 wait for the producer lane before the closing barrier
     } else if (warp == 1) {
         // ----------------------------------------------------------------- MMA
         if (lane == 0) {
@@ -315,6 +303,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 record_failure(status, abort, kRoleDrain);
             }
         }
+        __syncwarp();  // lanes 1-31 wait for the MMA lane before the closing barrier
     } else {
         // ------------------------------------------------------------ epilogue
         const int quarter = warp % 4;  // TMEM lanes this warp may access

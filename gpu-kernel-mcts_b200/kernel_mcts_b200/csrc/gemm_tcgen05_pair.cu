@@ -372,6 +372,7 @@ __global__ void __launch_bounds__(pair_threads<SLOTS>(), 1)
         ptx::tmem_alloc_pair(tmem_slot, L::kTmemCols);
         ptx::tmem_relinquish_pair();
     }
+    __syncwarp();  // every warp meets the CTA barrier converged
     ptx::tc_fence_before();
     __syncthreads();
     ptx::cluster_sync();  // the leader's barriers exist before the peer signals them
@@ -444,6 +445,7 @@ __global__ void __launch_bounds__(pair_threads<SLOTS>(), 1)
                     record_failure(status, abort, kRoleDrain);
             }
         }
+        __syncwarp();  // lanes 1-31 wait for the producer lane before the closing barrier
     } else if (warp == 1) {
         // ----------------------------------------------------------------- MMA
         if (lane == 0 && leader) {

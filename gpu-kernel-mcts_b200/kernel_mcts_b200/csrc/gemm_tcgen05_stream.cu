@@ -110,6 +110,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ptx::tmem_alloc(tmem_slot, 2 * kAccCols);
         ptx::tmem_relinquish();
     }
+    __syncwarp();  // every warp meets the CTA barrier converged
     ptx::tc_fence_before();
     __syncthreads();
     ptx::tc_fence_after();
@@ -162,6 +163,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
         }
+        __syncwarp();  // lanes 1-31 wait for the producer lane before the closing barrier
     } else if (warp == 1) {
         // ----------------------------------------------------------------- MMA
         if (lane == 0) {
@@ -217,6 +219,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 record_failure(status, abort, kRoleDrain);
             }
         }
+        __syncwarp();  // lanes 1-31 wait for the MMA lane before the closing barrier
     } else {
         // ------------------------------------------------------------ epilogue
         const int quarter = warp % 4;  // TMEM lanes (C columns) this warp may access
