@@ -151,12 +151,13 @@ int kmcts_select_config(int M, int N, int K, int b_layout, kmcts_gemm_config* cf
         small.k_splits = choose_splits((N + small.tile_n - 1) / small.tile_n, K, sms);
         small.flags |= KMCTS_FLAG_B_EVICT_FIRST;  // one tile row: B is read once
         // The splits of a tile add up in shared memory, as one cluster, up to
-        // as many as its receive buffer holds; fewer splits there beat more
-        // through the workspace (L2 flushed: 16 x 2048 x 16384 26.4 us with
-        // four against 32.4 with eight, 16 x 8192 x 8192 33.1 against 34.6
-        // with two each).
+        // as many as split 0 can receive and at most six: sixteen clusters of
+        // eight do not all fit at once (L2 flushed: 16 x 1024 x 16384 22.6 us
+        // with six splits, 34.5 with eight, 32.4 with eight through the
+        // workspace; 16 x 8192 x 8192 33.1 against 34.6 with two each).
         if (small.k_splits > 1) {
-            const int cap = cluster_split_cap(small, b_layout);
+            int cap = cluster_split_cap(small, b_layout);
+            if (cap > 6) cap = 6;
             if (cap > 1) {
                 if (small.k_splits > cap) small.k_splits = cap;
                 small.flags |= KMCTS_FLAG_SPLIT_CLUSTER;

@@ -89,13 +89,19 @@ struct Layout {
 // their FP32 values into rank 0's shared memory (same block layout, one slot
 // per sending rank) and arrive on its receive barrier; rank 0 adds them to
 // its own accumulator in split order and writes C.  The sum order is the
-// global path's, so both give the same bits.
+// global path's, so both give the same bits.  Where rank 0 receives:
+//   kClusterBuffer  a buffer past its barriers (the launch adds its size);
+//   kClusterStages  its pipeline stages, free once its UMMAs are done: rank 0
+//                   then signals each sender's go barrier, senders wait for
+//                   it before storing, and the cluster syncs before exit.
+constexpr int kClusterBuffer = 1, kClusterStages = 2;
+
 struct SplitK {
     int splits;
     float* partials;
     unsigned long long* counters;  // [tile][lane quarter]: epoch << 32 | units arrived
     int epoch;
-    int cluster;
+    int cluster;  // 0 (workspace), kClusterBuffer or kClusterStages
 };
 
 template <int BN>
@@ -127,12 +133,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* tmem_empty = tmem_full + 2;
     uint64_t* drain = tmem_empty + 2;
     uint64_t* recv_full = drain + 1;  // cluster split K: rank 0 receives the other ranks' values
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(recv_full + 1);
+    uint64_t* go_bar = recv_full + 1;  // kClusterStages: rank 0's stages are free to receive
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(go_bar + 1);
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
     volatile int* no_abort = abort + 1;
     // Cluster split K's receive buffer: past the barriers (which take well
-    // under 1 KB of the reserve); the launch adds its size to the shared memory.
-    float4* recv = reinterpret_cast<float4*>(smem + L::kBarrierOffset + 1024);
+    // under 1 KB of the reserve; the launch adds its size to the shared
+    // memory), or the pipeline stages.
+    float4* recv = reinterpret_cast<float4*>(sk.cluster == kClusterStages ? smem : smem + L::kBarrierOffset + 1024);
 
     if (status == nullptr) status = &g_default_status;
     const int warp = threadIdx.x / 32;
@@ -201,6 +209,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ptx::mbar_init(drain, 1);
         // Every lane of every epilogue warp of each sending rank arrives once.
         ptx::mbar_init(recv_full, sk.cluster ? static_cast<uint32_t>((splits - 1) * kEpilogueWarps * 32) : 1u);
+        ptx::mbar_init(go_bar, 1);
         *abort = 0;
         *no_abort = 0;
         ptx::fence_mbarrier_init();
@@ -335,6 +344,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 break;
             }
             ptx::tc_fence_after();
+            if (receiver && sk.cluster == kClusterStages && e == 0 && lane == 0) {
+                // Every UMMA of this CTA has completed, so no stage is read
+                // any more (its one unit's loads were all consumed): the
+                // other ranks may store into them.
+                ptx::fence_proxy_async_smem();
+                for (int r = 1; r < splits; ++r)
+                    ptx::mbar_arrive_release_cluster(ptx::mapa_shared(ptx::smem_addr(go_bar), static_cast<uint32_t>(r)));
+            }
             const uint32_t row_addr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                                       static_cast<uint32_t>(acc * BN);
             if (m0 + quarter * 32 >= M) {
@@ -344,6 +361,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (lane == 0) ptx::mbar_arrive(&tmem_empty[acc]);
                 if (sender) ptx::mbar_arrive_release_cluster(recv_full_remote);
                 continue;
+            }
+            if (sender && sk.cluster == kClusterStages) {
+                bool go = ptx::mbar_wait_cluster(go_bar, 0, limit_ns, abort);
+                go = __all_sync(0xffffffffu, go);
+                if (!go) {
+                    // Rank 0 never freed its stages: store nothing and do not
+                    // arrive; its own bounded wait for the values gives up.
+                    if (lane == 0) record_failure(status, abort, kRoleEpilogue);
+                    ptx::tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) ptx::mbar_arrive(&tmem_empty[acc]);
+                    continue;
+                }
             }
             bool received = false;
 #pragma unroll 1
@@ -484,6 +514,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (sk.cluster && warp < 2) ptx::cluster_wait();  // pairs this thread's arrive after set-up
     ptx::tc_fence_before();
     __syncthreads();
+    // Receiving in its stages, rank 0 signalled the other ranks' barriers and
+    // they stored into its shared memory: no CTA leaves before all are done.
+    if (sk.cluster == kClusterStages) ptx::cluster_sync();
     if (warp == 1) {
         ptx::tc_fence_after();
         ptx::tmem_dealloc(tmem_base, L::kTmemCols);
@@ -498,17 +531,28 @@ int cluster_recv_bytes(int bn, int ar, int splits) {
     return (splits - 1) * ar * bn * 4;
 }
 
-// K splits of a cluster split K for this launch, or 0 when the workspace
-// path runs: flag off, fewer than 2 or more than 8 splits, receive buffer
-// beyond 227 KB, or (persistent launches) more units than SMs.
-int cluster_splits(int flags, int k_splits, int num_kb, int tiles, bool persistent, int64_t own_smem, int bn,
-                   int ar) {
+// Where rank 0 of a cluster split K of `s` splits receives: a buffer past
+// its own shared memory when that stays within 227 KB, else its pipeline
+// stages when they hold the other ranks' values, else nowhere (0).
+int cluster_receive_mode(int s, int64_t own_smem, int64_t stage_bytes, int bn, int ar) {
+    if (own_smem + cluster_recv_bytes(bn, ar, s) <= kMaxSmem) return kClusterBuffer;
+    if (cluster_recv_bytes(bn, ar, s) <= stage_bytes) return kClusterStages;
+    return 0;
+}
+
+// K splits of a cluster split K for this launch (and where rank 0 receives,
+// in *mode), or 0 when the workspace path runs: flag off, fewer than 2 or
+// more than 8 splits, nowhere to receive, or (persistent launches) more
+// units than SMs.
+int cluster_splits(int flags, int k_splits, int num_kb, int tiles, bool persistent, int64_t own_smem,
+                   int64_t stage_bytes, int bn, int ar, int* mode) {
+    *mode = 0;
     if (!(flags & KMCTS_FLAG_SPLIT_CLUSTER)) return 0;
     const int s = k_splits < num_kb ? k_splits : num_kb;
     if (s < 2 || s > kMaxClusterSplits) return 0;
-    if (own_smem + cluster_recv_bytes(bn, ar, s) > kMaxSmem) return 0;
     if (persistent && static_cast<int64_t>(tiles) * s > multiprocessor_count()) return 0;
-    return s;
+    *mode = cluster_receive_mode(s, own_smem, stage_bytes, bn, ar);
+    return *mode ? s : 0;
 }
 
 // K splits a launch can use: at most one per K block; 1 when the stream's
@@ -558,11 +602,13 @@ int launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorM
     const int tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
     const int sms = multiprocessor_count();
     SplitK sk = {1, nullptr, nullptr, 0, 0};
-    int splits = cluster_splits(flags, k_splits, (K + BK - 1) / BK, tiles, persistent, L::kSmemBytes, BN, AR);
+    int mode = 0;
+    int splits = cluster_splits(flags, k_splits, (K + BK - 1) / BK, tiles, persistent, L::kSmemBytes,
+                                static_cast<int64_t>(STAGES) * L::kStageBytes, BN, AR, &mode);
     int smem = L::kSmemBytes;
     if (splits > 0) {
-        sk = SplitK{splits, nullptr, nullptr, 0, 1};
-        smem += cluster_recv_bytes(BN, AR, splits);
+        sk = SplitK{splits, nullptr, nullptr, 0, mode};
+        if (mode == kClusterBuffer) smem += cluster_recv_bytes(BN, AR, splits);
     } else splits = resolve_splits<BN, BK>(M, N, K, k_splits, stream, &sk);
     const int units = tiles * splits;
     int grid = units;
@@ -662,8 +708,9 @@ int cluster_split_cap(const kmcts_gemm_config& cfg, int b_layout) {
     if (!is_one_cta(cfg) || is_swapped(cfg) || cfg.tile_n <= 0) return 1;
     const int64_t own = tcgen05_smem_bytes(cfg, b_layout);
     const int ar = cfg.tile_m == 32 ? 32 : kBM;
+    const int64_t stage_bytes = static_cast<int64_t>(cfg.stages) * (ar + cfg.tile_n) * cfg.tile_k * 2;
     int cap = 1;
-    while (cap < kMaxClusterSplits && own + cluster_recv_bytes(cfg.tile_n, ar, cap + 1) <= kMaxSmem) ++cap;
+    while (cap < kMaxClusterSplits && cluster_receive_mode(cap + 1, own, stage_bytes, cfg.tile_n, ar)) ++cap;
     return cap;
 }
 
@@ -875,13 +922,15 @@ int plan_tcgen05(const kmcts_gemm_config& cfg, int M, int N, int K, int b_layout
     plan.ctas = cfg.persistent ? (plan.units < plan.workers ? plan.units : plan.workers) : plan.units;
     plan.smem_bytes = static_cast<int32_t>(tcgen05_smem_bytes(cfg, b_layout));
     const int ar = cfg.tile_m == 32 ? 32 : kBM;
+    int mode = 0;
     const int cs = cluster_splits(cfg.flags, cfg.k_splits, num_kb, plan.tiles, cfg.persistent != 0, plan.smem_bytes,
-                                  cfg.tile_n, ar);
+                                  static_cast<int64_t>(cfg.stages) * (ar + cfg.tile_n) * cfg.tile_k * 2, cfg.tile_n,
+                                  ar, &mode);
     if (cs > 0) {
         plan.cluster_size = cs;
         plan.workers = plan.workers / cs;  // at most: one CTA per SM, whole clusters
         plan.ctas = plan.units;
-        plan.smem_bytes += cluster_recv_bytes(cfg.tile_n, ar, cs);
+        if (mode == kClusterBuffer) plan.smem_bytes += cluster_recv_bytes(cfg.tile_n, ar, cs);
     }
     *out = plan;
     return KMCTS_OK;

@@ -89,10 +89,12 @@ extern "C" {
  * thread-block cluster (one CTA per split).  The other splits store their
  * FP32 values into split 0's shared memory, which adds them in split order
  * and writes C: no partial goes through the workspace, and the sum order,
- * hence every output bit, is the workspace path's.  It needs
- * (k_splits - 1) x rows x tile_n x 4 bytes more shared memory (rows = 32 for
- * tile_m 32, else 128) within 227 KB, and every unit in its own CTA (units
- * no more than the SMs when persistent); otherwise the workspace path runs. */
+ * hence every output bit, is the workspace path's.  The values take
+ * (k_splits - 1) x rows x tile_n x 4 bytes (rows = 32 for tile_m 32, else
+ * 128): split 0 receives them in extra shared memory when that stays within
+ * 227 KB, else in its pipeline stages once its own MMAs are done (when they
+ * are large enough).  Every unit runs in its own CTA (units no more than the
+ * SMs when persistent); otherwise the workspace path runs. */
 #define KMCTS_FLAG_SPLIT_CLUSTER 64
 
 #define KMCTS_TAIL_NONE 0     /* kmcts_gemm_plan.tail_split: every tile whole */

@@ -644,13 +644,18 @@ def test_skinny_a_rows_integer_exact(cuda_device, layout, tile_n, tile_k, stages
     (32, 128, 64, 9, (7, 2048, 1032), 3, 3),     # ragged K: 17 K blocks over 3 splits
     (32, 256, 64, 5, (16, 1024, 2048), 2, 2),
     (128, 128, 64, 4, (100, 520, 1032), 2, 2),   # four lane quarters, ragged M
-    (32, 128, 128, 4, (16, 520, 8192), 8, 1),    # receive buffer over 227 KB: workspace path
+    (32, 128, 128, 4, (16, 520, 8192), 8, 8),    # buffer over 227 KB: received in the stages
     (32, 128, 128, 4, (16, 1024, 256), 4, 2),    # two K blocks: two splits
+    (128, 128, 128, 3, (512, 512, 8192), 4, 4),  # received in the stages
+    (128, 128, 128, 3, (100, 520, 1032), 3, 3),  # ragged M, N and K, in the stages
+    (128, 256, 64, 4, (300, 520, 2048), 2, 2),   # 256-column tiles, in the stages
+    (128, 128, 128, 3, (256, 256, 16384), 12, 1),  # more than 8 splits: workspace path
 ])
 def test_cluster_split_k_same_bits_as_workspace_split_k(cuda_device, layout, tile_m, tile_n, tile_k, stages, shape,
                                                         splits, cluster):
     """KMCTS_FLAG_SPLIT_CLUSTER runs a tile's K splits as one cluster that
-    adds them in split 0's shared memory: exact on integer inputs, and on
+    adds them in split 0's shared memory (a buffer of its own, or its
+    pipeline stages once its MMAs are done): exact on integer inputs, and on
     N(0,1) inputs the same bits as the workspace reduction (same sum order),
     launch after launch."""
     m, n, k = shape

@@ -59,12 +59,15 @@ def test_select_config_splits_k_for_skinny_shapes():
     wide = km.select_config(8, 28672, 8192, km.B_ROW)
     assert (wide.tile_m, wide.tile_n, wide.k_splits) == (32, 256, 0)  # 112 tiles: no split
     assert not wide.flags & _native.FLAG_SPLIT_CLUSTER
-    # Narrow N: 64-column tiles; the split count capped at the four whose
-    # FP32 values fit one CTA's shared memory beside its stages.
+    # Narrow N: 64-column tiles; 32 of them fill the SMs with four splits each,
+    # added up in shared memory.
     narrow = km.select_config(16, 2048, 16384, km.B_ROW)
     assert (narrow.tile_m, narrow.tile_n, narrow.tile_k, narrow.stages, narrow.k_splits) == (32, 64, 128, 8, 4)
     assert narrow.flags & _native.FLAG_SPLIT_CLUSTER
     assert km.select_config(16, 4096, 8192, km.B_ROW).k_splits == 4  # 32 tiles of 128 columns
+    # Nine splits would fill the SMs; clusters of more than six are not selected.
+    long_k = km.select_config(16, 1024, 32768, km.B_ROW)
+    assert (long_k.tile_n, long_k.k_splits) == (64, 6) and long_k.flags & _native.FLAG_SPLIT_CLUSTER
     assert km.select_config(64, 8192, 8192, km.B_ROW).tile_m == 128
     assert km.select_config(512, 512, 8192, km.B_ROW).k_splits == 4
     assert km.select_config(1024, 1024, 1024, km.B_ROW).k_splits == 0  # short K: no split
