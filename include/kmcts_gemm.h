@@ -77,13 +77,13 @@ extern "C" {
 /* tile_m 32 (M <= 32), tile_n 128, tile_k 64 with 10 stages or 128 with 5:
  * the operands swap roles, C^T = B^T * A^T, so B's 128-column tiles are the
  * MMA's 128 rows and A's M rows its N (16 or 32): no tensor work is padding.
- * The (tile, K block) pairs are cut into one contiguous range per SM (at
- * least four K blocks each); a tile cut by range boundaries is summed from
- * FP32 partials in a per-stream library workspace, in range order, by the
- * range that finishes it last (deterministic; exact on integer inputs,
- * within the parity bound otherwise).  B's loads are evict-first; k_splits
- * is ignored.  Without a workspace (growth under graph capture) each CTA
- * takes one whole tile. */
+ * Each tile runs as S units, S = min(8, SMs / tiles, K blocks / 4); unit s
+ * takes K blocks s, s + S, s + 2S, ..., so a tile's units move down B's rows
+ * together.  The unit that finishes a tile last adds the FP32 partials, kept
+ * in a per-stream library workspace, in unit order (deterministic; exact on
+ * integer inputs, within the parity bound otherwise).  B's loads are
+ * evict-first; k_splits is ignored.  Without a workspace (growth under graph
+ * capture) each CTA takes one whole tile. */
 #define KMCTS_FLAG_SWAP_AB 16
 /* One-CTA schedules with k_splits 2..8: the K splits of each tile run as one
  * thread-block cluster (one CTA per split).  The other splits store their
