@@ -216,6 +216,18 @@ int kmcts_select_config(int M, int N, int K, int b_layout, kmcts_gemm_config* cf
     // by a 512 MiB write: 128 x 16384 x 4096 31.8 us against 37.8 without the
     // hint and 36.8 for cuBLAS; 16 x 8192 x 8192 34.4 against 38.6).
     if (M <= 128) small.flags |= KMCTS_FLAG_B_EVICT_FIRST;
+    // M <= 64: the K splits add up in split 0's pipeline stages, one cluster
+    // per tile (L2 flushed: 64 x 2048 x 8192 23.4 us against 26.4 through
+    // the workspace, 48 x 4096 x 8192 26.8 against 27.9; at M = 128 the
+    // workspace wins, 128 x 4096 x 8192 29.0 against 29.1-30.2).
+    if (M <= 64 && small.k_splits > 1) {
+        int cap = cluster_split_cap(small, b_layout);
+        if (cap > 6) cap = 6;
+        if (cap > 1) {
+            if (small.k_splits > cap) small.k_splits = cap;
+            small.flags |= KMCTS_FLAG_SPLIT_CLUSTER;
+        }
+    }
     if (tcgen05_legal(small, M, N, K, b_layout, nullptr, 0) == KMCTS_OK) *cfg = small;
     return KMCTS_OK;
 }

@@ -679,7 +679,7 @@ def test_cluster_split_k_same_bits_as_workspace_split_k(cuda_device, layout, til
 
 
 @pytest.mark.parametrize("layout", ["col", "row"])
-@pytest.mark.parametrize("shape", [(16, 8192, 8192), (128, 16384, 4096), (100, 1000, 2048)])
+@pytest.mark.parametrize("shape", [(16, 8192, 8192), (128, 16384, 4096), (100, 1000, 2048), (48, 4096, 8192)])
 def test_skinny_selection_streams_b_evict_first_same_bits(cuda_device, layout, shape):
     """The NULL-config selection for one-tile-row shapes sets the evict-first
     policy; its results equal the same schedule without it, bit for bit, and

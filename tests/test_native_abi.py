@@ -69,6 +69,9 @@ def test_select_config_splits_k_for_skinny_shapes():
     long_k = km.select_config(16, 1024, 32768, km.B_ROW)
     assert (long_k.tile_n, long_k.k_splits) == (64, 6) and long_k.flags & _native.FLAG_SPLIT_CLUSTER
     assert km.select_config(64, 8192, 8192, km.B_ROW).tile_m == 128
+    mid = km.select_config(64, 2048, 8192, km.B_ROW)  # 16 tiles of 128 x 128, four splits in the stages
+    assert (mid.tile_m, mid.k_splits) == (128, 4) and mid.flags & _native.FLAG_SPLIT_CLUSTER
+    assert not km.select_config(128, 4096, 8192, km.B_ROW).flags & _native.FLAG_SPLIT_CLUSTER
     assert km.select_config(512, 512, 8192, km.B_ROW).k_splits == 4
     assert km.select_config(1024, 1024, 1024, km.B_ROW).k_splits == 0  # short K: no split
     assert km.select_config(4096, 4096, 4096, km.B_ROW).k_splits == 0
