@@ -170,6 +170,40 @@ int kmcts_select_config(int M, int N, int K, int b_layout, kmcts_gemm_config* cf
         small = *cfg;
         small.cluster_m = 1;
     }
+    if (M > 32 && M <= 64) {
+        // 64 rows of A per tile; 64-column tiles while two splits of them fit
+        // the SMs, else 128-column tiles (three stages when split, leaving
+        // split 0 room to receive; four unsplit).  Measured, L2 flushed
+        // (against the 128-row schedule): 33 x 1024 x 16384 22.5 us against
+        // 30.6, 64 x 2048 x 8192 20.6 against 23.7, 64 x 4096 x 4096 18.6
+        // against 22.5, 64 x 8192 x 8192 33.9 against 35.1, 64 x 16384 x 4096
+        // 30.8 against 31.5.
+        small.tile_m = 64;
+        small.tile_k = 128;
+        if (2 * ((N + 63) / 64) <= sms) {
+            small.tile_n = 64;
+            small.stages = 6;
+        } else {
+            small.tile_n = 128;
+        }
+        small.k_splits = choose_splits((N + small.tile_n - 1) / small.tile_n, K, sms);
+        if (small.tile_n == 128) small.stages = small.k_splits > 1 ? 3 : 4;
+        small.flags |= KMCTS_FLAG_B_EVICT_FIRST;
+        if (small.k_splits > 1) {
+            int cap = cluster_split_cap(small, b_layout);
+            if (cap > 6) cap = 6;
+            if (cap > 1) {
+                if (small.k_splits > cap) small.k_splits = cap;
+                small.flags |= KMCTS_FLAG_SPLIT_CLUSTER;
+            }
+        }
+        if (tcgen05_legal(small, M, N, K, b_layout, nullptr, 0) == KMCTS_OK) {
+            *cfg = small;
+            return KMCTS_OK;
+        }
+        small = *cfg;
+        small.cluster_m = 1;
+    }
     const long long pair_tiles = static_cast<long long>((M + 255) / 256) * ((N + 255) / 256);
     if (pair_tiles >= workers) {
         // Short K (at most six 128-deep blocks per tile): 64-deep stages keep
@@ -216,10 +250,11 @@ int kmcts_select_config(int M, int N, int K, int b_layout, kmcts_gemm_config* cf
     // by a 512 MiB write: 128 x 16384 x 4096 31.8 us against 37.8 without the
     // hint and 36.8 for cuBLAS; 16 x 8192 x 8192 34.4 against 38.6).
     if (M <= 128) small.flags |= KMCTS_FLAG_B_EVICT_FIRST;
-    // M <= 64: the K splits add up in split 0's pipeline stages, one cluster
-    // per tile (L2 flushed: 64 x 2048 x 8192 23.4 us against 26.4 through
-    // the workspace, 48 x 4096 x 8192 26.8 against 27.9; at M = 128 the
-    // workspace wins, 128 x 4096 x 8192 29.0 against 29.1-30.2).
+    // M <= 64 (reached only when no 64-row schedule is legal): the K splits
+    // add up in split 0's pipeline stages, one cluster per tile (L2 flushed:
+    // 64 x 2048 x 8192 23.4 us against 26.4 through the workspace, 48 x 4096
+    // x 8192 26.8 against 27.9; at M = 128 the workspace wins, 128 x 4096 x
+    // 8192 29.0 against 29.1-30.2).
     if (M <= 64 && small.k_splits > 1) {
         int cap = cluster_split_cap(small, b_layout);
         if (cap > 6) cap = 6;

@@ -56,10 +56,10 @@ constexpr int kBM = 128;
 constexpr int kMaxDevices = 64;
 constexpr int kMaxClusterSplits = 8;  // portable cluster size
 
-// AR: rows of A staged per tile.  128 normally; 32 for skinny GEMMs (M <= 32):
-// the MMA still computes 128 rows, but rows 32-127 read whatever follows A's
-// 32 rows in the stage and are never stored, and the freed shared memory
-// holds more B stages in flight.
+// AR: rows of A staged per tile.  128 normally; 32 or 64 for skinny GEMMs
+// (M <= AR): the MMA still computes 128 rows, but rows AR-127 read whatever
+// follows A's AR rows in the stage and are never stored, and the freed shared
+// memory holds more B stages in flight.
 template <int BN, int BK, int STAGES, bool B_MN, int AR = kBM>
 struct Layout {
     static constexpr int kAHalf = AR * 128;  // one 64-wide K half of A
@@ -67,15 +67,15 @@ struct Layout {
     static constexpr int kBBytes = BN * BK * 2;
     static constexpr int kStageBytes = kABytes + kBBytes;
     static constexpr int kStagingOffset = STAGES * kStageBytes;
-    // With 32 rows of A only the warp of TMEM lanes 0-31 ever stores C.
-    static constexpr int kStagingWarps = AR == kBM ? kEpilogueWarps : 1;
+    // Only the warps of TMEM lanes below AR ever store C.
+    static constexpr int kStagingWarps = AR / 32;
     static constexpr int kBarrierOffset = kStagingOffset + kStagingWarps * 2 * kStagingBytes;
     static constexpr int kSmemBytes = kBarrierOffset + kSmemReserve;
     static constexpr uint32_t kTmemCols = tmem_columns_for(2 * BN);
     static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "BN must be 64..256, step 64");
     static_assert(BK == 64 || BK == 128, "BK must be 64 or 128");
     static_assert(kSmemBytes <= kMaxSmem, "shared memory budget exceeded");
-    static_assert(AR == kBM || AR == 32, "A is staged as 128 or 32 rows");
+    static_assert(AR == kBM || AR == 32 || AR == 64, "A is staged as 128, 64 or 32 rows");
     // The MMA reads 128 rows (16 KB) from each A half: that must stay inside the stage.
     static_assert(AR == kBM || (BK / 64 - 1) * kAHalf + kBM * 128 <= kStageBytes, "A over-read leaves the stage");
 };
@@ -317,7 +317,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ------------------------------------------------------------ epilogue
         const int quarter = warp % 4;  // TMEM lanes this warp may access
         const int e = warp - 2;
-        uint8_t* staging = smem + L::kStagingOffset + (L::kStagingWarps == 1 ? 0 : e) * 2 * kStagingBytes;
+        // A warp whose lanes hold rows of C has a staging pair of its own
+        // (warps of lanes at or past AR never store).
+        uint8_t* staging =
+            smem + L::kStagingOffset + (L::kStagingWarps == kEpilogueWarps ? e : quarter) * 2 * kStagingBytes;
         int local = 0;
         int chunk_count = 0;
         // Cluster split K: rank 0's receive buffer and barrier as this CTA
@@ -647,6 +650,7 @@ struct Variant {
 
 #define KMCTS_VARIANT(BN, BK, ST, MN) {BN, BK, ST, MN, kBM, &launch_variant<BN, BK, ST, MN, kBM>}
 #define KMCTS_SKINNY(BN, BK, ST, MN) {BN, BK, ST, MN, 32, &launch_variant<BN, BK, ST, MN, 32>}
+#define KMCTS_HALF(BN, BK, ST, MN) {BN, BK, ST, MN, 64, &launch_variant<BN, BK, ST, MN, 64>}
 
 // The compiled 1-CTA schedule space: every (tile_n, tile_k, stages) of the
 // sweep grid that fits 227 KB (stages*(128+BN)*BK*2 + 32 KB staging + 2 KB),
@@ -668,12 +672,19 @@ const Variant kVariants[] = {
     KMCTS_SKINNY(128, 64, 9, false),  KMCTS_SKINNY(128, 64, 9, true),
     KMCTS_SKINNY(128, 128, 4, false), KMCTS_SKINNY(128, 128, 4, true),
     KMCTS_SKINNY(64, 128, 8, false),  KMCTS_SKINNY(64, 128, 8, true),
+    // tile_m 64 (M <= 64): A staged as 64 rows, two warps' epilogue staging.
+    KMCTS_HALF(128, 128, 4, false),   KMCTS_HALF(128, 128, 4, true),
+    KMCTS_HALF(128, 128, 3, false),   KMCTS_HALF(128, 128, 3, true),
+    KMCTS_HALF(64, 128, 6, false),    KMCTS_HALF(64, 128, 6, true),
 };
+
+// Rows of A a one-CTA schedule stages per tile: 32 or 64 for skinny M, else 128.
+int a_rows(const kmcts_gemm_config& cfg) { return cfg.tile_m == 32 || cfg.tile_m == 64 ? cfg.tile_m : kBM; }
 
 const Variant* find_variant(const kmcts_gemm_config& cfg, int b_layout) {
     for (const Variant& v : kVariants) {
         if (v.bn == cfg.tile_n && v.bk == cfg.tile_k && v.stages == cfg.stages &&
-            v.b_mn == (b_layout == KMCTS_B_ROW ? 1 : 0) && v.ar == (cfg.tile_m == 32 ? 32 : kBM)) {
+            v.b_mn == (b_layout == KMCTS_B_ROW ? 1 : 0) && v.ar == a_rows(cfg)) {
             return &v;
         }
     }
@@ -688,7 +699,7 @@ void put_reason(char* why, int len, const char* text) {
 }
 
 bool is_pair(const kmcts_gemm_config& cfg) { return cfg.tile_m == 256; }
-bool is_one_cta(const kmcts_gemm_config& cfg) { return cfg.tile_m == kBM || cfg.tile_m == 32; }
+bool is_one_cta(const kmcts_gemm_config& cfg) { return cfg.tile_m == kBM || cfg.tile_m == 64 || cfg.tile_m == 32; }
 
 }  // namespace
 
@@ -699,15 +710,15 @@ int64_t tcgen05_smem_bytes(const kmcts_gemm_config& cfg, int b_layout) {
     if (cfg.tile_n <= 0 || cfg.tile_k <= 0 || cfg.stages <= 0) return 0;
     if (is_swapped(cfg)) return cfg.tile_m == 32 ? stream_smem_bytes(cfg.tile_k, cfg.stages) : 0;
     if (cfg.tile_m == 256) return pair_smem_bytes(cfg.tile_n, cfg.tile_k, cfg.stages);
-    if (cfg.tile_m != kBM && cfg.tile_m != 32) return 0;
+    if (cfg.tile_m != kBM && cfg.tile_m != 64 && cfg.tile_m != 32) return 0;
     return static_cast<int64_t>(cfg.stages) * (cfg.tile_m + cfg.tile_n) * cfg.tile_k * 2 +
-           (cfg.tile_m == 32 ? 1 : kEpilogueWarps) * 2 * kStagingBytes + kSmemReserve;
+           (cfg.tile_m / 32) * 2 * kStagingBytes + kSmemReserve;
 }
 
 int cluster_split_cap(const kmcts_gemm_config& cfg, int b_layout) {
     if (!is_one_cta(cfg) || is_swapped(cfg) || cfg.tile_n <= 0) return 1;
     const int64_t own = tcgen05_smem_bytes(cfg, b_layout);
-    const int ar = cfg.tile_m == 32 ? 32 : kBM;
+    const int ar = a_rows(cfg);
     const int64_t stage_bytes = static_cast<int64_t>(cfg.stages) * (ar + cfg.tile_n) * cfg.tile_k * 2;
     int cap = 1;
     while (cap < kMaxClusterSplits && cluster_receive_mode(cap + 1, own, stage_bytes, cfg.tile_n, ar)) ++cap;
@@ -777,11 +788,15 @@ int tcgen05_legal(const kmcts_gemm_config& cfg, int M, int N, int K, int b_layou
     }
     if (is_one_cta(cfg)) {
         if (cfg.cluster_m != 1) {
-            put_reason(why, len, "tile_m 128 and 32 run one CTA per tile (cluster 1x1)");
+            put_reason(why, len, "tile_m 128, 64 and 32 run one CTA per tile (cluster 1x1)");
             return KMCTS_ENOTSUP;
         }
         if (cfg.tile_m == 32 && M > 32) {
             put_reason(why, len, "tile_m 32 stages 32 rows of A: it takes M <= 32");
+            return KMCTS_ENOTSUP;
+        }
+        if (cfg.tile_m == 64 && M > 64) {
+            put_reason(why, len, "tile_m 64 stages 64 rows of A: it takes M <= 64");
             return KMCTS_ENOTSUP;
         }
     } else if (cfg.tile_m == 256) {
@@ -794,7 +809,7 @@ int tcgen05_legal(const kmcts_gemm_config& cfg, int M, int N, int K, int b_layou
             return KMCTS_ENOTSUP;
         }
     } else {
-        put_reason(why, len, "tile_m must be 128 or 32 (one CTA) or 256 (CTA pair)");
+        put_reason(why, len, "tile_m must be 128, 64 or 32 (one CTA) or 256 (CTA pair)");
         return KMCTS_ENOTSUP;
     }
     const int64_t smem = tcgen05_smem_bytes(cfg, b_layout);
@@ -844,7 +859,8 @@ int launch_tcgen05(const void* A, const void* B, void* C, int M, int N, int K, i
     // Each CTA stages 128 rows of A, and BN (one CTA) or BN/2 (pair) of B.
     const uint32_t b_rows = pair ? cfg.tile_n / 2 : cfg.tile_n;
     CUtensorMap ma, mb, mb_half, mc;
-    bool ok = encode_tensor_map_2d(&ma, A, K, M, static_cast<uint64_t>(K) * 2, 64, cfg.tile_m == 32 ? 32 : kBM);
+    bool ok = encode_tensor_map_2d(&ma, A, K, M, static_cast<uint64_t>(K) * 2, 64,
+                                   pair ? kBM : static_cast<uint32_t>(a_rows(cfg)));
     if (b_layout == KMCTS_B_COL) {
         ok = ok && encode_tensor_map_2d(&mb, B, K, N, static_cast<uint64_t>(K) * 2, 64, b_rows);
         // Half-width units of a pair stage b_rows / 2 columns of B.
@@ -921,7 +937,7 @@ int plan_tcgen05(const kmcts_gemm_config& cfg, int M, int N, int K, int b_layout
     plan.units = plan.tiles * plan.k_splits;
     plan.ctas = cfg.persistent ? (plan.units < plan.workers ? plan.units : plan.workers) : plan.units;
     plan.smem_bytes = static_cast<int32_t>(tcgen05_smem_bytes(cfg, b_layout));
-    const int ar = cfg.tile_m == 32 ? 32 : kBM;
+    const int ar = a_rows(cfg);
     int mode = 0;
     const int cs = cluster_splits(cfg.flags, cfg.k_splits, num_kb, plan.tiles, cfg.persistent != 0, plan.smem_bytes,
                                   static_cast<int64_t>(cfg.stages) * (ar + cfg.tile_n) * cfg.tile_k * 2, cfg.tile_n,

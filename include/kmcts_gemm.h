@@ -68,7 +68,7 @@ extern "C" {
  * Deterministic; exact on integer inputs, within the parity bound otherwise.
  * Without a workspace (growth under graph capture) the N split runs. */
 #define KMCTS_FLAG_TAIL_SPLIT_K 32
-/* One-CTA schedules (tile_m 128 or 32): B's loads carry an L2 evict-first
+/* One-CTA schedules (tile_m 128, 64 or 32): B's loads carry an L2 evict-first
  * policy.  For shapes whose M fits one tile row B is read exactly once, and
  * streaming it through L2 at normal priority would push out everything else
  * there (dirty lines cost a DRAM write-back on eviction).  Results are
@@ -90,8 +90,8 @@ extern "C" {
  * FP32 values into split 0's shared memory, which adds them in split order
  * and writes C: no partial goes through the workspace, and the sum order,
  * hence every output bit, is the workspace path's.  The values take
- * (k_splits - 1) x rows x tile_n x 4 bytes (rows = 32 for tile_m 32, else
- * 128): split 0 receives them in extra shared memory when that stays within
+ * (k_splits - 1) x rows x tile_n x 4 bytes (rows = tile_m for tile_m 32 or
+ * 64, else 128): split 0 receives them in extra shared memory when that stays within
  * 227 KB, else in its pipeline stages once its own MMAs are done (when they
  * are large enough).  Every unit runs in its own CTA (units no more than the
  * SMs when persistent); otherwise the workspace path runs. */
@@ -105,11 +105,12 @@ extern "C" {
 /* Kernel schedule.  Zero-initialise and call kmcts_default_config() first. */
 typedef struct kmcts_gemm_config {
     int32_t tile_m;       /* 128: one CTA per tile; 256: one CTA pair per tile;
-                             32: one CTA per tile staging 32 rows of A (M <= 32) */
+                             32 or 64: one CTA per tile staging 32 or 64 rows of A
+                             (M <= 32 or M <= 64) */
     int32_t tile_n;       /* tile columns: 64, 128, 192, 256 (one CTA); 128, 256 (pair) */
     int32_t tile_k;       /* K per pipeline stage: 64 or 128 */
     int32_t stages;       /* shared-memory pipeline depth: 2..6 (9 for some tile_m 32 schedules) */
-    int32_t cluster_m;    /* 1 with tile_m 128 or 32; 2 with tile_m 256 (tcgen05 cta_group::2) */
+    int32_t cluster_m;    /* 1 with tile_m 128, 64 or 32; 2 with tile_m 256 (tcgen05 cta_group::2) */
     int32_t cluster_n;    /* 1; or 2 with tile_m 256, tile_n 256, tile_k 128, 3 stages: two CTA
                              pairs per 4-CTA cluster share A over distributed shared memory
                              (no TMA multicast); bit-identical to cluster_n 1, and slower */
@@ -123,7 +124,7 @@ typedef struct kmcts_gemm_config {
     int32_t reserved;     /* zero */
 } kmcts_gemm_config;
 
-/* Split K (tile_m 128 or 32, and tile_m 256 pairs in clusters of two; it takes
+/* Split K (tile_m 128, 64 or 32, and tile_m 256 pairs in clusters of two; it takes
  * precedence over the pairs' tail splits).  With k_splits = S > 1 each output tile runs as S
  * units over consecutive K ranges, so a shape with few tiles (skinny M or N)
  * still streams its operands through every SM.  Each unit stores its FP32
@@ -144,8 +145,10 @@ typedef struct kmcts_gemm_config {
  * x 128, 3-stage schedule that is fastest at 4096^3). Returns KMCTS_OK. */
 int kmcts_default_config(kmcts_gemm_config* cfg);
 
-/* Fills *cfg with the schedule a NULL cfg selects for this shape: for M <= 32,
- * one CTA per tile staging 32 rows of A (tile_m 32); else the default when its
+/* Fills *cfg with the schedule a NULL cfg selects for this shape: for M <= 32
+ * or M <= 64, one CTA per tile staging 32 or 64 rows of A (tile_m 32 or 64),
+ * its K splits added up in shared memory (KMCTS_FLAG_SPLIT_CLUSTER, at most
+ * six); else the default when its
  * 256 x 256 pair tiles fill the co-resident CTA pairs (with 64-deep stages when
  * K <= 768), or in two K splits when those fill three quarters of them and
  * K >= 8192; else one CTA per

@@ -637,8 +637,42 @@ def test_skinny_a_rows_integer_exact(cuda_device, layout, tile_n, tile_k, stages
         np.testing.assert_array_equal(bits_of(c), expect)
 
 
+HALF = [(128, 128, 4), (128, 128, 3), (64, 128, 6)]
+
+
+@pytest.mark.parametrize("layout", ["col", "row"])
+@pytest.mark.parametrize("tile_n,tile_k,stages", HALF)
+@pytest.mark.parametrize("shape,splits", [((64, 520, 1032), 1), ((33, 1024, 2048), 3), ((50, 264, 4096), 4),
+                                          ((1, 2048, 512), 1)])
+def test_64_row_staging_integer_exact(cuda_device, layout, tile_n, tile_k, stages, shape, splits):
+    """tile_m 64 stages 64 rows of A; the MMA's other 64 rows are discarded.
+    Exact on integer inputs with and without split K, evict-first or not."""
+    m, n, k = shape
+    a_t, b_t = oracle.integer_inputs(m, n, k, seed=m + splits)
+    expect = oracle.torch_bits(oracle.torch_reference(a_t, b_t))
+    for flags in (0, _native.FLAG_B_EVICT_FIRST):
+        c = run(a_t.cuda(), b_for(layout, b_t.cuda()), layout, kernel=_native.KERNEL_TCGEN05, tile_m=64,
+                cluster_m=1, tile_n=tile_n, tile_k=tile_k, stages=stages, k_splits=splits, flags=flags)
+        np.testing.assert_array_equal(bits_of(c), expect)
+
+
+@pytest.mark.parametrize("layout", ["col", "row"])
+def test_64_row_staging_same_bits_as_128(cuda_device, layout):
+    """Staging 64 rows of A instead of 128 changes which rows the MMA reads
+    past M, not the K order of any stored row: the same bits on N(0,1)."""
+    m, n, k = 64, 1024, 4096
+    a_t, b_t = oracle.randn_inputs(m, n, k, seed=4, b_layout=layout)
+    a, b = a_t.cuda(), b_t.cuda()
+    common = dict(kernel=_native.KERNEL_TCGEN05, cluster_m=1, tile_n=128, tile_k=128, stages=3)
+    c64 = run(a, b, layout, tile_m=64, **common)
+    c128 = run(a, b, layout, tile_m=128, **common)
+    assert torch.equal(c64.view(torch.int16), c128.view(torch.int16))
+
+
 @pytest.mark.parametrize("layout", ["col", "row"])
 @pytest.mark.parametrize("tile_m,tile_n,tile_k,stages,shape,splits,cluster", [
+    (64, 64, 128, 6, (64, 2048, 8192), 4, 4),    # 64 rows: received in the stages
+    (64, 128, 128, 3, (50, 1000, 4096), 3, 3),   # 64 rows, ragged: in a receive buffer
     (32, 128, 128, 4, (16, 1024, 2048), 2, 2),
     (32, 128, 128, 4, (32, 264, 4096), 4, 4),    # ragged N
     (32, 128, 64, 9, (7, 2048, 1032), 3, 3),     # ragged K: 17 K blocks over 3 splits
@@ -679,14 +713,15 @@ def test_cluster_split_k_same_bits_as_workspace_split_k(cuda_device, layout, til
 
 
 @pytest.mark.parametrize("layout", ["col", "row"])
-@pytest.mark.parametrize("shape", [(16, 8192, 8192), (128, 16384, 4096), (100, 1000, 2048), (48, 4096, 8192)])
+@pytest.mark.parametrize("shape", [(16, 8192, 8192), (128, 16384, 4096), (100, 1000, 2048), (48, 4096, 8192),
+                                   (64, 2048, 8192)])
 def test_skinny_selection_streams_b_evict_first_same_bits(cuda_device, layout, shape):
     """The NULL-config selection for one-tile-row shapes sets the evict-first
     policy; its results equal the same schedule without it, bit for bit, and
     are exact on integer inputs."""
     m, n, k = shape
     sel = _native.select_config(m, n, k, _native.B_ROW if layout == "row" else _native.B_COL)
-    assert sel.flags & _native.FLAG_B_EVICT_FIRST and sel.tile_m in (32, 128)
+    assert sel.flags & _native.FLAG_B_EVICT_FIRST and sel.tile_m in (32, 64, 128)
     a_t, b_t = oracle.integer_inputs(m, n, k, seed=5)
     expect = oracle.torch_bits(oracle.torch_reference(a_t, b_t))
     a, b = a_t.cuda(), b_for(layout, b_t.cuda())

@@ -52,6 +52,17 @@ def test_skinny_a_rows_take_at_most_32_rows():
     assert km.config_legal(km.make_config(tile_m=32, cluster_m=2), 16, 4096, 4096)[0] == _native.KMCTS_ENOTSUP
 
 
+def test_64_row_staging_takes_at_most_64_rows():
+    cfg = km.make_config(tile_m=64, cluster_m=1, tile_n=128, tile_k=128, stages=4)
+    assert km.config_legal(cfg, 64, 4096, 4096, km.B_ROW) == (0, "ok")
+    code, why = km.config_legal(cfg, 65, 4096, 4096, km.B_ROW)
+    assert code == _native.KMCTS_ENOTSUP and "M <= 64" in why
+    # 4 x (64 + 128) x 128 x 2 of stages, two warps' staging buffers, reserve
+    assert km.config_smem_bytes(cfg) == 4 * 192 * 128 * 2 + 2 * 2 * 4096 + 2048
+    assert km.config_legal(km.make_config(tile_m=64, cluster_m=1, tile_n=256, tile_k=64, stages=4),
+                           64, 4096, 4096)[0] == _native.KMCTS_ENOTSUP  # not compiled
+
+
 def test_select_config_splits_k_for_skinny_shapes():
     cfg = km.select_config(16, 8192, 8192, km.B_ROW)
     assert (cfg.tile_m, cfg.tile_n, cfg.k_splits) == (32, 128, 2)  # 64 tiles -> 128 units
@@ -68,9 +79,14 @@ def test_select_config_splits_k_for_skinny_shapes():
     # Nine splits would fill the SMs; clusters of more than six are not selected.
     long_k = km.select_config(16, 1024, 32768, km.B_ROW)
     assert (long_k.tile_n, long_k.k_splits) == (64, 6) and long_k.flags & _native.FLAG_SPLIT_CLUSTER
-    assert km.select_config(64, 8192, 8192, km.B_ROW).tile_m == 128
-    mid = km.select_config(64, 2048, 8192, km.B_ROW)  # 16 tiles of 128 x 128, four splits in the stages
-    assert (mid.tile_m, mid.k_splits) == (128, 4) and mid.flags & _native.FLAG_SPLIT_CLUSTER
+    assert km.select_config(65, 8192, 8192, km.B_ROW).tile_m == 128
+    mid = km.select_config(64, 2048, 8192, km.B_ROW)  # 32 tiles of 64 x 64 rows/columns, four splits
+    assert (mid.tile_m, mid.tile_n, mid.stages, mid.k_splits) == (64, 64, 6, 4) and mid.flags & _native.FLAG_SPLIT_CLUSTER
+    wide64 = km.select_config(64, 16384, 4096, km.B_ROW)  # 128 tiles of 128 columns: unsplit, four stages
+    assert (wide64.tile_m, wide64.tile_n, wide64.stages, wide64.k_splits) == (64, 128, 4, 0)
+    split64 = km.select_config(64, 8192, 8192, km.B_ROW)  # 64 tiles: two splits, three stages
+    assert (split64.tile_m, split64.tile_n, split64.stages, split64.k_splits) == (64, 128, 3, 2)
+    assert km.select_config(33, 1024, 16384, km.B_ROW).k_splits == 6
     assert not km.select_config(128, 4096, 8192, km.B_ROW).flags & _native.FLAG_SPLIT_CLUSTER
     assert km.select_config(512, 512, 8192, km.B_ROW).k_splits == 4
     assert km.select_config(1024, 1024, 1024, km.B_ROW).k_splits == 0  # short K: no split
