@@ -205,7 +205,14 @@ int kmcts_select_config(int M, int N, int K, int b_layout, kmcts_gemm_config* cf
         small.cluster_m = 1;
     }
     const long long pair_tiles = static_cast<long long>((M + 255) / 256) * ((N + 255) / 256);
+    // One row of pair tiles (M <= 256): each B column is read by one pair
+    // (per K range), so B streams through L2 at evict-first priority
+    // (measured, L2 flushed: 256 x 16384 x 4096 37.8 us against 43.8,
+    // 200 x 16384 x 8192 62.6 against 70.8, 256 x 8192 x 8192 split in two
+    // 43.7 against 48.8; bit-identical).
+    const int pair_b_flags = M <= 256 ? KMCTS_FLAG_B_EVICT_FIRST : 0;
     if (pair_tiles >= workers) {
+        cfg->flags |= pair_b_flags;
         // Short K (at most six 128-deep blocks per tile): 64-deep stages keep
         // the pipeline full through each tile's few K blocks; six of them,
         // five below K = 256 (measured, L2 flushed: 8192^2 x 768 78.9 us
@@ -227,6 +234,7 @@ int kmcts_select_config(int M, int N, int K, int b_layout, kmcts_gemm_config* cf
         split.tile_k = 64;
         split.stages = 6;
         split.k_splits = 2;
+        split.flags |= pair_b_flags;
         if (tcgen05_legal(split, M, N, K, b_layout, nullptr, 0) == KMCTS_OK) {
             *cfg = split;
             return KMCTS_OK;
@@ -235,7 +243,10 @@ int kmcts_select_config(int M, int N, int K, int b_layout, kmcts_gemm_config* cf
     small.tile_m = 128;
     const long long wide_tiles = static_cast<long long>((M + 127) / 128) * ((N + 255) / 256);
     if (wide_tiles >= workers) {
-        if (K >= 4096) return KMCTS_OK;
+        if (K >= 4096) {
+            cfg->flags |= pair_b_flags;  // the pair schedule after all
+            return KMCTS_OK;
+        }
         small.tile_n = 256;
         small.tile_k = 64;
         small.stages = 4;

@@ -115,6 +115,7 @@ struct TailSplit {
     int splits;                    // split K: K ranges per tile
     int epoch;
     int mode;
+    int b_evict_first;  // B's loads at L2 evict-first priority (B read once: one pair-tile row)
 };
 
 struct Unit {
@@ -386,6 +387,7 @@ __global__ void __launch_bounds__(pair_threads<SLOTS>(), 1)
             uint32_t phase = 0;
             uint32_t issued = 0, issued_phase = 0;
             bool ok = true;
+            const uint64_t b_policy = tail.b_evict_first ? ptx::policy_evict_first() : 0ull;
             for (int u = 0; u < num_units && ok; ++u) {
                 const Unit w = unit_at(u);
                 const int m0 = w.m_blk * 256 + static_cast<int>(rank) * 128;
@@ -419,11 +421,17 @@ __global__ void __launch_bounds__(pair_threads<SLOTS>(), 1)
                         }
                         if constexpr (B_MN) {
                             for (int nb = 0; nb < b_cols / 64; ++nb) {
-                                ptx::tma_load_2d_pair(sb + (kh * (L::kHalfN / 64) + nb) * 8192, &map_b, bar,
-                                                      nb0 + nb * 64, k0);
+                                uint8_t* dst = sb + (kh * (L::kHalfN / 64) + nb) * 8192;
+                                if (tail.b_evict_first)
+                                    ptx::tma_load_2d_pair_hint(dst, &map_b, bar, nb0 + nb * 64, k0, b_policy);
+                                else
+                                    ptx::tma_load_2d_pair(dst, &map_b, bar, nb0 + nb * 64, k0);
                             }
                         } else {
-                            ptx::tma_load_2d_pair(sb + kh * (L::kHalfN * 128), mb, bar, k0, nb0);
+                            if (tail.b_evict_first)
+                                ptx::tma_load_2d_pair_hint(sb + kh * (L::kHalfN * 128), mb, bar, k0, nb0, b_policy);
+                            else
+                                ptx::tma_load_2d_pair(sb + kh * (L::kHalfN * 128), mb, bar, k0, nb0);
                         }
                     }
                     issued |= 1u << stage;
@@ -1104,7 +1112,7 @@ bool split_smem_configured() {
 template <int BN, int BK, int STAGES, bool B_MN, bool ALLGATHER = false, bool SLOTS = false>
 int launch_pair_variant_peers(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb_half,
                               const CUtensorMap& mc, int M, int N, int K, int group, bool persistent, int tail_req,
-                              int k_splits, uint64_t limit_ns, cudaStream_t stream, int* status,
+                              int k_splits, bool b_evict_first, uint64_t limit_ns, cudaStream_t stream, int* status,
                               const PeerOutputs& peers) {
     using L = PairLayout<BN, BK, STAGES, B_MN>;
     if (status == nullptr) status = default_status_ptr();
@@ -1131,6 +1139,7 @@ int launch_pair_variant_peers(const CUtensorMap& ma, const CUtensorMap& mb, cons
                                                                        group, 0, &plan);
         if (rc != KMCTS_OK) return rc;
     }
+    tail.b_evict_first = b_evict_first ? 1 : 0;
     tail.mode = plan.k_splits > 1                           ? kSplitK
                 : plan.tail_split == KMCTS_TAIL_STREAM_K ? kTailStreamK
                 : plan.tail_split == KMCTS_TAIL_SPLIT_K  ? kTailSplitK
@@ -1174,10 +1183,11 @@ int launch_pair_variant_peers(const CUtensorMap& ma, const CUtensorMap& mb, cons
 template <int BN, int BK, int STAGES, bool B_MN, bool SLOTS>
 int launch_pair_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb_half,
                         const CUtensorMap& mc, int M, int N, int K, int group, bool persistent, int tail_req,
-                        int k_splits, uint64_t limit_ns, cudaStream_t stream, int* status) {
+                        int k_splits, bool b_evict_first, uint64_t limit_ns, cudaStream_t stream, int* status) {
     const PeerOutputs none = {};
-    return launch_pair_variant_peers<BN, BK, STAGES, B_MN, false, SLOTS>(
-        ma, mb, mb_half, mc, M, N, K, group, persistent, tail_req, k_splits, limit_ns, stream, status, none);
+    return launch_pair_variant_peers<BN, BK, STAGES, B_MN, false, SLOTS>(ma, mb, mb_half, mc, M, N, K, group,
+                                                                         persistent, tail_req, k_splits, b_evict_first,
+                                                                         limit_ns, stream, status, none);
 }
 
 template <int BN, int BK, int STAGES, bool B_MN, bool SLOTS>
@@ -1186,7 +1196,7 @@ int plan_variant(int M, int N, int K, bool persistent, int tail, int group, int 
 }
 
 using PairLauncher = int (*)(const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, int,
-                             int, int, int, bool, int, int, uint64_t, cudaStream_t, int*);
+                             int, int, int, bool, int, int, bool, uint64_t, cudaStream_t, int*);
 
 using PairPlanner = int (*)(int, int, int, bool, int, int, int, kmcts_gemm_plan*);
 
@@ -1267,9 +1277,9 @@ int launch_pair_allgather(const CUtensorMap& ma, const CUtensorMap& mb, const CU
     if (b_layout == KMCTS_B_ROW)
         return launch_pair_variant_peers<256, 128, 3, true, true>(ma, mb, mb_half, mc, M, N_shard, K,
                                                                   cfg.raster_group, cfg.persistent != 0, split, 0,
-                                                                  limit_ns, stream, status, peers);
+                                                                  false, limit_ns, stream, status, peers);
     return launch_pair_variant_peers<256, 128, 3, false, true>(ma, mb, mb_half, mc, M, N_shard, K, cfg.raster_group,
-                                                               cfg.persistent != 0, split, 0, limit_ns, stream,
+                                                               cfg.persistent != 0, split, 0, false, limit_ns, stream,
                                                                status, peers);
 }
 
@@ -1279,7 +1289,7 @@ int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap&
     const PairVariant* v = find_pair_variant(cfg, b_layout);
     if (!v) return KMCTS_ENOTSUP;
     return v->fn(ma, mb, mb_half, mc, M, N, K, cfg.raster_group, cfg.persistent != 0, requested_tail(cfg.flags),
-                 cfg.k_splits, limit_ns, stream, status);
+                 cfg.k_splits, (cfg.flags & KMCTS_FLAG_B_EVICT_FIRST) != 0, limit_ns, stream, status);
 }
 
 }  // namespace kmcts

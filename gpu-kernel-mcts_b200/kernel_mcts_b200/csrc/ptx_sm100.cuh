@@ -341,6 +341,16 @@ __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* m
         : "memory");
 }
 
+// tma_load_2d_pair with an L2 cache policy (from createpolicy).
+__device__ __forceinline__ void tma_load_2d_pair_hint(void* dst, const CUtensorMap* map, uint32_t bar_cluster_addr,
+                                                      int32_t c0, int32_t c1, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster_addr), "r"(c0), "r"(c1), "l"(policy)
+        : "memory");
+}
+
 // Bulk copy of `bytes` (a multiple of 16, both addresses 16-byte aligned)
 // from this CTA's shared memory into another CTA's of the cluster
 // (`dst_cluster_addr`), completion counted in bytes on an mbarrier in the

@@ -637,6 +637,34 @@ def test_skinny_a_rows_integer_exact(cuda_device, layout, tile_n, tile_k, stages
         np.testing.assert_array_equal(bits_of(c), expect)
 
 
+@pytest.mark.parametrize("layout", ["col", "row"])
+@pytest.mark.parametrize("shape,cfg", [
+    ((256, 2048, 4096), {}),                                   # default pair, last wave N-split
+    ((200, 1024, 8192), dict(tile_k=64, stages=6, k_splits=2)),  # pair split K, ragged M
+    ((256, 4096, 1024), dict(tile_n=128, tile_k=128, stages=4)),  # half-width pair tiles
+])
+def test_cta_pair_b_evict_first_same_bits(cuda_device, layout, shape, cfg):
+    """B's loads at L2 evict-first priority on the CTA pair (selected for one
+    row of pair tiles) change the cache policy only: exact on integer
+    inputs, and the same bits as without the hint on N(0,1) inputs."""
+    m, n, k = shape
+    base = dict(kernel=_native.KERNEL_TCGEN05, **cfg)
+    a_t, b_t = oracle.integer_inputs(m, n, k, seed=9)
+    expect = oracle.torch_bits(oracle.torch_reference(a_t, b_t))
+    c = run(a_t.cuda(), b_for(layout, b_t.cuda()), layout, flags=_native.FLAG_B_EVICT_FIRST, **base)
+    np.testing.assert_array_equal(bits_of(c), expect)
+    a_t, b_t = oracle.randn_inputs(m, n, k, seed=5, b_layout=layout)
+    a, b = a_t.cuda(), b_t.cuda()
+    hinted = run(a, b, layout, flags=_native.FLAG_B_EVICT_FIRST, **base)
+    plain = run(a, b, layout, **base)
+    assert torch.equal(hinted.view(torch.int16), plain.view(torch.int16))
+    sel = _native.select_config(m, n, k, kg.layout_code(layout))
+    if sel.tile_m == 256:
+        assert sel.flags & _native.FLAG_B_EVICT_FIRST  # one row of pair tiles
+        np.testing.assert_array_equal(bits_of(run(a, b, layout)), bits_of(run(a, b, layout, **{
+            nm: getattr(sel, nm) for nm, _ in sel._fields_})))
+
+
 HALF = [(128, 128, 4), (128, 128, 3), (64, 128, 6)]
 
 
