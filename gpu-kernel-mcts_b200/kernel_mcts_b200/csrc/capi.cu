@@ -205,12 +205,15 @@ int kmcts_select_config(int M, int N, int K, int b_layout, kmcts_gemm_config* cf
         small.cluster_m = 1;
     }
     const long long pair_tiles = static_cast<long long>((M + 255) / 256) * ((N + 255) / 256);
-    // One row of pair tiles (M <= 256): each B column is read by one pair
-    // (per K range), so B streams through L2 at evict-first priority
-    // (measured, L2 flushed: 256 x 16384 x 4096 37.8 us against 43.8,
-    // 200 x 16384 x 8192 62.6 against 70.8, 256 x 8192 x 8192 split in two
-    // 43.7 against 48.8; bit-identical).
-    const int pair_b_flags = M <= 256 ? KMCTS_FLAG_B_EVICT_FIRST : 0;
+    // One or two rows of pair tiles (M <= 512): each B column is read by one
+    // or two pairs, close together in time, so B streams through L2 at
+    // evict-first priority (measured, L2 flushed: 256 x 16384 x 4096 37.8 us
+    // against 43.8, 200 x 16384 x 8192 62.6 against 70.8, 256 x 8192 x 8192
+    // split in two 43.7 against 48.8, 512 x 8192 x 8192 56.0 against 61.5,
+    // 512 x 16384 x 4096 57.5 against 62.0; bit-identical).  With more rows
+    // the re-reads miss: 1024 x 16384 x 4096 95.7 against 96.4, 4096^3 96.1
+    // against 95.3, 8192^3 811 against 783.
+    const int pair_b_flags = M <= 512 ? KMCTS_FLAG_B_EVICT_FIRST : 0;
     if (pair_tiles >= workers) {
         cfg->flags |= pair_b_flags;
         // Short K (at most six 128-deep blocks per tile): 64-deep stages keep

@@ -69,9 +69,10 @@ extern "C" {
  * Without a workspace (growth under graph capture) the N split runs. */
 #define KMCTS_FLAG_TAIL_SPLIT_K 32
 /* One-CTA schedules (tile_m 128, 64 or 32) and CTA pairs: B's loads carry an
- * L2 evict-first policy.  For shapes whose M fits one tile row B is read
- * exactly once, and streaming it through L2 at normal priority would push out
- * everything else there (dirty lines cost a DRAM write-back on eviction).
+ * L2 evict-first policy.  For shapes whose M fits one or two tile rows B is
+ * read once or twice, and streaming it through L2 at normal priority would
+ * push out everything else there (dirty lines cost a DRAM write-back on
+ * eviction).
  * Results are unchanged; only the cache policy differs.  The fused
  * all-gather ignores it. */
 #define KMCTS_FLAG_B_EVICT_FIRST 8
@@ -155,8 +156,8 @@ int kmcts_default_config(kmcts_gemm_config* cfg);
  * K >= 8192; else one CTA per
  * 128 x 256 tile while those fill them (the default again from K = 4096),
  * else one CTA per 128 x 128 tile.  Few tiles over a long K get split K; one-CTA
- * schedules for M <= 128 and pair schedules for M <= 256 (one tile row) add
- * KMCTS_FLAG_B_EVICT_FIRST.  Every
+ * schedules for M <= 128 and pair schedules for M <= 512 (one or two tile
+ * rows) add KMCTS_FLAG_B_EVICT_FIRST.  Every
  * schedule gives results within the parity criterion and bit-exact ones on
  * integer inputs.  Returns KMCTS_OK or KMCTS_EINVAL. */
 int kmcts_select_config(int M, int N, int K, int b_layout, kmcts_gemm_config* cfg);

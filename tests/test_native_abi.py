@@ -96,11 +96,11 @@ def test_select_config_splits_k_for_skinny_shapes():
     pair_split = km.select_config(4096, 512, 16384, km.B_ROW)
     assert (pair_split.tile_m, pair_split.tile_k, pair_split.stages, pair_split.k_splits) == (256, 64, 6, 2)
     assert km.select_config(256, 8192, 8192, km.B_ROW).k_splits == 2
-    # One row of pair tiles: B streams at evict-first priority; two rows: not.
-    for shape in ((256, 8192, 8192), (256, 16384, 4096), (200, 28672, 8192)):
+    # One or two rows of pair tiles: B streams at evict-first priority; more: not.
+    for shape in ((256, 8192, 8192), (256, 16384, 4096), (200, 28672, 8192), (512, 16384, 4096)):
         sel = km.select_config(*shape, km.B_ROW)
         assert sel.tile_m == 256 and sel.flags & _native.FLAG_B_EVICT_FIRST, shape
-    assert not km.select_config(512, 16384, 4096, km.B_ROW).flags & _native.FLAG_B_EVICT_FIRST
+    assert not km.select_config(1024, 16384, 4096, km.B_ROW).flags & _native.FLAG_B_EVICT_FIRST
     assert not km.select_config(4096, 4096, 4096, km.B_ROW).flags & _native.FLAG_B_EVICT_FIRST
     # ... not at K = 4096: one CTA per 128 x 256 tile.
     assert km.select_config(2048, 1024, 4096, km.B_ROW).tile_m == 128
