@@ -48,6 +48,7 @@ FLAG_TAIL_SPLIT_K = 32
 FLAG_B_EVICT_FIRST = 8
 FLAG_SWAP_AB = 16
 FLAG_SPLIT_CLUSTER = 64
+FLAG_A_EVICT_FIRST = 128
 
 TAIL_NONE = 0
 TAIL_SPLIT_N = 1

@@ -106,8 +106,8 @@ int choose_splits(long long tiles, int K, int sms) {
 
 }  // namespace
 
-int kmcts_select_config(int M, int N, int K, int b_layout, kmcts_gemm_config* cfg) {
-    if (!cfg || M < 0 || N < 0 || K < 0) return KMCTS_EINVAL;
+// The schedule for the shape; kmcts_select_config adds the A-side cache policy.
+static int select_schedule(int M, int N, int K, int b_layout, kmcts_gemm_config* cfg) {
     kmcts_default_config(cfg);
     // Measured on B200 (CUDA-graph replays, warm L2):
     // * M <= 32: one CTA per tile staging 32 rows of A (more B in flight per
@@ -205,6 +205,11 @@ int kmcts_select_config(int M, int N, int K, int b_layout, kmcts_gemm_config* cf
         small.cluster_m = 1;
     }
     const long long pair_tiles = static_cast<long long>((M + 255) / 256) * ((N + 255) / 256);
+    // N <= 128 leaves half of every 256-column pair tile empty: one CTA per
+    // 128 x 128 tile instead (L2 flushed, A at evict-first priority:
+    // 16384 x 128 x 4096 33.1 us against 36.7 for the pair, 16384 x 64 x 8192
+    // 55.5 against 59.6).
+    const bool pair_fits_n = N > 128;
     // One or two rows of pair tiles (M <= 512): each B column is read by one
     // or two pairs, close together in time, so B streams through L2 at
     // evict-first priority (measured, L2 flushed: 256 x 16384 x 4096 37.8 us
@@ -214,7 +219,7 @@ int kmcts_select_config(int M, int N, int K, int b_layout, kmcts_gemm_config* cf
     // the re-reads miss: 1024 x 16384 x 4096 95.7 against 96.4, 4096^3 96.1
     // against 95.3, 8192^3 811 against 783.
     const int pair_b_flags = M <= 512 ? KMCTS_FLAG_B_EVICT_FIRST : 0;
-    if (pair_tiles >= workers) {
+    if (pair_tiles >= workers && pair_fits_n) {
         cfg->flags |= pair_b_flags;
         // Short K (at most six 128-deep blocks per tile): 64-deep stages keep
         // the pipeline full through each tile's few K blocks; six of them,
@@ -232,7 +237,7 @@ int kmcts_select_config(int M, int N, int K, int b_layout, kmcts_gemm_config* cf
     // 256 x 8192 x 8192 49.0 against 52.4; at K = 4096, or with four splits,
     // one-CTA tiles win).  Not for M <= 128, where a 256-row pair tile would
     // be mostly empty.
-    if (M > 128 && 2 * pair_tiles <= workers && 8 * pair_tiles >= 3 * workers && K >= 8192) {
+    if (M > 128 && pair_fits_n && 2 * pair_tiles <= workers && 8 * pair_tiles >= 3 * workers && K >= 8192) {
         kmcts_gemm_config split = *cfg;
         split.tile_k = 64;
         split.stages = 6;
@@ -245,7 +250,7 @@ int kmcts_select_config(int M, int N, int K, int b_layout, kmcts_gemm_config* cf
     }
     small.tile_m = 128;
     const long long wide_tiles = static_cast<long long>((M + 127) / 128) * ((N + 255) / 256);
-    if (wide_tiles >= workers) {
+    if (wide_tiles >= workers && pair_fits_n) {
         if (K >= 4096) {
             cfg->flags |= pair_b_flags;  // the pair schedule after all
             return KMCTS_OK;
@@ -279,6 +284,20 @@ int kmcts_select_config(int M, int N, int K, int b_layout, kmcts_gemm_config* cf
     }
     if (tcgen05_legal(small, M, N, K, b_layout, nullptr, 0) == KMCTS_OK) *cfg = small;
     return KMCTS_OK;
+}
+
+int kmcts_select_config(int M, int N, int K, int b_layout, kmcts_gemm_config* cfg) {
+    if (!cfg || M < 0 || N < 0 || K < 0) return KMCTS_EINVAL;
+    const int rc = select_schedule(M, N, K, b_layout, cfg);
+    // N within one or two tile columns: every A byte is read by one or two
+    // CTAs (pairs), close together in time, so A streams through L2 at
+    // evict-first priority (measured, L2 flushed by a 512 MiB write:
+    // 28672 x 256 x 4096 63.0 us against 70.4, 8192 x 512 x 4096 35.3
+    // against 39.4, 2048 x 256 x 8192 26.8 against 28.4; bit-identical).
+    if (rc == KMCTS_OK && cfg->tile_n > 0 && N > 0 && (N + cfg->tile_n - 1) / cfg->tile_n <= 2 &&
+        tcgen05_legal(*cfg, M, N, K, b_layout, nullptr, 0) == KMCTS_OK)
+        cfg->flags |= KMCTS_FLAG_A_EVICT_FIRST;
+    return rc;
 }
 
 const char* kmcts_version(void) { return "kmcts_gemm_sm100 0.1.0 (sm_100a tcgen05)"; }

@@ -111,7 +111,7 @@ __device__ __forceinline__ float4* split_chunk(const SplitK& sk, int tile, int s
 }
 
 // Float4 offset of (sending rank's slot, lane quarter, chunk) in rank 0's
-// receive buffer.  `rows` is the rows of A staged per tile (32 or 128).
+// receive buffer.  `rows` is the rows of A staged per tile (32, 64 or 128).
 template <int BN>
 __device__ __forceinline__ int recv_chunk(int slot, int quarter, int c, int rows) {
     return ((slot * (rows / 32) + quarter) * (BN / 64) + c) * 16 * 32;
@@ -122,7 +122,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_tcgen05(const __grid_constant__ CUtensorMap map_a,
                       const __grid_constant__ CUtensorMap map_b,
                       const __grid_constant__ CUtensorMap map_c, int M, int N, int K, int group,
-                      uint64_t limit_ns, int* status, const SplitK sk, int b_evict_first) {
+                      uint64_t limit_ns, int* status, const SplitK sk, int evict_first) {
     using L = Layout<BN, BK, STAGES, B_MN, AR>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -156,8 +156,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     int stage_p = 0;
     uint32_t phase_p = 0;
     uint32_t issued = 0, issued_phase = 0;
-    // B read once (one M tile): its lines go first when L2 needs room.
+    // Operands read once (one tile row for B, one tile column for A): their
+    // lines go first when L2 needs room.  Bit 0: B, bit 1: A.
+    const bool b_evict_first = (evict_first & 1) != 0;
+    const bool a_evict_first = (evict_first & 2) != 0;
     const uint64_t b_policy = b_evict_first ? ptx::policy_evict_first() : 0ull;
+    const uint64_t a_policy = a_evict_first ? ptx::policy_evict_first() : 0ull;
     // Waits for the next stage to be free, then TMA-loads K block kb of the
     // tile at (m0, n0) into it.  False when the wait gave up.
     auto load_stage = [&](int kb, int m0, int n0) -> bool {
@@ -171,7 +175,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int kh = 0; kh < BK / 64; ++kh) {
             const int k0 = kb * BK + kh * 64;
-            ptx::tma_load_2d(sa + kh * L::kAHalf, &map_a, &full[stage_p], k0, m0);
+            if (a_evict_first)
+                ptx::tma_load_2d_hint(sa + kh * L::kAHalf, &map_a, &full[stage_p], k0, m0, a_policy);
+            else
+                ptx::tma_load_2d(sa + kh * L::kAHalf, &map_a, &full[stage_p], k0, m0);
             if constexpr (B_MN) {
 #pragma unroll
                 for (int nb = 0; nb < BN / 64; ++nb) {
@@ -616,7 +623,8 @@ int launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorM
     const int units = tiles * splits;
     int grid = units;
     if (persistent && !sk.cluster) grid = units < sms ? units : sms;
-    const int b_evict_first = (flags & KMCTS_FLAG_B_EVICT_FIRST) ? 1 : 0;
+    const int evict_first =
+        ((flags & KMCTS_FLAG_B_EVICT_FIRST) ? 1 : 0) | ((flags & KMCTS_FLAG_A_EVICT_FIRST) ? 2 : 0);
     if (sk.cluster) {
         cudaLaunchConfig_t lc = {};
         lc.gridDim = dim3(static_cast<unsigned>(grid));
@@ -630,11 +638,11 @@ int launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorM
         attr[0].val.clusterDim.z = 1;
         lc.attrs = attr;
         lc.numAttrs = 1;
-        if (cudaLaunchKernelEx(&lc, kernel, ma, mb, mc, M, N, K, group, limit_ns, status, sk, b_evict_first) !=
+        if (cudaLaunchKernelEx(&lc, kernel, ma, mb, mc, M, N, K, group, limit_ns, status, sk, evict_first) !=
             cudaSuccess)
             return KMCTS_EGEMM;
     } else {
-        kernel<<<grid, kThreads, smem, stream>>>(ma, mb, mc, M, N, K, group, limit_ns, status, sk, b_evict_first);
+        kernel<<<grid, kThreads, smem, stream>>>(ma, mb, mc, M, N, K, group, limit_ns, status, sk, evict_first);
     }
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return cudaGetLastError() == cudaSuccess ? KMCTS_OK : KMCTS_EGEMM;

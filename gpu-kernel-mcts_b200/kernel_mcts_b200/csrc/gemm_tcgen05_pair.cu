@@ -115,7 +115,7 @@ struct TailSplit {
     int splits;                    // split K: K ranges per tile
     int epoch;
     int mode;
-    int b_evict_first;  // B's loads at L2 evict-first priority (B read once: one pair-tile row)
+    int evict_first;  // L2 evict-first loads for operands read once or twice: bit 0 B, bit 1 A
 };
 
 struct Unit {
@@ -387,7 +387,10 @@ __global__ void __launch_bounds__(pair_threads<SLOTS>(), 1)
             uint32_t phase = 0;
             uint32_t issued = 0, issued_phase = 0;
             bool ok = true;
-            const uint64_t b_policy = tail.b_evict_first ? ptx::policy_evict_first() : 0ull;
+            const bool b_evict_first = (tail.evict_first & 1) != 0;
+            const bool a_evict_first = (tail.evict_first & 2) != 0;
+            const uint64_t b_policy = b_evict_first ? ptx::policy_evict_first() : 0ull;
+            const uint64_t a_policy = a_evict_first ? ptx::policy_evict_first() : 0ull;
             for (int u = 0; u < num_units && ok; ++u) {
                 const Unit w = unit_at(u);
                 const int m0 = w.m_blk * 256 + static_cast<int>(rank) * 128;
@@ -412,7 +415,10 @@ __global__ void __launch_bounds__(pair_threads<SLOTS>(), 1)
                     for (int kh = 0; kh < BK / 64; ++kh) {
                         const int k0 = kb * BK + kh * 64;
                         if (!quad) {
-                            ptx::tma_load_2d_pair(sa + kh * (128 * 128), &map_a, bar, k0, m0);
+                            if (a_evict_first)
+                                ptx::tma_load_2d_pair_hint(sa + kh * (128 * 128), &map_a, bar, k0, m0, a_policy);
+                            else
+                                ptx::tma_load_2d_pair(sa + kh * (128 * 128), &map_a, bar, k0, m0);
                         } else if (kh == pair_id) {
                             // This CTA's K half of its A rows; warp 6 copies
                             // it to the partner once it lands.
@@ -422,13 +428,13 @@ __global__ void __launch_bounds__(pair_threads<SLOTS>(), 1)
                         if constexpr (B_MN) {
                             for (int nb = 0; nb < b_cols / 64; ++nb) {
                                 uint8_t* dst = sb + (kh * (L::kHalfN / 64) + nb) * 8192;
-                                if (tail.b_evict_first)
+                                if (b_evict_first)
                                     ptx::tma_load_2d_pair_hint(dst, &map_b, bar, nb0 + nb * 64, k0, b_policy);
                                 else
                                     ptx::tma_load_2d_pair(dst, &map_b, bar, nb0 + nb * 64, k0);
                             }
                         } else {
-                            if (tail.b_evict_first)
+                            if (b_evict_first)
                                 ptx::tma_load_2d_pair_hint(sb + kh * (L::kHalfN * 128), mb, bar, k0, nb0, b_policy);
                             else
                                 ptx::tma_load_2d_pair(sb + kh * (L::kHalfN * 128), mb, bar, k0, nb0);
@@ -1112,7 +1118,7 @@ bool split_smem_configured() {
 template <int BN, int BK, int STAGES, bool B_MN, bool ALLGATHER = false, bool SLOTS = false>
 int launch_pair_variant_peers(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb_half,
                               const CUtensorMap& mc, int M, int N, int K, int group, bool persistent, int tail_req,
-                              int k_splits, bool b_evict_first, uint64_t limit_ns, cudaStream_t stream, int* status,
+                              int k_splits, int evict_first, uint64_t limit_ns, cudaStream_t stream, int* status,
                               const PeerOutputs& peers) {
     using L = PairLayout<BN, BK, STAGES, B_MN>;
     if (status == nullptr) status = default_status_ptr();
@@ -1139,7 +1145,7 @@ int launch_pair_variant_peers(const CUtensorMap& ma, const CUtensorMap& mb, cons
                                                                        group, 0, &plan);
         if (rc != KMCTS_OK) return rc;
     }
-    tail.b_evict_first = b_evict_first ? 1 : 0;
+    tail.evict_first = evict_first;
     tail.mode = plan.k_splits > 1                           ? kSplitK
                 : plan.tail_split == KMCTS_TAIL_STREAM_K ? kTailStreamK
                 : plan.tail_split == KMCTS_TAIL_SPLIT_K  ? kTailSplitK
@@ -1183,10 +1189,10 @@ int launch_pair_variant_peers(const CUtensorMap& ma, const CUtensorMap& mb, cons
 template <int BN, int BK, int STAGES, bool B_MN, bool SLOTS>
 int launch_pair_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb_half,
                         const CUtensorMap& mc, int M, int N, int K, int group, bool persistent, int tail_req,
-                        int k_splits, bool b_evict_first, uint64_t limit_ns, cudaStream_t stream, int* status) {
+                        int k_splits, int evict_first, uint64_t limit_ns, cudaStream_t stream, int* status) {
     const PeerOutputs none = {};
     return launch_pair_variant_peers<BN, BK, STAGES, B_MN, false, SLOTS>(ma, mb, mb_half, mc, M, N, K, group,
-                                                                         persistent, tail_req, k_splits, b_evict_first,
+                                                                         persistent, tail_req, k_splits, evict_first,
                                                                          limit_ns, stream, status, none);
 }
 
@@ -1196,7 +1202,7 @@ int plan_variant(int M, int N, int K, bool persistent, int tail, int group, int 
 }
 
 using PairLauncher = int (*)(const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, int,
-                             int, int, int, bool, int, int, bool, uint64_t, cudaStream_t, int*);
+                             int, int, int, bool, int, int, int, uint64_t, cudaStream_t, int*);
 
 using PairPlanner = int (*)(int, int, int, bool, int, int, int, kmcts_gemm_plan*);
 
@@ -1277,9 +1283,9 @@ int launch_pair_allgather(const CUtensorMap& ma, const CUtensorMap& mb, const CU
     if (b_layout == KMCTS_B_ROW)
         return launch_pair_variant_peers<256, 128, 3, true, true>(ma, mb, mb_half, mc, M, N_shard, K,
                                                                   cfg.raster_group, cfg.persistent != 0, split, 0,
-                                                                  false, limit_ns, stream, status, peers);
+                                                                  0, limit_ns, stream, status, peers);
     return launch_pair_variant_peers<256, 128, 3, false, true>(ma, mb, mb_half, mc, M, N_shard, K, cfg.raster_group,
-                                                               cfg.persistent != 0, split, 0, false, limit_ns, stream,
+                                                               cfg.persistent != 0, split, 0, 0, limit_ns, stream,
                                                                status, peers);
 }
 
@@ -1289,7 +1295,9 @@ int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap&
     const PairVariant* v = find_pair_variant(cfg, b_layout);
     if (!v) return KMCTS_ENOTSUP;
     return v->fn(ma, mb, mb_half, mc, M, N, K, cfg.raster_group, cfg.persistent != 0, requested_tail(cfg.flags),
-                 cfg.k_splits, (cfg.flags & KMCTS_FLAG_B_EVICT_FIRST) != 0, limit_ns, stream, status);
+                 cfg.k_splits,
+                 ((cfg.flags & KMCTS_FLAG_B_EVICT_FIRST) ? 1 : 0) | ((cfg.flags & KMCTS_FLAG_A_EVICT_FIRST) ? 2 : 0),
+                 limit_ns, stream, status);
 }
 
 }  // namespace kmcts

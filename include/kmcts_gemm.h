@@ -76,6 +76,9 @@ extern "C" {
  * Results are unchanged; only the cache policy differs.  The fused
  * all-gather ignores it. */
 #define KMCTS_FLAG_B_EVICT_FIRST 8
+/* The same policy on A's loads, for shapes whose N fits one or two tile
+ * columns (A read once or twice).  Results are unchanged. */
+#define KMCTS_FLAG_A_EVICT_FIRST 128
 /* tile_m 32 (M <= 32), tile_n 128, tile_k 64 with 10 stages or 128 with 5:
  * the operands swap roles, C^T = B^T * A^T, so B's 128-column tiles are the
  * MMA's 128 rows and A's M rows its N (16 or 32): no tensor work is padding.

@@ -665,6 +665,32 @@ def test_cta_pair_b_evict_first_same_bits(cuda_device, layout, shape, cfg):
             nm: getattr(sel, nm) for nm, _ in sel._fields_})))
 
 
+@pytest.mark.parametrize("layout", ["col", "row"])
+@pytest.mark.parametrize("shape,cfg", [
+    ((2048, 256, 4096), dict(tile_m=128, cluster_m=1, tile_n=128, tile_k=128, stages=3)),
+    ((2048, 256, 8192), dict(tile_m=128, cluster_m=1, tile_n=128, tile_k=128, stages=3, k_splits=4)),
+    ((3000, 512, 2048), {}),  # CTA pair, ragged M
+])
+def test_a_evict_first_same_bits(cuda_device, layout, shape, cfg):
+    """A's loads at L2 evict-first priority (selected when N fits one or two
+    tile columns) change the cache policy only: exact on integer inputs, the
+    same bits as without the hint on N(0,1) inputs."""
+    m, n, k = shape
+    base = dict(kernel=_native.KERNEL_TCGEN05, **cfg)
+    a_t, b_t = oracle.integer_inputs(m, n, k, seed=12)
+    expect = oracle.torch_bits(oracle.torch_reference(a_t, b_t))
+    c = run(a_t.cuda(), b_for(layout, b_t.cuda()), layout, flags=_native.FLAG_A_EVICT_FIRST, **base)
+    np.testing.assert_array_equal(bits_of(c), expect)
+    a_t, b_t = oracle.randn_inputs(m, n, k, seed=6, b_layout=layout)
+    a, b = a_t.cuda(), b_t.cuda()
+    hinted = run(a, b, layout, flags=_native.FLAG_A_EVICT_FIRST | _native.FLAG_B_EVICT_FIRST, **base)
+    plain = run(a, b, layout, **base)
+    assert torch.equal(hinted.view(torch.int16), plain.view(torch.int16))
+    sel = _native.select_config(m, n, k, kg.layout_code(layout))
+    columns = -(-n // sel.tile_n)
+    assert bool(sel.flags & _native.FLAG_A_EVICT_FIRST) == (columns <= 2), (sel.tile_n, columns)
+
+
 HALF = [(128, 128, 4), (128, 128, 3), (64, 128, 6)]
 
 

@@ -101,6 +101,13 @@ def test_select_config_splits_k_for_skinny_shapes():
         sel = km.select_config(*shape, km.B_ROW)
         assert sel.tile_m == 256 and sel.flags & _native.FLAG_B_EVICT_FIRST, shape
     assert not km.select_config(1024, 16384, 4096, km.B_ROW).flags & _native.FLAG_B_EVICT_FIRST
+    # One or two tile columns: A streams at evict-first priority; N <= 128
+    # leaves the pair (half of its 256-column tile would be empty).
+    tall = km.select_config(16384, 128, 4096, km.B_ROW)
+    assert (tall.tile_m, tall.tile_n) == (128, 128) and tall.flags & _native.FLAG_A_EVICT_FIRST
+    narrow_pair = km.select_config(28672, 256, 4096, km.B_ROW)
+    assert narrow_pair.tile_m == 256 and narrow_pair.flags & _native.FLAG_A_EVICT_FIRST
+    assert not km.select_config(4096, 4096, 4096, km.B_ROW).flags & _native.FLAG_A_EVICT_FIRST
     assert not km.select_config(4096, 4096, 4096, km.B_ROW).flags & _native.FLAG_B_EVICT_FIRST
     # ... not at K = 4096: one CTA per 128 x 256 tile.
     assert km.select_config(2048, 1024, 4096, km.B_ROW).tile_m == 128
