@@ -160,7 +160,8 @@ int kmcts_default_config(kmcts_gemm_config* cfg);
  * 128 x 256 tile while those fill them (the default again from K = 4096),
  * else one CTA per 128 x 128 tile.  Few tiles over a long K get split K; one-CTA
  * schedules for M <= 128 and pair schedules for M <= 512 (one or two tile
- * rows) add KMCTS_FLAG_B_EVICT_FIRST.  Every
+ * rows) add KMCTS_FLAG_B_EVICT_FIRST, schedules whose tiles span N in one or
+ * two columns KMCTS_FLAG_A_EVICT_FIRST; N <= 128 takes one CTA per tile.  Every
  * schedule gives results within the parity criterion and bit-exact ones on
  * integer inputs.  Returns KMCTS_OK or KMCTS_EINVAL. */
 int kmcts_select_config(int M, int N, int K, int b_layout, kmcts_gemm_config* cfg);
