@@ -53,6 +53,7 @@ def parse_args() -> argparse.Namespace:
     p.add_argument("--eval-repeat", type=int, default=3)
     p.add_argument("--no-sharded", action="store_true", help="skip the sharded 8192x28672x8192 GEMM")
     p.add_argument("--no-skinny", action="store_true", help="skip the HBM-bound skinny shapes")
+    p.add_argument("--no-shapes", action="store_true", help="skip the one-shape-per-class comparison")
     return p.parse_args()
 
 
@@ -289,6 +290,67 @@ def time_interleaved(fns, steps: int, stream, flush) -> list[list[float]]:
 
 
 SKINNY_SHAPES = ((16, 8192, 8192), (128, 16384, 4096))
+
+# One shape per class of the library's schedule selection, beside same-run
+# cuBLAS: where each class stands (the mid-size class is the one behind).
+SHAPE_CLASSES = (
+    ("M <= 32, long K: K splits added in shared memory", (16, 1024, 16384)),
+    ("33 <= M <= 64: 64 rows of A per tile", (64, 8192, 8192)),
+    ("one row of pair tiles: B at L2 evict-first", (256, 16384, 4096)),
+    ("two rows of pair tiles: B at L2 evict-first", (512, 8192, 8192)),
+    ("N <= 128: one CTA per 128 x 128 tile, A at L2 evict-first", (16384, 128, 4096)),
+    ("two columns of pair tiles: A at L2 evict-first", (28672, 256, 4096)),
+    ("rectangular, CTA pair", (8192, 4096, 4096)),
+    ("mid-size, few tiles over a long K", (512, 512, 8192)),
+)
+
+FLAG_NAMES = (("B_EVICT_FIRST", 8), ("A_EVICT_FIRST", 128), ("SPLIT_CLUSTER", 64), ("SWAP_AB", 16))
+
+
+def shape_classes(device, stream, flush, steps: int = 40) -> list[dict]:
+    """The NULL-config call (the library's selection) on one shape per class
+    against same-run cuBLAS, L2 flushed, interleaved; B row-major, N(0,1)
+    seed 0.  `speedup` = cuBLAS mean / our mean (above 1: ahead)."""
+    import torch
+
+    from kernel_mcts_b200 import _native
+    from kernel_mcts_b200 import gemm as kg
+
+    rows = []
+    for name, (m, n, k) in SHAPE_CLASSES:
+        g = torch.Generator(device=device).manual_seed(0)
+        a = torch.randn((m, k), generator=g, device=device).to(torch.bfloat16)
+        b = torch.randn((k, n), generator=g, device=device).to(torch.bfloat16)
+        c = torch.empty((m, n), dtype=torch.bfloat16, device=device)
+        c_ref = torch.empty_like(c)
+        status = torch.zeros(1, dtype=torch.int32, device=device)
+        cfg = _native.select_config(m, n, k, _native.B_ROW)
+        ours = kg.PreparedGemm(a, b, c, b_layout="row", config=cfg, stream=stream, status=status)
+
+        def cublas():
+            torch.matmul(a, b, out=c_ref)
+
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                ours.launch()
+                cublas()
+        ours_us, cublas_us = time_interleaved([ours.launch, cublas], steps, stream, flush)
+        if int(status.item()) != 0:
+            raise RuntimeError(f"device status {int(status.item()):#x}")
+        parity = kg.compare(c, c_ref, stream=stream)
+        mean, mean_ref = statistics.fmean(ours_us), statistics.fmean(cublas_us)
+        rows.append({
+            "class": name, "shape": [m, n, k],
+            "schedule": {"tile_m": cfg.tile_m, "tile_n": cfg.tile_n, "tile_k": cfg.tile_k, "stages": cfg.stages,
+                         "k_splits": max(1, cfg.k_splits),
+                         "flags": [nm for nm, bit in FLAG_NAMES if cfg.flags & bit]},
+            "median_us": statistics.median(ours_us), "cublas_median_us": statistics.median(cublas_us),
+            "mean_us": mean, "cublas_mean_us": mean_ref, "speedup": mean_ref / mean,
+            "tflops": 2.0 * m * n * k / (mean * 1e-6) / 1e12,
+            "parity_vs_cublas": {"success": parity.success, "max_ulp": parity.max_ulp},
+        })
+        del a, b, c, c_ref
+    return rows
 
 
 def skinny_gemms(device, stream, flush, steps: int = 60) -> dict:
@@ -625,6 +687,9 @@ def run_ours(args: argparse.Namespace) -> None:
     skinny = None
     if not args.no_skinny:
         skinny = skinny_gemms(device, stream, flush)
+    classes = None
+    if not args.no_shapes:
+        classes = shape_classes(device, stream, flush)
 
     evaluations = None
     if not args.no_evals:
@@ -699,6 +764,7 @@ def run_ours(args: argparse.Namespace) -> None:
             "evaluations": evaluations,
             "sharded_gemm": sharded,
             "skinny_hbm": skinny,
+            "shape_classes": classes,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -117,13 +117,17 @@ __device__ __forceinline__ int recv_chunk(int slot, int quarter, int c, int rows
     return ((slot * (rows / 32) + quarter) * (BN / 64) + c) * 16 * 32;
 }
 
-template <int BN, int BK, int STAGES, bool B_MN, int AR>
+// FEAT instantiations carry the cache-hinted loads and the cluster split K;
+// the others compile without them, so the common schedules pay nothing for
+// either (the launcher picks FEAT only when the schedule asks for one).
+template <int BN, int BK, int STAGES, bool B_MN, int AR, bool FEAT = false>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_tcgen05(const __grid_constant__ CUtensorMap map_a,
                       const __grid_constant__ CUtensorMap map_b,
                       const __grid_constant__ CUtensorMap map_c, int M, int N, int K, int group,
                       uint64_t limit_ns, int* status, const SplitK sk, int evict_first) {
     using L = Layout<BN, BK, STAGES, B_MN, AR>;
+    const int cluster_mode = FEAT ? sk.cluster : 0;  // compile-time 0 without FEAT
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~uintptr_t(1023));
@@ -140,7 +144,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Cluster split K's receive buffer: past the barriers (which take well
     // under 1 KB of the reserve; the launch adds its size to the shared
     // memory), or the pipeline stages.
-    float4* recv = reinterpret_cast<float4*>(sk.cluster == kClusterStages ? smem : smem + L::kBarrierOffset + 1024);
+    float4* recv = reinterpret_cast<float4*>(cluster_mode == kClusterStages ? smem : smem + L::kBarrierOffset + 1024);
 
     if (status == nullptr) status = &g_default_status;
     const int warp = threadIdx.x / 32;
@@ -158,8 +162,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t issued = 0, issued_phase = 0;
     // Operands read once (one tile row for B, one tile column for A): their
     // lines go first when L2 needs room.  Bit 0: B, bit 1: A.
-    const bool b_evict_first = (evict_first & 1) != 0;
-    const bool a_evict_first = (evict_first & 2) != 0;
+    const bool b_evict_first = FEAT && (evict_first & 1) != 0;
+    const bool a_evict_first = FEAT && (evict_first & 2) != 0;
     const uint64_t b_policy = b_evict_first ? ptx::policy_evict_first() : 0ull;
     const uint64_t a_policy = a_evict_first ? ptx::policy_evict_first() : 0ull;
     // Waits for the next stage to be free, then TMA-loads K block kb of the
@@ -215,7 +219,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         ptx::mbar_init(drain, 1);
         // Every lane of every epilogue warp of each sending rank arrives once.
-        ptx::mbar_init(recv_full, sk.cluster ? static_cast<uint32_t>((splits - 1) * kEpilogueWarps * 32) : 1u);
+        ptx::mbar_init(recv_full, cluster_mode ? static_cast<uint32_t>((splits - 1) * kEpilogueWarps * 32) : 1u);
         ptx::mbar_init(go_bar, 1);
         *abort = 0;
         *no_abort = 0;
@@ -232,7 +236,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Cluster split K: every thread arrives on the cluster barrier once rank
     // 0's receive barrier is initialised; a thread waits on it before its
     // first access to another CTA (or at the end), so no CTA idles here.
-    if (sk.cluster) ptx::cluster_arrive();
+    if (cluster_mode) ptx::cluster_arrive();
     ptx::tc_fence_before();
     __syncthreads();
     ptx::tc_fence_after();
@@ -332,11 +336,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         int chunk_count = 0;
         // Cluster split K: rank 0's receive buffer and barrier as this CTA
         // addresses them (the same offsets in every CTA of the launch).
-        const uint32_t recv_remote = sk.cluster ? ptx::mapa_shared(ptx::smem_addr(recv), 0) : 0u;
-        const uint32_t recv_full_remote = sk.cluster ? ptx::mapa_shared(ptx::smem_addr(recv_full), 0) : 0u;
+        const uint32_t recv_remote = cluster_mode ? ptx::mapa_shared(ptx::smem_addr(recv), 0) : 0u;
+        const uint32_t recv_full_remote = cluster_mode ? ptx::mapa_shared(ptx::smem_addr(recv_full), 0) : 0u;
         // Rank 0's receive barrier is initialised (every thread of the
         // cluster arrived after set-up) before any store or arrive reaches it.
-        if (sk.cluster) ptx::cluster_wait();
+        if (cluster_mode) ptx::cluster_wait();
         bool got_recv = false;  // rank 0: the other ranks' values are all here
         for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++local) {
             const int t = u / splits, s = u % splits;
@@ -345,8 +349,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int n0 = tc.n_blk * BN;
             const int acc = local & 1;
             const uint32_t acc_phase = (local >> 1) & 1;
-            const bool sender = sk.cluster && s != 0;
-            const bool receiver = sk.cluster && s == 0;
+            const bool sender = cluster_mode && s != 0;
+            const bool receiver = cluster_mode && s == 0;
             bool ok = ptx::mbar_wait(&tmem_full[acc], acc_phase, limit_ns, abort);
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) {
@@ -354,7 +358,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 break;
             }
             ptx::tc_fence_after();
-            if (receiver && sk.cluster == kClusterStages && e == 0 && lane == 0) {
+            if (receiver && cluster_mode == kClusterStages && e == 0 && lane == 0) {
                 // Every UMMA of this CTA has completed, so no stage is read
                 // any more (its one unit's loads were all consumed): the
                 // other ranks may store into them.
@@ -372,7 +376,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (sender) ptx::mbar_arrive_release_cluster(recv_full_remote);
                 continue;
             }
-            if (sender && sk.cluster == kClusterStages) {
+            if (sender && cluster_mode == kClusterStages) {
                 bool go = ptx::mbar_wait_cluster(go_bar, 0, limit_ns, abort);
                 go = __all_sync(0xffffffffu, go);
                 if (!go) {
@@ -517,16 +521,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Rank 0 leaves only after the other ranks' stores into its buffer
         // are released, also when one of its own waits gave up (a rank that
         // gave up itself never stores: this wait then ends at its bound).
-        if (sk.cluster && blockIdx.x % splits == 0 && !got_recv)
+        if (cluster_mode && blockIdx.x % splits == 0 && !got_recv)
             ptx::mbar_wait_cluster(recv_full, 0, drain_limit(limit_ns), no_abort);
     }
 
-    if (sk.cluster && warp < 2) ptx::cluster_wait();  // pairs this thread's arrive after set-up
+    if (cluster_mode && warp < 2) ptx::cluster_wait();  // pairs this thread's arrive after set-up
     ptx::tc_fence_before();
     __syncthreads();
     // Receiving in its stages, rank 0 signalled the other ranks' barriers and
     // they stored into its shared memory: no CTA leaves before all are done.
-    if (sk.cluster == kClusterStages) ptx::cluster_sync();
+    if (cluster_mode == kClusterStages) ptx::cluster_sync();
     if (warp == 1) {
         ptx::tc_fence_after();
         ptx::tmem_dealloc(tmem_base, L::kTmemCols);
@@ -591,7 +595,8 @@ int launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorM
                    int N, int K, int group, bool persistent, int k_splits, int flags,
                    uint64_t limit_ns, cudaStream_t stream, int* status) {
     using L = Layout<BN, BK, STAGES, B_MN, AR>;
-    auto kernel = gemm_bf16_tcgen05<BN, BK, STAGES, B_MN, AR>;
+    auto plain_kernel = gemm_bf16_tcgen05<BN, BK, STAGES, B_MN, AR, false>;
+    auto feat_kernel = gemm_bf16_tcgen05<BN, BK, STAGES, B_MN, AR, true>;
     // The shared-memory opt-in is per device; set it once on each, to the
     // most any launch of this variant asks for (a cluster split K's receive
     // buffer comes on top of the variant's own layout).
@@ -603,8 +608,10 @@ int launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorM
     {
         std::lock_guard<std::mutex> lock(mu);
         if (!configured[device]) {
-            if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem) !=
-                cudaSuccess)
+            if (cudaFuncSetAttribute(plain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem) !=
+                    cudaSuccess ||
+                cudaFuncSetAttribute(feat_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem) !=
+                    cudaSuccess)
                 return KMCTS_EGEMM;
             configured[device] = true;
         }
@@ -625,6 +632,7 @@ int launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorM
     if (persistent && !sk.cluster) grid = units < sms ? units : sms;
     const int evict_first =
         ((flags & KMCTS_FLAG_B_EVICT_FIRST) ? 1 : 0) | ((flags & KMCTS_FLAG_A_EVICT_FIRST) ? 2 : 0);
+    auto kernel = (evict_first || sk.cluster) ? feat_kernel : plain_kernel;
     if (sk.cluster) {
         cudaLaunchConfig_t lc = {};
         lc.gridDim = dim3(static_cast<unsigned>(grid));

@@ -283,7 +283,11 @@ constexpr int pair_threads() {
 // SPLITK instantiations run the split-K schedule (tail.mode kSplitK) and
 // nothing else; the others never see it, so their code is the same as
 // without split K.
-template <int BN, int BK, int STAGES, bool B_MN, bool ALLGATHER, bool SLOTS, bool SPLITK>
+// EF instantiations issue every operand load with an L2 cache policy
+// (evict-first for the operands tail.evict_first names, normal for the
+// other); the others issue plain loads, so the choice costs the common
+// schedule nothing.
+template <int BN, int BK, int STAGES, bool B_MN, bool ALLGATHER, bool SLOTS, bool SPLITK, bool EF = false>
 __global__ void __launch_bounds__(pair_threads<SLOTS>(), 1)
     gemm_bf16_tcgen05_pair(const __grid_constant__ CUtensorMap map_a,
                            const __grid_constant__ CUtensorMap map_b,
@@ -387,10 +391,11 @@ __global__ void __launch_bounds__(pair_threads<SLOTS>(), 1)
             uint32_t phase = 0;
             uint32_t issued = 0, issued_phase = 0;
             bool ok = true;
-            const bool b_evict_first = (tail.evict_first & 1) != 0;
-            const bool a_evict_first = (tail.evict_first & 2) != 0;
-            const uint64_t b_policy = b_evict_first ? ptx::policy_evict_first() : 0ull;
-            const uint64_t a_policy = a_evict_first ? ptx::policy_evict_first() : 0ull;
+            uint64_t a_policy = 0, b_policy = 0;
+            if constexpr (EF) {
+                b_policy = (tail.evict_first & 1) ? ptx::policy_evict_first() : ptx::policy_evict_normal();
+                a_policy = (tail.evict_first & 2) ? ptx::policy_evict_first() : ptx::policy_evict_normal();
+            }
             for (int u = 0; u < num_units && ok; ++u) {
                 const Unit w = unit_at(u);
                 const int m0 = w.m_blk * 256 + static_cast<int>(rank) * 128;
@@ -415,7 +420,7 @@ __global__ void __launch_bounds__(pair_threads<SLOTS>(), 1)
                     for (int kh = 0; kh < BK / 64; ++kh) {
                         const int k0 = kb * BK + kh * 64;
                         if (!quad) {
-                            if (a_evict_first)
+                            if constexpr (EF)
                                 ptx::tma_load_2d_pair_hint(sa + kh * (128 * 128), &map_a, bar, k0, m0, a_policy);
                             else
                                 ptx::tma_load_2d_pair(sa + kh * (128 * 128), &map_a, bar, k0, m0);
@@ -428,13 +433,13 @@ __global__ void __launch_bounds__(pair_threads<SLOTS>(), 1)
                         if constexpr (B_MN) {
                             for (int nb = 0; nb < b_cols / 64; ++nb) {
                                 uint8_t* dst = sb + (kh * (L::kHalfN / 64) + nb) * 8192;
-                                if (b_evict_first)
+                                if constexpr (EF)
                                     ptx::tma_load_2d_pair_hint(dst, &map_b, bar, nb0 + nb * 64, k0, b_policy);
                                 else
                                     ptx::tma_load_2d_pair(dst, &map_b, bar, nb0 + nb * 64, k0);
                             }
                         } else {
-                            if (b_evict_first)
+                            if constexpr (EF)
                                 ptx::tma_load_2d_pair_hint(sb + kh * (L::kHalfN * 128), mb, bar, k0, nb0, b_policy);
                             else
                                 ptx::tma_load_2d_pair(sb + kh * (L::kHalfN * 128), mb, bar, k0, nb0);
@@ -1096,17 +1101,18 @@ bool split_workspace(cudaStream_t stream, int tiles, int splits, TailSplit* out)
     return true;
 }
 
-// The split-K instantiation's shared-memory opt-in (per device, once); its
-// occupancy is the plain one's (same shared memory and block).
-template <int BN, int BK, int STAGES, bool B_MN>
-bool split_smem_configured() {
+// The shared-memory opt-in of a split-K or cache-hinted instantiation (per
+// device, once); its occupancy is the plain one's (same shared memory and
+// block).
+template <int BN, int BK, int STAGES, bool B_MN, bool SPLITK, bool EF>
+bool plain_smem_configured() {
     static std::mutex mu;
     static bool done[kMaxDevices] = {};
     int device = 0;
     if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kMaxDevices) return false;
     std::lock_guard<std::mutex> lock(mu);
     if (!done[device]) {
-        if (cudaFuncSetAttribute(gemm_bf16_tcgen05_pair<BN, BK, STAGES, B_MN, false, false, true>,
+        if (cudaFuncSetAttribute(gemm_bf16_tcgen05_pair<BN, BK, STAGES, B_MN, false, false, SPLITK, EF>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  PairLayout<BN, BK, STAGES, B_MN>::kSmemBytes) != cudaSuccess)
             return false;
@@ -1171,11 +1177,30 @@ int launch_pair_variant_peers(const CUtensorMap& ma, const CUtensorMap& mb, cons
     config.numAttrs = SLOTS ? 2 : 1;
     cudaError_t err;
     if constexpr (!SLOTS && !ALLGATHER) {
-        if (tail.mode == kSplitK) {
-            auto split_kernel = gemm_bf16_tcgen05_pair<BN, BK, STAGES, B_MN, false, false, true>;
-            if (!split_smem_configured<BN, BK, STAGES, B_MN>()) return KMCTS_EGEMM;
-            err = cudaLaunchKernelEx(&config, split_kernel, ma, mb, mb_half, mc, M, N, K, group, plan.full_tiles,
-                                     limit_ns, status, peers, tail);
+        // Split K, and cache-hinted loads, run their own instantiations.
+        const bool split = tail.mode == kSplitK;
+        if (split || evict_first) {
+            bool configured = false;
+            if (split && evict_first) {
+                configured = plain_smem_configured<BN, BK, STAGES, B_MN, true, true>();
+                if (configured)
+                    err = cudaLaunchKernelEx(&config, gemm_bf16_tcgen05_pair<BN, BK, STAGES, B_MN, false, false, true, true>,
+                                             ma, mb, mb_half, mc, M, N, K, group, plan.full_tiles, limit_ns, status,
+                                             peers, tail);
+            } else if (split) {
+                configured = plain_smem_configured<BN, BK, STAGES, B_MN, true, false>();
+                if (configured)
+                    err = cudaLaunchKernelEx(&config, gemm_bf16_tcgen05_pair<BN, BK, STAGES, B_MN, false, false, true, false>,
+                                             ma, mb, mb_half, mc, M, N, K, group, plan.full_tiles, limit_ns, status,
+                                             peers, tail);
+            } else {
+                configured = plain_smem_configured<BN, BK, STAGES, B_MN, false, true>();
+                if (configured)
+                    err = cudaLaunchKernelEx(&config, gemm_bf16_tcgen05_pair<BN, BK, STAGES, B_MN, false, false, false, true>,
+                                             ma, mb, mb_half, mc, M, N, K, group, plan.full_tiles, limit_ns, status,
+                                             peers, tail);
+            }
+            if (!configured) return KMCTS_EGEMM;
             g_launches.fetch_add(1, std::memory_order_relaxed);
             return err == cudaSuccess ? KMCTS_OK : KMCTS_EGEMM;
         }

@@ -112,6 +112,14 @@ __device__ __forceinline__ uint64_t policy_evict_first() {
     return policy;
 }
 
+// The default L2 priority as an explicit policy, for loads issued with a
+// cache hint whose operand is not read once.
+__device__ __forceinline__ uint64_t policy_evict_normal() {
+    uint64_t policy;
+    asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(policy));
+    return policy;
+}
+
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int32_t c0,
                                              int32_t c1) {
     asm volatile(
