@@ -117,17 +117,20 @@ __device__ __forceinline__ int recv_chunk(int slot, int quarter, int c, int rows
     return ((slot * (rows / 32) + quarter) * (BN / 64) + c) * 16 * 32;
 }
 
-// FEAT instantiations carry the cache-hinted loads and the cluster split K;
-// the others compile without them, so the common schedules pay nothing for
-// either (the launcher picks FEAT only when the schedule asks for one).
-template <int BN, int BK, int STAGES, bool B_MN, int AR, bool FEAT = false>
+// FEAT selects what an instantiation carries: bit 0 the cache-hinted loads,
+// bit 1 the cluster split K.  Code a schedule does not use is compiled out
+// (a runtime branch in the producer's loop costs the common schedules 1-2
+// us per launch); the launcher picks the smallest instantiation that serves.
+constexpr int kFeatHints = 1, kFeatCluster = 2;
+
+template <int BN, int BK, int STAGES, bool B_MN, int AR, int FEAT = 0>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_tcgen05(const __grid_constant__ CUtensorMap map_a,
                       const __grid_constant__ CUtensorMap map_b,
                       const __grid_constant__ CUtensorMap map_c, int M, int N, int K, int group,
                       uint64_t limit_ns, int* status, const SplitK sk, int evict_first) {
     using L = Layout<BN, BK, STAGES, B_MN, AR>;
-    const int cluster_mode = FEAT ? sk.cluster : 0;  // compile-time 0 without FEAT
+    const int cluster_mode = (FEAT & kFeatCluster) ? sk.cluster : 0;  // compile-time 0 otherwise
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~uintptr_t(1023));
@@ -162,8 +165,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t issued = 0, issued_phase = 0;
     // Operands read once (one tile row for B, one tile column for A): their
     // lines go first when L2 needs room.  Bit 0: B, bit 1: A.
-    const bool b_evict_first = FEAT && (evict_first & 1) != 0;
-    const bool a_evict_first = FEAT && (evict_first & 2) != 0;
+    const bool b_evict_first = (FEAT & kFeatHints) && (evict_first & 1) != 0;
+    const bool a_evict_first = (FEAT & kFeatHints) && (evict_first & 2) != 0;
     const uint64_t b_policy = b_evict_first ? ptx::policy_evict_first() : 0ull;
     const uint64_t a_policy = a_evict_first ? ptx::policy_evict_first() : 0ull;
     // Waits for the next stage to be free, then TMA-loads K block kb of the
@@ -595,8 +598,9 @@ int launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorM
                    int N, int K, int group, bool persistent, int k_splits, int flags,
                    uint64_t limit_ns, cudaStream_t stream, int* status) {
     using L = Layout<BN, BK, STAGES, B_MN, AR>;
-    auto plain_kernel = gemm_bf16_tcgen05<BN, BK, STAGES, B_MN, AR, false>;
-    auto feat_kernel = gemm_bf16_tcgen05<BN, BK, STAGES, B_MN, AR, true>;
+    auto plain_kernel = gemm_bf16_tcgen05<BN, BK, STAGES, B_MN, AR, 0>;
+    auto hint_kernel = gemm_bf16_tcgen05<BN, BK, STAGES, B_MN, AR, kFeatHints>;
+    auto cluster_kernel = gemm_bf16_tcgen05<BN, BK, STAGES, B_MN, AR, kFeatHints | kFeatCluster>;
     // The shared-memory opt-in is per device; set it once on each, to the
     // most any launch of this variant asks for (a cluster split K's receive
     // buffer comes on top of the variant's own layout).
@@ -610,7 +614,9 @@ int launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorM
         if (!configured[device]) {
             if (cudaFuncSetAttribute(plain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem) !=
                     cudaSuccess ||
-                cudaFuncSetAttribute(feat_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem) !=
+                cudaFuncSetAttribute(hint_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem) !=
+                    cudaSuccess ||
+                cudaFuncSetAttribute(cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem) !=
                     cudaSuccess)
                 return KMCTS_EGEMM;
             configured[device] = true;
@@ -632,7 +638,7 @@ int launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorM
     if (persistent && !sk.cluster) grid = units < sms ? units : sms;
     const int evict_first =
         ((flags & KMCTS_FLAG_B_EVICT_FIRST) ? 1 : 0) | ((flags & KMCTS_FLAG_A_EVICT_FIRST) ? 2 : 0);
-    auto kernel = (evict_first || sk.cluster) ? feat_kernel : plain_kernel;
+    auto kernel = sk.cluster ? cluster_kernel : evict_first ? hint_kernel : plain_kernel;
     if (sk.cluster) {
         cudaLaunchConfig_t lc = {};
         lc.gridDim = dim3(static_cast<unsigned>(grid));
