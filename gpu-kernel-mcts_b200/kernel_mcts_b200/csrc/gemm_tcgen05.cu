@@ -17,6 +17,11 @@
 //               round to BF16 (RNE), stage through swizzled shared memory and
 //               TMA-store.  Two TMEM accumulators let the epilogue of tile i
 //               overlap the main loop of tile i+1.
+// Skinny shapes stage only 32 or 64 rows of A (AR), leaving shared memory for
+// more of B.  Split K runs each tile as k_splits K ranges whose FP32 values
+// meet either in a per-stream workspace (the last unit to arrive adds them)
+// or, as one thread-block cluster per tile, in split 0's shared memory.
+// Operands read once can stream through L2 at evict-first priority.
 // Every wait is bounded (limit_ns); on timeout the kernel records
 // KMCTS_ETIMEOUT in *status, drains its own copies and MMAs, frees TMEM and
 // returns.  No TMA multicast is used.

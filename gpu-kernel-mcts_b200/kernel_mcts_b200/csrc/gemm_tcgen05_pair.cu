@@ -21,6 +21,8 @@
 // The slot schedule (cluster_n 2, 256 threads) runs two such pairs in a 4-CTA
 // cluster that share their rows of A: warps 6 and 7 exchange K halves of A
 // between the pairs over distributed shared memory (see "A exchange" below).
+// EF instantiations load A and B with an L2 cache policy (evict-first for an
+// operand read by one or two rows or columns of pair tiles).
 // Every wait is bounded; see gemm_tcgen05.cu for the failure protocol.
 #include <cstring>
 #include <mutex>
