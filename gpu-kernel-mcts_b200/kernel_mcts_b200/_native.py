@@ -49,6 +49,9 @@ FLAG_B_EVICT_FIRST = 8
 FLAG_SWAP_AB = 16
 FLAG_SPLIT_CLUSTER = 64
 FLAG_A_EVICT_FIRST = 128
+FLAG_SPLIT_SCATTER = 256
+
+SPLIT_WORKSPACE, SPLIT_CLUSTER, SPLIT_SCATTER = 0, 1, 2
 
 TAIL_NONE = 0
 TAIL_SPLIT_N = 1
@@ -135,6 +138,7 @@ class GemmPlan(ctypes.Structure):
         ("tail_clusters", ctypes.c_int32),
         ("tail_segments", ctypes.c_int32),
         ("k_splits", ctypes.c_int32),
+        ("split_reduce", ctypes.c_int32),
     ]
 
     def as_dict(self) -> dict[str, int]:

@@ -104,6 +104,53 @@ int choose_splits(long long tiles, int K, int sms) {
     return splits >= 2 ? static_cast<int>(splits) : 0;
 }
 
+// Resident clusters of `splits` one-CTA-per-SM CTAs as the occupancy
+// calculator placed them on a 148-SM B200 (GPC by GPC), for when it cannot
+// be asked (no device): 74, 45, 33, 26, 22, 15, 15 for 2..8.
+int fallback_cluster_capacity(int splits, int sms) {
+    static const int kB200[9] = {0, 148, 74, 45, 33, 26, 22, 15, 15};
+    return splits >= 1 && splits <= 8 ? kB200[splits] * sms / 148 : 0;
+}
+
+// Few 128 x 128 tiles over a long K: each tile as S K ranges on one cluster
+// whose CTAs add up one share of the tile each (KMCTS_FLAG_SPLIT_SCATTER).
+// S is the most splits that keep every unit on its own SM, every cluster
+// resident at once, and K ranges of at least 512 (at most 8); two splits
+// only from K = 4096 (below, the exchange costs more than the second SM
+// saves: 1024 x 1024 x 2048 18.5 us against 17.4 unsplit).  Stages are
+// 64 deep x 4 where a short range or eight splits leave room to receive
+// outside the stages, else 128 deep x 3.  Measured, L2 flushed (workspace
+// split -> scatter, cuBLAS): 512 x 512 x 8192 25.6 -> 22.7 us (19.0),
+// 384 x 384 x 8192 25.6 -> 20.7 (17.9), 256 x 512 x 16384 31.5 -> 25.8
+// (23.3), 1024 x 1024 x 8192 32.6 -> 31.0 (26.1), 2048 x 256 x 8192 27.2 ->
+// 25.3 (21.8), 512 x 1024 x 4096 22.9 -> 20.1 (14.2), and unsplit before:
+// 300 x 1000 x 2048 18.7 -> 16.7 (11.2).  Returns false when no split fits.
+bool scatter_schedule(long long tiles, int K, int b_layout, int sms, kmcts_gemm_config* cfg) {
+    if (tiles <= 0 || 2 * tiles > sms) return false;
+    int s = static_cast<int>(sms / tiles);
+    if (s > 8) s = 8;
+    const int max_by_k = K / 512;
+    if (s > max_by_k) s = max_by_k;
+    for (; s >= 2; --s) {
+        if (s == 2 && K < 4096) break;
+        kmcts_gemm_config c = *cfg;
+        c.tile_m = 128;
+        c.tile_n = 128;
+        c.k_splits = s;
+        c.flags |= KMCTS_FLAG_SPLIT_CLUSTER | KMCTS_FLAG_SPLIT_SCATTER;
+        const bool shallow = s == 8 || (s <= 5 && K / s <= 1024);
+        c.tile_k = shallow ? 64 : 128;
+        c.stages = shallow ? 4 : 3;
+        int capacity = cluster_capacity(c, b_layout, s);
+        if (capacity <= 0) capacity = fallback_cluster_capacity(s, sms);
+        if (tiles <= capacity && cluster_split_cap(c, b_layout) >= s) {
+            *cfg = c;
+            return true;
+        }
+    }
+    return false;
+}
+
 }  // namespace
 
 // The schedule for the shape; kmcts_select_config adds the A-side cache policy.
@@ -262,7 +309,11 @@ static int select_schedule(int M, int N, int K, int b_layout, kmcts_gemm_config*
         small.tile_n = 128;
         small.tile_k = 128;
         small.stages = 3;
-        small.k_splits = choose_splits(static_cast<long long>((M + 127) / 128) * ((N + 127) / 128), K, sms);
+        const long long tiles = static_cast<long long>((M + 127) / 128) * ((N + 127) / 128);
+        // More than eight workspace splits (a tile or two over a very long
+        // K) beat a cluster's eight: 128 x 128 x 65536 48.8 us against 53.4.
+        small.k_splits = choose_splits(tiles, K, sms);
+        if (M > 64 && small.k_splits <= 8) scatter_schedule(tiles, K, b_layout, sms, &small);
     }
     // M within one 128-row tile: every B byte is read by one CTA only, so its
     // loads stream through L2 at evict-first priority (measured, L2 flushed

@@ -27,7 +27,9 @@
 // returns.  No TMA multicast is used.
 #include <cstdio>
 #include <cstring>
+#include <map>
 #include <mutex>
+#include <tuple>
 
 #include "gemm_common.cuh"
 #include "kmcts_internal.h"
@@ -99,15 +101,38 @@ struct Layout {
 //   kClusterStages  its pipeline stages, free once its UMMAs are done: rank 0
 //                   then signals each sender's go barrier, senders wait for
 //                   it before storing, and the cluster syncs before exit.
-constexpr int kClusterBuffer = 1, kClusterStages = 2;
+// kClusterScatter (128-row tiles) spreads the additions over the cluster:
+// the tile's pieces of 32 rows x 64 columns (lane quarter q, chunk c) are
+// numbered q * (BN / 64) + c, and piece p belongs to rank p % splits.  Each
+// rank stores every piece it does not own into the owner's shared memory
+// (one slot per sending rank), then adds its own pieces in split order and
+// writes them: a rank receives about 1/splits of what rank 0 receives
+// otherwise.  In its stages mode every rank signals every other rank's go
+// barrier; the cluster syncs before exit in both modes.
+constexpr int kClusterBuffer = 1, kClusterStages = 2, kClusterScatter = 4;
 
 struct SplitK {
     int splits;
     float* partials;
     unsigned long long* counters;  // [tile][lane quarter]: epoch << 32 | units arrived
     int epoch;
-    int cluster;  // 0 (workspace), kClusterBuffer or kClusterStages
+    int cluster;  // 0 (workspace), or kClusterBuffer or kClusterStages, with kClusterScatter
 };
+
+// Lane quarters of a 128-row tile holding at least one piece that rank
+// `rank` owns under kClusterScatter (chunks = BN / 64 pieces per quarter).
+__host__ __device__ __forceinline__ int scatter_quarters(int rank, int splits, int chunks) {
+    int n = 0;
+    for (int q = 0; q < 4; ++q) {
+        for (int c = 0; c < chunks; ++c) {
+            if ((q * chunks + c) % splits == rank) {
+                ++n;
+                break;
+            }
+        }
+    }
+    return n;
+}
 
 template <int BN>
 __device__ __forceinline__ float4* split_chunk(const SplitK& sk, int tile, int split, int quarter, int c) {
@@ -123,10 +148,11 @@ __device__ __forceinline__ int recv_chunk(int slot, int quarter, int c, int rows
 }
 
 // FEAT selects what an instantiation carries: bit 0 the cache-hinted loads,
-// bit 1 the cluster split K.  Code a schedule does not use is compiled out
-// (a runtime branch in the producer's loop costs the common schedules 1-2
-// us per launch); the launcher picks the smallest instantiation that serves.
-constexpr int kFeatHints = 1, kFeatCluster = 2;
+// bit 1 the cluster split K, bit 2 its scatter form (128-row tiles).  Code a
+// schedule does not use is compiled out (a runtime branch in the producer's
+// loop costs the common schedules 1-2 us per launch); the launcher picks the
+// smallest instantiation that serves.
+constexpr int kFeatHints = 1, kFeatCluster = 2, kFeatScatter = 4;
 
 template <int BN, int BK, int STAGES, bool B_MN, int AR, int FEAT = 0>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -135,7 +161,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                       const __grid_constant__ CUtensorMap map_c, int M, int N, int K, int group,
                       uint64_t limit_ns, int* status, const SplitK sk, int evict_first) {
     using L = Layout<BN, BK, STAGES, B_MN, AR>;
+    constexpr bool kScatter = (FEAT & kFeatScatter) != 0;
+    static_assert(!kScatter || ((FEAT & kFeatCluster) && AR == kBM), "the scatter split takes 128-row tiles");
     const int cluster_mode = (FEAT & kFeatCluster) ? sk.cluster : 0;  // compile-time 0 otherwise
+    const int recv_mode = cluster_mode & (kClusterBuffer | kClusterStages);
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~uintptr_t(1023));
@@ -152,7 +181,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Cluster split K's receive buffer: past the barriers (which take well
     // under 1 KB of the reserve; the launch adds its size to the shared
     // memory), or the pipeline stages.
-    float4* recv = reinterpret_cast<float4*>(cluster_mode == kClusterStages ? smem : smem + L::kBarrierOffset + 1024);
+    float4* recv = reinterpret_cast<float4*>(recv_mode == kClusterStages ? smem : smem + L::kBarrierOffset + 1024);
 
     if (status == nullptr) status = &g_default_status;
     const int warp = threadIdx.x / 32;
@@ -226,9 +255,21 @@ __global__ void __launch_bounds__(kThreads, 1)
             ptx::mbar_init(&tmem_empty[a], kEpilogueWarps);
         }
         ptx::mbar_init(drain, 1);
-        // Every lane of every epilogue warp of each sending rank arrives once.
-        ptx::mbar_init(recv_full, cluster_mode ? static_cast<uint32_t>((splits - 1) * kEpilogueWarps * 32) : 1u);
-        ptx::mbar_init(go_bar, 1);
+        // Every lane of every epilogue warp of each sending rank arrives once
+        // (scatter: each lane of a sending warp arrives once at each rank
+        // owning one of its pieces).
+        uint32_t recv_count = 1, go_count = 1;
+        if (cluster_mode) {
+            if constexpr (kScatter) {
+                recv_count = static_cast<uint32_t>(
+                    32 * (splits - 1) * scatter_quarters(static_cast<int>(blockIdx.x % splits), splits, BN / 64));
+                if (recv_mode == kClusterStages) go_count = static_cast<uint32_t>(splits - 1);
+            } else {
+                recv_count = static_cast<uint32_t>((splits - 1) * kEpilogueWarps * 32);
+            }
+        }
+        ptx::mbar_init(recv_full, recv_count);
+        ptx::mbar_init(go_bar, go_count);
         *abort = 0;
         *no_abort = 0;
         ptx::fence_mbarrier_init();
@@ -357,8 +398,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int n0 = tc.n_blk * BN;
             const int acc = local & 1;
             const uint32_t acc_phase = (local >> 1) & 1;
-            const bool sender = cluster_mode && s != 0;
-            const bool receiver = cluster_mode && s == 0;
+            const bool sender = !kScatter && cluster_mode && s != 0;
+            const bool receiver = !kScatter && cluster_mode && s == 0;
             bool ok = ptx::mbar_wait(&tmem_full[acc], acc_phase, limit_ns, abort);
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) {
@@ -366,7 +407,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 break;
             }
             ptx::tc_fence_after();
-            if (receiver && cluster_mode == kClusterStages && e == 0 && lane == 0) {
+            if (receiver && recv_mode == kClusterStages && e == 0 && lane == 0) {
                 // Every UMMA of this CTA has completed, so no stage is read
                 // any more (its one unit's loads were all consumed): the
                 // other ranks may store into them.
@@ -376,6 +417,138 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             const uint32_t row_addr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                                       static_cast<uint32_t>(acc * BN);
+            if constexpr (kScatter) {
+                // One unit per CTA.  Send the pieces of this warp's quarter
+                // that other ranks own, then add up and store the own ones.
+                constexpr int kChunks = BN / 64;
+                if (recv_mode == kClusterStages && e == 0 && lane == 0) {
+                    // Every UMMA of this CTA has completed: its stages may
+                    // receive the other ranks' values.
+                    ptx::fence_proxy_async_smem();
+                    for (int r = 0; r < splits; ++r)
+                        if (r != s)
+                            ptx::mbar_arrive_release_cluster(
+                                ptx::mapa_shared(ptx::smem_addr(go_bar), static_cast<uint32_t>(r)));
+                }
+                bool go = true;
+                if (recv_mode == kClusterStages) {
+                    go = ptx::mbar_wait_cluster(go_bar, 0, limit_ns, abort);
+                    go = __all_sync(0xffffffffu, go);
+                    // A rank that never freed its stages gets nothing: its
+                    // own bounded wait for the values gives up.
+                    if (!go && lane == 0) record_failure(status, abort, kRoleEpilogue);
+                }
+                if (go) {
+                    uint32_t sent = 0;  // ranks this warp stored into
+#pragma unroll 1
+                    for (int c = 0; c < kChunks; ++c) {
+                        const int piece = quarter * kChunks + c;
+                        const int owner = piece % splits;
+                        if (owner == s) continue;
+                        uint32_t lo[32], hi[32];
+                        ptx::tmem_ld_32x32b_x32(row_addr + c * 64, lo);
+                        ptx::tmem_ld_32x32b_x32(row_addr + c * 64 + 32, hi);
+                        ptx::tmem_wait_ld();
+                        // Slot (owner's piece index, sender) of 32 x 64 FP32.
+                        const int slot = (piece / splits) * (splits - 1) + (s < owner ? s : s - 1);
+                        const uint32_t dst = ptx::mapa_shared(ptx::smem_addr(recv), static_cast<uint32_t>(owner)) +
+                                             static_cast<uint32_t>(slot) * 8192u;
+#pragma unroll
+                        for (int q = 0; q < 8; ++q)
+                            ptx::st_cluster_v4(dst + (q * 32 + lane) * 16, __uint_as_float(lo[4 * q]),
+                                               __uint_as_float(lo[4 * q + 1]), __uint_as_float(lo[4 * q + 2]),
+                                               __uint_as_float(lo[4 * q + 3]));
+#pragma unroll
+                        for (int q = 0; q < 8; ++q)
+                            ptx::st_cluster_v4(dst + ((8 + q) * 32 + lane) * 16, __uint_as_float(hi[4 * q]),
+                                               __uint_as_float(hi[4 * q + 1]), __uint_as_float(hi[4 * q + 2]),
+                                               __uint_as_float(hi[4 * q + 3]));
+                        sent |= 1u << owner;
+                    }
+                    // Each lane releases its own stores, once per owner.
+                    for (int r = 0; r < splits; ++r)
+                        if (sent & (1u << r))
+                            ptx::mbar_arrive_release_cluster(
+                                ptx::mapa_shared(ptx::smem_addr(recv_full), static_cast<uint32_t>(r)));
+                }
+                bool waited = false;
+#pragma unroll 1
+                for (int c = 0; c < kChunks && go; ++c) {
+                    const int piece = quarter * kChunks + c;
+                    if (piece % splits != s) continue;
+                    if (!waited) {
+                        bool got = ptx::mbar_wait_cluster(recv_full, 0, limit_ns, abort);
+                        got = __all_sync(0xffffffffu, got);
+                        waited = true;
+                        if (!got) {
+                            if (lane == 0) record_failure(status, abort, kRoleEpilogue);
+                            break;
+                        }
+                    }
+                    const float4* slots = recv + (piece / splits) * (splits - 1) * 512;
+                    uint32_t lo[32], hi[32];
+                    // Split order, as the workspace path adds: split 0 first.
+                    if (s == 0) {
+                        ptx::tmem_ld_32x32b_x32(row_addr + c * 64, lo);
+                        ptx::tmem_ld_32x32b_x32(row_addr + c * 64 + 32, hi);
+                        ptx::tmem_wait_ld();
+                    } else {
+#pragma unroll
+                        for (int q = 0; q < 8; ++q) {
+                            const float4 f = slots[q * 32 + lane];
+                            const float4 g = slots[(8 + q) * 32 + lane];
+                            lo[4 * q] = __float_as_uint(f.x);
+                            lo[4 * q + 1] = __float_as_uint(f.y);
+                            lo[4 * q + 2] = __float_as_uint(f.z);
+                            lo[4 * q + 3] = __float_as_uint(f.w);
+                            hi[4 * q] = __float_as_uint(g.x);
+                            hi[4 * q + 1] = __float_as_uint(g.y);
+                            hi[4 * q + 2] = __float_as_uint(g.z);
+                            hi[4 * q + 3] = __float_as_uint(g.w);
+                        }
+                    }
+#pragma unroll 1
+                    for (int j = 1; j < splits; ++j) {
+                        if (j == s) {
+                            uint32_t own[32];
+                            ptx::tmem_ld_32x32b_x32(row_addr + c * 64, own);
+                            ptx::tmem_wait_ld();
+#pragma unroll
+                            for (int i = 0; i < 32; ++i)
+                                lo[i] = __float_as_uint(__uint_as_float(lo[i]) + __uint_as_float(own[i]));
+                            ptx::tmem_ld_32x32b_x32(row_addr + c * 64 + 32, own);
+                            ptx::tmem_wait_ld();
+#pragma unroll
+                            for (int i = 0; i < 32; ++i)
+                                hi[i] = __float_as_uint(__uint_as_float(hi[i]) + __uint_as_float(own[i]));
+                            continue;
+                        }
+                        const float4* part = slots + (j < s ? j : j - 1) * 512;
+#pragma unroll
+                        for (int q = 0; q < 8; ++q) {
+                            const float4 f = part[q * 32 + lane];
+                            lo[4 * q] = __float_as_uint(__uint_as_float(lo[4 * q]) + f.x);
+                            lo[4 * q + 1] = __float_as_uint(__uint_as_float(lo[4 * q + 1]) + f.y);
+                            lo[4 * q + 2] = __float_as_uint(__uint_as_float(lo[4 * q + 2]) + f.z);
+                            lo[4 * q + 3] = __float_as_uint(__uint_as_float(lo[4 * q + 3]) + f.w);
+                        }
+#pragma unroll
+                        for (int q = 0; q < 8; ++q) {
+                            const float4 f = part[(8 + q) * 32 + lane];
+                            hi[4 * q] = __float_as_uint(__uint_as_float(hi[4 * q]) + f.x);
+                            hi[4 * q + 1] = __float_as_uint(__uint_as_float(hi[4 * q + 1]) + f.y);
+                            hi[4 * q + 2] = __float_as_uint(__uint_as_float(hi[4 * q + 2]) + f.z);
+                            hi[4 * q + 3] = __float_as_uint(__uint_as_float(hi[4 * q + 3]) + f.w);
+                        }
+                    }
+                    if (m0 + quarter * 32 < M)
+                        store_chunk(&map_c, staging, chunk_count, lo, hi, lane, n0 + c * 64, m0 + quarter * 32);
+                }
+                ptx::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) ptx::mbar_arrive(&tmem_empty[acc]);
+                continue;
+            }
             if (m0 + quarter * 32 >= M) {
                 // None of this warp's rows exist: nothing to store.
                 ptx::tc_fence_before();
@@ -384,7 +557,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (sender) ptx::mbar_arrive_release_cluster(recv_full_remote);
                 continue;
             }
-            if (sender && cluster_mode == kClusterStages) {
+            if (sender && recv_mode == kClusterStages) {
                 bool go = ptx::mbar_wait_cluster(go_bar, 0, limit_ns, abort);
                 go = __all_sync(0xffffffffu, go);
                 if (!go) {
@@ -529,7 +702,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Rank 0 leaves only after the other ranks' stores into its buffer
         // are released, also when one of its own waits gave up (a rank that
         // gave up itself never stores: this wait then ends at its bound).
-        if (cluster_mode && blockIdx.x % splits == 0 && !got_recv)
+        // (The scatter form syncs the cluster below instead.)
+        if (!kScatter && cluster_mode && blockIdx.x % splits == 0 && !got_recv)
             ptx::mbar_wait_cluster(recv_full, 0, drain_limit(limit_ns), no_abort);
     }
 
@@ -537,8 +711,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::tc_fence_before();
     __syncthreads();
     // Receiving in its stages, rank 0 signalled the other ranks' barriers and
-    // they stored into its shared memory: no CTA leaves before all are done.
-    if (cluster_mode == kClusterStages) ptx::cluster_sync();
+    // they stored into its shared memory; under the scatter form every rank
+    // receives: no CTA leaves before all are done.
+    if (recv_mode == kClusterStages || (kScatter && cluster_mode)) ptx::cluster_sync();
     if (warp == 1) {
         ptx::tc_fence_after();
         ptx::tmem_dealloc(tmem_base, L::kTmemCols);
@@ -547,22 +722,34 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // ------------------------------------------------------------------ host side
 
-// Shared memory rank 0 of a cluster split K needs beyond the kernel's own:
-// one slot of FP32 values per other rank.
-int cluster_recv_bytes(int bn, int ar, int splits) {
+// Pieces (32 rows x 64 columns) of a 128-row tile, and whether a scatter
+// split of `splits` ranks runs: 128-row tiles, every rank owning a piece.
+int scatter_pieces(int bn) { return 4 * (bn / 64); }
+bool scatter_fits(int bn, int ar, int splits) { return ar == kBM && splits <= scatter_pieces(bn); }
+
+// Shared memory a receiving rank of a cluster split K needs beyond the
+// kernel's own: rank 0, one slot of FP32 values per other rank; scatter, a
+// 32 x 64 FP32 slot per other rank for each piece the busiest rank owns.
+int cluster_recv_bytes(int bn, int ar, int splits, bool scatter) {
+    if (scatter) {
+        const int owned = (scatter_pieces(bn) + splits - 1) / splits;
+        return owned * (splits - 1) * 32 * 64 * 4;
+    }
     return (splits - 1) * ar * bn * 4;
 }
 
-// Where rank 0 of a cluster split K of `s` splits receives: a buffer past
-// its own shared memory when that stays within 227 KB, else its pipeline
-// stages when they hold the other ranks' values, else nowhere (0).
-int cluster_receive_mode(int s, int64_t own_smem, int64_t stage_bytes, int bn, int ar) {
-    if (own_smem + cluster_recv_bytes(bn, ar, s) <= kMaxSmem) return kClusterBuffer;
-    if (cluster_recv_bytes(bn, ar, s) <= stage_bytes) return kClusterStages;
-    return 0;
+// Where the receiving ranks of a cluster split K of `s` splits receive: a
+// buffer past their own shared memory when that stays within 227 KB, else
+// their pipeline stages when those hold the values, else nowhere (0); with
+// kClusterScatter when the scatter form is asked for and fits.
+int cluster_receive_mode(int s, int64_t own_smem, int64_t stage_bytes, int bn, int ar, bool scatter) {
+    scatter = scatter && scatter_fits(bn, ar, s);
+    const int64_t bytes = cluster_recv_bytes(bn, ar, s, scatter);
+    const int mode = own_smem + bytes <= kMaxSmem ? kClusterBuffer : bytes <= stage_bytes ? kClusterStages : 0;
+    return mode && scatter ? mode | kClusterScatter : mode;
 }
 
-// K splits of a cluster split K for this launch (and where rank 0 receives,
+// K splits of a cluster split K for this launch (and where ranks receive,
 // in *mode), or 0 when the workspace path runs: flag off, fewer than 2 or
 // more than 8 splits, nowhere to receive, or (persistent launches) more
 // units than SMs.
@@ -573,7 +760,7 @@ int cluster_splits(int flags, int k_splits, int num_kb, int tiles, bool persiste
     const int s = k_splits < num_kb ? k_splits : num_kb;
     if (s < 2 || s > kMaxClusterSplits) return 0;
     if (persistent && static_cast<int64_t>(tiles) * s > multiprocessor_count()) return 0;
-    *mode = cluster_receive_mode(s, own_smem, stage_bytes, bn, ar);
+    *mode = cluster_receive_mode(s, own_smem, stage_bytes, bn, ar, (flags & KMCTS_FLAG_SPLIT_SCATTER) != 0);
     return *mode ? s : 0;
 }
 
@@ -598,35 +785,77 @@ int resolve_splits(int M, int N, int K, int requested, cudaStream_t stream, Spli
     return splits;
 }
 
+// The four instantiations of a one-CTA schedule: plain, cache hints only,
+// cluster split K (with hints), and its scatter form.  The scatter form
+// exists for 128-row tiles only (elsewhere the same instantiation as the
+// cluster kernel; cluster_receive_mode never asks for it).
+template <int BN, int BK, int STAGES, bool B_MN, int AR>
+struct Kernels {
+    static constexpr int kScatterFeat =
+        AR == kBM ? (kFeatHints | kFeatCluster | kFeatScatter) : (kFeatHints | kFeatCluster);
+    static constexpr auto plain = gemm_bf16_tcgen05<BN, BK, STAGES, B_MN, AR, 0>;
+    static constexpr auto hint = gemm_bf16_tcgen05<BN, BK, STAGES, B_MN, AR, kFeatHints>;
+    static constexpr auto cluster = gemm_bf16_tcgen05<BN, BK, STAGES, B_MN, AR, kFeatHints | kFeatCluster>;
+    static constexpr auto scatter = gemm_bf16_tcgen05<BN, BK, STAGES, B_MN, AR, kScatterFeat>;
+
+    // The shared-memory opt-in is per device; set it once on each, to the
+    // most any launch of this variant asks for (a cluster split K's receive
+    // buffer comes on top of the variant's own layout).
+    static bool configure() {
+        static std::mutex mu;
+        static bool configured[kMaxDevices] = {};
+        int device = 0;
+        if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kMaxDevices) return false;
+        std::lock_guard<std::mutex> lock(mu);
+        if (!configured[device]) {
+            for (auto fn : {plain, hint, cluster, scatter})
+                if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem) != cudaSuccess)
+                    return false;
+            configured[device] = true;
+        }
+        return true;
+    }
+};
+
+// Clusters of `splits` CTAs of this schedule's cluster split K (receive
+// `mode`) that can be resident at once on the current device, as the
+// occupancy calculator places them (GPC by GPC); 0 when it cannot say.
+template <int BN, int BK, int STAGES, bool B_MN, int AR>
+int variant_cluster_capacity(int splits, int mode) {
+    using L = Layout<BN, BK, STAGES, B_MN, AR>;
+    using KS = Kernels<BN, BK, STAGES, B_MN, AR>;
+    if (!KS::configure()) return 0;
+    const bool scatter = (mode & kClusterScatter) != 0;
+    int smem = L::kSmemBytes;
+    if (mode & kClusterBuffer) smem += cluster_recv_bytes(BN, AR, splits, scatter);
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3(static_cast<unsigned>(splits));
+    lc.blockDim = dim3(kThreads);
+    lc.dynamicSmemBytes = static_cast<size_t>(smem);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(splits);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    lc.attrs = attr;
+    lc.numAttrs = 1;
+    int clusters = 0;
+    const cudaError_t rc = scatter ? cudaOccupancyMaxActiveClusters(&clusters, KS::scatter, &lc)
+                                   : cudaOccupancyMaxActiveClusters(&clusters, KS::cluster, &lc);
+    if (rc != cudaSuccess) {
+        (void)cudaGetLastError();
+        return 0;
+    }
+    return clusters;
+}
+
 template <int BN, int BK, int STAGES, bool B_MN, int AR>
 int launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, int M,
                    int N, int K, int group, bool persistent, int k_splits, int flags,
                    uint64_t limit_ns, cudaStream_t stream, int* status) {
     using L = Layout<BN, BK, STAGES, B_MN, AR>;
-    auto plain_kernel = gemm_bf16_tcgen05<BN, BK, STAGES, B_MN, AR, 0>;
-    auto hint_kernel = gemm_bf16_tcgen05<BN, BK, STAGES, B_MN, AR, kFeatHints>;
-    auto cluster_kernel = gemm_bf16_tcgen05<BN, BK, STAGES, B_MN, AR, kFeatHints | kFeatCluster>;
-    // The shared-memory opt-in is per device; set it once on each, to the
-    // most any launch of this variant asks for (a cluster split K's receive
-    // buffer comes on top of the variant's own layout).
-    static std::mutex mu;
-    static bool configured[kMaxDevices] = {};
-    int device = 0;
-    if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kMaxDevices)
-        return KMCTS_EHANDLE;
-    {
-        std::lock_guard<std::mutex> lock(mu);
-        if (!configured[device]) {
-            if (cudaFuncSetAttribute(plain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem) !=
-                    cudaSuccess ||
-                cudaFuncSetAttribute(hint_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem) !=
-                    cudaSuccess ||
-                cudaFuncSetAttribute(cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem) !=
-                    cudaSuccess)
-                return KMCTS_EGEMM;
-            configured[device] = true;
-        }
-    }
+    using KS = Kernels<BN, BK, STAGES, B_MN, AR>;
+    if (!KS::configure()) return KMCTS_EGEMM;
     const int tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
     const int sms = multiprocessor_count();
     SplitK sk = {1, nullptr, nullptr, 0, 0};
@@ -636,14 +865,17 @@ int launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorM
     int smem = L::kSmemBytes;
     if (splits > 0) {
         sk = SplitK{splits, nullptr, nullptr, 0, mode};
-        if (mode == kClusterBuffer) smem += cluster_recv_bytes(BN, AR, splits);
+        if (mode & kClusterBuffer) smem += cluster_recv_bytes(BN, AR, splits, (mode & kClusterScatter) != 0);
     } else splits = resolve_splits<BN, BK>(M, N, K, k_splits, stream, &sk);
     const int units = tiles * splits;
     int grid = units;
     if (persistent && !sk.cluster) grid = units < sms ? units : sms;
     const int evict_first =
         ((flags & KMCTS_FLAG_B_EVICT_FIRST) ? 1 : 0) | ((flags & KMCTS_FLAG_A_EVICT_FIRST) ? 2 : 0);
-    auto kernel = sk.cluster ? cluster_kernel : evict_first ? hint_kernel : plain_kernel;
+    auto kernel = (sk.cluster & kClusterScatter) ? KS::scatter
+                  : sk.cluster                      ? KS::cluster
+                  : evict_first                     ? KS::hint
+                                                    : KS::plain;
     if (sk.cluster) {
         cudaLaunchConfig_t lc = {};
         lc.gridDim = dim3(static_cast<unsigned>(grid));
@@ -673,11 +905,14 @@ using Launcher = int (*)(const CUtensorMap&, const CUtensorMap&, const CUtensorM
 struct Variant {
     int bn, bk, stages, b_mn, ar;
     Launcher fn;
+    int (*capacity)(int splits, int mode);  // resident clusters of a cluster split K
 };
 
-#define KMCTS_VARIANT(BN, BK, ST, MN) {BN, BK, ST, MN, kBM, &launch_variant<BN, BK, ST, MN, kBM>}
-#define KMCTS_SKINNY(BN, BK, ST, MN) {BN, BK, ST, MN, 32, &launch_variant<BN, BK, ST, MN, 32>}
-#define KMCTS_HALF(BN, BK, ST, MN) {BN, BK, ST, MN, 64, &launch_variant<BN, BK, ST, MN, 64>}
+#define KMCTS_VARIANT_AR(BN, BK, ST, MN, AR) \
+    {BN, BK, ST, MN, AR, &launch_variant<BN, BK, ST, MN, AR>, &variant_cluster_capacity<BN, BK, ST, MN, AR>}
+#define KMCTS_VARIANT(BN, BK, ST, MN) KMCTS_VARIANT_AR(BN, BK, ST, MN, kBM)
+#define KMCTS_SKINNY(BN, BK, ST, MN) KMCTS_VARIANT_AR(BN, BK, ST, MN, 32)
+#define KMCTS_HALF(BN, BK, ST, MN) KMCTS_VARIANT_AR(BN, BK, ST, MN, 64)
 
 // The compiled 1-CTA schedule space: every (tile_n, tile_k, stages) of the
 // sweep grid that fits 227 KB (stages*(128+BN)*BK*2 + 32 KB staging + 2 KB),
@@ -748,8 +983,40 @@ int cluster_split_cap(const kmcts_gemm_config& cfg, int b_layout) {
     const int ar = a_rows(cfg);
     const int64_t stage_bytes = static_cast<int64_t>(cfg.stages) * (ar + cfg.tile_n) * cfg.tile_k * 2;
     int cap = 1;
-    while (cap < kMaxClusterSplits && cluster_receive_mode(cap + 1, own, stage_bytes, cfg.tile_n, ar)) ++cap;
+    const bool scatter = (cfg.flags & KMCTS_FLAG_SPLIT_SCATTER) != 0;
+    while (cap < kMaxClusterSplits && cluster_receive_mode(cap + 1, own, stage_bytes, cfg.tile_n, ar, scatter)) ++cap;
     return cap;
+}
+
+int cluster_capacity(const kmcts_gemm_config& cfg, int b_layout, int splits) {
+    if (!is_one_cta(cfg) || is_swapped(cfg) || splits < 2 || splits > kMaxClusterSplits) return 0;
+    const Variant* v = find_variant(cfg, b_layout);
+    if (v == nullptr) return 0;
+    const int64_t own = tcgen05_smem_bytes(cfg, b_layout);
+    const int ar = a_rows(cfg);
+    const int64_t stage_bytes = static_cast<int64_t>(cfg.stages) * (ar + cfg.tile_n) * cfg.tile_k * 2;
+    const int mode = cluster_receive_mode(splits, own, stage_bytes, cfg.tile_n, ar,
+                                          (cfg.flags & KMCTS_FLAG_SPLIT_SCATTER) != 0);
+    if (mode == 0) return 0;
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kMaxDevices) {
+        (void)cudaGetLastError();
+        return 0;
+    }
+    // The answer depends on the device, the instantiation and the launch
+    // shape only: ask the occupancy calculator once for each.
+    static std::mutex mu;
+    static std::map<std::tuple<int, const Variant*, int, int>, int> cache;
+    const auto key = std::make_tuple(device, v, splits, mode);
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        const auto it = cache.find(key);
+        if (it != cache.end()) return it->second;
+    }
+    const int clusters = v->capacity(splits, mode);
+    std::lock_guard<std::mutex> lock(mu);
+    cache[key] = clusters;
+    return clusters;
 }
 
 int tcgen05_legal(const kmcts_gemm_config& cfg, int M, int N, int K, int b_layout, char* why,
@@ -971,9 +1238,14 @@ int plan_tcgen05(const kmcts_gemm_config& cfg, int M, int N, int K, int b_layout
                                   ar, &mode);
     if (cs > 0) {
         plan.cluster_size = cs;
-        plan.workers = plan.workers / cs;  // at most: one CTA per SM, whole clusters
+        // Resident clusters as the occupancy calculator places them; at most
+        // one CTA per SM in whole clusters where it cannot say.
+        const int capacity = cluster_capacity(cfg, b_layout, cs);
+        plan.workers = capacity > 0 ? capacity : plan.workers / cs;
         plan.ctas = plan.units;
-        if (mode == kClusterBuffer) plan.smem_bytes += cluster_recv_bytes(cfg.tile_n, ar, cs);
+        if (mode & kClusterBuffer)
+            plan.smem_bytes += cluster_recv_bytes(cfg.tile_n, ar, cs, (mode & kClusterScatter) != 0);
+        plan.split_reduce = (mode & kClusterScatter) ? KMCTS_SPLIT_SCATTER : KMCTS_SPLIT_CLUSTER;
     }
     *out = plan;
     return KMCTS_OK;

@@ -101,6 +101,16 @@ extern "C" {
  * are large enough).  Every unit runs in its own CTA (units no more than the
  * SMs when persistent); otherwise the workspace path runs. */
 #define KMCTS_FLAG_SPLIT_CLUSTER 64
+/* With KMCTS_FLAG_SPLIT_CLUSTER on tile_m 128: the additions spread over the
+ * cluster instead of meeting in split 0.  The tile's pieces of 32 rows x 64
+ * columns are numbered quarter * (tile_n / 64) + chunk, and piece p belongs
+ * to split p % k_splits: every split stores the pieces it does not own into
+ * their owners' shared memory, then adds its own pieces in split order (the
+ * same bits as the workspace path) and writes them.  A split receives
+ * ceil(pieces / k_splits) x (k_splits - 1) x 8 KB, extra shared memory or its
+ * pipeline stages as above.  Where k_splits exceeds the pieces, or tile_m is
+ * not 128, the splits add up in split 0 as without this flag. */
+#define KMCTS_FLAG_SPLIT_SCATTER 256
 
 #define KMCTS_TAIL_NONE 0     /* kmcts_gemm_plan.tail_split: every tile whole */
 #define KMCTS_TAIL_SPLIT_N 1  /* last wave as half-width units */
@@ -206,7 +216,12 @@ typedef struct kmcts_gemm_plan {
     int32_t tail_clusters; /* pairs that share the tiles after full_tiles */
     int32_t tail_segments; /* most units one tile runs as (2 when split) */
     int32_t k_splits;     /* split K: K ranges per tile (1 = none) */
+    int32_t split_reduce; /* KMCTS_SPLIT_*: where a split tile's K ranges add up */
 } kmcts_gemm_plan;
+
+#define KMCTS_SPLIT_WORKSPACE 0 /* per-stream workspace, last unit adds (or no split) */
+#define KMCTS_SPLIT_CLUSTER 1   /* one cluster per tile, split 0 adds */
+#define KMCTS_SPLIT_SCATTER 2   /* one cluster per tile, each split adds its pieces */
 
 /* Fills *out with the launch shape kmcts_bf16_gemm_ex would use for this
  * schedule and shape on the current device (queries occupancy; launches

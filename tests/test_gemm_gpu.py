@@ -767,6 +767,69 @@ def test_cluster_split_k_same_bits_as_workspace_split_k(cuda_device, layout, til
 
 
 @pytest.mark.parametrize("layout", ["col", "row"])
+@pytest.mark.parametrize("tile_n,tile_k,stages,shape,splits,reduce", [
+    (128, 128, 3, (512, 512, 8192), 6, _native.SPLIT_SCATTER),   # 8 pieces over 6 ranks, in the stages
+    (128, 128, 3, (512, 512, 8192), 8, _native.SPLIT_SCATTER),   # more clusters than fit at once
+    (128, 64, 4, (384, 384, 8192), 8, _native.SPLIT_SCATTER),    # one piece per rank, in a buffer
+    (128, 64, 4, (300, 1000, 2048), 4, _native.SPLIT_SCATTER),   # ragged M and N
+    (128, 128, 3, (70, 520, 1032), 3, _native.SPLIT_SCATTER),    # a quarter past M, ragged K
+    (128, 128, 3, (128, 128, 4096), 7, _native.SPLIT_SCATTER),   # rank 0 owns two pieces
+    (64, 64, 6, (512, 512, 4096), 4, _native.SPLIT_SCATTER),     # 64-column tiles: 4 pieces
+    (256, 64, 3, (384, 768, 4096), 8, _native.SPLIT_SCATTER),    # 16 pieces, two per rank
+    (256, 64, 3, (200, 520, 1000), 5, _native.SPLIT_SCATTER),    # 16 pieces over 5 ranks, ragged
+    (64, 64, 6, (256, 256, 2048), 5, _native.SPLIT_CLUSTER),     # more ranks than pieces: split 0 adds
+])
+def test_scatter_split_k_same_bits_as_workspace_split_k(cuda_device, layout, tile_n, tile_k, stages, shape, splits,
+                                                        reduce):
+    """KMCTS_FLAG_SPLIT_SCATTER spreads a cluster split K's additions over
+    the cluster (piece p of 32 rows x 64 columns to rank p % splits): exact
+    on integer inputs, and on N(0,1) inputs the same bits as the workspace
+    reduction (each piece adds its splits in split order), launch after
+    launch.  With more splits than pieces the splits add up in split 0."""
+    m, n, k = shape
+    base = dict(kernel=_native.KERNEL_TCGEN05, tile_m=128, cluster_m=1, tile_n=tile_n, tile_k=tile_k,
+                stages=stages, k_splits=splits)
+    flagged = dict(base, flags=_native.FLAG_SPLIT_CLUSTER | _native.FLAG_SPLIT_SCATTER)
+    plan = plan_of(m, n, k, layout, **flagged)
+    assert plan["cluster_size"] == splits and plan["split_reduce"] == reduce, plan
+    assert plan_of(m, n, k, layout, **base)["split_reduce"] == _native.SPLIT_WORKSPACE
+    a_t, b_t = oracle.integer_inputs(m, n, k, seed=splits + m)
+    expect = oracle.torch_bits(oracle.torch_reference(a_t, b_t))
+    c = run(a_t.cuda(), b_for(layout, b_t.cuda()), layout, **flagged)
+    np.testing.assert_array_equal(bits_of(c), expect)
+    a_t, b_t = oracle.randn_inputs(m, n, k, seed=6, b_layout=layout)
+    a, b = a_t.cuda(), b_t.cuda()
+    workspace = run(a, b, layout, **base)
+    first = run(a, b, layout, **flagged)
+    second = run(a, b, layout, **flagged)
+    assert torch.equal(first.view(torch.int16), workspace.view(torch.int16))
+    assert torch.equal(second.view(torch.int16), workspace.view(torch.int16))
+
+
+@pytest.mark.parametrize("layout", ["col", "row"])
+@pytest.mark.parametrize("shape", [(512, 512, 8192), (384, 384, 8192), (300, 1000, 2048), (2048, 256, 8192),
+                                   (1024, 1024, 8192)])
+def test_scatter_selection_within_bound_and_exact_on_integers(cuda_device, layout, shape):
+    """The NULL-config selection for few 128 x 128 tiles over a long K runs
+    the scatter split: within the parity bound of the CPU oracle on N(0,1)
+    inputs, exact on integer inputs."""
+    m, n, k = shape
+    bl = _native.B_ROW if layout == "row" else _native.B_COL
+    sel = _native.select_config(m, n, k, bl)
+    assert sel.flags & _native.FLAG_SPLIT_SCATTER and sel.k_splits >= 2
+    assert _native.plan(sel, m, n, k, bl)["split_reduce"] == _native.SPLIT_SCATTER
+    a_t, b_t = oracle.integer_inputs(m, n, k, seed=9)
+    c = run(a_t.cuda(), b_for(layout, b_t.cuda()), layout)  # NULL config
+    np.testing.assert_array_equal(bits_of(c), oracle.torch_bits(oracle.torch_reference(a_t, b_t)))
+    a_t, b_t = oracle.randn_inputs(m, n, k, seed=10, b_layout=layout)
+    c = run(a_t.cuda(), b_t.cuda(), layout)
+    ref32 = oracle.torch_bits(oracle.torch_reference(a_t, b_t, layout))
+    ref64, mag = oracle.fp64_reference(a_t, b_t, layout)
+    report = oracle.parity_report(bits_of(c), ref32, ref64, mag, k)
+    assert report["passed"], report
+
+
+@pytest.mark.parametrize("layout", ["col", "row"])
 @pytest.mark.parametrize("shape", [(16, 8192, 8192), (128, 16384, 4096), (100, 1000, 2048), (48, 4096, 8192),
                                    (64, 2048, 8192)])
 def test_skinny_selection_streams_b_evict_first_same_bits(cuda_device, layout, shape):

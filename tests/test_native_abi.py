@@ -87,8 +87,28 @@ def test_select_config_splits_k_for_skinny_shapes():
     split64 = km.select_config(64, 8192, 8192, km.B_ROW)  # 64 tiles: two splits, three stages
     assert (split64.tile_m, split64.tile_n, split64.stages, split64.k_splits) == (64, 128, 3, 2)
     assert km.select_config(33, 1024, 16384, km.B_ROW).k_splits == 6
-    assert not km.select_config(128, 4096, 8192, km.B_ROW).flags & _native.FLAG_SPLIT_CLUSTER
-    assert km.select_config(512, 512, 8192, km.B_ROW).k_splits == 4
+    # Few 128 x 128 tiles over a long K: each tile's K splits run as one
+    # cluster whose CTAs add up one share of the tile each, as many splits
+    # as keep every cluster resident (the B200 capacities without a GPU:
+    # 16 clusters of 6, not of 7 or 8).
+    m128 = km.select_config(128, 4096, 8192, km.B_ROW)
+    scatter = _native.FLAG_SPLIT_CLUSTER | _native.FLAG_SPLIT_SCATTER
+    assert (m128.tile_n, m128.tile_k, m128.stages, m128.k_splits) == (128, 128, 3, 4)
+    assert m128.flags & scatter == scatter and m128.flags & _native.FLAG_B_EVICT_FIRST
+    sq = km.select_config(512, 512, 8192, km.B_ROW)
+    assert (sq.tile_n, sq.tile_k, sq.stages, sq.k_splits) == (128, 128, 3, 6) and sq.flags & scatter == scatter
+    # Eight splits (nine tiles) or short ranges: 64-deep stages, receiving outside them.
+    eight = km.select_config(384, 384, 8192, km.B_ROW)
+    assert (eight.tile_k, eight.stages, eight.k_splits) == (64, 4, 8) and eight.flags & scatter == scatter
+    short = km.select_config(300, 1000, 2048, km.B_ROW)
+    assert (short.tile_k, short.stages, short.k_splits) == (64, 4, 4) and short.flags & scatter == scatter
+    assert km.select_config(1024, 1024, 8192, km.B_ROW).k_splits == 2
+    assert km.select_config(1024, 1024, 2048, km.B_ROW).k_splits == 0  # two splits only from K = 4096
+    assert km.select_config(768, 768, 2048, km.B_ROW).k_splits == 3
+    for shape in ((512, 512, 8192), (384, 384, 8192), (300, 1000, 2048), (128, 4096, 8192)):
+        plan = _native.plan(km.select_config(*shape, km.B_ROW), *shape, km.B_ROW)
+        assert plan["split_reduce"] == _native.SPLIT_SCATTER, shape
+        assert plan["tiles"] <= plan["workers"], shape  # every cluster resident at once
     assert km.select_config(1024, 1024, 1024, km.B_ROW).k_splits == 0  # short K: no split
     assert km.select_config(4096, 4096, 4096, km.B_ROW).k_splits == 0
     assert km.select_config(256, 256, 256, km.B_ROW).k_splits == 0  # K too short to split
@@ -112,7 +132,9 @@ def test_select_config_splits_k_for_skinny_shapes():
     # ... not at K = 4096: one CTA per 128 x 256 tile.
     assert km.select_config(2048, 1024, 4096, km.B_ROW).tile_m == 128
     assert km.select_config(2048, 256, 8192, km.B_ROW).k_splits == 4  # 32 tiles -> 128 units, one wave
-    assert km.select_config(128, 128, 65536, km.B_ROW).k_splits == 16  # one tile: at most 16 splits
+    # One tile over a very long K: sixteen workspace splits, more than a cluster holds.
+    one_tile = km.select_config(128, 128, 65536, km.B_ROW)
+    assert one_tile.k_splits == 16 and not one_tile.flags & _native.FLAG_SPLIT_CLUSTER
 
 
 @pytest.mark.parametrize(
