@@ -168,7 +168,10 @@ int kmcts_default_config(kmcts_gemm_config* cfg);
  * K <= 768), or in two K splits when those fill three quarters of them and
  * K >= 8192; else one CTA per
  * 128 x 256 tile while those fill them (the default again from K = 4096),
- * else one CTA per 128 x 128 tile.  Few tiles over a long K get split K; one-CTA
+ * else one CTA per 128 x 128 tile.  Few tiles over a long K get split K: for
+ * M > 64 as scatter clusters (KMCTS_FLAG_SPLIT_SCATTER) of as many splits as
+ * keep every cluster resident (at most 8; two only from K = 4096), unless
+ * the workspace path would take more than 8; one-CTA
  * schedules for M <= 128 and pair schedules for M <= 512 (one or two tile
  * rows) add KMCTS_FLAG_B_EVICT_FIRST, schedules whose tiles span N in one or
  * two columns KMCTS_FLAG_A_EVICT_FIRST; N <= 128 takes one CTA per tile.  Every
