@@ -301,10 +301,11 @@ SHAPE_CLASSES = (
     ("N <= 128: one CTA per 128 x 128 tile, A at L2 evict-first", (16384, 128, 4096)),
     ("two columns of pair tiles: A at L2 evict-first", (28672, 256, 4096)),
     ("rectangular, CTA pair", (8192, 4096, 4096)),
-    ("mid-size, few tiles over a long K", (512, 512, 8192)),
+    ("mid-size, few tiles over a long K: K splits added across a cluster", (512, 512, 8192)),
 )
 
-FLAG_NAMES = (("B_EVICT_FIRST", 8), ("A_EVICT_FIRST", 128), ("SPLIT_CLUSTER", 64), ("SWAP_AB", 16))
+FLAG_NAMES = (("B_EVICT_FIRST", 8), ("A_EVICT_FIRST", 128), ("SPLIT_CLUSTER", 64), ("SPLIT_SCATTER", 256),
+              ("SWAP_AB", 16))
 
 
 def shape_classes(device, stream, flush, steps: int = 40) -> list[dict]:
