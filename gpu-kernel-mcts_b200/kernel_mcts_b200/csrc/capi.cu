@@ -117,14 +117,15 @@ int fallback_cluster_capacity(int splits, int sms) {
 // S is the most splits that keep every unit on its own SM, every cluster
 // resident at once, and K ranges of at least 512 (at most 8); two splits
 // only from K = 4096 (below, the exchange costs more than the second SM
-// saves: 1024 x 1024 x 2048 18.5 us against 17.4 unsplit).  Stages are
-// 64 deep x 4 where a short range or eight splits leave room to receive
-// outside the stages, else 128 deep x 3.  Measured, L2 flushed (workspace
-// split -> scatter, cuBLAS): 512 x 512 x 8192 25.6 -> 22.7 us (19.0),
-// 384 x 384 x 8192 25.6 -> 20.7 (17.9), 256 x 512 x 16384 31.5 -> 25.8
-// (23.3), 1024 x 1024 x 8192 32.6 -> 31.0 (26.1), 2048 x 256 x 8192 27.2 ->
-// 25.3 (21.8), 512 x 1024 x 4096 22.9 -> 20.1 (14.2), and unsplit before:
-// 300 x 1000 x 2048 18.7 -> 16.7 (11.2).  Returns false when no split fits.
+// saves: 1024 x 1024 x 2048 18.5 us against 17.4 unsplit).  Ranges of at
+// most 1024 take 64-deep x 4 stages (the copies received past them), longer
+// ones 128-deep x 3.  Measured, L2 flushed (workspace split -> scatter,
+// cuBLAS): 512 x 512 x 8192 25.3 -> 21.7 us (18.1), 384 x 384 x 8192 24.9 ->
+// 20.3 (18.0), 256 x 512 x 16384 30.9 -> 23.6 (23.6), 1024 x 1024 x 8192
+// 32.0 -> 29.9 (25.0), 2048 x 256 x 8192 26.7 -> 23.8 (21.3), 128 x 2048 x
+// 8192 26.7 -> 22.6 (19.7), and unsplit before: 300 x 1000 x 2048 18.5 ->
+// 16.3 (10.9), 200 x 600 x 3000 28.4 -> 16.5 (12.2).  Returns false when no
+// split fits.
 bool scatter_schedule(long long tiles, int K, int b_layout, int sms, kmcts_gemm_config* cfg) {
     if (tiles <= 0 || 2 * tiles > sms) return false;
     int s = static_cast<int>(sms / tiles);
@@ -138,12 +139,12 @@ bool scatter_schedule(long long tiles, int K, int b_layout, int sms, kmcts_gemm_
         c.tile_n = 128;
         c.k_splits = s;
         c.flags |= KMCTS_FLAG_SPLIT_CLUSTER | KMCTS_FLAG_SPLIT_SCATTER;
-        const bool shallow = s == 8 || (s <= 5 && K / s <= 1024);
+        const bool shallow = K / s <= 1024;
         c.tile_k = shallow ? 64 : 128;
         c.stages = shallow ? 4 : 3;
         int capacity = cluster_capacity(c, b_layout, s);
         if (capacity <= 0) capacity = fallback_cluster_capacity(s, sms);
-        if (tiles <= capacity && cluster_split_cap(c, b_layout) >= s) {
+        if (tiles <= capacity && cluster_split_fits(c, b_layout, s)) {
             *cfg = c;
             return true;
         }

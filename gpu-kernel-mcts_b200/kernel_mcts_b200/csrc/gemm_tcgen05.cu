@@ -104,11 +104,19 @@ struct Layout {
 // kClusterScatter (128-row tiles) spreads the additions over the cluster:
 // the tile's pieces of 32 rows x 64 columns (lane quarter q, chunk c) are
 // numbered q * (BN / 64) + c, and piece p belongs to rank p % splits.  Each
-// rank stores every piece it does not own into the owner's shared memory
-// (one slot per sending rank), then adds its own pieces in split order and
-// writes them: a rank receives about 1/splits of what rank 0 receives
-// otherwise.  In its stages mode every rank signals every other rank's go
-// barrier; the cluster syncs before exit in both modes.
+// rank writes the FP32 values of every piece it does not own into its own
+// pipeline stages (free once its UMMAs are done; piece p at p x 8 KB), then
+// one lane per warp copies each of them into its owner's shared memory with
+// a bulk shared::cta -> shared::cluster copy that completes its bytes on the
+// owner's receive barrier (armed at set-up with the bytes the rank will
+// receive).  The owner waits once, adds its pieces' values in split order
+// and writes them.  The copies land
+//   with kClusterBuffer  in a buffer past the barriers: free from the start,
+//                        so each rank copies as soon as its pieces are written;
+//   with kClusterStages  in the stages past the pieces: the cluster meets
+//                        first (every rank's UMMAs are then done).
+// The cluster syncs before exit, so no CTA leaves while a copy reads its
+// stages or writes its shared memory.
 constexpr int kClusterBuffer = 1, kClusterStages = 2, kClusterScatter = 4;
 
 struct SplitK {
@@ -119,20 +127,8 @@ struct SplitK {
     int cluster;  // 0 (workspace), or kClusterBuffer or kClusterStages, with kClusterScatter
 };
 
-// Lane quarters of a 128-row tile holding at least one piece that rank
-// `rank` owns under kClusterScatter (chunks = BN / 64 pieces per quarter).
-__host__ __device__ __forceinline__ int scatter_quarters(int rank, int splits, int chunks) {
-    int n = 0;
-    for (int q = 0; q < 4; ++q) {
-        for (int c = 0; c < chunks; ++c) {
-            if ((q * chunks + c) % splits == rank) {
-                ++n;
-                break;
-            }
-        }
-    }
-    return n;
-}
+// Pieces (32 rows x 64 columns) of a 128-row tile.
+__host__ __device__ constexpr int scatter_pieces_of(int bn) { return 4 * (bn / 64); }
 
 template <int BN>
 __device__ __forceinline__ float4* split_chunk(const SplitK& sk, int tile, int split, int quarter, int c) {
@@ -255,21 +251,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             ptx::mbar_init(&tmem_empty[a], kEpilogueWarps);
         }
         ptx::mbar_init(drain, 1);
-        // Every lane of every epilogue warp of each sending rank arrives once
-        // (scatter: each lane of a sending warp arrives once at each rank
-        // owning one of its pieces).
-        uint32_t recv_count = 1, go_count = 1;
-        if (cluster_mode) {
-            if constexpr (kScatter) {
-                recv_count = static_cast<uint32_t>(
-                    32 * (splits - 1) * scatter_quarters(static_cast<int>(blockIdx.x % splits), splits, BN / 64));
-                if (recv_mode == kClusterStages) go_count = static_cast<uint32_t>(splits - 1);
-            } else {
-                recv_count = static_cast<uint32_t>((splits - 1) * kEpilogueWarps * 32);
-            }
-        }
+        // Every lane of every epilogue warp of each sending rank arrives once.
+        uint32_t recv_count = 1;
+        if (cluster_mode && !kScatter) recv_count = static_cast<uint32_t>((splits - 1) * kEpilogueWarps * 32);
         ptx::mbar_init(recv_full, recv_count);
-        ptx::mbar_init(go_bar, go_count);
+        ptx::mbar_init(go_bar, 1);
+        if (kScatter && cluster_mode) {
+            // The bytes the other ranks copy in: 8 KB per owned piece and sender.
+            const int owned = (scatter_pieces_of(BN) - static_cast<int>(blockIdx.x % splits) + splits - 1) / splits;
+            ptx::fence_mbarrier_init();
+            ptx::mbar_arrive_expect_tx(recv_full, static_cast<uint32_t>(owned * (splits - 1) * 8192));
+        }
         *abort = 0;
         *no_abort = 0;
         ptx::fence_mbarrier_init();
@@ -391,6 +383,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // cluster arrived after set-up) before any store or arrive reaches it.
         if (cluster_mode) ptx::cluster_wait();
         bool got_recv = false;  // rank 0: the other ranks' values are all here
+        bool met = false;       // scatter: this warp passed the cluster barrier between write and read
         for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++local) {
             const int t = u / splits, s = u % splits;
             const TileCoord tc = tile_coord(t, num_m, num_n, group);
@@ -418,62 +411,61 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t row_addr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                                       static_cast<uint32_t>(acc * BN);
             if constexpr (kScatter) {
-                // One unit per CTA.  Send the pieces of this warp's quarter
-                // that other ranks own, then add up and store the own ones.
+                // One unit per CTA.  Write the pieces of this warp's quarter
+                // that other ranks own into this CTA's stages (free: every
+                // UMMA has completed and the unit's loads were all consumed),
+                // meet the cluster (every rank's stages are then free and its
+                // pieces written), copy each piece into its owner's stages,
+                // then add the own pieces' values in split order.
                 constexpr int kChunks = BN / 64;
-                if (recv_mode == kClusterStages && e == 0 && lane == 0) {
-                    // Every UMMA of this CTA has completed: its stages may
-                    // receive the other ranks' values.
-                    ptx::fence_proxy_async_smem();
-                    for (int r = 0; r < splits; ++r)
-                        if (r != s)
-                            ptx::mbar_arrive_release_cluster(
-                                ptx::mapa_shared(ptx::smem_addr(go_bar), static_cast<uint32_t>(r)));
-                }
-                bool go = true;
-                if (recv_mode == kClusterStages) {
-                    go = ptx::mbar_wait_cluster(go_bar, 0, limit_ns, abort);
-                    go = __all_sync(0xffffffffu, go);
-                    // A rank that never freed its stages gets nothing: its
-                    // own bounded wait for the values gives up.
-                    if (!go && lane == 0) record_failure(status, abort, kRoleEpilogue);
-                }
-                if (go) {
-                    uint32_t sent = 0;  // ranks this warp stored into
+                float4* parts = reinterpret_cast<float4*>(smem);  // piece p at p * 512 float4
+                // Received copies: past the pieces in the stages, or in the
+                // buffer past the barriers (free from the start: no meeting).
+                const bool in_stages = recv_mode == kClusterStages;
+                float4* received = in_stages ? parts + scatter_pieces_of(BN) * 512 : recv;
+                ptx::fence_proxy_async_smem();  // generic writes after the async proxy's use
 #pragma unroll 1
+                for (int c = 0; c < kChunks; ++c) {
+                    const int piece = quarter * kChunks + c;
+                    if (piece % splits == s) continue;
+                    uint32_t lo[32], hi[32];
+                    ptx::tmem_ld_32x32b_x32(row_addr + c * 64, lo);
+                    ptx::tmem_ld_32x32b_x32(row_addr + c * 64 + 32, hi);
+                    ptx::tmem_wait_ld();
+                    float4* dst = parts + piece * 512;
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) {
+                        dst[q * 32 + lane] = make_float4(__uint_as_float(lo[4 * q]), __uint_as_float(lo[4 * q + 1]),
+                                                         __uint_as_float(lo[4 * q + 2]), __uint_as_float(lo[4 * q + 3]));
+                        dst[(8 + q) * 32 + lane] =
+                            make_float4(__uint_as_float(hi[4 * q]), __uint_as_float(hi[4 * q + 1]),
+                                        __uint_as_float(hi[4 * q + 2]), __uint_as_float(hi[4 * q + 3]));
+                    }
+                }
+                ptx::fence_proxy_async_smem();  // the copies (async proxy) read what this thread wrote
+                if (in_stages) {
+                    // Every rank's stages are free and its pieces written.
+                    ptx::cluster_arrive();
+                    ptx::cluster_wait();
+                    met = true;
+                } else {
+                    __syncwarp();  // lane 0 copies what the warp wrote
+                }
+                if (lane == 0) {
                     for (int c = 0; c < kChunks; ++c) {
                         const int piece = quarter * kChunks + c;
                         const int owner = piece % splits;
                         if (owner == s) continue;
-                        uint32_t lo[32], hi[32];
-                        ptx::tmem_ld_32x32b_x32(row_addr + c * 64, lo);
-                        ptx::tmem_ld_32x32b_x32(row_addr + c * 64 + 32, hi);
-                        ptx::tmem_wait_ld();
-                        // Slot (owner's piece index, sender) of 32 x 64 FP32.
                         const int slot = (piece / splits) * (splits - 1) + (s < owner ? s : s - 1);
-                        const uint32_t dst = ptx::mapa_shared(ptx::smem_addr(recv), static_cast<uint32_t>(owner)) +
-                                             static_cast<uint32_t>(slot) * 8192u;
-#pragma unroll
-                        for (int q = 0; q < 8; ++q)
-                            ptx::st_cluster_v4(dst + (q * 32 + lane) * 16, __uint_as_float(lo[4 * q]),
-                                               __uint_as_float(lo[4 * q + 1]), __uint_as_float(lo[4 * q + 2]),
-                                               __uint_as_float(lo[4 * q + 3]));
-#pragma unroll
-                        for (int q = 0; q < 8; ++q)
-                            ptx::st_cluster_v4(dst + ((8 + q) * 32 + lane) * 16, __uint_as_float(hi[4 * q]),
-                                               __uint_as_float(hi[4 * q + 1]), __uint_as_float(hi[4 * q + 2]),
-                                               __uint_as_float(hi[4 * q + 3]));
-                        sent |= 1u << owner;
+                        ptx::bulk_copy_to_cluster(
+                            ptx::mapa_shared(ptx::smem_addr(received + slot * 512), static_cast<uint32_t>(owner)),
+                            ptx::smem_addr(parts + piece * 512), 8192u,
+                            ptx::mapa_shared(ptx::smem_addr(recv_full), static_cast<uint32_t>(owner)));
                     }
-                    // Each lane releases its own stores, once per owner.
-                    for (int r = 0; r < splits; ++r)
-                        if (sent & (1u << r))
-                            ptx::mbar_arrive_release_cluster(
-                                ptx::mapa_shared(ptx::smem_addr(recv_full), static_cast<uint32_t>(r)));
                 }
                 bool waited = false;
 #pragma unroll 1
-                for (int c = 0; c < kChunks && go; ++c) {
+                for (int c = 0; c < kChunks; ++c) {
                     const int piece = quarter * kChunks + c;
                     if (piece % splits != s) continue;
                     if (!waited) {
@@ -485,7 +477,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             break;
                         }
                     }
-                    const float4* slots = recv + (piece / splits) * (splits - 1) * 512;
+                    const float4* slots = received + (piece / splits) * (splits - 1) * 512;
                     uint32_t lo[32], hi[32];
                     // Split order, as the workspace path adds: split 0 first.
                     if (s == 0) {
@@ -705,9 +697,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         // (The scatter form syncs the cluster below instead.)
         if (!kScatter && cluster_mode && blockIdx.x % splits == 0 && !got_recv)
             ptx::mbar_wait_cluster(recv_full, 0, drain_limit(limit_ns), no_abort);
+        // A scatter warp that gave up before the meeting (stages mode)
+        // still takes its phase, so the other CTAs' barrier completes.
+        if (kScatter && recv_mode == kClusterStages && !met) {
+            ptx::cluster_arrive();
+            ptx::cluster_wait();
+        }
     }
 
-    if (cluster_mode && warp < 2) ptx::cluster_wait();  // pairs this thread's arrive after set-up
+    if (cluster_mode && warp < 2) {
+        ptx::cluster_wait();  // pairs this thread's arrive after set-up
+        if (kScatter && recv_mode == kClusterStages) {
+            // The scatter form's meeting counts every thread.
+            ptx::cluster_arrive();
+            ptx::cluster_wait();
+        }
+    }
     ptx::tc_fence_before();
     __syncthreads();
     // Receiving in its stages, rank 0 signalled the other ranks' barriers and
@@ -722,31 +727,34 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // ------------------------------------------------------------------ host side
 
-// Pieces (32 rows x 64 columns) of a 128-row tile, and whether a scatter
-// split of `splits` ranks runs: 128-row tiles, every rank owning a piece.
-int scatter_pieces(int bn) { return 4 * (bn / 64); }
-bool scatter_fits(int bn, int ar, int splits) { return ar == kBM && splits <= scatter_pieces(bn); }
+// Whether a scatter split of `splits` ranks runs: 128-row tiles, every rank
+// owning a piece, and the stages holding every piece (8 KB of FP32 each)
+// plus the busiest rank's received copies.
+// Copies the busiest rank of a scatter split receives (8 KB each).
+int scatter_received(int bn, int splits) { return (scatter_pieces_of(bn) + splits - 1) / splits * (splits - 1); }
 
 // Shared memory a receiving rank of a cluster split K needs beyond the
-// kernel's own: rank 0, one slot of FP32 values per other rank; scatter, a
-// 32 x 64 FP32 slot per other rank for each piece the busiest rank owns.
+// kernel's own: rank 0, one slot of FP32 values per other rank; scatter,
+// its received copies.
 int cluster_recv_bytes(int bn, int ar, int splits, bool scatter) {
-    if (scatter) {
-        const int owned = (scatter_pieces(bn) + splits - 1) / splits;
-        return owned * (splits - 1) * 32 * 64 * 4;
-    }
-    return (splits - 1) * ar * bn * 4;
+    return scatter ? scatter_received(bn, splits) * 8192 : (splits - 1) * ar * bn * 4;
 }
 
-// Where the receiving ranks of a cluster split K of `s` splits receive: a
-// buffer past their own shared memory when that stays within 227 KB, else
-// their pipeline stages when those hold the values, else nowhere (0); with
-// kClusterScatter when the scatter form is asked for and fits.
+// How a cluster split K of `s` splits adds up.  Scatter (asked for; 128-row
+// tiles, every rank owning a piece, the pieces in the stages): receiving in
+// a buffer past the kernel's own shared memory when that stays within 227
+// KB, else past the pieces in the stages when they hold both.  Otherwise
+// rank 0 receives: in such a buffer, else in its stages, else nowhere (0).
 int cluster_receive_mode(int s, int64_t own_smem, int64_t stage_bytes, int bn, int ar, bool scatter) {
-    scatter = scatter && scatter_fits(bn, ar, s);
-    const int64_t bytes = cluster_recv_bytes(bn, ar, s, scatter);
-    const int mode = own_smem + bytes <= kMaxSmem ? kClusterBuffer : bytes <= stage_bytes ? kClusterStages : 0;
-    return mode && scatter ? mode | kClusterScatter : mode;
+    const int pieces = scatter_pieces_of(bn);
+    if (scatter && ar == kBM && s <= pieces && static_cast<int64_t>(pieces) * 8192 <= stage_bytes) {
+        if (own_smem + cluster_recv_bytes(bn, ar, s, true) <= kMaxSmem) return kClusterScatter | kClusterBuffer;
+        if (static_cast<int64_t>(pieces + scatter_received(bn, s)) * 8192 <= stage_bytes)
+            return kClusterScatter | kClusterStages;
+    }
+    if (own_smem + cluster_recv_bytes(bn, ar, s, false) <= kMaxSmem) return kClusterBuffer;
+    if (cluster_recv_bytes(bn, ar, s, false) <= stage_bytes) return kClusterStages;
+    return 0;
 }
 
 // K splits of a cluster split K for this launch (and where ranks receive,
@@ -986,6 +994,15 @@ int cluster_split_cap(const kmcts_gemm_config& cfg, int b_layout) {
     const bool scatter = (cfg.flags & KMCTS_FLAG_SPLIT_SCATTER) != 0;
     while (cap < kMaxClusterSplits && cluster_receive_mode(cap + 1, own, stage_bytes, cfg.tile_n, ar, scatter)) ++cap;
     return cap;
+}
+
+bool cluster_split_fits(const kmcts_gemm_config& cfg, int b_layout, int splits) {
+    if (!is_one_cta(cfg) || is_swapped(cfg) || cfg.tile_n <= 0 || splits < 2 || splits > kMaxClusterSplits) return false;
+    const int ar = a_rows(cfg);
+    const int64_t stage_bytes = static_cast<int64_t>(cfg.stages) * (ar + cfg.tile_n) * cfg.tile_k * 2;
+    const int mode = cluster_receive_mode(splits, tcgen05_smem_bytes(cfg, b_layout), stage_bytes, cfg.tile_n, ar,
+                                          (cfg.flags & KMCTS_FLAG_SPLIT_SCATTER) != 0);
+    return mode != 0 && ((mode & kClusterScatter) != 0) == ((cfg.flags & KMCTS_FLAG_SPLIT_SCATTER) != 0);
 }
 
 int cluster_capacity(const kmcts_gemm_config& cfg, int b_layout, int splits) {

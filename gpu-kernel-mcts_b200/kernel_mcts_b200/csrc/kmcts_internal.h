@@ -33,6 +33,9 @@ int64_t tcgen05_smem_bytes(const kmcts_gemm_config& cfg, int b_layout);
 // (KMCTS_FLAG_SPLIT_CLUSTER): the receive buffer must fit beside its own
 // shared memory, and a cluster holds at most 8 CTAs.  1 when none fits.
 int cluster_split_cap(const kmcts_gemm_config& cfg, int b_layout);
+// Whether a cluster split K of `splits` CTAs runs for cfg's schedule in the
+// form its flags ask for (the scatter form's fit is not monotonic in splits).
+bool cluster_split_fits(const kmcts_gemm_config& cfg, int b_layout, int splits);
 // Clusters of a cluster split K of `splits` CTAs (cfg's schedule and split
 // flags) that can be resident at once on the current device, from the
 // occupancy calculator; 0 where it cannot say (no device, or no such split).

@@ -285,6 +285,26 @@ __device__ __forceinline__ void st_cluster_v4(uint32_t cluster_addr, float a, fl
                  : "memory");
 }
 
+// Bulk copy of `bytes` (a multiple of 16; both addresses 16-byte aligned)
+// from this CTA's shared memory into the shared memory of a CTA of the
+// cluster (`dst` and `bar` from mapa_shared), completing that many
+// transaction bytes on the destination CTA's mbarrier `bar`.  No multicast.
+__device__ __forceinline__ void bulk_copy_to_cluster(uint32_t dst, uint32_t src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(dst), "r"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+
+// 16-byte load from the shared memory of any CTA of the cluster.
+__device__ __forceinline__ float4 ld_cluster_v4(uint32_t cluster_addr) {
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(cluster_addr)
+                 : "memory");
+    return v;
+}
+
 // Arrive on an mbarrier of any CTA of the cluster, releasing this thread's
 // earlier writes (its st_cluster_v4 stores included) at cluster scope.
 __device__ __forceinline__ void mbar_arrive_release_cluster(uint32_t cluster_addr) {

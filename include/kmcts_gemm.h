@@ -104,12 +104,15 @@ extern "C" {
 /* With KMCTS_FLAG_SPLIT_CLUSTER on tile_m 128: the additions spread over the
  * cluster instead of meeting in split 0.  The tile's pieces of 32 rows x 64
  * columns are numbered quarter * (tile_n / 64) + chunk, and piece p belongs
- * to split p % k_splits: every split stores the pieces it does not own into
- * their owners' shared memory, then adds its own pieces in split order (the
- * same bits as the workspace path) and writes them.  A split receives
- * ceil(pieces / k_splits) x (k_splits - 1) x 8 KB, extra shared memory or its
- * pipeline stages as above.  Where k_splits exceeds the pieces, or tile_m is
- * not 128, the splits add up in split 0 as without this flag. */
+ * to split p % k_splits: every split copies the FP32 values of the pieces it
+ * does not own into their owners' shared memory (bulk shared-memory copies,
+ * no multicast), then adds its own pieces in split order (the same bits as
+ * the workspace path) and writes them.  A split receives ceil(pieces /
+ * k_splits) x (k_splits - 1) x 8 KB: in extra shared memory when that stays
+ * within 227 KB, else in its pipeline stages once every split's MMAs are
+ * done (the stages also hold its outgoing pieces).  Where k_splits exceeds
+ * the pieces, or tile_m is not 128, the splits add up in split 0 as without
+ * this flag; where neither fits, through the workspace. */
 #define KMCTS_FLAG_SPLIT_SCATTER 256
 
 #define KMCTS_TAIL_NONE 0     /* kmcts_gemm_plan.tail_split: every tile whole */

@@ -775,9 +775,10 @@ def test_cluster_split_k_same_bits_as_workspace_split_k(cuda_device, layout, til
     (128, 128, 3, (70, 520, 1032), 3, _native.SPLIT_SCATTER),    # a quarter past M, ragged K
     (128, 128, 3, (128, 128, 4096), 7, _native.SPLIT_SCATTER),   # rank 0 owns two pieces
     (64, 64, 6, (512, 512, 4096), 4, _native.SPLIT_SCATTER),     # 64-column tiles: 4 pieces
-    (256, 64, 3, (384, 768, 4096), 8, _native.SPLIT_SCATTER),    # 16 pieces, two per rank
-    (256, 64, 3, (200, 520, 1000), 5, _native.SPLIT_SCATTER),    # 16 pieces over 5 ranks, ragged
+    (256, 128, 2, (384, 768, 4096), 2, _native.SPLIT_SCATTER),   # 16 pieces, eight per rank
+    (128, 64, 5, (200, 520, 1000), 5, _native.SPLIT_SCATTER),    # 8 pieces over 5 ranks, ragged
     (64, 64, 6, (256, 256, 2048), 5, _native.SPLIT_CLUSTER),     # more ranks than pieces: split 0 adds
+    (256, 64, 3, (384, 768, 4096), 8, _native.SPLIT_WORKSPACE),  # pieces and copies exceed the stages
 ])
 def test_scatter_split_k_same_bits_as_workspace_split_k(cuda_device, layout, tile_n, tile_k, stages, shape, splits,
                                                         reduce):
@@ -785,13 +786,16 @@ def test_scatter_split_k_same_bits_as_workspace_split_k(cuda_device, layout, til
     the cluster (piece p of 32 rows x 64 columns to rank p % splits): exact
     on integer inputs, and on N(0,1) inputs the same bits as the workspace
     reduction (each piece adds its splits in split order), launch after
-    launch.  With more splits than pieces the splits add up in split 0."""
+    launch.  With more splits than pieces the splits add up in split 0; where
+    the pieces and the copies received do not fit the stages, the workspace
+    path runs."""
     m, n, k = shape
     base = dict(kernel=_native.KERNEL_TCGEN05, tile_m=128, cluster_m=1, tile_n=tile_n, tile_k=tile_k,
                 stages=stages, k_splits=splits)
     flagged = dict(base, flags=_native.FLAG_SPLIT_CLUSTER | _native.FLAG_SPLIT_SCATTER)
     plan = plan_of(m, n, k, layout, **flagged)
-    assert plan["cluster_size"] == splits and plan["split_reduce"] == reduce, plan
+    clustered = reduce != _native.SPLIT_WORKSPACE
+    assert plan["cluster_size"] == (splits if clustered else 1) and plan["split_reduce"] == reduce, plan
     assert plan_of(m, n, k, layout, **base)["split_reduce"] == _native.SPLIT_WORKSPACE
     a_t, b_t = oracle.integer_inputs(m, n, k, seed=splits + m)
     expect = oracle.torch_bits(oracle.torch_reference(a_t, b_t))

@@ -97,9 +97,11 @@ def test_select_config_splits_k_for_skinny_shapes():
     assert m128.flags & scatter == scatter and m128.flags & _native.FLAG_B_EVICT_FIRST
     sq = km.select_config(512, 512, 8192, km.B_ROW)
     assert (sq.tile_n, sq.tile_k, sq.stages, sq.k_splits) == (128, 128, 3, 6) and sq.flags & scatter == scatter
-    # Eight splits (nine tiles) or short ranges: 64-deep stages, receiving outside them.
+    # Ranges of at most 1024: 64-deep stages, receiving past them; longer: 128-deep.
     eight = km.select_config(384, 384, 8192, km.B_ROW)
     assert (eight.tile_k, eight.stages, eight.k_splits) == (64, 4, 8) and eight.flags & scatter == scatter
+    deep = km.select_config(256, 512, 16384, km.B_ROW)
+    assert (deep.tile_k, deep.stages, deep.k_splits) == (128, 3, 8) and deep.flags & scatter == scatter
     short = km.select_config(300, 1000, 2048, km.B_ROW)
     assert (short.tile_k, short.stages, short.k_splits) == (64, 4, 4) and short.flags & scatter == scatter
     assert km.select_config(1024, 1024, 8192, km.B_ROW).k_splits == 2
