@@ -101,9 +101,10 @@ struct Layout {
 //   kClusterStages  its pipeline stages, free once its UMMAs are done: rank 0
 //                   then signals each sender's go barrier, senders wait for
 //                   it before storing, and the cluster syncs before exit.
-// kClusterScatter (128-row tiles) spreads the additions over the cluster:
-// the tile's pieces of 32 rows x 64 columns (lane quarter q, chunk c) are
-// numbered q * (BN / 64) + c, and piece p belongs to rank p % splits.  Each
+// kClusterScatter spreads the additions over the cluster: the tile's pieces
+// of 32 rows x 64 columns (lane quarter q < AR / 32, chunk c) are numbered
+// q * (BN / 64) + c, and piece p belongs to rank p % splits (ranks past the
+// pieces own none and only send).  Each
 // rank writes the FP32 values of every piece it does not own into its own
 // pipeline stages (free once its UMMAs are done; piece p at p x 8 KB), then
 // one lane per warp copies each of them into its owner's shared memory with
@@ -127,8 +128,8 @@ struct SplitK {
     int cluster;  // 0 (workspace), or kClusterBuffer or kClusterStages, with kClusterScatter
 };
 
-// Pieces (32 rows x 64 columns) of a 128-row tile.
-__host__ __device__ constexpr int scatter_pieces_of(int bn) { return 4 * (bn / 64); }
+// Pieces (32 rows x 64 columns) of a tile staging `ar` rows of A.
+__host__ __device__ constexpr int scatter_pieces_of(int bn, int ar) { return (ar / 32) * (bn / 64); }
 
 template <int BN>
 __device__ __forceinline__ float4* split_chunk(const SplitK& sk, int tile, int split, int quarter, int c) {
@@ -144,7 +145,7 @@ __device__ __forceinline__ int recv_chunk(int slot, int quarter, int c, int rows
 }
 
 // FEAT selects what an instantiation carries: bit 0 the cache-hinted loads,
-// bit 1 the cluster split K, bit 2 its scatter form (128-row tiles).  Code a
+// bit 1 the cluster split K, bit 2 its scatter form.  Code a
 // schedule does not use is compiled out (a runtime branch in the producer's
 // loop costs the common schedules 1-2 us per launch); the launcher picks the
 // smallest instantiation that serves.
@@ -158,7 +159,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                       uint64_t limit_ns, int* status, const SplitK sk, int evict_first) {
     using L = Layout<BN, BK, STAGES, B_MN, AR>;
     constexpr bool kScatter = (FEAT & kFeatScatter) != 0;
-    static_assert(!kScatter || ((FEAT & kFeatCluster) && AR == kBM), "the scatter split takes 128-row tiles");
+    static_assert(!kScatter || (FEAT & kFeatCluster), "the scatter split is a cluster split K");
     const int cluster_mode = (FEAT & kFeatCluster) ? sk.cluster : 0;  // compile-time 0 otherwise
     const int recv_mode = cluster_mode & (kClusterBuffer | kClusterStages);
     extern __shared__ uint8_t smem_raw[];
@@ -258,7 +259,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         ptx::mbar_init(go_bar, 1);
         if (kScatter && cluster_mode) {
             // The bytes the other ranks copy in: 8 KB per owned piece and sender.
-            const int owned = (scatter_pieces_of(BN) - static_cast<int>(blockIdx.x % splits) + splits - 1) / splits;
+            // (None for ranks past the pieces: they only send.)
+            const int owned =
+                (scatter_pieces_of(BN, AR) - static_cast<int>(blockIdx.x % splits) + splits - 1) / splits;
             ptx::fence_mbarrier_init();
             ptx::mbar_arrive_expect_tx(recv_full, static_cast<uint32_t>(owned * (splits - 1) * 8192));
         }
@@ -422,10 +425,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // Received copies: past the pieces in the stages, or in the
                 // buffer past the barriers (free from the start: no meeting).
                 const bool in_stages = recv_mode == kClusterStages;
-                float4* received = in_stages ? parts + scatter_pieces_of(BN) * 512 : recv;
+                float4* received = in_stages ? parts + scatter_pieces_of(BN, AR) * 512 : recv;
+                // Only the lane quarters below AR hold rows of the tile.
+                const int quarter_chunks = quarter < AR / 32 ? kChunks : 0;
                 ptx::fence_proxy_async_smem();  // generic writes after the async proxy's use
 #pragma unroll 1
-                for (int c = 0; c < kChunks; ++c) {
+                for (int c = 0; c < quarter_chunks; ++c) {
                     const int piece = quarter * kChunks + c;
                     if (piece % splits == s) continue;
                     uint32_t lo[32], hi[32];
@@ -452,7 +457,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     __syncwarp();  // lane 0 copies what the warp wrote
                 }
                 if (lane == 0) {
-                    for (int c = 0; c < kChunks; ++c) {
+                    for (int c = 0; c < quarter_chunks; ++c) {
                         const int piece = quarter * kChunks + c;
                         const int owner = piece % splits;
                         if (owner == s) continue;
@@ -465,7 +470,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 bool waited = false;
 #pragma unroll 1
-                for (int c = 0; c < kChunks; ++c) {
+                for (int c = 0; c < quarter_chunks; ++c) {
                     const int piece = quarter * kChunks + c;
                     if (piece % splits != s) continue;
                     if (!waited) {
@@ -731,25 +736,27 @@ __global__ void __launch_bounds__(kThreads, 1)
 // owning a piece, and the stages holding every piece (8 KB of FP32 each)
 // plus the busiest rank's received copies.
 // Copies the busiest rank of a scatter split receives (8 KB each).
-int scatter_received(int bn, int splits) { return (scatter_pieces_of(bn) + splits - 1) / splits * (splits - 1); }
+int scatter_received(int bn, int ar, int splits) {
+    return (scatter_pieces_of(bn, ar) + splits - 1) / splits * (splits - 1);
+}
 
 // Shared memory a receiving rank of a cluster split K needs beyond the
 // kernel's own: rank 0, one slot of FP32 values per other rank; scatter,
 // its received copies.
 int cluster_recv_bytes(int bn, int ar, int splits, bool scatter) {
-    return scatter ? scatter_received(bn, splits) * 8192 : (splits - 1) * ar * bn * 4;
+    return scatter ? scatter_received(bn, ar, splits) * 8192 : (splits - 1) * ar * bn * 4;
 }
 
-// How a cluster split K of `s` splits adds up.  Scatter (asked for; 128-row
-// tiles, every rank owning a piece, the pieces in the stages): receiving in
-// a buffer past the kernel's own shared memory when that stays within 227
-// KB, else past the pieces in the stages when they hold both.  Otherwise
-// rank 0 receives: in such a buffer, else in its stages, else nowhere (0).
+// How a cluster split K of `s` splits adds up.  Scatter (asked for, the
+// pieces in the stages): receiving in a buffer past the kernel's own shared
+// memory when that stays within 227 KB, else past the pieces in the stages
+// when they hold both.  Otherwise rank 0 receives: in such a buffer, else in
+// its stages, else nowhere (0).
 int cluster_receive_mode(int s, int64_t own_smem, int64_t stage_bytes, int bn, int ar, bool scatter) {
-    const int pieces = scatter_pieces_of(bn);
-    if (scatter && ar == kBM && s <= pieces && static_cast<int64_t>(pieces) * 8192 <= stage_bytes) {
+    const int pieces = scatter_pieces_of(bn, ar);
+    if (scatter && static_cast<int64_t>(pieces) * 8192 <= stage_bytes) {
         if (own_smem + cluster_recv_bytes(bn, ar, s, true) <= kMaxSmem) return kClusterScatter | kClusterBuffer;
-        if (static_cast<int64_t>(pieces + scatter_received(bn, s)) * 8192 <= stage_bytes)
+        if (static_cast<int64_t>(pieces + scatter_received(bn, ar, s)) * 8192 <= stage_bytes)
             return kClusterScatter | kClusterStages;
     }
     if (own_smem + cluster_recv_bytes(bn, ar, s, false) <= kMaxSmem) return kClusterBuffer;
@@ -794,13 +801,10 @@ int resolve_splits(int M, int N, int K, int requested, cudaStream_t stream, Spli
 }
 
 // The four instantiations of a one-CTA schedule: plain, cache hints only,
-// cluster split K (with hints), and its scatter form.  The scatter form
-// exists for 128-row tiles only (elsewhere the same instantiation as the
-// cluster kernel; cluster_receive_mode never asks for it).
+// cluster split K (with hints), and its scatter form.
 template <int BN, int BK, int STAGES, bool B_MN, int AR>
 struct Kernels {
-    static constexpr int kScatterFeat =
-        AR == kBM ? (kFeatHints | kFeatCluster | kFeatScatter) : (kFeatHints | kFeatCluster);
+    static constexpr int kScatterFeat = kFeatHints | kFeatCluster | kFeatScatter;
     static constexpr auto plain = gemm_bf16_tcgen05<BN, BK, STAGES, B_MN, AR, 0>;
     static constexpr auto hint = gemm_bf16_tcgen05<BN, BK, STAGES, B_MN, AR, kFeatHints>;
     static constexpr auto cluster = gemm_bf16_tcgen05<BN, BK, STAGES, B_MN, AR, kFeatHints | kFeatCluster>;

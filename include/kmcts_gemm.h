@@ -101,18 +101,19 @@ extern "C" {
  * are large enough).  Every unit runs in its own CTA (units no more than the
  * SMs when persistent); otherwise the workspace path runs. */
 #define KMCTS_FLAG_SPLIT_CLUSTER 64
-/* With KMCTS_FLAG_SPLIT_CLUSTER on tile_m 128: the additions spread over the
- * cluster instead of meeting in split 0.  The tile's pieces of 32 rows x 64
- * columns are numbered quarter * (tile_n / 64) + chunk, and piece p belongs
- * to split p % k_splits: every split copies the FP32 values of the pieces it
- * does not own into their owners' shared memory (bulk shared-memory copies,
- * no multicast), then adds its own pieces in split order (the same bits as
- * the workspace path) and writes them.  A split receives ceil(pieces /
- * k_splits) x (k_splits - 1) x 8 KB: in extra shared memory when that stays
- * within 227 KB, else in its pipeline stages once every split's MMAs are
- * done (the stages also hold its outgoing pieces).  Where k_splits exceeds
- * the pieces, or tile_m is not 128, the splits add up in split 0 as without
- * this flag; where neither fits, through the workspace. */
+/* With KMCTS_FLAG_SPLIT_CLUSTER: the additions spread over the cluster
+ * instead of meeting in split 0.  The tile's pieces of 32 rows x 64 columns
+ * (rows = tile_m for tile_m 32 or 64, else 128) are numbered quarter *
+ * (tile_n / 64) + chunk, and piece p belongs to split p % k_splits (splits
+ * past the pieces own none): every split copies the FP32 values of the
+ * pieces it does not own into their owners' shared memory (bulk
+ * shared-memory copies, no multicast), then adds its own pieces in split
+ * order (the same bits as the workspace path) and writes them.  A split
+ * receives at most ceil(pieces / k_splits) x (k_splits - 1) x 8 KB: in extra
+ * shared memory when that stays within 227 KB, else in its pipeline stages
+ * once every split's MMAs are done (the stages also hold its outgoing
+ * pieces).  Where neither fits, the splits add up in split 0 as without
+ * this flag, or through the workspace. */
 #define KMCTS_FLAG_SPLIT_SCATTER 256
 
 #define KMCTS_TAIL_NONE 0     /* kmcts_gemm_plan.tail_split: every tile whole */

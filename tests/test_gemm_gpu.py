@@ -777,7 +777,7 @@ def test_cluster_split_k_same_bits_as_workspace_split_k(cuda_device, layout, til
     (64, 64, 6, (512, 512, 4096), 4, _native.SPLIT_SCATTER),     # 64-column tiles: 4 pieces
     (256, 128, 2, (384, 768, 4096), 2, _native.SPLIT_SCATTER),   # 16 pieces, eight per rank
     (128, 64, 5, (200, 520, 1000), 5, _native.SPLIT_SCATTER),    # 8 pieces over 5 ranks, ragged
-    (64, 64, 6, (256, 256, 2048), 5, _native.SPLIT_CLUSTER),     # more ranks than pieces: split 0 adds
+    (64, 64, 6, (256, 256, 2048), 5, _native.SPLIT_SCATTER),     # more ranks than pieces: rank 4 only sends
     (256, 64, 3, (384, 768, 4096), 8, _native.SPLIT_WORKSPACE),  # pieces and copies exceed the stages
 ])
 def test_scatter_split_k_same_bits_as_workspace_split_k(cuda_device, layout, tile_n, tile_k, stages, shape, splits,
@@ -786,9 +786,8 @@ def test_scatter_split_k_same_bits_as_workspace_split_k(cuda_device, layout, til
     the cluster (piece p of 32 rows x 64 columns to rank p % splits): exact
     on integer inputs, and on N(0,1) inputs the same bits as the workspace
     reduction (each piece adds its splits in split order), launch after
-    launch.  With more splits than pieces the splits add up in split 0; where
-    the pieces and the copies received do not fit the stages, the workspace
-    path runs."""
+    launch.  Splits past the pieces only send; where the pieces and the
+    copies received do not fit the stages, the workspace path runs."""
     m, n, k = shape
     base = dict(kernel=_native.KERNEL_TCGEN05, tile_m=128, cluster_m=1, tile_n=tile_n, tile_k=tile_k,
                 stages=stages, k_splits=splits)
@@ -808,6 +807,35 @@ def test_scatter_split_k_same_bits_as_workspace_split_k(cuda_device, layout, til
     second = run(a, b, layout, **flagged)
     assert torch.equal(first.view(torch.int16), workspace.view(torch.int16))
     assert torch.equal(second.view(torch.int16), workspace.view(torch.int16))
+
+
+@pytest.mark.parametrize("layout", ["col", "row"])
+@pytest.mark.parametrize("tile_m,tile_n,tile_k,stages,shape,splits", [
+    (32, 128, 128, 4, (16, 8192, 8192), 2),    # 2 pieces, one per rank
+    (32, 64, 128, 8, (16, 1024, 16384), 6),    # 1 piece: ranks 1-5 only send
+    (32, 128, 128, 4, (7, 2048, 1032), 3),     # ragged M and K
+    (32, 256, 64, 5, (16, 1024, 2048), 2),     # 4 pieces
+    (64, 128, 128, 3, (64, 8192, 8192), 2),    # two lane quarters: 4 pieces
+    (64, 64, 128, 6, (50, 1000, 4096), 4),     # ragged, 2 pieces over 4 ranks
+])
+def test_scatter_split_k_skinny_same_bits_as_workspace_split_k(cuda_device, layout, tile_m, tile_n, tile_k, stages,
+                                                               shape, splits):
+    """The scatter form on tiles staging 32 or 64 rows of A (only their lane
+    quarters hold pieces): exact on integer inputs and the workspace path's
+    bits on N(0,1) inputs."""
+    m, n, k = shape
+    base = dict(kernel=_native.KERNEL_TCGEN05, tile_m=tile_m, cluster_m=1, tile_n=tile_n, tile_k=tile_k,
+                stages=stages, k_splits=splits)
+    flagged = dict(base, flags=_native.FLAG_SPLIT_CLUSTER | _native.FLAG_SPLIT_SCATTER)
+    plan = plan_of(m, n, k, layout, **flagged)
+    assert plan["cluster_size"] == splits and plan["split_reduce"] == _native.SPLIT_SCATTER, plan
+    a_t, b_t = oracle.integer_inputs(m, n, k, seed=splits + m + 1)
+    c = run(a_t.cuda(), b_for(layout, b_t.cuda()), layout, **flagged)
+    np.testing.assert_array_equal(bits_of(c), oracle.torch_bits(oracle.torch_reference(a_t, b_t)))
+    a_t, b_t = oracle.randn_inputs(m, n, k, seed=7, b_layout=layout)
+    a, b = a_t.cuda(), b_t.cuda()
+    workspace = run(a, b, layout, **base)
+    assert torch.equal(run(a, b, layout, **flagged).view(torch.int16), workspace.view(torch.int16))
 
 
 @pytest.mark.parametrize("layout", ["col", "row"])
