@@ -152,16 +152,48 @@ bool scatter_schedule(long long tiles, int K, int b_layout, int sms, kmcts_gemm_
     return false;
 }
 
+// M <= 64 (tiles staging 32 or 64 rows of A, 128 columns wide, one tile
+// row), K >= 4096: the tile's K splits as one cluster, as many as keep every
+// unit on its own SM, every cluster resident and K ranges of at least 512
+// (at most 8), added up by the scatter form (two splits of 32-row tiles by
+// split 0).  Measured, L2 flushed, means (previous selection: 64-column tiles
+// for narrow N and at most six splits, added up in split 0 -> this, cuBLAS):
+// 16 x 1024 x 32768 32.3 -> 27.8 us (36.0), 16 x 1024 x 16384 22.6 -> 20.5
+// (23.6), 16 x 2048 x 16384 27.0 -> 24.7 (37.6), 16 x 2048 x 8192 20.2 ->
+// 18.5 (18.6), 33 x 1024 x 16384 23.3 -> 22.2 (27.3), 48 x 4096 x 8192 26.5 ->
+// 24.0 (22.9), 64 x 2048 x 8192 21.3 -> 20.2 (19.8), 64 x 1024 x 8192 19.1 ->
+// 18.2 (17.7), 64 x 4096 x 4096 19.6 -> 18.8 (16.2).  False when none fits.
+bool skinny_cluster_split(long long tiles, int K, int b_layout, int sms, kmcts_gemm_config* cfg) {
+    if (tiles <= 0 || 2 * tiles > sms || K < 4096) return false;
+    int s = static_cast<int>(sms / tiles);
+    if (s > 8) s = 8;
+    if (s > K / 512) s = K / 512;
+    for (; s >= 2; --s) {
+        kmcts_gemm_config c = *cfg;
+        c.k_splits = s;
+        c.flags |= KMCTS_FLAG_SPLIT_CLUSTER;
+        if (!(c.tile_m == 32 && s == 2)) c.flags |= KMCTS_FLAG_SPLIT_SCATTER;
+        int capacity = cluster_capacity(c, b_layout, s);
+        if (capacity <= 0) capacity = fallback_cluster_capacity(s, sms);
+        if (tiles <= capacity && cluster_split_fits(c, b_layout, s)) {
+            *cfg = c;
+            return true;
+        }
+    }
+    return false;
+}
+
 }  // namespace
 
 // The schedule for the shape; kmcts_select_config adds the A-side cache policy.
 static int select_schedule(int M, int N, int K, int b_layout, kmcts_gemm_config* cfg) {
     kmcts_default_config(cfg);
     // Measured on B200 (CUDA-graph replays, warm L2):
-    // * M <= 32: one CTA per tile staging 32 rows of A (more B in flight per
-    //   SM; the problem is bound by reading B): 128 x 256 tiles when they
-    //   fill the SMs' pairs count, else 128 x 128 with split K on long K;
-    //   B's loads at L2 evict-first priority (it is read once);
+    // * M <= 64: one CTA per tile staging 32 or 64 rows of A (more B in
+    //   flight per SM; the problem is bound by reading B): for M <= 32,
+    //   128 x 256 tiles when they fill the SMs' pairs count; else 128-column
+    //   tiles with split K over one cluster per tile on long K; B's loads at
+    //   L2 evict-first priority (it is read once);
     // * the CTA-pair 256 x 256 schedule once its tiles fill the co-resident
     //   pairs (with 64-deep stages when K <= 768), or, split in two along K,
     //   when two units per tile fill three quarters of them and K >= 8192;
@@ -181,6 +213,16 @@ static int select_schedule(int M, int N, int K, int b_layout, kmcts_gemm_config*
     small.cluster_m = 1;
     if (M > 0 && M <= 32) {
         small.tile_m = 32;
+        kmcts_gemm_config split = small;
+        split.tile_n = 128;
+        split.tile_k = 128;
+        split.stages = 4;
+        split.flags |= KMCTS_FLAG_B_EVICT_FIRST;  // one tile row: B is read once
+        if ((N + 255) / 256 < workers && skinny_cluster_split((N + 127) / 128, K, b_layout, sms, &split) &&
+            tcgen05_legal(split, M, N, K, b_layout, nullptr, 0) == KMCTS_OK) {
+            *cfg = split;
+            return KMCTS_OK;
+        }
         if ((N + 255) / 256 >= workers) {
             small.tile_n = 256;
             small.tile_k = 64;
@@ -227,6 +269,16 @@ static int select_schedule(int M, int N, int K, int b_layout, kmcts_gemm_config*
         // against 22.5, 64 x 8192 x 8192 33.9 against 35.1, 64 x 16384 x 4096
         // 30.8 against 31.5.
         small.tile_m = 64;
+        kmcts_gemm_config split = small;
+        split.tile_n = 128;
+        split.tile_k = 128;
+        split.stages = 3;
+        split.flags |= KMCTS_FLAG_B_EVICT_FIRST;
+        if (skinny_cluster_split((N + 127) / 128, K, b_layout, sms, &split) &&
+            tcgen05_legal(split, M, N, K, b_layout, nullptr, 0) == KMCTS_OK) {
+            *cfg = split;
+            return KMCTS_OK;
+        }
         small.tile_k = 128;
         if (2 * ((N + 63) / 64) <= sms) {
             small.tile_n = 64;

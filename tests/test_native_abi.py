@@ -70,29 +70,31 @@ def test_select_config_splits_k_for_skinny_shapes():
     wide = km.select_config(8, 28672, 8192, km.B_ROW)
     assert (wide.tile_m, wide.tile_n, wide.k_splits) == (32, 256, 0)  # 112 tiles: no split
     assert not wide.flags & _native.FLAG_SPLIT_CLUSTER
-    # Narrow N: 64-column tiles; 32 of them fill the SMs with four splits each,
-    # added up in shared memory.
+    # Fewer tiles: as many splits as keep every cluster resident (at most 8;
+    # the B200 capacities without a GPU: 16 clusters of 6, not of 7 or 8),
+    # added up across the cluster (scatter).
+    scatter = _native.FLAG_SPLIT_CLUSTER | _native.FLAG_SPLIT_SCATTER
     narrow = km.select_config(16, 2048, 16384, km.B_ROW)
-    assert (narrow.tile_m, narrow.tile_n, narrow.tile_k, narrow.stages, narrow.k_splits) == (32, 64, 128, 8, 4)
-    assert narrow.flags & _native.FLAG_SPLIT_CLUSTER
+    assert (narrow.tile_m, narrow.tile_n, narrow.tile_k, narrow.stages, narrow.k_splits) == (32, 128, 128, 4, 6)
+    assert narrow.flags & scatter == scatter
+    assert not cfg.flags & _native.FLAG_SPLIT_SCATTER  # two splits of 32-row tiles: split 0 adds
     assert km.select_config(16, 4096, 8192, km.B_ROW).k_splits == 4  # 32 tiles of 128 columns
-    # Nine splits would fill the SMs; clusters of more than six are not selected.
     long_k = km.select_config(16, 1024, 32768, km.B_ROW)
-    assert (long_k.tile_n, long_k.k_splits) == (64, 6) and long_k.flags & _native.FLAG_SPLIT_CLUSTER
+    assert (long_k.tile_n, long_k.k_splits) == (128, 8) and long_k.flags & scatter == scatter
     assert km.select_config(65, 8192, 8192, km.B_ROW).tile_m == 128
-    mid = km.select_config(64, 2048, 8192, km.B_ROW)  # 32 tiles of 64 x 64 rows/columns, four splits
-    assert (mid.tile_m, mid.tile_n, mid.stages, mid.k_splits) == (64, 64, 6, 4) and mid.flags & _native.FLAG_SPLIT_CLUSTER
+    mid = km.select_config(64, 2048, 8192, km.B_ROW)  # 16 tiles of 64 x 128, six splits
+    assert (mid.tile_m, mid.tile_n, mid.stages, mid.k_splits) == (64, 128, 3, 6) and mid.flags & scatter == scatter
     wide64 = km.select_config(64, 16384, 4096, km.B_ROW)  # 128 tiles of 128 columns: unsplit, four stages
     assert (wide64.tile_m, wide64.tile_n, wide64.stages, wide64.k_splits) == (64, 128, 4, 0)
     split64 = km.select_config(64, 8192, 8192, km.B_ROW)  # 64 tiles: two splits, three stages
     assert (split64.tile_m, split64.tile_n, split64.stages, split64.k_splits) == (64, 128, 3, 2)
-    assert km.select_config(33, 1024, 16384, km.B_ROW).k_splits == 6
-    # Few 128 x 128 tiles over a long K: each tile's K splits run as one
-    # cluster whose CTAs add up one share of the tile each, as many splits
-    # as keep every cluster resident (the B200 capacities without a GPU:
-    # 16 clusters of 6, not of 7 or 8).
+    assert split64.flags & scatter == scatter
+    assert km.select_config(33, 1024, 16384, km.B_ROW).k_splits == 8
+    for shape in ((16, 2048, 16384), (64, 2048, 8192), (33, 1024, 16384)):
+        plan = _native.plan(km.select_config(*shape, km.B_ROW), *shape, km.B_ROW)
+        assert plan["split_reduce"] == _native.SPLIT_SCATTER and plan["tiles"] <= plan["workers"], shape
+    # Few 128 x 128 tiles over a long K: the same, on 128-row tiles.
     m128 = km.select_config(128, 4096, 8192, km.B_ROW)
-    scatter = _native.FLAG_SPLIT_CLUSTER | _native.FLAG_SPLIT_SCATTER
     assert (m128.tile_n, m128.tile_k, m128.stages, m128.k_splits) == (128, 128, 3, 4)
     assert m128.flags & scatter == scatter and m128.flags & _native.FLAG_B_EVICT_FIRST
     sq = km.select_config(512, 512, 8192, km.B_ROW)
