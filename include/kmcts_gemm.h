@@ -166,8 +166,9 @@ int kmcts_default_config(kmcts_gemm_config* cfg);
 
 /* Fills *cfg with the schedule a NULL cfg selects for this shape: for M <= 32
  * or M <= 64, one CTA per tile staging 32 or 64 rows of A (tile_m 32 or 64),
- * its K splits added up in shared memory (KMCTS_FLAG_SPLIT_CLUSTER, at most
- * six); else the default when its
+ * 128 columns wide, and from K = 4096 its K splits as one cluster per tile
+ * (KMCTS_FLAG_SPLIT_CLUSTER; KMCTS_FLAG_SPLIT_SCATTER except for two splits
+ * of tile_m 32), as many as keep every cluster resident (at most 8); else the default when its
  * 256 x 256 pair tiles fill the co-resident CTA pairs (with 64-deep stages when
  * K <= 768), or in two K splits when those fill three quarters of them and
  * K >= 8192; else one CTA per
