@@ -337,7 +337,45 @@ static int select_schedule(int M, int N, int K, int b_layout, kmcts_gemm_config*
     // 256 x 8192 x 8192 49.0 against 52.4; at K = 4096, or with four splits,
     // one-CTA tiles win).  Not for M <= 128, where a 256-row pair tile would
     // be mostly empty.
+    // Three K splits when those fill at least three quarters of the pairs
+    // and two do not (L2 flushed, means, against the one-CTA 128 x 128
+    // schedule unsplit: 768 x 2048 x 8192 39.4 us against 43.3, 1024 x 1536 x
+    // 8192 38.9 against 42.7, 640 x 2048 x 8192 38.7 against 42.8).
+    if (M > 128 && pair_fits_n && 3 * pair_tiles <= workers && 4 * pair_tiles >= workers && K >= 8192) {
+        kmcts_gemm_config split = *cfg;
+        split.tile_k = 64;
+        split.stages = 6;
+        split.k_splits = 3;
+        split.flags |= pair_b_flags;
+        if (tcgen05_legal(split, M, N, K, b_layout, nullptr, 0) == KMCTS_OK) {
+            *cfg = split;
+            return KMCTS_OK;
+        }
+    }
     if (M > 128 && pair_fits_n && 2 * pair_tiles <= workers && 8 * pair_tiles >= 3 * workers && K >= 8192) {
+        // With more than two tile columns, one CTA per 128 x 256 tile in two
+        // K splits added up across a 2-CTA cluster does a little better
+        // (L2 flushed, means: 512 x 4096 x 8192 41.3 us against 43.5 for the
+        // pairs, 1024 x 2048 x 8192 41.8 against 42.8, 256 x 8192 x 8192 44.2
+        // against 44.5; 4096 x 512 x 16384 66.0 against 65.0 keeps the pairs).
+        if ((N + 255) / 256 > 2) {
+            kmcts_gemm_config wide = *cfg;
+            wide.tile_m = 128;
+            wide.cluster_m = 1;
+            wide.tile_n = 256;
+            wide.tile_k = 64;
+            wide.stages = 4;
+            wide.k_splits = 2;
+            wide.flags |= pair_b_flags | KMCTS_FLAG_SPLIT_CLUSTER | KMCTS_FLAG_SPLIT_SCATTER;
+            const long long wide_units = 2LL * ((M + 127) / 128) * ((N + 255) / 256);
+            int capacity = cluster_capacity(wide, b_layout, 2);
+            if (capacity <= 0) capacity = fallback_cluster_capacity(2, sms);
+            if (wide_units <= sms && wide_units / 2 <= capacity && cluster_split_fits(wide, b_layout, 2) &&
+                tcgen05_legal(wide, M, N, K, b_layout, nullptr, 0) == KMCTS_OK) {
+                *cfg = wide;
+                return KMCTS_OK;
+            }
+        }
         kmcts_gemm_config split = *cfg;
         split.tile_k = 64;
         split.stages = 6;

@@ -840,7 +840,7 @@ def test_scatter_split_k_skinny_same_bits_as_workspace_split_k(cuda_device, layo
 
 @pytest.mark.parametrize("layout", ["col", "row"])
 @pytest.mark.parametrize("shape", [(512, 512, 8192), (384, 384, 8192), (300, 1000, 2048), (2048, 256, 8192),
-                                   (1024, 1024, 8192)])
+                                   (1024, 1024, 8192), (512, 4096, 8192), (16, 2048, 16384), (48, 4096, 8192)])
 def test_scatter_selection_within_bound_and_exact_on_integers(cuda_device, layout, shape):
     """The NULL-config selection for few 128 x 128 tiles over a long K runs
     the scatter split: within the parity bound of the CPU oracle on N(0,1)
@@ -858,6 +858,29 @@ def test_scatter_selection_within_bound_and_exact_on_integers(cuda_device, layou
     ref32 = oracle.torch_bits(oracle.torch_reference(a_t, b_t, layout))
     ref64, mag = oracle.fp64_reference(a_t, b_t, layout)
     report = oracle.parity_report(bits_of(c), ref32, ref64, mag, k)
+    assert report["passed"], report
+
+
+@pytest.mark.parametrize("layout", ["col", "row"])
+@pytest.mark.parametrize("shape", [(768, 2048, 8192), (640, 2000, 8200)])
+def test_pair_three_split_selection_within_bound_and_exact_on_integers(cuda_device, layout, shape):
+    """19-24 pair tiles over a long K select three K splits of the CTA-pair
+    tiles (workspace reduction): within the parity bound of the CPU oracle,
+    exact on integer inputs, deterministic."""
+    m, n, k = shape
+    bl = _native.B_ROW if layout == "row" else _native.B_COL
+    sel = _native.select_config(m, n, k, bl)
+    assert (sel.tile_m, sel.k_splits) == (256, 3)
+    a_t, b_t = oracle.integer_inputs(m, n, k, seed=11)
+    c = run(a_t.cuda(), b_for(layout, b_t.cuda()), layout)
+    np.testing.assert_array_equal(bits_of(c), oracle.torch_bits(oracle.torch_reference(a_t, b_t)))
+    a_t, b_t = oracle.randn_inputs(m, n, k, seed=12, b_layout=layout)
+    first = run(a_t.cuda(), b_t.cuda(), layout)
+    second = run(a_t.cuda(), b_t.cuda(), layout)
+    assert torch.equal(first.view(torch.int16), second.view(torch.int16))
+    ref32 = oracle.torch_bits(oracle.torch_reference(a_t, b_t, layout))
+    ref64, mag = oracle.fp64_reference(a_t, b_t, layout)
+    report = oracle.parity_report(bits_of(first), ref32, ref64, mag, k)
     assert report["passed"], report
 
 

@@ -119,9 +119,19 @@ def test_select_config_splits_k_for_skinny_shapes():
     # 32 pair tiles over a long K: the pair schedule in two K splits.
     pair_split = km.select_config(4096, 512, 16384, km.B_ROW)
     assert (pair_split.tile_m, pair_split.tile_k, pair_split.stages, pair_split.k_splits) == (256, 64, 6, 2)
-    assert km.select_config(256, 8192, 8192, km.B_ROW).k_splits == 2
+    # 19-24 pair tiles over a long K: three K splits of the pair tiles.
+    three = km.select_config(768, 2048, 8192, km.B_ROW)
+    assert (three.tile_m, three.tile_k, three.stages, three.k_splits) == (256, 64, 6, 3)
+    assert km.select_config(768, 2048, 4096, km.B_ROW).k_splits == 0  # K = 4096: unsplit
+    # ... with more than two tile columns, one CTA per 128 x 256 tile in two K
+    # splits added up across a 2-CTA cluster instead.
+    wide_split = km.select_config(256, 8192, 8192, km.B_ROW)
+    assert (wide_split.tile_m, wide_split.tile_n, wide_split.tile_k, wide_split.stages, wide_split.k_splits) == \
+        (128, 256, 64, 4, 2)
+    assert wide_split.flags & scatter == scatter and wide_split.flags & _native.FLAG_B_EVICT_FIRST
+    assert _native.plan(wide_split, 256, 8192, 8192, km.B_ROW)["split_reduce"] == _native.SPLIT_SCATTER
     # One or two rows of pair tiles: B streams at evict-first priority; more: not.
-    for shape in ((256, 8192, 8192), (256, 16384, 4096), (200, 28672, 8192), (512, 16384, 4096)):
+    for shape in ((256, 16384, 4096), (200, 28672, 8192), (512, 16384, 4096)):
         sel = km.select_config(*shape, km.B_ROW)
         assert sel.tile_m == 256 and sel.flags & _native.FLAG_B_EVICT_FIRST, shape
     assert not km.select_config(1024, 16384, 4096, km.B_ROW).flags & _native.FLAG_B_EVICT_FIRST
