@@ -170,8 +170,9 @@ int kmcts_default_config(kmcts_gemm_config* cfg);
  * (KMCTS_FLAG_SPLIT_CLUSTER; KMCTS_FLAG_SPLIT_SCATTER except for two splits
  * of tile_m 32), as many as keep every cluster resident (at most 8); else the default when its
  * 256 x 256 pair tiles fill the co-resident CTA pairs (with 64-deep stages when
- * K <= 768), or in two K splits when those fill three quarters of them and
- * K >= 8192; else one CTA per
+ * K <= 768), or in two (three) K splits when those fill three quarters of them
+ * and K >= 8192 (two splits with more than two tile columns as one CTA per
+ * 128 x 256 tile, scatter); else one CTA per
  * 128 x 256 tile while those fill them (the default again from K = 4096),
  * else one CTA per 128 x 128 tile.  Few tiles over a long K get split K: for
  * M > 64 as scatter clusters (KMCTS_FLAG_SPLIT_SCATTER) of as many splits as
