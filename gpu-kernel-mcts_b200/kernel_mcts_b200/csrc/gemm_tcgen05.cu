@@ -252,7 +252,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             ptx::mbar_init(&tmem_empty[a], kEpilogueWarps);
         }
         ptx::mbar_init(drain, 1);
-        // Every lane of every epilogue warp of each sending rank arrives once.
+        // Gather: every lane of every epilogue warp of each sending rank
+        // arrives once.  Scatter: one arrival (below), then the copies' bytes.
         uint32_t recv_count = 1;
         if (cluster_mode && !kScatter) recv_count = static_cast<uint32_t>((splits - 1) * kEpilogueWarps * 32);
         ptx::mbar_init(recv_full, recv_count);
@@ -417,8 +418,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // One unit per CTA.  Write the pieces of this warp's quarter
                 // that other ranks own into this CTA's stages (free: every
                 // UMMA has completed and the unit's loads were all consumed),
-                // meet the cluster (every rank's stages are then free and its
-                // pieces written), copy each piece into its owner's stages,
+                // copy each into its owner's receive slots (in stages mode
+                // after the cluster meets, when every rank's stages are free),
                 // then add the own pieces' values in split order.
                 constexpr int kChunks = BN / 64;
                 float4* parts = reinterpret_cast<float4*>(smem);  // piece p at p * 512 float4

@@ -224,3 +224,26 @@ def test_bad_arguments_rejected_without_gpu_work():
     assert lib.kmcts_bf16_gemm_ex(None, None, None, 4, 4, 4, 7, None, None, None) == _native.KMCTS_EINVAL
     assert lib.kmcts_bf16_gemm_ex(None, None, None, 4, 4, 4, 0, None, None, None) == _native.KMCTS_EINVAL
     assert lib.kmcts_default_config(None) == _native.KMCTS_EINVAL
+
+
+@pytest.mark.parametrize("tile_m,tile_n,tile_k,stages,splits,reduce,extra", [
+    # 128 x 64-deep x 4 stages (162 KB own): received copies fit past it.
+    (128, 128, 64, 4, 8, _native.SPLIT_SCATTER, 7 * 8192),       # one piece per rank, 7 copies
+    (128, 128, 64, 4, 5, _native.SPLIT_SCATTER, 2 * 4 * 8192),   # two pieces for rank 0
+    (128, 128, 64, 4, 6, _native.SPLIT_WORKSPACE, 0),            # neither a buffer nor the stages hold them
+    # 128 x 128-deep x 3 stages (226 KB own): received in the stages.
+    (128, 128, 128, 3, 6, _native.SPLIT_SCATTER, 0),
+    # 32-row tiles: 2 pieces, splits past them only send.
+    (32, 128, 128, 4, 6, _native.SPLIT_SCATTER, 1 * 5 * 8192),
+])
+def test_scatter_receive_placement(tile_m, tile_n, tile_k, stages, splits, reduce, extra):
+    """Where a scatter split's copies land: a buffer past the schedule's own
+    shared memory when that fits 227 KB (the plan adds its size), else the
+    stages past the outgoing pieces, else no cluster split at all."""
+    m = 32 if tile_m == 32 else 512
+    cfg = km.make_config(tile_m=tile_m, cluster_m=1, tile_n=tile_n, tile_k=tile_k, stages=stages, k_splits=splits,
+                         flags=_native.FLAG_SPLIT_CLUSTER | _native.FLAG_SPLIT_SCATTER)
+    plan = _native.plan(cfg, m, 512, 8192, km.B_ROW)
+    assert plan["split_reduce"] == reduce, plan
+    assert plan["smem_bytes"] == km.config_smem_bytes(cfg) + extra, plan
+
