@@ -814,15 +814,59 @@ __global__ void __launch_bounds__(pair_threads<SLOTS>(), 1)
                 if (lane == 0) order = arrive_counted(counter, tail.epoch);
                 if (__shfl_sync(0xffffffffu, order, 0) == tail.splits - 1) {
                     __threadfence();
+                    // In the cluster's last unit the stages are free (every
+                    // MMA done, no TMA load left): each chunk's partials of
+                    // every split come on chip by bulk loads, the next chunk's
+                    // in flight while this one is added, instead of one
+                    // dependent L2 round trip per split and chunk.
+                    constexpr int kWarpStageBytes = L::kStagingOffset / kEpilogueWarps;
+                    const int set_bytes = tail.splits * 8192;  // one chunk of every split
+                    const bool on_chip = u == num_units - 1 && 2 * set_bytes <= kWarpStageBytes;
+                    uint8_t* wbuf = smem + (warp - 2) * kWarpStageBytes;
+                    auto fetch = [&](int c) {
+                        if (lane == 0) {
+                            uint8_t* dst = wbuf + (c & 1) * set_bytes;
+                            ptx::mbar_arrive_expect_tx(&partial_full[warp - 2], static_cast<uint32_t>(set_bytes));
+                            for (int j = 0; j < tail.splits; ++j)
+                                ptx::bulk_load(dst + j * 8192,
+                                               split_partial_chunk<BN>(tail, w.tile, j, static_cast<int>(rank), quarter, c),
+                                               8192u, &partial_full[warp - 2]);
+                        }
+                    };
+                    if (on_chip) {
+                        if (lane == 0) ptx::fence_proxy_async_global();  // the partials were written by generic stores
+                        fetch(0);
+                    }
+                    uint32_t set_phase = 0;
+                    bool fine = true;
 #pragma unroll 1
-                    for (int c = 0; c < chunks; ++c) {
+                    for (int c = 0; c < chunks && fine; ++c) {
                         float sum[64];
+                        const float4* set = nullptr;
+                        if (on_chip) {
+                            fine = __all_sync(0xffffffffu,
+                                              ptx::mbar_wait(&partial_full[warp - 2], set_phase, limit_ns, abort));
+                            set_phase ^= 1u;
+                            if (!fine) {
+                                if (lane == 0) record_failure(status, abort, kRoleEpilogue);
+                                break;
+                            }
+                            if (c + 1 < chunks) {
+                                // The other buffer was last read for chunk c - 1.
+                                ptx::fence_proxy_async_smem();
+                                __syncwarp();
+                                fetch(c + 1);
+                            }
+                            set = reinterpret_cast<const float4*>(wbuf + (c & 1) * set_bytes);
+                        }
 #pragma unroll 1
                         for (int j = 0; j < tail.splits; ++j) {
-                            const float4* part = split_partial_chunk<BN>(tail, w.tile, j, static_cast<int>(rank), quarter, c);
+                            const float4* part =
+                                on_chip ? set + j * 512
+                                        : split_partial_chunk<BN>(tail, w.tile, j, static_cast<int>(rank), quarter, c);
 #pragma unroll
                             for (int q = 0; q < 16; ++q) {
-                                const float4 f = __ldcg(part + q * 32 + lane);
+                                const float4 f = on_chip ? part[q * 32 + lane] : __ldcg(part + q * 32 + lane);
                                 if (j == 0) {
                                     sum[4 * q] = f.x;
                                     sum[4 * q + 1] = f.y;
@@ -846,7 +890,7 @@ __global__ void __launch_bounds__(pair_threads<SLOTS>(), 1)
                                     m0 + quarter * 32, ALLGATHER ? peers.map : nullptr, ALLGATHER ? peers.count : 0);
                     }
                     __syncwarp();
-                    if (lane == 0) *counter = 0ull;  // every unit of the tile has arrived: clear for replays
+                    if (fine && lane == 0) *counter = 0ull;  // every unit of the tile has arrived: clear for replays
                 }
             }
             if (split) {

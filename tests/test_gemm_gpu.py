@@ -582,12 +582,16 @@ def test_cta_pair_split_k_persistent_round_robin_bit_exact(cuda_device, layout):
 
 
 @pytest.mark.parametrize("layout", ["col", "row"])
-def test_cta_pair_split_k_randn_within_criterion_and_deterministic(cuda_device, layout):
+@pytest.mark.parametrize("splits", [2, 3, 4])
+def test_cta_pair_split_k_randn_within_criterion_and_deterministic(cuda_device, layout, splits):
+    """Two or three splits: the last unit brings the partials on chip by bulk
+    loads (its stages are free); four: it reads them from L2.  Either way the
+    same split order, deterministic, within the criterion."""
     m, n, k = 512, 1024, 8192
     a_t, b_t = oracle.randn_inputs(m, n, k, seed=8, b_layout=layout)
     a, b = a_t.cuda(), b_t.cuda()
-    c = run(a, b, layout, k_splits=4, **PAIR_128K)
-    again = run(a, b, layout, k_splits=4, **PAIR_128K)
+    c = run(a, b, layout, k_splits=splits, **PAIR_128K)
+    again = run(a, b, layout, k_splits=splits, **PAIR_128K)
     assert torch.equal(c.view(torch.int16), again.view(torch.int16))  # fixed split order
     whole = run(a, b, layout, **PAIR_128K)
     ref64, mag = oracle.fp64_reference(a_t, b_t, layout)
