@@ -134,6 +134,11 @@ bool scatter_schedule(long long tiles, int K, int b_layout, int sms, kmcts_gemm_
     if (s > max_by_k) s = max_by_k;
     for (; s >= 2; --s) {
         if (s == 2 && K < 4096) break;
+        // Where eight clusters' worth do not fit (16-24 tiles), five splits
+        // beat six (L2 flushed, means of 120: 512 x 512 x 8192 20.6 us
+        // against 21.0, 256 x 1024 x 8192 21.0 against 22.1, 128 x 2048 x 8192
+        // 21.9 against 22.9).
+        if (s == 6 || s == 7) continue;
         kmcts_gemm_config c = *cfg;
         c.tile_m = 128;
         c.tile_n = 128;
