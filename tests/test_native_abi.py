@@ -248,3 +248,32 @@ def test_scatter_receive_placement(tile_m, tile_n, tile_k, stages, splits, reduc
     assert plan["split_reduce"] == reduce, plan
     assert plan["smem_bytes"] == km.config_smem_bytes(cfg) + extra, plan
 
+
+
+def test_selection_properties_over_a_shape_grid():
+    """Over a grid of shapes (148 SMs and the B200 cluster capacities assumed
+    without a GPU): every selected schedule is legal, a cluster split keeps
+    every cluster resident with one unit per SM and at most 8 splits, and a
+    workspace split never asks for more than 16."""
+    dims_m = (1, 16, 33, 64, 100, 128, 200, 256, 384, 512, 768, 1024, 2048, 4096)
+    dims_n = (128, 256, 512, 1000, 1024, 2048, 4096, 8192, 16384)
+    dims_k = (256, 1024, 2048, 4096, 8192, 16384, 32768)
+    checked = 0
+    for m in dims_m:
+        for n in dims_n:
+            for k in dims_k:
+                cfg = km.select_config(m, n, k, km.B_ROW)
+                code, why = _native.config_legal(cfg, m, n, k, km.B_ROW)
+                assert code == _native.KMCTS_OK, (m, n, k, why)
+                checked += 1
+                if cfg.tile_m == 256:
+                    continue  # a pair's plan asks the occupancy calculator: it needs a device
+                plan = _native.plan(cfg, m, n, k, km.B_ROW)
+                if plan["cluster_size"] > 1 and cfg.tile_m != 256:
+                    assert cfg.flags & _native.FLAG_SPLIT_CLUSTER, (m, n, k)
+                    assert 2 <= plan["k_splits"] <= 8 and plan["cluster_size"] == plan["k_splits"], (m, n, k, plan)
+                    assert plan["ctas"] <= 148 and plan["tiles"] <= plan["workers"], (m, n, k, plan)
+                    assert plan["split_reduce"] in (_native.SPLIT_CLUSTER, _native.SPLIT_SCATTER), (m, n, k, plan)
+                else:
+                    assert plan["k_splits"] <= 16, (m, n, k, plan)
+    assert checked == len(dims_m) * len(dims_n) * len(dims_k)
